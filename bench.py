@@ -1,0 +1,362 @@
+"""Benchmark: hierarchical byte-model training step (fwd + bwd + AdamW) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: launched by torch.distributed.run, one rank per GPU, NCCL)
+
+Workload ("C3"): per GPU batch 8 x 4096 Zipf(1.1) bytes, patch 8;
+local encoder/decoder d256 x 2 layers each (4 heads, window 128, SwiGLU 768); global d768 x 8
+layers, HQ12/HK4, SwiGLU 2048; bf16 with f32 accumulation; AdamW.  Data-parallel: each rank
+trains its own batch, gradients summed over NCCL (weak scaling).
+
+Metric: bytes/s of the whole job (BASELINE metric "train ms/step & bytes/s", the unit of
+crates/sejong-cli/src/benchmark.rs:325).  `value` times K graph replays with the K batches
+already resident in HBM; `e2e` times the same K steps through the public API with each
+step's bytes copied from pinned host memory and the loss read back.  Both are CUDA-event
+times on the launching stream, barrier + synchronize on both sides, max over ranks.  The
+per-step working set (several GB of activations) exceeds the 126 MB L2, so no flush runs.
+
+`roofline` covers the dominant kernel family (timed live with CUDA events in an extra eager
+step); `cpu_baseline` times the CPU restatement in oracle/ (PyTorch fp32, all host threads)
+on a bounded sample of the same workload (rank 0, N = 1 only).
+`--impl reference` times that CPU restatement alone (the reference itself has no CPU path and
+its Rust/HIP host cannot be built here).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "train_bytes_per_s"
+UNIT = "bytes/s"
+CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ = 1, 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=8, help="per-GPU batch")
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-timing", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm": p["hbm_gbs"], "bf16": p["bf16_tflops"], "bf16_sustained": p["bf16_tflops_sustained"],
+                "source": "measured"}
+    except Exception:
+        return {"hbm": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": float(rows[0][2]) if rows else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- CPU restatement (oracle) timing
+def cpu_step_rate(steps, warmup, threads=None):
+    """bytes/s of the oracle's fp32 CPU training step on the bounded C3 sample."""
+    import numpy as np
+    import torch
+
+    from oracle import model as omodel
+    from oracle.corpus import synthetic_corpus
+    from oracle.rng import Rng
+    if threads:
+        torch.set_num_threads(threads)
+    c = omodel.config_c3()
+    params = omodel.initialize(c)
+    corp = synthetic_corpus(1000, 1 << 20)
+    rng = Rng(123)
+    state = omodel.AdamState()
+    tc = omodel.TrainConfig(sequence=CPU_SAMPLE_SEQ, batch=CPU_SAMPLE_BATCH)
+    times = []
+    for i in range(warmup + steps):
+        ids, tg = corp.batch(rng, CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ)
+        t0 = time.perf_counter()
+        loss, grads = omodel.loss_and_grads(params, c, ids, tg, CPU_SAMPLE_SEQ, dtype=torch.float32)
+        params, _ = omodel.adam_update(params, grads, state, tc)
+        params = {k: np.asarray(v, dtype=np.float32) for k, v in params.items()}
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    return CPU_SAMPLE_BATCH * CPU_SAMPLE_SEQ / sec, sec, torch.get_num_threads()
+
+
+def cpu_sample_text(steps):
+    return (f"C3 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
+            f"fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps")
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps, warmup = max(1, min(args.steps, 10)), max(0, min(args.warmup, 2))
+    rate, sec, cores = cpu_step_rate(steps, warmup)
+    line = {"metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
+            "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic Zipf(1.1) bytes, random-init N(0,0.02) weights",
+            "config": {"workload": "C3 hierarchical byte model fwd+bwd+AdamW (bounded CPU sample)",
+                       "per_gpu_batch": CPU_SAMPLE_BATCH, "seq_len": CPU_SAMPLE_SEQ, "parallelism": "none"},
+            "impl": "reference",
+            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": cpu_sample_text(steps)},
+            "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference has no CPU execution path (Engine::new needs HIP) and its Rust host cannot "
+                    "be built in this image; this arm times the CPU restatement of its step in oracle/"}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def kernel_timing(trainer):
+    """One eager step with CUDA events around every C-ABI call: per-family time and FLOPs."""
+    import torch
+    stream = torch.cuda.current_stream()
+    records = []
+    original = trainer._call
+
+    def timed(name, *a):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        original(name, *a)
+        e.record(stream)
+        flops = 2.0 * a[9] * a[10] * a[11] if name == "sj_gemm" else 0.0
+        records.append((name, s, e, flops))
+
+    trainer._call = timed
+    try:
+        trainer.step()
+    finally:
+        trainer._call = original
+    torch.cuda.synchronize()
+    fam = {}
+    for name, s, e, flops in records:
+        ms = s.elapsed_time(e)
+        f = fam.setdefault(name, {"ms": 0.0, "calls": 0, "flops": 0.0})
+        f["ms"] += ms
+        f["calls"] += 1
+        f["flops"] += flops
+    return fam
+
+
+def run_ours(args):
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from sejong_b200 import model as pm
+    from sejong_b200.train import ByteTrainer, TrainConfig, corpus_batch, synthetic_corpus_tokens
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        pg = dist.group.WORLD
+    cfg = pm.config_c3()
+    tc = TrainConfig(sequence=args.seq, batch=args.batch, warmup_steps=0, steps=10000)
+    trainer = ByteTrainer(cfg, tc, device=local, process_group=pg)
+    rows = tc.batch * tc.sequence
+    total = args.warmup + args.steps
+    toks = synthetic_corpus_tokens(1000 + rank, 1 << 22)
+    st = ctypes.c_uint64(123 + rank)
+    host_ids = torch.empty(total, rows, dtype=torch.int32).pin_memory()
+    host_tg = torch.empty(total, rows, dtype=torch.int32).pin_memory()
+    for i in range(total):
+        x, y = corpus_batch(toks, st, tc.batch, tc.sequence)
+        host_ids[i].copy_(torch.from_numpy(x))
+        host_tg[i].copy_(torch.from_numpy(y))
+    dev_ids = host_ids.to(trainer.dev)
+    dev_tg = host_tg.to(trainer.dev)
+    loss_host = torch.zeros(total, dtype=torch.float64).pin_memory()
+
+    trainer.stage_batch(dev_ids[0], dev_tg[0])
+    trainer.step()  # eager first step: sets kernel attributes, checks the path runs
+    torch.cuda.synchronize()
+    trainer.capture()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=trainer.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(args.warmup):
+        trainer.ids.copy_(host_ids[i], non_blocking=True)
+        trainer.targets.copy_(host_tg[i], non_blocking=True)
+        trainer.replay()
+        loss_host[i].copy_(trainer.loss_sum[0], non_blocking=True)
+    barrier()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    # device-resident inputs
+    launches_before = trainer.launches
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.warmup, total):
+        trainer.ids.copy_(dev_ids[i])
+        trainer.targets.copy_(dev_tg[i])
+        trainer.replay()
+    t1.record(stream)
+    barrier()
+    dev_ms = max_over_ranks(t0.elapsed_time(t1))
+    # end to end through the public API: H2D of the step's bytes, D2H of its loss
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for i in range(args.warmup, total):
+        trainer.ids.copy_(host_ids[i], non_blocking=True)
+        trainer.targets.copy_(host_tg[i], non_blocking=True)
+        trainer.replay()
+        loss_host[i].copy_(trainer.loss_sum[0], non_blocking=True)
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    assert trainer.device_error() == 0, "device error word set during the benchmark"
+    losses = loss_host.numpy()
+    assert np.all(np.isfinite(losses)), "non-finite loss"
+
+    per_step_launches = sum(trainer.KERNELS.get(n, 1) for n in _call_names(trainer))
+    fam = {} if args.no_kernel_timing else kernel_timing(trainer)
+    if world > 1:
+        trainer.release_graphs()
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    K = args.steps
+    ms = dev_ms / K
+    global_bytes = rows * world
+    value = global_bytes / (ms / 1e3)
+    e2e_value = global_bytes / ((e2e_ms / K) / 1e3)
+    pk = peaks()
+    step_flops = trainer.step_flops()
+    tensor_frac = step_flops / (ms / 1e3) / (pk["bf16_sustained"] * 1e12)
+    roofline = None
+    if fam:
+        g = fam.get("sj_gemm")
+        if g and g["ms"] > 0:
+            achieved = g["flops"] / (g["ms"] / 1e3) / 1e12
+            roofline = {"bound": "tensor", "kernel": "gemm_tcgen05 (all GEMMs of one step)",
+                        "achieved": achieved, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                        "frac": achieved / pk["bf16_sustained"], "peak_source": pk["source"] + " sustained bf16",
+                        "traffic": None, "launches": g["calls"], "ms_per_step": g["ms"]}
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: Zipf(1.1) bytes from the reference Rng (seed 1000+rank); random-init N(0,0.02) weights",
+        "config": {"workload": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
+                   "model": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
+                   "global_batch": tc.batch * world, "per_gpu_batch": tc.batch, "seq_len": tc.sequence,
+                   "parallelism": f"dp{world}", "l2": "per-step working set of several GB > 126 MB L2; no flush"},
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * rows * 4, "d2h_bytes_per_step": 8},
+        "gpu_launches": per_step_launches * K,
+        "roofline": roofline,
+        "tensor_frac_of_step": tensor_frac,
+        "step_tflop": step_flops / 1e12,
+        "loss_first_last": [float(losses[0]), float(losses[-1])],
+    }
+    if clk:
+        line["clocks"] = clk
+    if fam:
+        line["kernel_ms_per_step"] = {k.replace("sj_", ""): round(v["ms"], 4) for k, v in sorted(fam.items())}
+    if world == 1 and not args.no_cpu_baseline:
+        rate, _, cores = cpu_step_rate(2, 1)
+        line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+                                "sample": cpu_sample_text(2)}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def _call_names(trainer):
+    """Names of the C-ABI calls one step makes (recorded without launching anything)."""
+    names = []
+    original = trainer._call
+    trainer._call = lambda name, *a: names.append(name)
+    try:
+        trainer.step()
+    finally:
+        trainer._call = original
+    return names
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,198 @@
+/*
+ * sejong.h — C ABI of libsejong_b200.so, the sm_100a (B200) replacement for the
+ * GPU operations of Sejong's byte / NativeValue Transformer training step.
+ *
+ * The reference reaches its kernels through Rust `Engine` methods that all end
+ * in `Engine::launch(name, args, constants, grid)` (crates/sejong-gpu/src/lib.rs:
+ * 366-487).  Each function below is the C-ABI form of one of those methods (or of a
+ * fused group of them); the comment on each names the reference method and
+ * kernel it replaces (file:line, paths relative to the reference project).
+ *
+ * Conventions
+ *  - Plain device pointers, element counts and leading dimensions (in elements);
+ *    matrices are row-major.  The caller owns every buffer; the library never
+ *    allocates or frees caller memory.  Scratch ("workspace") is passed in.
+ *  - Every call takes the `cudaStream_t` to launch on as `void* stream` and does
+ *    not synchronise.
+ *  - Return value: SJ_OK (0) or one of the SJ_ERR_* codes; `sj_last_error()`
+ *    returns a thread-local message for the last failing call on this thread
+ *    (mirrors sejong_core::Error, crates/sejong-core/src/lib.rs:8-25).
+ *  - Device-side failures (a bounded wait that expired) never trap: the kernel
+ *    writes a code into a device error word and returns; `sj_device_error()`
+ *    reads (and optionally clears) it.
+ */
+#ifndef SEJONG_B200_H
+#define SEJONG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum {
+  SJ_OK = 0,
+  SJ_ERR_SHAPE = 1,       /* shape / dimension mismatch (reference: Error::Message from ensure) */
+  SJ_ERR_CAPACITY = 2,    /* not enough device memory / workspace (Error::Capacity) */
+  SJ_ERR_CUDA = 3,        /* a CUDA runtime or driver call failed */
+  SJ_ERR_NCCL = 4,        /* a collective failed */
+  SJ_ERR_TIMEOUT = 5,     /* a bounded device-side wait expired */
+  SJ_ERR_ARGUMENT = 6,    /* bad pointer alignment, dtype or flag */
+  SJ_ERR_UNSUPPORTED = 7  /* valid request this build does not implement */
+};
+
+/* dtype codes: the reference's DType discriminants (crates/sejong-core/src/lib.rs:34-41) plus bf16 */
+enum { SJ_F32 = 0, SJ_F64 = 1, SJ_F16 = 2, SJ_I32 = 3, SJ_BF16 = 4 };
+
+/* device error codes written by kernels */
+enum {
+  SJ_DEV_GEMM_PRODUCER_WAIT = 101,
+  SJ_DEV_GEMM_MMA_WAIT = 102,
+  SJ_DEV_GEMM_EPILOGUE_WAIT = 103,
+  SJ_DEV_GEMM_DRAIN_WAIT = 104,
+  SJ_DEV_BAD_INDEX = 110
+};
+
+int sj_version(void);
+const char* sj_last_error(void);
+/* Initialise `device` (make current, resolve cuTensorMapEncodeTiled, set kernel
+ * shared-memory limits).  Replaces Engine::new's device setup
+ * (crates/sejong-gpu/src/lib.rs:197-233, hip.rs:126-178). */
+int sj_device_init(int device);
+/* Free / total device memory: the budget source of the reference allocator and
+ * batch planner (crates/sejong-gpu/src/hip.rs:154-160,182-194). */
+int sj_mem_info(size_t* free_bytes, size_t* total_bytes);
+/* Read the device error word; clear it when `clear` != 0.  Synchronises `stream`. */
+int sj_device_error(int* code, int clear, void* stream);
+/* Zero `bytes` bytes at `ptr` on `stream` (Engine::full(.., 0), crates/sejong-gpu/src/lib.rs:544-553). */
+int sj_zero(void* ptr, size_t bytes, void* stream);
+
+/* ------------------------------------------------------------------ host: RNG and bytes (bit-exact) */
+/* Rng::next_u64 (crates/sejong-core/src/lib.rs:599-605). */
+uint64_t sj_rng_next_u64(uint64_t* state);
+/* Rng::index (lib.rs:609-618). */
+uint64_t sj_rng_index(uint64_t* state, uint64_t size);
+/* n draws of Rng::normal (lib.rs:619-621) times `scale`, f32 arithmetic. */
+int sj_rng_normal_fill(uint64_t* state, float* out, size_t n, float scale);
+/* Synthetic document: n bytes i.i.d. Zipf(s) over 0..255 by inverse CDF of Rng::uniform. */
+int sj_zipf_bytes(uint64_t seed, double s, uint8_t* out, size_t n);
+/* Corpus::batch (crates/sejong-train/src/lib.rs:72-88) over the token stream
+ * `tokens` (EOS + bytes + ... + EOS, lib.rs:24-71). */
+int sj_corpus_batch(const int32_t* tokens, size_t n_tokens, uint64_t* rng_state, int batch, int sequence,
+                    int32_t* inputs, int32_t* targets);
+
+/* ------------------------------------------------------------------ GEMM (tcgen05 / TMEM / TMA) */
+/* Epilogues of sj_gemm. */
+enum {
+  SJ_EPI_STORE = 0,    /* C = alpha*acc                         (C bf16 or f32) */
+  SJ_EPI_ACCUM = 1,    /* C += alpha*acc                        (C f32; split-K allowed) */
+  SJ_EPI_RESIDUAL = 2, /* C = aux + alpha*acc                   (C, aux bf16, aux row stride ld_aux) */
+  SJ_EPI_SWIGLU = 3,   /* C = round(acc) (gate/up interleaved by 16 columns, bf16);
+                          aux = silu(g)*u  [M, N/2] bf16 with row stride ld_aux */
+  SJ_EPI_ROPE = 4      /* C = RoPE(acc) on columns < rope_cols (head dim 64, pairs 2i,2i+1,
+                          position = row mod rope_t), bf16 */
+};
+/* C[M,N] = op(A)[M,K] * op(B)[K,N], bf16 operands, f32 accumulation in TMEM.
+ * a_trans: A stored [K,M] (lda >= M) instead of [M,K]; b_trans: B stored [N,K]
+ * instead of [K,N] — the TA/TB flags of Engine::matmul (crates/sejong-gpu/src/
+ * lib.rs:594-649, kernel python/sejong_kernels/ops/kernels.py:23-39) and of the
+ * tape's backward rules dA = dY*B^T, dB = A^T*dY (crates/sejong-gpu/src/graph.rs:
+ * 817-853).  Also covers Engine::project_qkv (projection_ops.rs:6-43, with
+ * SJ_EPI_ROPE folding Engine::rope, lib.rs:734-758) and Engine::gate_up
+ * (projection_ops.rs:45-79, SJ_EPI_SWIGLU).  `split_k` > 1 is valid with
+ * SJ_EPI_ACCUM only.  Leading dimensions must be multiples of 8 elements and
+ * A/B 16-byte aligned (TMA). */
+int sj_gemm(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc, int c_dtype,
+            int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux, int rope_cols, int rope_t,
+            float rope_theta, int split_k, void* stream);
+
+/* ------------------------------------------------------------------ normalisation, embedding, elementwise */
+/* Engine::norm / rmsnorm (crates/sejong-gpu/src/lib.rs:688-699; kernels.py:54-61).
+ * x [rows,d] (x_dtype bf16 or f32), w f32 [d]; y bf16 [rows,d]; inv_rms f32 [rows] (optional). */
+int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* inv_rms, int rows, int d, float eps,
+                   void* stream);
+/* Engine::norm_backward (crates/sejong-gpu/src/norm_ops.rs:14-134; kernels.py:63-87) fused with the
+ * residual gradient accumulation of the tape (graph.rs:503-513):
+ *   dres[r,:] += rms_dx(x, w, dz) ;  dres_bf16 = bf16(dres) (optional) ;  dw += sum_r dz*x*inv.
+ * x bf16, dz f32, dres f32 (in/out), dw f32 accumulated.  `partials` is workspace of
+ * ceil(rows/64)*d floats. */
+int sj_rmsnorm_bwd(const void* x, const float* w, const float* inv_rms, const float* dz, float* dres,
+                   void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream);
+/* Engine::embedding (lib.rs:650-665; kernels.py:41-45): y[i,:] = w[ids[i],:], bf16. */
+int sj_embedding_fwd(const void* w, const int32_t* ids, void* y, int n, int d, void* stream);
+/* Engine::embedding_backward (lib.rs:666-687; kernels.py:47-52): dw[ids[i],:] += dy[i,:] (f32). */
+int sj_embedding_bwd(const float* dy, const int32_t* ids, float* dw, int n, int d, int vocab, void* stream);
+/* Engine::rope (lib.rs:734-758; kernels.py:103-113) standalone: x,y [rows, heads*hd] bf16. */
+int sj_rope(const void* x, void* y, int rows, int heads, int head_dim, int t, int offset, float theta, int inverse,
+            void* stream);
+/* Engine::swiglu_backward (lib.rs:711-733; kernels.py:95-101): gu [rows,2f] bf16 interleaved by 16
+ * columns (as written by SJ_EPI_SWIGLU), dh [rows,f] bf16 -> dgu [rows,2f] bf16 (same interleave). */
+int sj_swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, void* stream);
+/* Engine::patch_pool (crates/sejong-gpu/src/hierarchy_ops.rs:149-205; hierarchy.py:107-131). */
+int sj_patch_pool_fwd(const void* x, void* y, int batch, int t, int d, int patch, void* stream);
+/* dx[b,t,:] += dy[b, t/P, :] / count  (f32 accumulate) */
+int sj_patch_pool_bwd(const float* dy, float* dx, int batch, int t, int d, int patch, void* stream);
+/* Engine::patch_broadcast (hierarchy_ops.rs:207-278; hierarchy.py:134-172) fused with the tape add
+ * (architecture.rs:386-387):  y[b,t,:] (+)= t/P >= 1 ? z[b, t/P - 1, :] : bos[:]  (bf16, accumulate when add != 0). */
+int sj_patch_broadcast_fwd(const void* z, const void* bos, void* y, int add, int batch, int t, int d, int patch,
+                           void* stream);
+/* dz[b,p,:] = sum of dy over the bytes of patch p+1 ; dbos = sum of dy over the first patch of every row.
+ * dy f32; dz [batch*patches, d] and dbos [d] bf16 (both feed the global_to_decoder backward GEMMs). */
+int sj_patch_broadcast_bwd(const float* dy, void* dz, void* dbos, int batch, int t, int d, int patch, void* stream);
+/* Engine::cross_entropy + cross_entropy_backward + loss_summary (lib.rs:881-912, 524-543;
+ * kernels.py:176-191, 254-262), fused: loss[r] = lse(logits[r]) - logits[r,target];
+ * dlogits[r,:] = (softmax - onehot) * seed (bf16, columns vocab..ld_d zeroed);
+ * loss_sum[0] (f64) = sum_r loss[r] * weight. logits f32 [rows, ld] (first `vocab` columns used). */
+int sj_cross_entropy(const float* logits, int ld, const int32_t* targets, int rows, int vocab, float seed,
+                     float* loss_rows, void* dlogits, int ld_d, double* loss_sum, double weight, void* stream);
+/* cast between f32 / bf16 / f64 (Engine::cast, lib.rs:554-571) */
+int sj_cast(const void* x, int x_dtype, void* y, int y_dtype, size_t n, void* stream);
+/* y = x + alpha*z (Engine::add / add_into, lib.rs:572-593; kernels.py:16-21), f32 or bf16 */
+int sj_add(const void* x, const void* z, void* y, size_t n, float alpha, int dtype, void* stream);
+
+/* ------------------------------------------------------------------ attention (GQA, causal, window) */
+/* Engine::attention_grouped (crates/sejong-gpu/src/hierarchy_ops.rs:10-72; hierarchy.py:7-39).
+ * q [batch*t, hq*64], k/v [batch*t, hk*64] (row strides ldq/ldk/ldv), bf16;  o bf16 (ldo);
+ * lse f32 [batch*t*hq] natural log, index row*hq + head.  window 0 = full causal. */
+int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, void* o, int ldo,
+                    float* lse, int batch, int t, int hq, int hk, int head_dim, int window, void* stream);
+/* Engine::attention_grouped_backward (hierarchy_ops.rs:74-147; hierarchy.py:42-104).
+ * do bf16 (lddo); dq/dk/dv bf16 with their own strides; when rope_theta > 0 the inverse rotation
+ * of Engine::rope(.., inverse=true) (graph.rs:879-882) is applied to dq and dk before the store.
+ * `delta` is workspace f32 [batch*t*hq]. */
+int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o, int ldo,
+                    const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk, int lddk, void* dv,
+                    int lddv, float* delta, int batch, int t, int hq, int hk, int head_dim, int window,
+                    float rope_theta, void* stream);
+
+/* ------------------------------------------------------------------ optimizer */
+/* FP64 sum of squares of a flat f32 buffer into `partials` (f64, sj_sumsq_partials(n) entries):
+ * Engine::gradient_norm (crates/sejong-gpu/src/lib.rs:494-523; kernels.py:265-287). */
+int sj_sumsq_partials(size_t n);
+int sj_grad_sumsq(const float* g, size_t n, double* partials, void* stream);
+/* Device-side step bookkeeping for Adam::update (crates/sejong-train/src/lib.rs:199-238) and
+ * TrainConfig::lr (crates/sejong-core/src/lib.rs:422-433): reduces `partials` to the global norm,
+ * derives clip scale = (clip_enabled && norm > clip ? clip/norm : 1)/loss_scale, increments the step
+ * counter in state[0] and writes hyper = {lr(step-1), 1/(1-b1^step), 1/(1-b2^step), scale, norm}.
+ * `state` (f64[2]: step, last norm) and `hyper` (f32[8]) are device buffers so the step needs no
+ * host round trip and can be captured in a CUDA graph. */
+int sj_optim_prepare(const double* partials, int n_partials, double* state, float* hyper, float learning_rate,
+                     float min_learning_rate, int warmup_steps, int total_steps, float beta1, float beta2,
+                     float clip_norm, int clip_enabled, float loss_scale, void* stream);
+/* Multi-tensor AdamW over one flat parameter buffer (kernels.py:193-202 per element; the reference
+ * launches it once per tensor, lib.rs:925-957).  Elements [0, n_decay) get decoupled weight decay
+ * (rank>1 tensors), the rest none.  w/g/m/v f32; w_bf16 (optional) receives the bf16 copy used by the
+ * next forward (Model::bind's per-step cast, crates/sejong-model/src/lib.rs:206-219). */
+int sj_adamw(float* w, const float* g, float* m, float* v, void* w_bf16, size_t n, size_t n_decay,
+             const float* hyper, float beta1, float beta2, float eps, float weight_decay, void* stream);
+/* Plain SGD over a flat buffer (crates/sejong-train/src/control_variate.rs:775-799):
+ * w = w*(1 - lr*decay) - lr*scale*g with decay on [0, n_decay). */
+int sj_sgd(float* w, const float* g, void* w_bf16, size_t n, size_t n_decay, const float* hyper, float weight_decay,
+           void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SEJONG_B200_H */

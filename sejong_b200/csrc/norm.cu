@@ -1,0 +1,183 @@
+// RMSNorm forward and backward (warp per row, 16-byte vectors, two-level dw reduction without
+// atomics).  Restates python/sejong_kernels/ops/kernels.py:54-87 and the host autotuned pair
+// rmsnorm_backward_partial/_reduce (crates/sejong-gpu/src/norm_ops.rs:14-134); the backward is
+// fused with the residual-gradient accumulation the tape performs with separate `add` launches
+// (crates/sejong-gpu/src/graph.rs:503-513).
+#include "common.cuh"
+#include "internal.h"
+
+namespace sj {
+
+constexpr int kNormMaxVec = 4;  // 4 x 8 elements per lane: d <= 1024
+constexpr int kNormWarps = 8;
+constexpr int kNormRowsPerCta = 64;
+
+template <typename T>
+SJ_DEVICE void load8(const T* p, float (&v)[8]);
+template <>
+SJ_DEVICE void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 w = *reinterpret_cast<const uint4*>(p);
+  float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z), d = unpack_bf16x2(w.w);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y; v[4] = c.x; v[5] = c.y; v[6] = d.x; v[7] = d.y;
+}
+template <>
+SJ_DEVICE void load8<float>(const float* p, float (&v)[8]) {
+  float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+SJ_DEVICE void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 w;
+  w.x = pack_bf16x2(v[0], v[1]);
+  w.y = pack_bf16x2(v[2], v[3]);
+  w.z = pack_bf16x2(v[4], v[5]);
+  w.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = w;
+}
+
+template <typename T>
+__global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                                   float* __restrict__ inv_rms, int rows, int d, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const size_t base = static_cast<size_t>(warp) * d;
+  float v[kNormMaxVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int col = (lane + 32 * i) * 8;
+    if (col < d) {
+      load8<T>(x + base + col, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int col = (lane + 32 * i) * 8;
+    if (col < d) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * w[col + j];
+      store8_bf16(y + base + col, o);
+    }
+  }
+  if (inv_rms && lane == 0) inv_rms[warp] = inv;
+}
+
+// One CTA = kNormWarps warps over kNormRowsPerCta rows; per-CTA dw partial row in `partials`.
+__global__ void __launch_bounds__(kNormWarps * 32)
+    rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                       const float* __restrict__ inv_rms, const float* __restrict__ dz, float* __restrict__ dres,
+                       __nv_bfloat16* __restrict__ dres_bf16, float* __restrict__ partials, int rows, int d) {
+  __shared__ float red[kNormWarps][1024];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float dw_acc[kNormMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dw_acc[i][j] = 0.f;
+  const float inv_d = 1.0f / static_cast<float>(d);
+  for (int r = blockIdx.x * kNormRowsPerCta + warp; r < min(rows, (blockIdx.x + 1) * kNormRowsPerCta);
+       r += kNormWarps) {
+    const size_t base = static_cast<size_t>(r) * d;
+    float xv[kNormMaxVec][8], gv[kNormMaxVec][8];
+    float dot = 0.f;
+    const float inv = inv_rms[r];
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; ++i) {
+      const int col = (lane + 32 * i) * 8;
+      if (col < d) {
+        load8<__nv_bfloat16>(x + base + col, xv[i]);
+        float dzv[8];
+        load8<float>(dz + base + col, dzv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          gv[i][j] = dzv[j] * w[col + j];
+          dot += gv[i][j] * xv[i][j];
+          dw_acc[i][j] += dzv[j] * xv[i][j] * inv;
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    const float coef = dot * inv_d * inv * inv;
+#pragma unroll
+    for (int i = 0; i < kNormMaxVec; ++i) {
+      const int col = (lane + 32 * i) * 8;
+      if (col < d) {
+        float o[8];
+        load8<float>(dres + base + col, o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += inv * (gv[i][j] - xv[i][j] * coef);
+        float4* dst = reinterpret_cast<float4*>(dres + base + col);
+        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+        if (dres_bf16) store8_bf16(dres_bf16 + base + col, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kNormMaxVec; ++i) {
+    const int col = (lane + 32 * i) * 8;
+    if (col < d)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) red[warp][col + j] = dw_acc[i][j];
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < d; col += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormWarps; ++k) s += red[k][col];
+    partials[static_cast<size_t>(blockIdx.x) * d + col] = s;
+  }
+}
+
+__global__ void column_reduce_add_kernel(const float* __restrict__ partials, int groups, int d,
+                                         float* __restrict__ out) {
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  if (col >= d) return;
+  float s = 0.f;
+  for (int g = 0; g < groups; ++g) s += partials[static_cast<size_t>(g) * d + col];
+  out[col] += s;
+}
+
+}  // namespace sj
+
+extern "C" int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* inv_rms, int rows, int d,
+                              float eps, void* stream) {
+  using namespace sj;
+  if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
+    return fail(SJ_ERR_SHAPE, "sj_rmsnorm_fwd: d=%d must be a multiple of 8 up to 1024", d);
+  if (!aligned16(x) || !aligned16(y)) return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd: x/y must be 16-byte aligned");
+  const int threads = 256, warps = threads / 32;
+  const int grid = (rows + warps - 1) / warps;
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == SJ_BF16)
+    rmsnorm_fwd_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), w,
+                                                                static_cast<__nv_bfloat16*>(y), inv_rms, rows, d, eps);
+  else if (x_dtype == SJ_F32)
+    rmsnorm_fwd_kernel<float><<<grid, threads, 0, s>>>(static_cast<const float*>(x), w, static_cast<__nv_bfloat16*>(y),
+                                                        inv_rms, rows, d, eps);
+  else
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd: x must be bf16 or f32");
+  SJ_LAUNCH_CHECK("rmsnorm_fwd");
+  return SJ_OK;
+}
+
+extern "C" int sj_rmsnorm_bwd(const void* x, const float* w, const float* inv_rms, const float* dz, float* dres,
+                              void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream) {
+  using namespace sj;
+  if (rows <= 0 || d <= 0 || d % 8 || d > 1024) return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd: bad d=%d", d);
+  if (!x || !w || !inv_rms || !dz || !dres || !dw || !partials)
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: null pointer");
+  const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
+  cudaStream_t s = as_stream(stream);
+  rmsnorm_bwd_kernel<<<groups, kNormWarps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(x), w, inv_rms, dz, dres,
+                                                        static_cast<__nv_bfloat16*>(dres_bf16), partials, rows, d);
+  SJ_LAUNCH_CHECK("rmsnorm_bwd");
+  column_reduce_add_kernel<<<(d + 255) / 256, 256, 0, s>>>(partials, groups, d, dw);
+  SJ_LAUNCH_CHECK("rmsnorm_bwd reduce");
+  return SJ_OK;
+}

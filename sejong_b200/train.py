@@ -1,0 +1,507 @@
+"""The byte-Transformer training step on one B200: an explicit schedule of fused kernels.
+
+Replaces the reference's per-observation tape (crates/sejong-gpu/src/graph.rs:67-913)
+and training loops (crates/sejong-train/src/lib.rs:387-453, AdamW;
+control_variate.rs:767-799, plain SGD) for the dense and hierarchical byte models
+(crates/sejong-model/src/architecture.rs:201-393).  Instead of a tape of ~1,400
+small launches per step, the step is a fixed sequence of C-ABI calls
+(include/sejong.h) over buffers allocated once:
+
+  forward   embedding -> blocks [RMSNorm, QKV GEMM + RoPE epilogue, GQA attention,
+            Wo GEMM + residual epilogue, RMSNorm, gate/up GEMM + SwiGLU epilogue,
+            down GEMM + residual epilogue] -> (hierarchy: encoder norm, patch pool,
+            global blocks, broadcast, decoder blocks) -> final norm -> head GEMM (f32
+            logits) -> fused cross entropy (loss, dlogits)
+  backward  the same in reverse: weight gradients as TN GEMMs accumulating into one
+            flat f32 gradient buffer, input gradients as NT GEMMs, RMSNorm backward
+            fused with the residual-gradient add, attention backward with the inverse
+            RoPE in its dq/dk store
+  update    FP64 gradient norm -> device-side clip / LR / bias correction -> one
+            multi-tensor AdamW (or SGD) launch that also writes the bf16 weights the
+            next forward reads.
+
+Every activation is retained (the reference's "retain" mode); the step issues no
+host synchronisation, so it can be captured in a CUDA graph (`capture`).
+Precision: bf16 weights and activations, f32 accumulation, f32 gradients, master
+weights and moments, FP64 loss and gradient norm.
+"""
+import ctypes
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import (EPI_ACCUM, EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call)
+from .model import HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage
+
+
+@dataclass
+class TrainConfig:
+    """sejong_core::TrainConfig fields used by the step (crates/sejong-core/src/lib.rs:308-434)."""
+    sequence: int
+    batch: int
+    optimizer: str = "adamw"          # "adamw" | "sgd"
+    learning_rate: float = 3e-4
+    min_learning_rate: float = 3e-5
+    warmup_steps: int = 0
+    steps: int = 10000
+    beta1: float = 0.9
+    beta2: float = 0.95
+    epsilon: float = 1e-8
+    weight_decay: float = 0.1
+    clip_norm: float = 1.0
+    clip_enabled: bool = True
+    loss_scale: float = 1.0
+    seed: int = 123
+
+
+def _ptr(t, offset_elems=0):
+    return t.data_ptr() + offset_elems * t.element_size()
+
+
+class _StageRun:
+    """Activation and gradient buffers of one stage (encoder, global or decoder)."""
+
+    def __init__(self, stage, batch, seq, dev):
+        self.stage, self.batch, self.seq = stage, batch, seq
+        n, d, f, cq = batch * seq, stage.width, stage.ffn, stage.qkv_width
+        self.rows = n
+        bf, f32 = torch.bfloat16, torch.float32
+        e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
+        self.x = [e(n, d) for _ in range(stage.layers + 1)]   # block inputs; x[L] is the stage output
+        self.layers = []
+        for _ in range(stage.layers):
+            self.layers.append(dict(z1=e(n, d), inv1=e(n, dt=f32), qkv=e(n, cq), o=e(n, d),
+                                    lse=e(n * stage.heads, dt=f32), x1=e(n, d), z2=e(n, d), inv2=e(n, dt=f32),
+                                    gu=e(n, 2 * f), h=e(n, f)))
+        # backward workspace
+        self.dx = e(n, d, dt=f32)
+        self.dxb = e(n, d)
+        self.dz = e(n, d, dt=f32)
+        self.dh = e(n, f)
+        self.dgu = e(n, 2 * f)
+        self.do = e(n, d)
+        self.dqkv = e(n, cq)
+        self.delta = e(n * stage.heads, dt=f32)
+        self.partials = e(((n + 63) // 64) * d, dt=f32)
+
+
+class ByteTrainer:
+    """One data-parallel replica of the byte-model training step on the current CUDA device."""
+
+    def __init__(self, config, train, device=None, params=None, process_group=None):
+        self.c, self.tc = config, train
+        self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        torch.cuda.set_device(self.dev)
+        self.lib = _lib.load()
+        call("sj_device_init", self.dev.index)
+        self.pg = process_group
+        self.world = torch.distributed.get_world_size(process_group) if process_group is not None else 1
+        self.layout = FlatLayout(config)
+        if params is None:
+            params = initialize(config, self.lib)
+        total = self.layout.total
+        f32 = torch.float32
+        self.w = torch.from_numpy(self.layout.pack(params)).to(self.dev)
+        self.wb = torch.empty(total, dtype=torch.bfloat16, device=self.dev)
+        self.g = torch.zeros(total, dtype=f32, device=self.dev)
+        self.m = torch.zeros(total, dtype=f32, device=self.dev)
+        self.v = torch.zeros(total, dtype=f32, device=self.dev)
+        self.n_partials = self.lib.sj_sumsq_partials(total)
+        self.partials = torch.zeros(self.n_partials, dtype=torch.float64, device=self.dev)
+        self.opt_state = torch.zeros(2, dtype=torch.float64, device=self.dev)
+        self.hyper = torch.zeros(8, dtype=f32, device=self.dev)
+        self.loss_sum = torch.zeros(1, dtype=torch.float64, device=self.dev)
+        self.stream = torch.cuda.current_stream(self.dev).cuda_stream
+        call("sj_cast", _ptr(self.w), SJ_F32, _ptr(self.wb), SJ_BF16, total, self.stream)
+
+        b, t = train.batch, train.sequence
+        self.rows = b * t
+        h = config.hierarchy
+        bf = torch.bfloat16
+        e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=self.dev)  # noqa: E731
+        self.ids = torch.zeros(self.rows, dtype=torch.int32, device=self.dev)
+        self.targets = torch.zeros(self.rows, dtype=torch.int32, device=self.dev)
+        if h is None:
+            self.runs = {"global": _StageRun(global_stage(config), b, t, self.dev)}
+            top_width = config.width
+        else:
+            assert t % h.patch_size == 0, "sequence must be a multiple of the patch size"
+            self.patches = t // h.patch_size
+            self.runs = {"encoder": _StageRun(local_stage(config, True), b, t, self.dev),
+                         "global": _StageRun(global_stage(config), b, self.patches, self.dev),
+                         "decoder": _StageRun(local_stage(config, False), b, t, self.dev)}
+            de, dg, dd = h.encoder_width, config.width, h.decoder_width
+            np_ = b * self.patches
+            self.zE, self.invE = e(self.rows, de), e(self.rows, dt=torch.float32)
+            self.pooled = e(np_, de)
+            self.zG, self.invG = e(np_, dg), e(np_, dt=torch.float32)
+            self.zd = e(np_, dd)
+            self.bos = e(8, dd)
+            self.zD, self.invD = e(self.rows, dd), e(self.rows, dt=torch.float32)
+            self.y = e(self.rows, dg)
+            # backward
+            self.dE = e(self.rows, de, dt=torch.float32)
+            self.dzd, self.dbos = e(np_, dd), e(8, dd)
+            self.dpool = e(np_, de, dt=torch.float32)
+            self.dy32 = e(self.rows, dg, dt=torch.float32)
+            self.dyb = e(self.rows, dg)
+            self.top_partials = e(((self.rows + 63) // 64) * max(dg, de, dd), dt=torch.float32)
+            top_width = dg
+        self.hf, self.invF = e(self.rows, top_width), e(self.rows, dt=torch.float32)
+        self.logits = e(self.rows, VOCAB_PAD, dt=torch.float32)
+        self.dlogits = e(self.rows, VOCAB_PAD)
+        self.dhead = e(self.rows, top_width, dt=torch.float32)
+        self.dheadb = e(self.rows, top_width)
+        if h is None:
+            self.top_partials = e(((self.rows + 63) // 64) * top_width, dt=torch.float32)
+        self.graph = None
+
+    # kernels each entry point launches (sj_zero is a memset, not a kernel)
+    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 3,
+               "sj_zero": 0}
+
+    def _call(self, name, *args):
+        call(name, *args)
+        self.launches += self.KERNELS.get(name, 1)
+
+    # ------------------------------------------------------------------ parameter pointers
+    def wb_ptr(self, name):
+        return _ptr(self.wb, self.layout[name].offset)
+
+    def w_ptr(self, name):
+        return _ptr(self.w, self.layout[name].offset)
+
+    def g_ptr(self, name):
+        return _ptr(self.g, self.layout[name].offset)
+
+    # ------------------------------------------------------------------ primitives
+    def _gemm(self, a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epi=EPI_STORE, aux=0, ld_aux=0,
+              rope_cols=0, rope_t=0, split_k=0):
+        self._call("sj_gemm", a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epi, 1.0, aux, ld_aux, rope_cols,
+             rope_t, float(self.c.rope_theta) if epi == EPI_ROPE else 0.0, split_k, self.stream)
+
+    def _norm(self, x, wname, y, inv, rows, d):
+        self._call("sj_rmsnorm_fwd", _ptr(x), SJ_BF16, self.w_ptr(wname), _ptr(y), _ptr(inv), rows, d,
+             float(self.c.norm_epsilon), self.stream)
+
+    def _norm_bwd(self, x, wname, inv, dz, dres, dres_b, partials, rows, d):
+        self._call("sj_rmsnorm_bwd", _ptr(x), self.w_ptr(wname), _ptr(inv), _ptr(dz), _ptr(dres),
+             _ptr(dres_b) if dres_b is not None else 0, self.g_ptr(wname), _ptr(partials), rows, d, self.stream)
+
+    def _zero(self, t):
+        self._call("sj_zero", _ptr(t), t.numel() * t.element_size(), self.stream)
+
+    # ------------------------------------------------------------------ blocks
+    def _block_fwd(self, run, i):
+        s, a = run.stage, run.layers[i]
+        n, d, f, cq, seq = run.rows, s.width, s.ffn, s.qkv_width, run.seq
+        p = f"{s.prefix}.{i}"
+        x, xn = run.x[i], run.x[i + 1]
+        self._norm(x, f"{p}.attention_norm", a["z1"], a["inv1"], n, d)
+        self._gemm(_ptr(a["z1"]), d, 0, self.wb_ptr(f"{p}.qkv"), cq, 0, _ptr(a["qkv"]), cq, SJ_BF16, n, cq, d,
+                   EPI_ROPE, rope_cols=(s.heads + s.kv_heads) * HEAD_DIM, rope_t=seq)
+        qkv = a["qkv"]
+        self._call("sj_attn_gqa_fwd", _ptr(qkv), cq, _ptr(qkv, s.heads * HEAD_DIM), cq,
+             _ptr(qkv, (s.heads + s.kv_heads) * HEAD_DIM), cq, _ptr(a["o"]), d, _ptr(a["lse"]), run.batch, seq,
+             s.heads, s.kv_heads, HEAD_DIM, s.window, self.stream)
+        self._gemm(_ptr(a["o"]), d, 0, self.wb_ptr(f"{p}.attention_output"), d, 0, _ptr(a["x1"]), d, SJ_BF16, n, d, d,
+                   EPI_RESIDUAL, aux=_ptr(x), ld_aux=d)
+        self._norm(a["x1"], f"{p}.ffn_norm", a["z2"], a["inv2"], n, d)
+        self._gemm(_ptr(a["z2"]), d, 0, self.wb_ptr(f"{p}.gate_up"), 2 * f, 0, _ptr(a["gu"]), 2 * f, SJ_BF16, n,
+                   2 * f, d, EPI_SWIGLU, aux=_ptr(a["h"]), ld_aux=f)
+        self._gemm(_ptr(a["h"]), f, 0, self.wb_ptr(f"{p}.down"), d, 0, _ptr(xn), d, SJ_BF16, n, d, f, EPI_RESIDUAL,
+                   aux=_ptr(a["x1"]), ld_aux=d)
+
+    def _block_bwd(self, run, i):
+        """run.dx / run.dxb hold dL/d(block output); on return dL/d(block input)."""
+        s, a = run.stage, run.layers[i]
+        n, d, f, cq, seq = run.rows, s.width, s.ffn, s.qkv_width, run.seq
+        p = f"{s.prefix}.{i}"
+        dx, dxb = run.dx, run.dxb
+        # FFN: down, SwiGLU, gate/up
+        self._gemm(_ptr(a["h"]), f, 1, _ptr(dxb), d, 0, self.g_ptr(f"{p}.down"), d, SJ_F32, f, d, n, EPI_ACCUM)
+        self._gemm(_ptr(dxb), d, 0, self.wb_ptr(f"{p}.down"), d, 1, _ptr(run.dh), f, SJ_BF16, n, f, d)
+        self._call("sj_swiglu_bwd", _ptr(a["gu"]), _ptr(run.dh), _ptr(run.dgu), n, f, self.stream)
+        self._gemm(_ptr(a["z2"]), d, 1, _ptr(run.dgu), 2 * f, 0, self.g_ptr(f"{p}.gate_up"), 2 * f, SJ_F32, d, 2 * f,
+                   n, EPI_ACCUM)
+        self._gemm(_ptr(run.dgu), 2 * f, 0, self.wb_ptr(f"{p}.gate_up"), 2 * f, 1, _ptr(run.dz), d, SJ_F32, n, d,
+                   2 * f)
+        self._norm_bwd(a["x1"], f"{p}.ffn_norm", a["inv2"], run.dz, dx, dxb, run.partials, n, d)
+        # attention: output projection, attention, QKV
+        self._gemm(_ptr(a["o"]), d, 1, _ptr(dxb), d, 0, self.g_ptr(f"{p}.attention_output"), d, SJ_F32, d, d, n,
+                   EPI_ACCUM)
+        self._gemm(_ptr(dxb), d, 0, self.wb_ptr(f"{p}.attention_output"), d, 1, _ptr(run.do), d, SJ_BF16, n, d, d)
+        qkv, dqkv = a["qkv"], run.dqkv
+        kq, vq = s.heads * HEAD_DIM, (s.heads + s.kv_heads) * HEAD_DIM
+        self._call("sj_attn_gqa_bwd", _ptr(qkv), cq, _ptr(qkv, kq), cq, _ptr(qkv, vq), cq, _ptr(a["o"]), d, _ptr(a["lse"]),
+             _ptr(run.do), d, _ptr(dqkv), cq, _ptr(dqkv, kq), cq, _ptr(dqkv, vq), cq, _ptr(run.delta), run.batch,
+             seq, s.heads, s.kv_heads, HEAD_DIM, s.window, float(self.c.rope_theta), self.stream)
+        self._gemm(_ptr(a["z1"]), d, 1, _ptr(dqkv), cq, 0, self.g_ptr(f"{p}.qkv"), cq, SJ_F32, d, cq, n, EPI_ACCUM)
+        self._gemm(_ptr(dqkv), cq, 0, self.wb_ptr(f"{p}.qkv"), cq, 1, _ptr(run.dz), d, SJ_F32, n, d, cq)
+        self._norm_bwd(run.x[i], f"{p}.attention_norm", a["inv1"], run.dz, dx, dxb, run.partials, n, d)
+
+    def _stage_fwd(self, run):
+        for i in range(run.stage.layers):
+            self._block_fwd(run, i)
+
+    def _stage_bwd(self, run):
+        for i in reversed(range(run.stage.layers)):
+            self._block_bwd(run, i)
+
+    # ------------------------------------------------------------------ model
+    def _forward(self):
+        c, h = self.c, self.c.hierarchy
+        n = self.rows
+        b = self.tc.batch
+        if h is None:
+            run = self.runs["global"]
+            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(run.x[0]), n, c.width,
+                 self.stream)
+            self._stage_fwd(run)
+            top = run.x[-1]
+            top_width = c.width
+        else:
+            enc, glob, dec = self.runs["encoder"], self.runs["global"], self.runs["decoder"]
+            de, dg, dd, pt = h.encoder_width, c.width, h.decoder_width, h.patch_size
+            np_ = b * self.patches
+            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(enc.x[0]), n, de, self.stream)
+            self._stage_fwd(enc)
+            self._norm(enc.x[-1], "encoder_norm", self.zE, self.invE, n, de)
+            self._call("sj_patch_pool_fwd", _ptr(self.zE), _ptr(self.pooled), b, self.tc.sequence, de, pt, self.stream)
+            self._gemm(_ptr(self.pooled), de, 0, self.wb_ptr("encoder_to_global"), dg, 0, _ptr(glob.x[0]), dg,
+                       SJ_BF16, np_, dg, de)
+            self._stage_fwd(glob)
+            self._norm(glob.x[-1], "global_norm", self.zG, self.invG, np_, dg)
+            self._gemm(_ptr(self.zG), dg, 0, self.wb_ptr("global_to_decoder"), dd, 0, _ptr(self.zd), dd, SJ_BF16,
+                       np_, dd, dg)
+            self._gemm(self.wb_ptr("global_bos"), dg, 0, self.wb_ptr("global_to_decoder"), dd, 0, _ptr(self.bos), dd,
+                       SJ_BF16, 1, dd, dg)
+            self._gemm(_ptr(self.zE), de, 0, self.wb_ptr("encoder_to_decoder"), dd, 0, _ptr(dec.x[0]), dd, SJ_BF16,
+                       n, dd, de)
+            self._call("sj_patch_broadcast_fwd", _ptr(self.zd), _ptr(self.bos), _ptr(dec.x[0]), 1, b, self.tc.sequence, dd,
+                 pt, self.stream)
+            self._stage_fwd(dec)
+            self._norm(dec.x[-1], "decoder_norm", self.zD, self.invD, n, dd)
+            self._gemm(_ptr(self.zD), dd, 0, self.wb_ptr("output_projection"), dg, 0, _ptr(self.y), dg, SJ_BF16, n,
+                       dg, dd)
+            top = self.y
+            top_width = dg
+        self._norm(top, "final_norm", self.hf, self.invF, n, top_width)
+        self._gemm(_ptr(self.hf), top_width, 0, self.wb_ptr("output"), VOCAB_PAD, 0, _ptr(self.logits), VOCAB_PAD,
+                   SJ_F32, n, VOCAB, top_width)
+        scale = 1.0 / (n * self.world)
+        self._call("sj_cross_entropy", _ptr(self.logits), VOCAB_PAD, _ptr(self.targets), n, VOCAB,
+             float(self.tc.loss_scale * scale), 0, _ptr(self.dlogits), VOCAB_PAD, _ptr(self.loss_sum), scale,
+             self.stream)
+        return top, top_width
+
+    def _backward(self, top, top_width):
+        c, h = self.c, self.c.hierarchy
+        n, b = self.rows, self.tc.batch
+        # head: dW_out += h^T dlogits ; dh = dlogits W_out^T
+        self._gemm(_ptr(self.hf), top_width, 1, _ptr(self.dlogits), VOCAB_PAD, 0, self.g_ptr("output"), VOCAB_PAD,
+                   SJ_F32, top_width, VOCAB, n, EPI_ACCUM)
+        self._gemm(_ptr(self.dlogits), VOCAB_PAD, 0, self.wb_ptr("output"), VOCAB_PAD, 1, _ptr(self.dhead), top_width,
+                   SJ_F32, n, top_width, VOCAB)
+        if h is None:
+            run = self.runs["global"]
+            self._zero(run.dx)
+            self._norm_bwd(top, "final_norm", self.invF, self.dhead, run.dx, run.dxb, self.top_partials, n, c.width)
+            self._stage_bwd(run)
+            self._call("sj_embedding_bwd", _ptr(run.dx), _ptr(self.ids), self.g_ptr("embedding"), n, c.width, VOCAB,
+                 self.stream)
+            return
+        enc, glob, dec = self.runs["encoder"], self.runs["global"], self.runs["decoder"]
+        de, dg, dd, pt = h.encoder_width, c.width, h.decoder_width, h.patch_size
+        np_, t = b * self.patches, self.tc.sequence
+        # final norm -> output_projection
+        self._zero(self.dy32)
+        self._norm_bwd(self.y, "final_norm", self.invF, self.dhead, self.dy32, self.dyb, self.top_partials, n, dg)
+        self._gemm(_ptr(self.zD), dd, 1, _ptr(self.dyb), dg, 0, self.g_ptr("output_projection"), dg, SJ_F32, dd, dg,
+                   n, EPI_ACCUM)
+        self._gemm(_ptr(self.dyb), dg, 0, self.wb_ptr("output_projection"), dg, 1, _ptr(dec.dz), dd, SJ_F32, n, dd, dg)
+        self._zero(dec.dx)
+        self._norm_bwd(dec.x[-1], "decoder_norm", self.invD, dec.dz, dec.dx, dec.dxb, dec.partials, n, dd)
+        self._stage_bwd(dec)
+        # decoder input = encoder_to_decoder(zE) + broadcast(global_to_decoder(zG), bos)
+        self._gemm(_ptr(self.zE), de, 1, _ptr(dec.dxb), dd, 0, self.g_ptr("encoder_to_decoder"), dd, SJ_F32, de, dd,
+                   n, EPI_ACCUM)
+        self._gemm(_ptr(dec.dxb), dd, 0, self.wb_ptr("encoder_to_decoder"), dd, 1, _ptr(self.dE), de, SJ_F32, n, de,
+                   dd)
+        self._call("sj_patch_broadcast_bwd", _ptr(dec.dx), _ptr(self.dzd), _ptr(self.dbos), b, t, dd, pt, self.stream)
+        self._gemm(_ptr(self.zG), dg, 1, _ptr(self.dzd), dd, 0, self.g_ptr("global_to_decoder"), dd, SJ_F32, dg, dd,
+                   np_, EPI_ACCUM)
+        self._gemm(self.wb_ptr("global_bos"), dg, 1, _ptr(self.dbos), dd, 0, self.g_ptr("global_to_decoder"), dd,
+                   SJ_F32, dg, dd, 1, EPI_ACCUM)
+        self._gemm(_ptr(self.dbos), dd, 0, self.wb_ptr("global_to_decoder"), dd, 1, self.g_ptr("global_bos"), dg,
+                   SJ_F32, 1, dg, dd, EPI_ACCUM)
+        self._gemm(_ptr(self.dzd), dd, 0, self.wb_ptr("global_to_decoder"), dd, 1, _ptr(glob.dz), dg, SJ_F32, np_, dg,
+                   dd)
+        self._zero(glob.dx)
+        self._norm_bwd(glob.x[-1], "global_norm", self.invG, glob.dz, glob.dx, glob.dxb, glob.partials, np_, dg)
+        self._stage_bwd(glob)
+        # encoder_to_global, patch pool
+        self._gemm(_ptr(self.pooled), de, 1, _ptr(glob.dxb), dg, 0, self.g_ptr("encoder_to_global"), dg, SJ_F32, de,
+                   dg, np_, EPI_ACCUM)
+        self._gemm(_ptr(glob.dxb), dg, 0, self.wb_ptr("encoder_to_global"), dg, 1, _ptr(self.dpool), de, SJ_F32, np_,
+                   de, dg)
+        self._call("sj_patch_pool_bwd", _ptr(self.dpool), _ptr(self.dE), b, t, de, pt, self.stream)
+        self._zero(enc.dx)
+        self._norm_bwd(enc.x[-1], "encoder_norm", self.invE, self.dE, enc.dx, enc.dxb, enc.partials, n, de)
+        self._stage_bwd(enc)
+        self._call("sj_embedding_bwd", _ptr(enc.dx), _ptr(self.ids), self.g_ptr("embedding"), n, de, VOCAB, self.stream)
+
+    # ------------------------------------------------------------------ public step API
+    def _local_forward_backward(self):
+        self.stream = torch.cuda.current_stream(self.dev).cuda_stream
+        self._zero(self.g)
+        self._zero(self.loss_sum)
+        top, width = self._forward()
+        self._backward(top, width)
+
+    def _exchange(self):
+        """Data-parallel exchange: sum of the per-rank gradients (each seeded with 1/global rows, so
+        the sum is the global-batch mean gradient) and of the loss, over NCCL."""
+        if self.world > 1:
+            torch.distributed.all_reduce(self.g, group=self.pg)
+            torch.distributed.all_reduce(self.loss_sum, group=self.pg)
+
+    def forward_backward(self):
+        """Loss (into self.loss_sum) and gradients (into self.g) for the staged batch."""
+        self._local_forward_backward()
+        self._exchange()
+
+    def optimizer_step(self):
+        """Adam::update (crates/sejong-train/src/lib.rs:199-238) or the dense SGD step, in two launches."""
+        self.stream = torch.cuda.current_stream(self.dev).cuda_stream
+        tc = self.tc
+        total = self.layout.total
+        self._call("sj_grad_sumsq", _ptr(self.g), total, _ptr(self.partials), self.stream)
+        self._call("sj_optim_prepare", _ptr(self.partials), self.n_partials, _ptr(self.opt_state), _ptr(self.hyper),
+             tc.learning_rate, tc.min_learning_rate, tc.warmup_steps, tc.steps, tc.beta1, tc.beta2, tc.clip_norm,
+             int(tc.clip_enabled), tc.loss_scale, self.stream)
+        if tc.optimizer == "adamw":
+            self._call("sj_adamw", _ptr(self.w), _ptr(self.g), _ptr(self.m), _ptr(self.v), _ptr(self.wb), total,
+                 self.layout.n_decay, _ptr(self.hyper), tc.beta1, tc.beta2, tc.epsilon, tc.weight_decay, self.stream)
+        else:
+            self._call("sj_sgd", _ptr(self.w), _ptr(self.g), _ptr(self.wb), total, self.layout.n_decay, _ptr(self.hyper),
+                 tc.weight_decay, self.stream)
+
+    def step(self):
+        self.forward_backward()
+        self.optimizer_step()
+
+    def stage_batch(self, ids, targets, non_blocking=True):
+        """Copy a batch (host or device int32 tensors) into the step's input buffers."""
+        self.ids.copy_(torch.as_tensor(ids, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
+        self.targets.copy_(torch.as_tensor(targets, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
+
+    def capture(self):
+        """Capture the step as CUDA graphs (replayed by `replay`).
+
+        One graph (forward + backward + update) on a single GPU.  With data parallelism the
+        forward/backward and the update are two graphs and the NCCL exchange runs between them
+        on the same stream, so no collective is captured."""
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        graphs = []
+        with torch.cuda.stream(s):
+            if self.world == 1:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    self.step()
+                graphs.append(g)
+            else:
+                g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g1, stream=s):
+                    self._local_forward_backward()
+                with torch.cuda.graph(g2, stream=s):
+                    self.optimizer_step()
+                graphs += [g1, g2]
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = graphs
+        return graphs
+
+    def replay(self):
+        if len(self.graph) == 1:
+            self.graph[0].replay()
+        else:
+            self.graph[0].replay()
+            self._exchange()
+            self.graph[1].replay()
+
+    def release_graphs(self):
+        """Drop captured graphs (before destroying a process group)."""
+        self.graph = None
+
+    # ------------------------------------------------------------------ inspection
+    def loss(self):
+        return float(self.loss_sum.item())
+
+    def gradients(self):
+        """Reference-named f32 gradients of the last forward_backward."""
+        return self.layout.unpack(self.g.detach().cpu().numpy())
+
+    def parameters(self):
+        return self.layout.unpack(self.w.detach().cpu().numpy())
+
+    def device_error(self):
+        code = ctypes.c_int(0)
+        self._call("sj_device_error", ctypes.byref(code), 1, self.stream)
+        return code.value
+
+    def step_flops(self):
+        """Algorithmic FLOPs of one step (FMA = 2; attention 4*B*H*64*pairs fwd, 8*... bwd; no recompute)."""
+        c, tc = self.c, self.tc
+        b, t = tc.batch, tc.sequence
+        lin = 0
+        att = 0
+
+        def stage_cost(s, rows, seq):
+            nonlocal lin, att
+            d, kv = s.width, s.kv_heads * HEAD_DIM
+            per = d * d + 2 * d * kv + d * d + 3 * d * s.ffn
+            lin += 2 * rows * per * s.layers
+            w = s.window or seq
+            pairs = sum(min(q + 1, w) for q in range(seq))
+            att += 4 * (rows // seq) * s.heads * HEAD_DIM * pairs * s.layers
+
+        h = c.hierarchy
+        if h is None:
+            stage_cost(global_stage(c), b * t, t)
+            lin += 2 * b * t * c.width * VOCAB
+        else:
+            p = t // h.patch_size
+            stage_cost(local_stage(c, True), b * t, t)
+            stage_cost(global_stage(c), b * p, p)
+            stage_cost(local_stage(c, False), b * t, t)
+            lin += 2 * b * p * h.encoder_width * c.width            # encoder_to_global
+            lin += 2 * b * p * c.width * h.decoder_width            # global_to_decoder
+            lin += 2 * b * t * h.encoder_width * h.decoder_width    # encoder_to_decoder
+            lin += 2 * b * t * h.decoder_width * c.width            # output_projection
+            lin += 2 * b * t * c.width * VOCAB                      # head
+        return 3 * lin + 3 * att  # fwd + (dX + dW) for linear; fwd (4) + bwd (8) for attention
+
+
+def synthetic_corpus_tokens(seed, length, s=1.1):
+    """Token stream of one synthetic Zipf document: EOS + bytes + EOS (Corpus layout, lib.rs:24-71)."""
+    buf = np.empty(length, dtype=np.uint8)
+    call("sj_zipf_bytes", seed, float(s), buf.ctypes.data, length)
+    toks = np.empty(length + 2, dtype=np.int32)
+    toks[0] = 256
+    toks[1:-1] = buf
+    toks[-1] = 256
+    return toks
+
+
+def corpus_batch(tokens, rng_state, batch, sequence):
+    """Corpus::batch (crates/sejong-train/src/lib.rs:72-88) via the library's Rng; rng_state: ctypes.c_uint64."""
+    tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+    inputs = np.empty(batch * sequence, dtype=np.int32)
+    targets = np.empty(batch * sequence, dtype=np.int32)
+    call("sj_corpus_batch", tokens.ctypes.data, tokens.size, ctypes.byref(rng_state), batch, sequence,
+         inputs.ctypes.data, targets.ctypes.data)
+    return inputs, targets
