@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
+    ap.add_argument("--kernel-report", default=None, help="write per-call kernel timings (JSON) to this path")
     return ap.parse_args()
 
 
@@ -161,8 +162,12 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- GPU arm
-def kernel_timing(trainer):
-    """One eager step with CUDA events around every C-ABI call: per-family time and FLOPs."""
+def kernel_timing(trainer, report=None):
+    """One eager step with CUDA events around every C-ABI call: per-family time and FLOPs.
+
+    The stream first runs a ~0.15 s sleep kernel so that the host has enqueued the whole step
+    (and its events) before the GPU reaches it: the events then bracket back-to-back kernels and
+    no host launch gap is counted as kernel time."""
     import torch
     stream = torch.cuda.current_stream()
     records = []
@@ -174,8 +179,11 @@ def kernel_timing(trainer):
         original(name, *a)
         e.record(stream)
         flops = 2.0 * a[9] * a[10] * a[11] if name == "sj_gemm" else 0.0
-        records.append((name, s, e, flops))
+        info = {"m": a[9], "n": a[10], "k": a[11], "epi": a[12], "a_t": a[2], "b_t": a[5]} if name == "sj_gemm" else {}
+        records.append((name, s, e, flops, info))
 
+    torch.cuda.synchronize()
+    torch.cuda._sleep(300_000_000)
     trainer._call = timed
     try:
         trainer.step()
@@ -183,12 +191,18 @@ def kernel_timing(trainer):
         trainer._call = original
     torch.cuda.synchronize()
     fam = {}
-    for name, s, e, flops in records:
+    rows = []
+    for name, s, e, flops, info in records:
         ms = s.elapsed_time(e)
         f = fam.setdefault(name, {"ms": 0.0, "calls": 0, "flops": 0.0})
         f["ms"] += ms
         f["calls"] += 1
         f["flops"] += flops
+        rows.append(dict(name=name, us=round(ms * 1e3, 2), tflops=round(flops / ms / 1e9, 1) if flops else None,
+                         **info))
+    if report:
+        with open(report, "w") as fh:
+            json.dump({"families": fam, "calls": rows}, fh, indent=1)
     return fam
 
 
@@ -285,7 +299,7 @@ def run_ours(args):
     assert np.all(np.isfinite(losses)), "non-finite loss"
 
     per_step_launches = sum(trainer.KERNELS.get(n, 1) for n in _call_names(trainer))
-    fam = {} if args.no_kernel_timing else kernel_timing(trainer)
+    fam = {} if args.no_kernel_timing else kernel_timing(trainer, args.kernel_report if rank == 0 else None)
     if world > 1:
         trainer.release_graphs()
 

@@ -88,7 +88,8 @@ int sj_corpus_batch(const int32_t* tokens, size_t n_tokens, uint64_t* rng_state,
 enum {
   SJ_EPI_STORE = 0,    /* C = alpha*acc                         (C bf16 or f32) */
   SJ_EPI_ACCUM = 1,    /* C += alpha*acc                        (C f32; split-K allowed) */
-  SJ_EPI_RESIDUAL = 2, /* C = aux + alpha*acc                   (C, aux bf16, aux row stride ld_aux) */
+  SJ_EPI_RESIDUAL = 2, /* C = aux + alpha*acc                   (C, aux both bf16 or both f32; aux row
+                          stride ld_aux) */
   SJ_EPI_SWIGLU = 3,   /* C = round(acc) (gate/up interleaved by 16 columns, bf16);
                           aux = silu(g)*u  [M, N/2] bf16 with row stride ld_aux */
   SJ_EPI_ROPE = 4      /* C = RoPE(acc) on columns < rope_cols (head dim 64, pairs 2i,2i+1,
@@ -116,12 +117,14 @@ int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* i
 /* Engine::norm_backward (crates/sejong-gpu/src/norm_ops.rs:14-134; kernels.py:63-87) fused with the
  * residual gradient accumulation of the tape (graph.rs:503-513):
  *   dres[r,:] += rms_dx(x, w, dz) ;  dres_bf16 = bf16(dres) (optional) ;  dw += sum_r dz*x*inv.
- * x bf16, dz f32, dres f32 (in/out), dw f32 accumulated.  `partials` is workspace of
- * ceil(rows/64)*d floats. */
-int sj_rmsnorm_bwd(const void* x, const float* w, const float* inv_rms, const float* dz, float* dres,
+ * x bf16 or f32 (x_dtype), dz f32, dres f32 (in/out), dw f32 accumulated.  `partials` is workspace
+ * of ceil(rows/64)*d floats. */
+int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz, float* dres,
                    void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream);
-/* Engine::embedding (lib.rs:650-665; kernels.py:41-45): y[i,:] = w[ids[i],:], bf16. */
-int sj_embedding_fwd(const void* w, const int32_t* ids, void* y, int n, int d, void* stream);
+/* Engine::embedding (lib.rs:650-665; kernels.py:41-45): y[i,:] = w[ids[i],:]; w bf16, y bf16 or f32
+ * (y_dtype; f32 starts an f32 residual stream).  Ids outside [0, vocab) are an error recorded in the
+ * device error word (row left zero). */
+int sj_embedding_fwd(const void* w, const int32_t* ids, void* y, int y_dtype, int n, int d, int vocab, void* stream);
 /* Engine::embedding_backward (lib.rs:666-687; kernels.py:47-52): dw[ids[i],:] += dy[i,:] (f32). */
 int sj_embedding_bwd(const float* dy, const int32_t* ids, float* dw, int n, int d, int vocab, void* stream);
 /* Engine::rope (lib.rs:734-758; kernels.py:103-113) standalone: x,y [rows, heads*hd] bf16. */
@@ -135,9 +138,10 @@ int sj_patch_pool_fwd(const void* x, void* y, int batch, int t, int d, int patch
 /* dx[b,t,:] += dy[b, t/P, :] / count  (f32 accumulate) */
 int sj_patch_pool_bwd(const float* dy, float* dx, int batch, int t, int d, int patch, void* stream);
 /* Engine::patch_broadcast (hierarchy_ops.rs:207-278; hierarchy.py:134-172) fused with the tape add
- * (architecture.rs:386-387):  y[b,t,:] (+)= t/P >= 1 ? z[b, t/P - 1, :] : bos[:]  (bf16, accumulate when add != 0). */
-int sj_patch_broadcast_fwd(const void* z, const void* bos, void* y, int add, int batch, int t, int d, int patch,
-                           void* stream);
+ * (architecture.rs:386-387):  y[b,t,:] (+)= t/P >= 1 ? z[b, t/P - 1, :] : bos[:]  (z, bos bf16; y bf16 or
+ * f32 per y_dtype; accumulate when add != 0). */
+int sj_patch_broadcast_fwd(const void* z, const void* bos, void* y, int y_dtype, int add, int batch, int t, int d,
+                           int patch, void* stream);
 /* dz[b,p,:] = sum of dy over the bytes of patch p+1 ; dbos = sum of dy over the first patch of every row.
  * dy f32; dz [batch*patches, d] and dbos [d] bf16 (both feed the global_to_decoder backward GEMMs). */
 int sj_patch_broadcast_bwd(const float* dy, void* dz, void* dbos, int batch, int t, int d, int patch, void* stream);

@@ -7,12 +7,27 @@
 namespace sj {
 
 // ---------------------------------------------------------------- embedding (kernels.py:41-52)
-__global__ void embedding_fwd_kernel(const uint4* __restrict__ w, const int32_t* __restrict__ ids,
-                                     uint4* __restrict__ y, int n, int vec_per_row) {
+// One thread per 8 columns (one 16-byte bf16 vector of the weight row).
+template <bool F32_OUT>
+__global__ void embedding_fwd_kernel(const uint4* __restrict__ w, const int32_t* __restrict__ ids, void* __restrict__ y,
+                                     int n, int vec_per_row, int vocab) {
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<size_t>(n) * vec_per_row) return;
   const int row = static_cast<int>(i / vec_per_row), c = static_cast<int>(i % vec_per_row);
-  y[i] = w[static_cast<size_t>(ids[row]) * vec_per_row + c];
+  const int id = ids[row];
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (id >= 0 && id < vocab)
+    v = w[static_cast<size_t>(id) * vec_per_row + c];
+  else if (c == 0)
+    record_error(SJ_DEV_BAD_INDEX);
+  if (!F32_OUT) {
+    reinterpret_cast<uint4*>(y)[i] = v;
+  } else {
+    const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y), cc = unpack_bf16x2(v.z), d = unpack_bf16x2(v.w);
+    float4* o = reinterpret_cast<float4*>(y) + 2 * i;
+    o[0] = make_float4(a.x, a.y, b.x, b.y);
+    o[1] = make_float4(cc.x, cc.y, d.x, d.y);
+  }
 }
 
 // Row-chunk x 32-column slices accumulated in shared memory, flushed with one atomic per
@@ -134,8 +149,9 @@ __global__ void patch_pool_bwd_kernel(const float* __restrict__ dy, float* __res
   *o = v;
 }
 
+template <bool F32_OUT>
 __global__ void patch_broadcast_fwd_kernel(const __nv_bfloat16* __restrict__ z, const __nv_bfloat16* __restrict__ bos,
-                                           __nv_bfloat16* __restrict__ y, int add, int batch, int t, int d, int patch) {
+                                           void* __restrict__ yv, int add, int batch, int t, int d, int patch) {
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // one per 8 columns
   const int vec = d / 8;
   if (i >= static_cast<size_t>(batch) * t * vec) return;
@@ -144,6 +160,20 @@ __global__ void patch_broadcast_fwd_kernel(const __nv_bfloat16* __restrict__ z, 
   const int patches = (t + patch - 1) / patch;
   const __nv_bfloat16* src = p >= 0 ? z + (static_cast<size_t>(b) * patches + p) * d + c : bos + c;
   const uint4 sw = *reinterpret_cast<const uint4*>(src);
+  if (F32_OUT) {
+    const float2 a = unpack_bf16x2(sw.x), bb = unpack_bf16x2(sw.y), cc = unpack_bf16x2(sw.z), dd = unpack_bf16x2(sw.w);
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(yv) + static_cast<size_t>(row) * d + c);
+    float4 o0 = make_float4(a.x, a.y, bb.x, bb.y), o1 = make_float4(cc.x, cc.y, dd.x, dd.y);
+    if (add) {
+      const float4 y0 = o[0], y1 = o[1];
+      o0.x += y0.x; o0.y += y0.y; o0.z += y0.z; o0.w += y0.w;
+      o1.x += y1.x; o1.y += y1.y; o1.z += y1.z; o1.w += y1.w;
+    }
+    o[0] = o0;
+    o[1] = o1;
+    return;
+  }
+  __nv_bfloat16* y = static_cast<__nv_bfloat16*>(yv);
   uint4* dst = reinterpret_cast<uint4*>(y + static_cast<size_t>(row) * d + c);
   if (!add) {
     *dst = sw;
@@ -234,13 +264,20 @@ static int grid_for(size_t n, int threads) {
 
 using namespace sj;
 
-extern "C" int sj_embedding_fwd(const void* w, const int32_t* ids, void* y, int n, int d, void* stream) {
-  if (n <= 0 || d <= 0 || d % 8) return fail(SJ_ERR_SHAPE, "sj_embedding_fwd: d=%d must be a multiple of 8", d);
+extern "C" int sj_embedding_fwd(const void* w, const int32_t* ids, void* y, int y_dtype, int n, int d, int vocab,
+                                void* stream) {
+  if (n <= 0 || d <= 0 || d % 8 || vocab <= 0)
+    return fail(SJ_ERR_SHAPE, "sj_embedding_fwd: d=%d must be a multiple of 8", d);
   if (!aligned16(w) || !aligned16(y)) return fail(SJ_ERR_ARGUMENT, "sj_embedding_fwd: 16-byte alignment required");
   const int vpr = d / 8;
   const size_t total = static_cast<size_t>(n) * vpr;
-  embedding_fwd_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, as_stream(stream)>>>(
-      static_cast<const uint4*>(w), ids, static_cast<uint4*>(y), n, vpr);
+  const unsigned grid = static_cast<unsigned>((total + 255) / 256);
+  if (y_dtype == SJ_BF16)
+    embedding_fwd_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const uint4*>(w), ids, y, n, vpr, vocab);
+  else if (y_dtype == SJ_F32)
+    embedding_fwd_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const uint4*>(w), ids, y, n, vpr, vocab);
+  else
+    return fail(SJ_ERR_ARGUMENT, "sj_embedding_fwd: y must be bf16 or f32");
   SJ_LAUNCH_CHECK("embedding_fwd");
   return SJ_OK;
 }
@@ -300,13 +337,19 @@ extern "C" int sj_patch_pool_bwd(const float* dy, float* dx, int batch, int t, i
   return SJ_OK;
 }
 
-extern "C" int sj_patch_broadcast_fwd(const void* z, const void* bos, void* y, int add, int batch, int t, int d,
-                                      int patch, void* stream) {
+extern "C" int sj_patch_broadcast_fwd(const void* z, const void* bos, void* y, int y_dtype, int add, int batch, int t,
+                                      int d, int patch, void* stream) {
   if (batch <= 0 || t <= 0 || d % 8 || patch <= 0) return fail(SJ_ERR_SHAPE, "sj_patch_broadcast_fwd: bad shape");
   const size_t threads = static_cast<size_t>(batch) * t * (d / 8);
-  patch_broadcast_fwd_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(z), static_cast<const __nv_bfloat16*>(bos), static_cast<__nv_bfloat16*>(y),
-      add, batch, t, d, patch);
+  const unsigned grid = static_cast<unsigned>((threads + 255) / 256);
+  const auto* zz = static_cast<const __nv_bfloat16*>(z);
+  const auto* bb = static_cast<const __nv_bfloat16*>(bos);
+  if (y_dtype == SJ_BF16)
+    patch_broadcast_fwd_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(zz, bb, y, add, batch, t, d, patch);
+  else if (y_dtype == SJ_F32)
+    patch_broadcast_fwd_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(zz, bb, y, add, batch, t, d, patch);
+  else
+    return fail(SJ_ERR_ARGUMENT, "sj_patch_broadcast_fwd: y must be bf16 or f32");
   SJ_LAUNCH_CHECK("patch_broadcast_fwd");
   return SJ_OK;
 }

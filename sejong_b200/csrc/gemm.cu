@@ -113,6 +113,23 @@ SJ_DEVICE void epilogue_chunk(const GemmParams& p, int row, int col0, float (&v)
       break;
     }
     case SJ_EPI_RESIDUAL: {
+      if (p.c_f32) {  // f32 residual stream: C = aux + acc, both f32
+        const float* res = reinterpret_cast<const float*>(p.aux) + static_cast<size_t>(row) * p.ld_aux;
+        float* dst = reinterpret_cast<float*>(p.c) + static_cast<size_t>(row) * p.ldc;
+        if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(res + col0) | reinterpret_cast<uintptr_t>(dst + col0)) & 15u) == 0) {
+          const float4* r4 = reinterpret_cast<const float4*>(res + col0);
+          float4* d4 = reinterpret_cast<float4*>(dst + col0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 r = r4[j];
+            d4[j] = make_float4(v[4 * j] + r.x, v[4 * j + 1] + r.y, v[4 * j + 2] + r.z, v[4 * j + 3] + r.w);
+          }
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.N) dst[col0 + j] = v[j] + res[col0 + j];
+        }
+        break;
+      }
       const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(p.aux) + static_cast<size_t>(row) * p.ld_aux;
       if (col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(res + col0) & 15u) == 0) {
         const uint4* r4 = reinterpret_cast<const uint4*>(res + col0);
@@ -415,7 +432,7 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
       if (c_dtype != SJ_F32) return fail(SJ_ERR_ARGUMENT, "sj_gemm: ACCUM needs an f32 C");
       break;
     case SJ_EPI_RESIDUAL:
-      if (c_dtype != SJ_BF16 || !aux) return fail(SJ_ERR_ARGUMENT, "sj_gemm: RESIDUAL needs bf16 C and aux");
+      if (!aux) return fail(SJ_ERR_ARGUMENT, "sj_gemm: RESIDUAL needs aux (same dtype as C)");
       break;
     case SJ_EPI_SWIGLU:
       if (c_dtype != SJ_BF16 || !aux || (n % 32))

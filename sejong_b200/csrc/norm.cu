@@ -68,8 +68,9 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
 }
 
 // One CTA = kNormWarps warps over kNormRowsPerCta rows; per-CTA dw partial row in `partials`.
+template <typename T>
 __global__ void __launch_bounds__(kNormWarps * 32)
-    rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+    rmsnorm_bwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
                        const float* __restrict__ inv_rms, const float* __restrict__ dz, float* __restrict__ dres,
                        __nv_bfloat16* __restrict__ dres_bf16, float* __restrict__ partials, int rows, int d) {
   __shared__ float red[kNormWarps][1024];
@@ -90,7 +91,7 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     for (int i = 0; i < kNormMaxVec; ++i) {
       const int col = (lane + 32 * i) * 8;
       if (col < d) {
-        load8<__nv_bfloat16>(x + base + col, xv[i]);
+        load8<T>(x + base + col, xv[i]);
         float dzv[8];
         load8<float>(dz + base + col, dzv);
 #pragma unroll
@@ -166,16 +167,25 @@ extern "C" int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* 
   return SJ_OK;
 }
 
-extern "C" int sj_rmsnorm_bwd(const void* x, const float* w, const float* inv_rms, const float* dz, float* dres,
-                              void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream) {
+extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz,
+                              float* dres, void* dres_bf16, float* dw, float* partials, int rows, int d,
+                              void* stream) {
   using namespace sj;
   if (rows <= 0 || d <= 0 || d % 8 || d > 1024) return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd: bad d=%d", d);
   if (!x || !w || !inv_rms || !dz || !dres || !dw || !partials)
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: null pointer");
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
   cudaStream_t s = as_stream(stream);
-  rmsnorm_bwd_kernel<<<groups, kNormWarps * 32, 0, s>>>(static_cast<const __nv_bfloat16*>(x), w, inv_rms, dz, dres,
-                                                        static_cast<__nv_bfloat16*>(dres_bf16), partials, rows, d);
+  if (x_dtype == SJ_BF16)
+    rmsnorm_bwd_kernel<__nv_bfloat16><<<groups, kNormWarps * 32, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), w, inv_rms, dz, dres, static_cast<__nv_bfloat16*>(dres_bf16), partials,
+        rows, d);
+  else if (x_dtype == SJ_F32)
+    rmsnorm_bwd_kernel<float><<<groups, kNormWarps * 32, 0, s>>>(static_cast<const float*>(x), w, inv_rms, dz, dres,
+                                                                 static_cast<__nv_bfloat16*>(dres_bf16), partials,
+                                                                 rows, d);
+  else
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: x must be bf16 or f32");
   SJ_LAUNCH_CHECK("rmsnorm_bwd");
   column_reduce_add_kernel<<<(d + 255) / 256, 256, 0, s>>>(partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd reduce");

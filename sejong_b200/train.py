@@ -70,12 +70,14 @@ class _StageRun:
         self.rows = n
         bf, f32 = torch.bfloat16, torch.float32
         e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
-        self.x = [e(n, d) for _ in range(stage.layers + 1)]   # block inputs; x[L] is the stage output
+        # the residual stream (block inputs x[i], x[L] = stage output, and the mid-block x1) is f32;
+        # GEMM operands (normalised activations, attention output, SwiGLU output) are bf16
+        self.x = [e(n, d, dt=f32) for _ in range(stage.layers + 1)]
         self.layers = []
         for _ in range(stage.layers):
             self.layers.append(dict(z1=e(n, d), inv1=e(n, dt=f32), qkv=e(n, cq), o=e(n, d),
-                                    lse=e(n * stage.heads, dt=f32), x1=e(n, d), z2=e(n, d), inv2=e(n, dt=f32),
-                                    gu=e(n, 2 * f), h=e(n, f)))
+                                    lse=e(n * stage.heads, dt=f32), x1=e(n, d, dt=f32), z2=e(n, d),
+                                    inv2=e(n, dt=f32), gu=e(n, 2 * f), h=e(n, f)))
         # backward workspace
         self.dx = e(n, d, dt=f32)
         self.dxb = e(n, d)
@@ -93,6 +95,7 @@ class ByteTrainer:
 
     def __init__(self, config, train, device=None, params=None, process_group=None):
         self.c, self.tc = config, train
+        self.launches = 0
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
         torch.cuda.set_device(self.dev)
         self.lib = _lib.load()
@@ -141,7 +144,7 @@ class ByteTrainer:
             self.zd = e(np_, dd)
             self.bos = e(8, dd)
             self.zD, self.invD = e(self.rows, dd), e(self.rows, dt=torch.float32)
-            self.y = e(self.rows, dg)
+            self.y = e(self.rows, dg, dt=torch.float32)
             # backward
             self.dE = e(self.rows, de, dt=torch.float32)
             self.dzd, self.dbos = e(np_, dd), e(8, dd)
@@ -183,12 +186,16 @@ class ByteTrainer:
         self._call("sj_gemm", a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epi, 1.0, aux, ld_aux, rope_cols,
              rope_t, float(self.c.rope_theta) if epi == EPI_ROPE else 0.0, split_k, self.stream)
 
+    @staticmethod
+    def _dt(t):
+        return SJ_F32 if t.dtype == torch.float32 else SJ_BF16
+
     def _norm(self, x, wname, y, inv, rows, d):
-        self._call("sj_rmsnorm_fwd", _ptr(x), SJ_BF16, self.w_ptr(wname), _ptr(y), _ptr(inv), rows, d,
+        self._call("sj_rmsnorm_fwd", _ptr(x), self._dt(x), self.w_ptr(wname), _ptr(y), _ptr(inv), rows, d,
              float(self.c.norm_epsilon), self.stream)
 
     def _norm_bwd(self, x, wname, inv, dz, dres, dres_b, partials, rows, d):
-        self._call("sj_rmsnorm_bwd", _ptr(x), self.w_ptr(wname), _ptr(inv), _ptr(dz), _ptr(dres),
+        self._call("sj_rmsnorm_bwd", _ptr(x), self._dt(x), self.w_ptr(wname), _ptr(inv), _ptr(dz), _ptr(dres),
              _ptr(dres_b) if dres_b is not None else 0, self.g_ptr(wname), _ptr(partials), rows, d, self.stream)
 
     def _zero(self, t):
@@ -207,12 +214,12 @@ class ByteTrainer:
         self._call("sj_attn_gqa_fwd", _ptr(qkv), cq, _ptr(qkv, s.heads * HEAD_DIM), cq,
              _ptr(qkv, (s.heads + s.kv_heads) * HEAD_DIM), cq, _ptr(a["o"]), d, _ptr(a["lse"]), run.batch, seq,
              s.heads, s.kv_heads, HEAD_DIM, s.window, self.stream)
-        self._gemm(_ptr(a["o"]), d, 0, self.wb_ptr(f"{p}.attention_output"), d, 0, _ptr(a["x1"]), d, SJ_BF16, n, d, d,
+        self._gemm(_ptr(a["o"]), d, 0, self.wb_ptr(f"{p}.attention_output"), d, 0, _ptr(a["x1"]), d, SJ_F32, n, d, d,
                    EPI_RESIDUAL, aux=_ptr(x), ld_aux=d)
         self._norm(a["x1"], f"{p}.ffn_norm", a["z2"], a["inv2"], n, d)
         self._gemm(_ptr(a["z2"]), d, 0, self.wb_ptr(f"{p}.gate_up"), 2 * f, 0, _ptr(a["gu"]), 2 * f, SJ_BF16, n,
                    2 * f, d, EPI_SWIGLU, aux=_ptr(a["h"]), ld_aux=f)
-        self._gemm(_ptr(a["h"]), f, 0, self.wb_ptr(f"{p}.down"), d, 0, _ptr(xn), d, SJ_BF16, n, d, f, EPI_RESIDUAL,
+        self._gemm(_ptr(a["h"]), f, 0, self.wb_ptr(f"{p}.down"), d, 0, _ptr(xn), d, SJ_F32, n, d, f, EPI_RESIDUAL,
                    aux=_ptr(a["x1"]), ld_aux=d)
 
     def _block_bwd(self, run, i):
@@ -258,8 +265,8 @@ class ByteTrainer:
         b = self.tc.batch
         if h is None:
             run = self.runs["global"]
-            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(run.x[0]), n, c.width,
-                 self.stream)
+            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(run.x[0]), SJ_F32, n,
+                       c.width, VOCAB, self.stream)
             self._stage_fwd(run)
             top = run.x[-1]
             top_width = c.width
@@ -267,25 +274,26 @@ class ByteTrainer:
             enc, glob, dec = self.runs["encoder"], self.runs["global"], self.runs["decoder"]
             de, dg, dd, pt = h.encoder_width, c.width, h.decoder_width, h.patch_size
             np_ = b * self.patches
-            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(enc.x[0]), n, de, self.stream)
+            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(enc.x[0]), SJ_F32, n, de,
+                       VOCAB, self.stream)
             self._stage_fwd(enc)
             self._norm(enc.x[-1], "encoder_norm", self.zE, self.invE, n, de)
             self._call("sj_patch_pool_fwd", _ptr(self.zE), _ptr(self.pooled), b, self.tc.sequence, de, pt, self.stream)
             self._gemm(_ptr(self.pooled), de, 0, self.wb_ptr("encoder_to_global"), dg, 0, _ptr(glob.x[0]), dg,
-                       SJ_BF16, np_, dg, de)
+                       SJ_F32, np_, dg, de)
             self._stage_fwd(glob)
             self._norm(glob.x[-1], "global_norm", self.zG, self.invG, np_, dg)
             self._gemm(_ptr(self.zG), dg, 0, self.wb_ptr("global_to_decoder"), dd, 0, _ptr(self.zd), dd, SJ_BF16,
                        np_, dd, dg)
             self._gemm(self.wb_ptr("global_bos"), dg, 0, self.wb_ptr("global_to_decoder"), dd, 0, _ptr(self.bos), dd,
                        SJ_BF16, 1, dd, dg)
-            self._gemm(_ptr(self.zE), de, 0, self.wb_ptr("encoder_to_decoder"), dd, 0, _ptr(dec.x[0]), dd, SJ_BF16,
+            self._gemm(_ptr(self.zE), de, 0, self.wb_ptr("encoder_to_decoder"), dd, 0, _ptr(dec.x[0]), dd, SJ_F32,
                        n, dd, de)
-            self._call("sj_patch_broadcast_fwd", _ptr(self.zd), _ptr(self.bos), _ptr(dec.x[0]), 1, b, self.tc.sequence, dd,
-                 pt, self.stream)
+            self._call("sj_patch_broadcast_fwd", _ptr(self.zd), _ptr(self.bos), _ptr(dec.x[0]), SJ_F32, 1, b,
+                       self.tc.sequence, dd, pt, self.stream)
             self._stage_fwd(dec)
             self._norm(dec.x[-1], "decoder_norm", self.zD, self.invD, n, dd)
-            self._gemm(_ptr(self.zD), dd, 0, self.wb_ptr("output_projection"), dg, 0, _ptr(self.y), dg, SJ_BF16, n,
+            self._gemm(_ptr(self.zD), dd, 0, self.wb_ptr("output_projection"), dg, 0, _ptr(self.y), dg, SJ_F32, n,
                        dg, dd)
             top = self.y
             top_width = dg

@@ -120,6 +120,9 @@ def test_gemm_residual_epilogue():
     res = bf(randn(m, n))
     c = gemm(a, 0, b, 0, m, n, k, c_dtype=torch.bfloat16, epi=2, aux=res, ld_aux=n)
     assert rel(c, res.float() + a.float() @ b.float()) < 1e-2
+    res32 = randn(m, n)
+    c32 = gemm(a, 0, b, 0, m, n, k, c_dtype=torch.float32, epi=2, aux=res32, ld_aux=n)
+    assert rel(c32, res32 + a.float() @ b.float()) < 1e-5
 
 
 def test_gemm_swiglu_epilogue():
@@ -159,13 +162,15 @@ def test_gemm_rejects_bad_arguments():
 
 
 # ------------------------------------------------------------------------------------- norms
+@pytest.mark.parametrize("x_f32", [False, True])
 @pytest.mark.parametrize("rows,d", [(1000, 256), (333, 768), (64, 1024)])
-def test_rmsnorm_forward_backward(rows, d):
-    x = bf(randn(rows, d))
+def test_rmsnorm_forward_backward(rows, d, x_f32):
+    x = randn(rows, d) if x_f32 else bf(randn(rows, d))
+    xdt = 0 if x_f32 else 4
     w = (1 + 0.1 * randn(d)).float()
     y = torch.empty(rows, d, dtype=torch.bfloat16, device=DEV)
     inv = torch.empty(rows, dtype=torch.float32, device=DEV)
-    call("sj_rmsnorm_fwd", ptr(x), 4, ptr(w), ptr(y), ptr(inv), rows, d, 1e-6, stream())
+    call("sj_rmsnorm_fwd", ptr(x), xdt, ptr(w), ptr(y), ptr(inv), rows, d, 1e-6, stream())
     ref = ops.rmsnorm(x.double().cpu(), w.double().cpu(), 1e-6)
     assert rel(y, ref) < 1e-2
     dz = randn(rows, d)
@@ -174,8 +179,8 @@ def test_rmsnorm_forward_backward(rows, d):
     dres_b = torch.empty(rows, d, dtype=torch.bfloat16, device=DEV)
     dw = torch.zeros(d, device=DEV)
     partials = torch.empty(((rows + 63) // 64) * d, device=DEV)
-    call("sj_rmsnorm_bwd", ptr(x), ptr(w), ptr(inv), ptr(dz), ptr(dres), ptr(dres_b), ptr(dw), ptr(partials), rows, d,
-         stream())
+    call("sj_rmsnorm_bwd", ptr(x), xdt, ptr(w), ptr(inv), ptr(dz), ptr(dres), ptr(dres_b), ptr(dw), ptr(partials),
+         rows, d, stream())
     torch.cuda.synchronize()
     rdx, rdw = ops.rmsnorm_backward(x.double().cpu(), w.double().cpu(), dz.double().cpu(), 1e-6)
     assert rel(dres - dres0, rdx) < 1e-4
@@ -258,9 +263,12 @@ def test_embedding_forward_backward():
     ids = torch.randint(0, 257, (n,), generator=GEN, dtype=torch.int32).to(DEV)
     ids[:1000] = 0  # a frequent byte
     y = torch.empty(n, d, dtype=torch.bfloat16, device=DEV)
-    call("sj_embedding_fwd", ptr(w), ptr(ids), ptr(y), n, d, stream())
+    call("sj_embedding_fwd", ptr(w), ptr(ids), ptr(y), 4, n, d, 257, stream())
+    y32 = torch.empty(n, d, dtype=torch.float32, device=DEV)
+    call("sj_embedding_fwd", ptr(w), ptr(ids), ptr(y32), 0, n, d, 257, stream())
     torch.cuda.synchronize()
     assert torch.equal(y, w[ids.long()])
+    assert torch.equal(y32, w[ids.long()].float())
     dy = randn(n, d)
     dw = torch.zeros(257, d, device=DEV)
     call("sj_embedding_bwd", ptr(dy), ptr(ids), ptr(dw), n, d, 257, stream())
@@ -304,9 +312,12 @@ def test_patch_pool_and_broadcast(t, patch):
     bos = bf(randn(1, d))
     base = bf(randn(b * t, d))
     yb = base.clone()
-    call("sj_patch_broadcast_fwd", ptr(z), ptr(bos), ptr(yb), 1, b, t, d, patch, stream())
+    call("sj_patch_broadcast_fwd", ptr(z), ptr(bos), ptr(yb), 4, 1, b, t, d, patch, stream())
+    y32 = base.float().clone()
+    call("sj_patch_broadcast_fwd", ptr(z), ptr(bos), ptr(y32), 0, 1, b, t, d, patch, stream())
     torch.cuda.synchronize()
     ref = base.double().cpu() + ops.patch_broadcast(z.double().cpu(), bos.double().cpu(), t, patch)
+    assert rel(y32, ref) < 1e-6
     assert rel(yb, ref) < 1e-2
     dyb = randn(b * t, d)
     dz = torch.empty(b * patches, d, dtype=torch.bfloat16, device=DEV)
