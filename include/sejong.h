@@ -118,7 +118,7 @@ int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* i
  * residual gradient accumulation of the tape (graph.rs:503-513):
  *   dres[r,:] += rms_dx(x, w, dz) ;  dres_bf16 = bf16(dres) (optional) ;  dw += sum_r dz*x*inv.
  * x bf16 or f32 (x_dtype), dz f32, dres f32 (in/out), dw f32 accumulated.  `partials` is workspace
- * of ceil(rows/64)*d floats. */
+ * of at least ceil(rows/128)*d floats. */
 int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz, float* dres,
                    void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream);
 /* Engine::embedding (lib.rs:650-665; kernels.py:41-45): y[i,:] = w[ids[i],:]; w bf16, y bf16 or f32

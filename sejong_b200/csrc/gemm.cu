@@ -5,12 +5,16 @@
 // dA = dY*B^T (NT) and dB = A^T*dY (TN) (crates/sejong-gpu/src/graph.rs:817-853).
 //
 // Design (one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte swizzle,
-//               STAGES-deep ring guarded by full/empty mbarriers.
-//   warp 1      allocates TMEM (2 x BN f32 columns = two accumulators) and one thread issues
+//   warp 0      TMA producer: 128x64 A tile + BNx64 B tile per stage, 128-byte swizzle, a
+//               `stages`-deep ring (sized at launch to the shared memory left) guarded by
+//               full/empty mbarriers.
+//   warp 1      allocates TMEM (2 x BN f32 columns = two accumulators); one thread issues
 //               tcgen05.mma (M=128, N=BN, K=16) and tcgen05.commit.
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, fused epilogue, global stores, while
-//               the MMA warp already fills the other accumulator.
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, fused epilogue math, then each warp
+//               stages its 32-row slab (128 bytes per row) in 128-byte-swizzled shared memory and
+//               one lane writes it with a TMA bulk-tensor store -- or a TMA reduce-add for
+//               accumulating (split-K) weight gradients -- while the MMA warp already fills the
+//               other accumulator.
 // A and B may each be K-major or MN-major in global memory (the UMMA descriptor's major bit), so
 // forward (A K-major, B N-major), input-gradient (A K-major, B K-major) and weight-gradient
 // (A M-major, B N-major) products all read their operands in place.
@@ -24,12 +28,11 @@ namespace sj {
 struct GemmParams {
   int M, N, K;
   int m_tiles, n_tiles, splits, kb_per_split, kb_total;
-  void* c;
-  int ldc;
+  int stages;
   int c_f32;
   int epilogue;
   float alpha;
-  void* aux;
+  const void* aux;  // residual source (same dtype as C)
   int ld_aux;
   int rope_cols, rope_t;
   float rope_log_theta;
@@ -38,171 +41,70 @@ struct GemmParams {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 192;
+constexpr int kSmemLimit = 232448;          // 227 KB: the sm_100 per-block opt-in maximum
+constexpr int kStagingC = 4 * 2 * 4096;      // 4 epilogue warps x 2 buffers x (32 rows x 128 B)
+constexpr int kStagingH = 4 * 2 * 2048;      // SwiGLU h output: 4 x 2 x (32 rows x 64 B)
+constexpr int kBarrierBytes = 256;
 
 template <int BN>
 struct GemmCfg {
-  static constexpr int STAGES = BN == 256 ? 4 : 6;
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;  // 256 or 512: powers of two
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-SJ_DEVICE void store_row_bf16(__nv_bfloat16* dst, int col0, int n, const float* v, int count) {
-  // count = 32 consecutive columns starting at col0; 16-byte vector stores when fully in range.
-  if (col0 + count <= n && (reinterpret_cast<uintptr_t>(dst + col0) & 15u) == 0) {
-    uint4* d = reinterpret_cast<uint4*>(dst + col0);
-#pragma unroll
-    for (int j = 0; j < count / 8; ++j) {
-      uint4 w;
-      w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-      d[j] = w;
-    }
-  } else {
-    for (int j = 0; j < count; ++j)
-      if (col0 + j < n) dst[col0 + j] = f2bf(v[j]);
-  }
+SJ_DEVICE void tma_store_2d(const CUtensorMap* map, const void* smem, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem)), "r"(x), "r"(y)
+               : "memory");
 }
+SJ_DEVICE void tma_reduce_add_2d(const CUtensorMap* map, const void* smem, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem)), "r"(x), "r"(y)
+               : "memory");
+}
+SJ_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+SJ_DEVICE void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+SJ_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+SJ_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-SJ_DEVICE void epilogue_chunk(const GemmParams& p, int row, int col0, float (&v)[32], bool atomic) {
-  if (row >= p.M) return;
-  const float alpha = p.alpha;
+// Row `lane` of a 32 x 128-byte slab in the SWIZZLE_128B layout: 16-byte chunk j of row r lives
+// at r*128 + ((j ^ (r & 7)) * 16).  Writes of 8 consecutive rows hit 8 distinct chunks.
+SJ_DEVICE void stage_row128(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] *= alpha;
-  switch (p.epilogue) {
-    case SJ_EPI_STORE: {
-      if (p.c_f32) {
-        float* dst = reinterpret_cast<float*>(p.c) + static_cast<size_t>(row) * p.ldc;
-        if (col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(dst + col0) & 15u) == 0) {
-          float4* d = reinterpret_cast<float4*>(dst + col0);
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+        make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+// Row `lane` of a 32 x 64-byte slab in the SWIZZLE_64B layout: chunk j of row r at
+// r*64 + ((j ^ ((r >> 1) & 3)) * 16).
+SJ_DEVICE void stage_row64(uint8_t* buf, int lane, const uint32_t (&w)[16]) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) d[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        } else {
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) dst[col0 + j] = v[j];
-        }
-      } else {
-        store_row_bf16(reinterpret_cast<__nv_bfloat16*>(p.c) + static_cast<size_t>(row) * p.ldc, col0, p.N, v, 32);
-      }
-      break;
-    }
-    case SJ_EPI_ACCUM: {
-      float* dst = reinterpret_cast<float*>(p.c) + static_cast<size_t>(row) * p.ldc;
-      if (atomic) {
-        for (int j = 0; j < 32; ++j)
-          if (col0 + j < p.N) atomicAdd(dst + col0 + j, v[j]);
-      } else if (col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(dst + col0) & 15u) == 0) {
-        float4* d = reinterpret_cast<float4*>(dst + col0);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 o = d[j];
-          o.x += v[4 * j];
-          o.y += v[4 * j + 1];
-          o.z += v[4 * j + 2];
-          o.w += v[4 * j + 3];
-          d[j] = o;
-        }
-      } else {
-        for (int j = 0; j < 32; ++j)
-          if (col0 + j < p.N) dst[col0 + j] += v[j];
-      }
-      break;
-    }
-    case SJ_EPI_RESIDUAL: {
-      if (p.c_f32) {  // f32 residual stream: C = aux + acc, both f32
-        const float* res = reinterpret_cast<const float*>(p.aux) + static_cast<size_t>(row) * p.ld_aux;
-        float* dst = reinterpret_cast<float*>(p.c) + static_cast<size_t>(row) * p.ldc;
-        if (col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(res + col0) | reinterpret_cast<uintptr_t>(dst + col0)) & 15u) == 0) {
-          const float4* r4 = reinterpret_cast<const float4*>(res + col0);
-          float4* d4 = reinterpret_cast<float4*>(dst + col0);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float4 r = r4[j];
-            d4[j] = make_float4(v[4 * j] + r.x, v[4 * j + 1] + r.y, v[4 * j + 2] + r.z, v[4 * j + 3] + r.w);
-          }
-        } else {
-          for (int j = 0; j < 32; ++j)
-            if (col0 + j < p.N) dst[col0 + j] = v[j] + res[col0 + j];
-        }
-        break;
-      }
-      const __nv_bfloat16* res = reinterpret_cast<const __nv_bfloat16*>(p.aux) + static_cast<size_t>(row) * p.ld_aux;
-      if (col0 + 32 <= p.N && (reinterpret_cast<uintptr_t>(res + col0) & 15u) == 0) {
-        const uint4* r4 = reinterpret_cast<const uint4*>(res + col0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 w = r4[j];
-          float2 a = unpack_bf16x2(w.x), b = unpack_bf16x2(w.y), c = unpack_bf16x2(w.z), d = unpack_bf16x2(w.w);
-          v[8 * j + 0] += a.x;
-          v[8 * j + 1] += a.y;
-          v[8 * j + 2] += b.x;
-          v[8 * j + 3] += b.y;
-          v[8 * j + 4] += c.x;
-          v[8 * j + 5] += c.y;
-          v[8 * j + 6] += d.x;
-          v[8 * j + 7] += d.y;
-        }
-      } else {
-        for (int j = 0; j < 32; ++j)
-          if (col0 + j < p.N) v[j] += bf2f(res[col0 + j]);
-      }
-      store_row_bf16(reinterpret_cast<__nv_bfloat16*>(p.c) + static_cast<size_t>(row) * p.ldc, col0, p.N, v, 32);
-      break;
-    }
-    case SJ_EPI_SWIGLU: {
-      // columns [col0, col0+16) are gate features f0..f0+15, [col0+16, col0+32) the matching up features.
-      // g and u are rounded to bf16 before h = silu(g)*u (projection.py:464-470).
-      float h[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float g = round_bf16(v[j]);
-        const float u = round_bf16(v[16 + j]);
-        h[j] = g / (1.0f + __expf(-g)) * u;
-      }
-      store_row_bf16(reinterpret_cast<__nv_bfloat16*>(p.c) + static_cast<size_t>(row) * p.ldc, col0, p.N, v, 32);
-      store_row_bf16(reinterpret_cast<__nv_bfloat16*>(p.aux) + static_cast<size_t>(row) * p.ld_aux, col0 / 2,
-                     p.N / 2, h, 16);
-      break;
-    }
-    case SJ_EPI_ROPE: {
-      if (col0 < p.rope_cols) {
-        const float pos = static_cast<float>(row % p.rope_t);
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int pair = ((col0 + j) & 63) >> 1;
-          const float inv_freq = expf((-2.0f * static_cast<float>(pair) / 64.0f) * p.rope_log_theta);
-          float s, c;
-          sincosf(pos * inv_freq, &s, &c);
-          const float a = v[j], b = v[j + 1];
-          v[j] = a * c - b * s;
-          v[j + 1] = a * s + b * c;
-        }
-      }
-      store_row_bf16(reinterpret_cast<__nv_bfloat16*>(p.c) + static_cast<size_t>(row) * p.ldc, col0, p.N, v, 32);
-      break;
-    }
-    default:
-      break;
-  }
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
 }
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_h,
                         const GemmParams p) {
   using Cfg = GemmCfg<BN>;
-  constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = umma_idesc_bf16(kBM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  const int stages = p.stages;
+  const bool swiglu = p.epilogue == SJ_EPI_SWIGLU;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* acc_full = empty + STAGES;
+  uint8_t* staging_c = smem + stages * Cfg::STAGE_BYTES;
+  uint8_t* staging_h = staging_c + kStagingC;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging_c + kStagingC + (swiglu ? kStagingH : 0));
+  uint64_t* empty = full + stages;
+  uint64_t* acc_full = empty + stages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -210,9 +112,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int tiles_mn = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -225,6 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbarrier_init();
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
+    tma_prefetch_map(&map_c);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -234,21 +138,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_tiles = p.m_tiles * p.n_tiles * p.splits;
+  const int total_tiles = tiles_mn * p.splits;
+  // work unit -> (split, m tile, n tile); the split index is slowest so that concurrently running
+  // CTAs share the K range of their A and B tiles in L2.
 
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
-        const int ks = tile % p.splits;
-        const int nb = (tile / p.splits) % p.n_tiles;
-        const int mb = tile / (p.splits * p.n_tiles);
+        const int ks = tile / tiles_mn;
+        const int mb = (tile % tiles_mn) / p.n_tiles;
+        const int nb = tile % p.n_tiles;
         const int m0 = mb * kBM, n0 = nb * BN;
         const int kb_begin = ks * p.kb_per_split;
         const int kb_end = min(kb_begin + p.kb_per_split, p.kb_total);
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t round = static_cast<uint32_t>(it / STAGES);
+          const int s = it % stages;
+          const uint32_t round = static_cast<uint32_t>(it / stages);
           if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag, SJ_DEV_GEMM_PRODUCER_WAIT)) break;
           uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
@@ -269,15 +175,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // drain: wait (bounded) for the copies still in flight into the most recent stages
-      for (int j = max(0, it - STAGES); j < it; ++j)
-        mbar_wait(&full[j % STAGES], static_cast<uint32_t>(j / STAGES) & 1u, nullptr, SJ_DEV_GEMM_DRAIN_WAIT);
+      for (int j = max(0, it - stages); j < it; ++j)
+        mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, nullptr, SJ_DEV_GEMM_DRAIN_WAIT);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       int it = 0, local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++local) {
-        const int ks = tile % p.splits;
+        const int ks = tile / tiles_mn;
         const int kb_begin = ks * p.kb_per_split;
         const int kb_end = min(kb_begin + p.kb_per_split, p.kb_total);
         const int buf = local & 1;
@@ -286,8 +192,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t round = static_cast<uint32_t>(it / STAGES);
+          const int s = it % stages;
+          const uint32_t round = static_cast<uint32_t>(it / stages);
           if (!mbar_wait(&full[s], round & 1u, abort_flag, SJ_DEV_GEMM_MMA_WAIT)) {
             ok = false;
             break;
@@ -312,34 +218,161 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
-    int local = 0;
+    uint8_t* my_c = staging_c + quarter * 2 * 4096;
+    uint8_t* my_h = staging_h + quarter * 2 * 2048;
+    int local = 0, unit = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
-      const int ks = tile % p.splits;
-      const int nb = (tile / p.splits) % p.n_tiles;
-      const int mb = tile / (p.splits * p.n_tiles);
+      const int mb = (tile % tiles_mn) / p.n_tiles;
+      const int nb = tile % p.n_tiles;
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
       if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, SJ_DEV_GEMM_EPILOGUE_WAIT)) break;
       tc_fence_after();
-      const int row = mb * kBM + quarter * 32 + lane;
+      const int r0 = mb * kBM + quarter * 32;
+      const int row = r0 + lane;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
-      const bool atomic = p.splits > 1;
+      if (p.c_f32) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, r);
-        tmem_wait_ld();
-        float v[32];
+        for (int c = 0; c < BN / 32; ++c) {
+          const int col0 = nb * BN + c * 32;
+          if (col0 >= p.N) break;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        const int col0 = nb * BN + c * 32;
-        if (col0 < p.N) epilogue_chunk(p, row, col0, v, atomic);
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * p.alpha);
+          if (p.epilogue == SJ_EPI_RESIDUAL && row < p.M) {
+            const float* res = static_cast<const float*>(p.aux) + static_cast<size_t>(row) * p.ld_aux + col0;
+            if (col0 + 32 <= p.N) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 a4 = reinterpret_cast<const float4*>(res)[j];
+                r[4 * j + 0] = __float_as_uint(__uint_as_float(r[4 * j + 0]) + a4.x);
+                r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) + a4.y);
+                r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) + a4.z);
+                r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) + a4.w);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.N) r[j] = __float_as_uint(__uint_as_float(r[j]) + res[j]);
+            }
+          }
+          uint8_t* sbuf = my_c + (unit & 1) * 4096;
+          if (lane == 0) bulk_wait_read1();
+          __syncwarp();
+          stage_row128(sbuf, lane, r);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (r0 < p.M) {  // boxes are clipped at M and N; a slab wholly past M is not issued
+              if (p.epilogue == SJ_EPI_ACCUM)
+                tma_reduce_add_2d(&map_c, sbuf, col0, r0);
+              else
+                tma_store_2d(&map_c, sbuf, col0, r0);
+            }
+            bulk_commit();
+          }
+          ++unit;
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          const int col0 = nb * BN + c * 64;
+          if (col0 >= p.N) break;
+          uint32_t r[32], r2[32];
+          tmem_ld_32x32b_x32(taddr + c * 64, r);
+          tmem_ld_32x32b_x32(taddr + c * 64 + 32, r2);
+          tmem_wait_ld();
+          float v[64];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __uint_as_float(r[j]) * p.alpha;
+            v[32 + j] = __uint_as_float(r2[j]) * p.alpha;
+          }
+          uint32_t hw[16];
+          if (p.epilogue == SJ_EPI_ROPE) {
+            if (col0 < p.rope_cols) {
+              const float pos = static_cast<float>(row % p.rope_t);
+#pragma unroll
+              for (int j = 0; j < 64; j += 2) {
+                const int pair = j >> 1;  // col0 is a multiple of 64: pair index within the head
+                const float inv_freq = expf((-2.0f * static_cast<float>(pair) / 64.0f) * p.rope_log_theta);
+                float s, co;
+                sincosf(pos * inv_freq, &s, &co);
+                const float a = v[j], b = v[j + 1];
+                v[j] = a * co - b * s;
+                v[j + 1] = a * s + b * co;
+              }
+            }
+          } else if (swiglu) {
+            // columns come as blocks of 16 gate then the same 16 up features; g and u are rounded to
+            // bf16 before h = silu(g) * u (projection.py:464-470)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 2) {
+                float hv[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  const float g = round_bf16(v[32 * half + j + e]);
+                  const float u = round_bf16(v[32 * half + 16 + j + e]);
+                  hv[e] = g / (1.0f + __expf(-g)) * u;
+                }
+                hw[8 * half + (j >> 1)] = pack_bf16x2(hv[0], hv[1]);
+              }
+            }
+          } else if (p.epilogue == SJ_EPI_RESIDUAL && row < p.M) {
+            const __nv_bfloat16* res =
+                static_cast<const __nv_bfloat16*>(p.aux) + static_cast<size_t>(row) * p.ld_aux + col0;
+            if (col0 + 64 <= p.N) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const uint4 w4 = reinterpret_cast<const uint4*>(res)[j];
+                const float2 a = unpack_bf16x2(w4.x), b = unpack_bf16x2(w4.y), cc = unpack_bf16x2(w4.z),
+                             d = unpack_bf16x2(w4.w);
+                v[8 * j + 0] += a.x;
+                v[8 * j + 1] += a.y;
+                v[8 * j + 2] += b.x;
+                v[8 * j + 3] += b.y;
+                v[8 * j + 4] += cc.x;
+                v[8 * j + 5] += cc.y;
+                v[8 * j + 6] += d.x;
+                v[8 * j + 7] += d.y;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 64; ++j)
+                if (col0 + j < p.N) v[j] += bf2f(res[j]);
+            }
+          }
+          uint32_t w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+          uint8_t* sbuf = my_c + (unit & 1) * 4096;
+          uint8_t* hbuf = my_h + (unit & 1) * 2048;
+          if (lane == 0) bulk_wait_read1();
+          __syncwarp();
+          stage_row128(sbuf, lane, w);
+          if (swiglu) stage_row64(hbuf, lane, hw);
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (r0 < p.M) {
+              tma_store_2d(&map_c, sbuf, col0, r0);
+              if (swiglu) tma_store_2d(&map_h, hbuf, col0 / 2, r0);
+            }
+            bulk_commit();
+          }
+          ++unit;
+        }
       }
-      (void)ks;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
+    if (lane == 0) bulk_wait_all();  // staged slabs must be read out before the CTA exits
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -369,46 +402,50 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows, row stride `ld` elements.
-static int make_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
-                    uint32_t box_outer) {
+// 2-D tensor map: `inner` contiguous elements per row, `outer` rows, row stride `ld` elements.
+static int make_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int esize, uint64_t inner,
+                    uint64_t outer, uint64_t ld, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(SJ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {ld * 2};
+  cuuint64_t strides[1] = {ld * static_cast<uint64_t>(esize)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SJ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return SJ_OK;
 }
 
+static int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+                    uint32_t box_inner, uint32_t box_outer) {
+  return make_map(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld, box_inner, box_outer,
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 template <int BN, bool A_MN, bool B_MN>
-static int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int grid,
-                       cudaStream_t stream) {
+static int launch_gemm(const CUtensorMap* maps, const GemmParams& p, int grid, int smem, cudaStream_t stream) {
   auto kernel = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
   static int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
     if (e != cudaSuccess) return cuda_check(e, "gemm shared-memory attribute");
     configured_device = dev;
   }
-  kernel<<<grid, kThreads, GemmCfg<BN>::SMEM, stream>>>(ma, mb, p);
+  kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("gemm launch");
   return SJ_OK;
 }
 
 template <int BN>
-static int dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p,
-                           int grid, cudaStream_t s) {
-  if (!a_mn && b_mn) return launch_gemm<BN, false, true>(ma, mb, p, grid, s);
-  if (!a_mn && !b_mn) return launch_gemm<BN, false, false>(ma, mb, p, grid, s);
-  if (a_mn && b_mn) return launch_gemm<BN, true, true>(ma, mb, p, grid, s);
-  return launch_gemm<BN, true, false>(ma, mb, p, grid, s);
+static int dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap* maps, const GemmParams& p, int grid, int smem,
+                           cudaStream_t s) {
+  if (!a_mn && b_mn) return launch_gemm<BN, false, true>(maps, p, grid, smem, s);
+  if (!a_mn && !b_mn) return launch_gemm<BN, false, false>(maps, p, grid, smem, s);
+  if (a_mn && b_mn) return launch_gemm<BN, true, true>(maps, p, grid, smem, s);
+  return launch_gemm<BN, true, false>(maps, p, grid, smem, s);
 }
 
 }  // namespace sj
@@ -419,12 +456,15 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   using namespace sj;
   if (m <= 0 || n <= 0 || k <= 0) return fail(SJ_ERR_SHAPE, "sj_gemm: empty problem %dx%dx%d", m, n, k);
   if (!a || !b || !c) return fail(SJ_ERR_ARGUMENT, "sj_gemm: null operand");
-  if (!aligned16(a) || !aligned16(b)) return fail(SJ_ERR_ARGUMENT, "sj_gemm: A/B must be 16-byte aligned");
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c))
+    return fail(SJ_ERR_ARGUMENT, "sj_gemm: A, B and C must be 16-byte aligned");
   if ((lda % 8) || (ldb % 8)) return fail(SJ_ERR_ARGUMENT, "sj_gemm: lda/ldb must be multiples of 8 elements");
   const int a_rows_min = a_trans ? m : k, b_rows_min = b_trans ? k : n;
   if (lda < a_rows_min || ldb < b_rows_min || ldc < n)
     return fail(SJ_ERR_SHAPE, "sj_gemm: leading dimension smaller than the matrix width");
   if (c_dtype != SJ_BF16 && c_dtype != SJ_F32) return fail(SJ_ERR_ARGUMENT, "sj_gemm: C must be bf16 or f32");
+  if ((c_dtype == SJ_BF16 && ldc % 8) || (c_dtype == SJ_F32 && ldc % 4))
+    return fail(SJ_ERR_ARGUMENT, "sj_gemm: C rows must be 16-byte multiples");
   switch (epilogue) {
     case SJ_EPI_STORE:
       break;
@@ -432,11 +472,12 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
       if (c_dtype != SJ_F32) return fail(SJ_ERR_ARGUMENT, "sj_gemm: ACCUM needs an f32 C");
       break;
     case SJ_EPI_RESIDUAL:
-      if (!aux) return fail(SJ_ERR_ARGUMENT, "sj_gemm: RESIDUAL needs aux (same dtype as C)");
+      if (!aux || !aligned16(aux) || (ld_aux % 8))
+        return fail(SJ_ERR_ARGUMENT, "sj_gemm: RESIDUAL needs a 16-byte aligned aux (same dtype as C)");
       break;
     case SJ_EPI_SWIGLU:
-      if (c_dtype != SJ_BF16 || !aux || (n % 32))
-        return fail(SJ_ERR_ARGUMENT, "sj_gemm: SWIGLU needs bf16 C, aux and N %% 32 == 0");
+      if (c_dtype != SJ_BF16 || !aux || !aligned16(aux) || (n % 64) || (ld_aux % 8))
+        return fail(SJ_ERR_ARGUMENT, "sj_gemm: SWIGLU needs bf16 C, an aligned aux and N %% 64 == 0");
       break;
     case SJ_EPI_ROPE:
       if (c_dtype != SJ_BF16 || rope_t <= 0 || (rope_cols % 64) || rope_theta <= 0.f)
@@ -459,25 +500,44 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
       splits = split_k;
     } else {
       const int tiles = m_tiles * n_tiles;
-      splits = tiles >= sms ? 1 : (2 * sms + tiles - 1) / tiles;
-      splits = std::min(splits, std::max(1, kb_total / 4));
+      splits = tiles >= sms ? 1 : (sms + tiles - 1) / tiles;
+      splits = std::min(splits, std::max(1, kb_total / 8));
     }
     splits = std::max(1, std::min(splits, kb_total));
   }
   const int kb_per_split = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per_split - 1) / kb_per_split;  // no empty split
 
-  CUtensorMap ma, mb;
+  const int stage_bytes = (kBM + bn) * kBK * 2;
+  const int staging = kStagingC + (epilogue == SJ_EPI_SWIGLU ? kStagingH : 0);
+  const int stages = std::min(8, (kSmemLimit - 1024 - kBarrierBytes - staging) / stage_bytes);
+  if (stages < 2) return fail(SJ_ERR_CAPACITY, "sj_gemm: shared memory too small for the pipeline");
+  const int smem = 1024 + stages * stage_bytes + staging + kBarrierBytes;
+
+  CUtensorMap maps[4];
   int rc;
   if (!a_trans)
-    rc = make_map(&ma, a, static_cast<uint64_t>(k), static_cast<uint64_t>(m), lda, 64, 128);
+    rc = bf16_map(&maps[0], a, static_cast<uint64_t>(k), static_cast<uint64_t>(m), lda, 64, 128);
   else
-    rc = make_map(&ma, a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), lda, 64, 64);
+    rc = bf16_map(&maps[0], a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), lda, 64, 64);
   if (rc) return rc;
   if (b_trans)
-    rc = make_map(&mb, b, static_cast<uint64_t>(k), static_cast<uint64_t>(n), ldb, 64, static_cast<uint32_t>(bn));
+    rc = bf16_map(&maps[1], b, static_cast<uint64_t>(k), static_cast<uint64_t>(n), ldb, 64, static_cast<uint32_t>(bn));
   else
-    rc = make_map(&mb, b, static_cast<uint64_t>(n), static_cast<uint64_t>(k), ldb, 64, 64);
+    rc = bf16_map(&maps[1], b, static_cast<uint64_t>(n), static_cast<uint64_t>(k), ldb, 64, 64);
+  if (rc) return rc;
+  if (c_dtype == SJ_F32)
+    rc = make_map(&maps[2], c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, static_cast<uint64_t>(n), static_cast<uint64_t>(m),
+                  ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    rc = make_map(&maps[2], c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(m),
+                  ldc, 64, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  if (epilogue == SJ_EPI_SWIGLU)
+    rc = make_map(&maps[3], aux, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(n / 2),
+                  static_cast<uint64_t>(m), ld_aux, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  else
+    maps[3] = maps[2];
   if (rc) return rc;
 
   GemmParams p;
@@ -489,8 +549,7 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   p.splits = splits;
   p.kb_per_split = kb_per_split;
   p.kb_total = kb_total;
-  p.c = c;
-  p.ldc = ldc;
+  p.stages = stages;
   p.c_f32 = c_dtype == SJ_F32;
   p.epilogue = epilogue;
   p.alpha = alpha;
@@ -503,6 +562,6 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   const int grid = std::min(total, sms);
   const bool a_mn = a_trans != 0;   // A stored [K, M]
   const bool b_mn = b_trans == 0;   // B stored [K, N]
-  if (bn == 256) return dispatch_majors<256>(a_mn, b_mn, ma, mb, p, grid, as_stream(stream));
-  return dispatch_majors<128>(a_mn, b_mn, ma, mb, p, grid, as_stream(stream));
+  if (bn == 256) return dispatch_majors<256>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
+  return dispatch_majors<128>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
 }

@@ -10,7 +10,7 @@ namespace sj {
 
 constexpr int kNormMaxVec = 4;  // 4 x 8 elements per lane: d <= 1024
 constexpr int kNormWarps = 8;
-constexpr int kNormRowsPerCta = 64;
+constexpr int kNormRowsPerCta = 128;
 
 template <typename T>
 SJ_DEVICE void load8(const T* p, float (&v)[8]);
@@ -34,17 +34,17 @@ SJ_DEVICE void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
   *reinterpret_cast<uint4*>(p) = w;
 }
 
-template <typename T>
+template <typename T, int VEC>
 __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                    float* __restrict__ inv_rms, int rows, int d, float eps) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
   const size_t base = static_cast<size_t>(warp) * d;
-  float v[kNormMaxVec][8];
+  float v[VEC][8];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i) {
+  for (int i = 0; i < VEC; ++i) {
     const int col = (lane + 32 * i) * 8;
     if (col < d) {
       load8<T>(x + base + col, v[i]);
@@ -55,7 +55,7 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
   ss = warp_sum(ss);
   const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i) {
+  for (int i = 0; i < VEC; ++i) {
     const int col = (lane + 32 * i) * 8;
     if (col < d) {
       float o[8];
@@ -68,27 +68,27 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
 }
 
 // One CTA = kNormWarps warps over kNormRowsPerCta rows; per-CTA dw partial row in `partials`.
-template <typename T>
+template <typename T, int VEC>
 __global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_bwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
                        const float* __restrict__ inv_rms, const float* __restrict__ dz, float* __restrict__ dres,
                        __nv_bfloat16* __restrict__ dres_bf16, float* __restrict__ partials, int rows, int d) {
-  __shared__ float red[kNormWarps][1024];
+  __shared__ float red[kNormWarps][VEC * 256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float dw_acc[kNormMaxVec][8];
+  float dw_acc[VEC][8];
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i)
+  for (int i = 0; i < VEC; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) dw_acc[i][j] = 0.f;
   const float inv_d = 1.0f / static_cast<float>(d);
   for (int r = blockIdx.x * kNormRowsPerCta + warp; r < min(rows, (blockIdx.x + 1) * kNormRowsPerCta);
        r += kNormWarps) {
     const size_t base = static_cast<size_t>(r) * d;
-    float xv[kNormMaxVec][8], gv[kNormMaxVec][8];
+    float xv[VEC][8], gv[VEC][8];
     float dot = 0.f;
     const float inv = inv_rms[r];
 #pragma unroll
-    for (int i = 0; i < kNormMaxVec; ++i) {
+    for (int i = 0; i < VEC; ++i) {
       const int col = (lane + 32 * i) * 8;
       if (col < d) {
         load8<T>(x + base + col, xv[i]);
@@ -105,7 +105,7 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     dot = warp_sum(dot);
     const float coef = dot * inv_d * inv * inv;
 #pragma unroll
-    for (int i = 0; i < kNormMaxVec; ++i) {
+    for (int i = 0; i < VEC; ++i) {
       const int col = (lane + 32 * i) * 8;
       if (col < d) {
         float o[8];
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     }
   }
 #pragma unroll
-  for (int i = 0; i < kNormMaxVec; ++i) {
+  for (int i = 0; i < VEC; ++i) {
     const int col = (lane + 32 * i) * 8;
     if (col < d)
 #pragma unroll
@@ -135,13 +135,66 @@ __global__ void __launch_bounds__(kNormWarps * 32)
   }
 }
 
-__global__ void column_reduce_add_kernel(const float* __restrict__ partials, int groups, int d,
-                                         float* __restrict__ out) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col >= d) return;
+// out[col] += sum over groups of partials[g][col]: 32 columns per CTA, the 8 warps split the
+// groups, coalesced 128-byte row reads, one shared-memory reduction.
+__global__ void __launch_bounds__(256) column_reduce_add_kernel(const float* __restrict__ partials, int groups, int d,
+                                                               float* __restrict__ out) {
+  __shared__ float red[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
   float s = 0.f;
-  for (int g = 0; g < groups; ++g) s += partials[static_cast<size_t>(g) * d + col];
-  out[col] += s;
+  if (col < d)
+    for (int g = warp; g < groups; g += 8) s += partials[static_cast<size_t>(g) * d + col];
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && col < d) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k][lane];
+    out[col] += t;
+  }
+}
+
+}  // namespace sj
+
+namespace sj {
+
+template <typename T, int VEC>
+static void launch_norm_fwd(const void* x, const float* w, void* y, float* inv, int rows, int d, float eps,
+                            cudaStream_t s) {
+  const int threads = 256, warps = threads / 32;
+  rmsnorm_fwd_kernel<T, VEC><<<(rows + warps - 1) / warps, threads, 0, s>>>(
+      static_cast<const T*>(x), w, static_cast<__nv_bfloat16*>(y), inv, rows, d, eps);
+}
+
+template <typename T, int VEC>
+static void launch_norm_bwd(const void* x, const float* w, const float* inv, const float* dz, float* dres,
+                            void* dres_b, float* partials, int rows, int d, cudaStream_t s) {
+  const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
+  rmsnorm_bwd_kernel<T, VEC><<<groups, kNormWarps * 32, 0, s>>>(static_cast<const T*>(x), w, inv, dz, dres,
+                                                                 static_cast<__nv_bfloat16*>(dres_b), partials, rows, d);
+}
+
+template <typename T>
+static void dispatch_norm_fwd(const void* x, const float* w, void* y, float* inv, int rows, int d, float eps,
+                              cudaStream_t s) {
+  switch ((d + 255) / 256) {
+    case 1: launch_norm_fwd<T, 1>(x, w, y, inv, rows, d, eps, s); break;
+    case 2: launch_norm_fwd<T, 2>(x, w, y, inv, rows, d, eps, s); break;
+    case 3: launch_norm_fwd<T, 3>(x, w, y, inv, rows, d, eps, s); break;
+    default: launch_norm_fwd<T, 4>(x, w, y, inv, rows, d, eps, s); break;
+  }
+}
+
+template <typename T>
+static void dispatch_norm_bwd(const void* x, const float* w, const float* inv, const float* dz, float* dres,
+                              void* dres_b, float* partials, int rows, int d, cudaStream_t s) {
+  switch ((d + 255) / 256) {
+    case 1: launch_norm_bwd<T, 1>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
+    case 2: launch_norm_bwd<T, 2>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
+    case 3: launch_norm_bwd<T, 3>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
+    default: launch_norm_bwd<T, 4>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
+  }
 }
 
 }  // namespace sj
@@ -152,15 +205,11 @@ extern "C" int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* 
   if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
     return fail(SJ_ERR_SHAPE, "sj_rmsnorm_fwd: d=%d must be a multiple of 8 up to 1024", d);
   if (!aligned16(x) || !aligned16(y)) return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd: x/y must be 16-byte aligned");
-  const int threads = 256, warps = threads / 32;
-  const int grid = (rows + warps - 1) / warps;
   cudaStream_t s = as_stream(stream);
   if (x_dtype == SJ_BF16)
-    rmsnorm_fwd_kernel<__nv_bfloat16><<<grid, threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), w,
-                                                                static_cast<__nv_bfloat16*>(y), inv_rms, rows, d, eps);
+    dispatch_norm_fwd<__nv_bfloat16>(x, w, y, inv_rms, rows, d, eps, s);
   else if (x_dtype == SJ_F32)
-    rmsnorm_fwd_kernel<float><<<grid, threads, 0, s>>>(static_cast<const float*>(x), w, static_cast<__nv_bfloat16*>(y),
-                                                        inv_rms, rows, d, eps);
+    dispatch_norm_fwd<float>(x, w, y, inv_rms, rows, d, eps, s);
   else
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd: x must be bf16 or f32");
   SJ_LAUNCH_CHECK("rmsnorm_fwd");
@@ -171,23 +220,20 @@ extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const 
                               float* dres, void* dres_bf16, float* dw, float* partials, int rows, int d,
                               void* stream) {
   using namespace sj;
-  if (rows <= 0 || d <= 0 || d % 8 || d > 1024) return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd: bad d=%d", d);
+  if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
+    return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd: bad d=%d", d);
   if (!x || !w || !inv_rms || !dz || !dres || !dw || !partials)
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: null pointer");
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
   cudaStream_t s = as_stream(stream);
   if (x_dtype == SJ_BF16)
-    rmsnorm_bwd_kernel<__nv_bfloat16><<<groups, kNormWarps * 32, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), w, inv_rms, dz, dres, static_cast<__nv_bfloat16*>(dres_bf16), partials,
-        rows, d);
+    dispatch_norm_bwd<__nv_bfloat16>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
   else if (x_dtype == SJ_F32)
-    rmsnorm_bwd_kernel<float><<<groups, kNormWarps * 32, 0, s>>>(static_cast<const float*>(x), w, inv_rms, dz, dres,
-                                                                 static_cast<__nv_bfloat16*>(dres_bf16), partials,
-                                                                 rows, d);
+    dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
   else
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: x must be bf16 or f32");
   SJ_LAUNCH_CHECK("rmsnorm_bwd");
-  column_reduce_add_kernel<<<(d + 255) / 256, 256, 0, s>>>(partials, groups, d, dw);
+  column_reduce_add_kernel<<<(d + 31) / 32, 256, 0, s>>>(partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd reduce");
   return SJ_OK;
 }
