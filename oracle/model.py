@@ -254,8 +254,31 @@ def hidden(p, c, ids, seq):
     return ops.rmsnorm(x, p["final_norm"], eps)
 
 
-def loss_and_grads(params, c, ids, targets, seq, dtype=torch.float64, scale=1.0):
-    """Mean next-byte CE and its gradients (seed scale/rows per row, graph.rs:539-549)."""
+def compute_cast(params, cast):
+    """The per-step cast of every leaf to the compute precision (crates/sejong-model/src/lib.rs:206-219).
+
+    `cast="bf16"` rounds every matrix (rank > 1) to bfloat16 -- the weights the bf16 compute path
+    binds -- and keeps the norm vectors (f32 in the compute path).  The reference's Cast backward
+    passes the gradient through unchanged (crates/sejong-gpu/src/graph.rs:807-812), so gradients
+    taken at the cast weights are the gradients of the f32 master weights.
+    """
+    if cast is None:
+        return params
+    if cast != "bf16":
+        raise ValueError(cast)
+    out = {}
+    for k, v in params.items():
+        if np.ndim(v) > 1:
+            out[k] = torch.tensor(np.asarray(v, dtype=np.float32)).to(torch.bfloat16).float().numpy()
+        else:
+            out[k] = v
+    return out
+
+
+def loss_and_grads(params, c, ids, targets, seq, dtype=torch.float64, scale=1.0, cast=None):
+    """Mean next-byte CE and its gradients (seed scale/rows per row, graph.rs:539-549), in `dtype`
+    arithmetic at the weights `compute_cast(params, cast)`."""
+    params = compute_cast(params, cast)
     p = {k: torch.tensor(v, dtype=dtype, requires_grad=True) for k, v in params.items()}
     ids = torch.as_tensor(np.asarray(ids, dtype=np.int64))
     targets = torch.as_tensor(np.asarray(targets, dtype=np.int64))

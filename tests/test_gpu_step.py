@@ -4,6 +4,12 @@ Bar: loss within 1e-3 absolute; every bf16-path gradient w
 relative L2 of the FP64 gradient; the optimizer update, fed the same gradients, within f32
 round-off of the FP64 AdamW transition.  Gradients that are exactly zero in the reference
 (input_projection: nothing is injected) must be exactly zero here too.
+
+The FP64 oracle runs at the weights the compute path binds: every matrix cast to bf16, as the
+reference casts every leaf to its compute precision each step (crates/sejong-model/src/lib.rs:
+206-219) and passes the gradient of the cast straight to the f32 master (graph.rs:807-812).
+What is compared is therefore the arithmetic of the bf16 path (bf16 activations, f32
+accumulation), not the choice of bf16 weights itself.
 """
 import ctypes
 
@@ -58,7 +64,7 @@ def run_parity(c, ids, targets, batch, seq, optimizer="adamw"):
     assert tr.device_error() == 0
     loss = tr.loss()
     grads = tr.gradients()
-    ref_loss, ref_grads = omodel.loss_and_grads(params, oracle_config(c), ids, targets, seq)
+    ref_loss, ref_grads = omodel.loss_and_grads(params, oracle_config(c), ids, targets, seq, cast="bf16")
     assert abs(loss - ref_loss) < LOSS_TOL, (loss, ref_loss)
     worst = {}
     for name, g in ref_grads.items():
