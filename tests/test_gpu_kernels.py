@@ -97,10 +97,12 @@ def test_gemm_bf16_out(m, n, k):
     a = bf(randn(m, k))
     b = torch.zeros(k, 264 if n == 257 else n, dtype=torch.bfloat16, device=DEV)
     b[:, :n] = bf(randn(k, n))
-    c = torch.zeros(m, n, dtype=torch.bfloat16, device=DEV)
-    call("sj_gemm", ptr(a), k, 0, ptr(b), b.shape[1], 0, ptr(c), n, 4, m, n, k, 0, 1.0, 0, 0, 0, 0, 0.0, 0, stream())
+    c = torch.zeros(m, b.shape[1], dtype=torch.bfloat16, device=DEV)  # C rows padded to 16-byte multiples
+    call("sj_gemm", ptr(a), k, 0, ptr(b), b.shape[1], 0, ptr(c), c.shape[1], 4, m, n, k, 0, 1.0, 0, 0, 0, 0, 0.0, 0,
+         stream())
     torch.cuda.synchronize()
-    assert rel(c, a.float() @ b[:, :n].float()) < 1e-2
+    assert rel(c[:, :n], a.float() @ b[:, :n].float()) < 1e-2
+    assert float(c[:, n:].float().abs().max() if c.shape[1] > n else 0.0) == 0.0  # padding untouched
 
 
 @pytest.mark.parametrize("split_k", [0, 1, 7])
