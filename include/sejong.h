@@ -93,8 +93,13 @@ enum {
   SJ_EPI_SWIGLU = 3,   /* C = round(acc) (gate/up interleaved by 16 columns, bf16);
                           aux = silu(g)*u  [M, N/2] bf16 with row stride ld_aux */
   SJ_EPI_ROPE = 4      /* C = RoPE(acc) on columns < rope_cols (head dim 64, pairs 2i,2i+1,
-                          position = row mod rope_t), bf16 */
+                          position = row mod rope_t), bf16; aux = the sj_rope_table of rope_t
+                          positions (or null: angles evaluated inline from rope_theta) */
 };
+/* table[p*hd/2 + i] = (cos, sin) of (p + offset) * exp((-2 i / hd) * ln theta) for p < t, in f32 as
+ * the reference's rope kernel evaluates it (python/sejong_kernels/ops/kernels.py:103-113).
+ * `table` holds t*hd floats (t*hd/2 pairs). */
+int sj_rope_table(float* table, int t, int head_dim, int offset, float theta, void* stream);
 /* C[M,N] = op(A)[M,K] * op(B)[K,N], bf16 operands, f32 accumulation in TMEM.
  * a_trans: A stored [K,M] (lda >= M) instead of [M,K]; b_trans: B stored [N,K]
  * instead of [K,N] — the TA/TB flags of Engine::matmul (crates/sejong-gpu/src/
@@ -118,7 +123,8 @@ int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* i
  * residual gradient accumulation of the tape (graph.rs:503-513):
  *   dres[r,:] += rms_dx(x, w, dz) ;  dres_bf16 = bf16(dres) (optional) ;  dw += sum_r dz*x*inv.
  * x bf16 or f32 (x_dtype), dz f32, dres f32 (in/out), dw f32 accumulated.  `partials` is workspace
- * of at least ceil(rows/128)*d floats. */
+ * of at least sj_rmsnorm_workspace(rows, d) floats. */
+size_t sj_rmsnorm_workspace(int rows, int d);
 int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz, float* dres,
                    void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream);
 /* Engine::embedding (lib.rs:650-665; kernels.py:41-45): y[i,:] = w[ids[i],:]; w bf16, y bf16 or f32
@@ -163,13 +169,14 @@ int sj_add(const void* x, const void* z, void* y, size_t n, float alpha, int dty
 int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, void* o, int ldo,
                     float* lse, int batch, int t, int hq, int hk, int head_dim, int window, void* stream);
 /* Engine::attention_grouped_backward (hierarchy_ops.rs:74-147; hierarchy.py:42-104).
- * do bf16 (lddo); dq/dk/dv bf16 with their own strides; when rope_theta > 0 the inverse rotation
- * of Engine::rope(.., inverse=true) (graph.rs:879-882) is applied to dq and dk before the store.
- * `delta` is workspace f32 [batch*t*hq]. */
+ * do bf16 (lddo); dq/dk/dv bf16 with their own strides; when rope_table (an sj_rope_table of t
+ * positions) is given, or else rope_theta > 0, the inverse rotation of Engine::rope(.., inverse=true)
+ * (graph.rs:879-882) is applied to dq and dk before the store.  `delta` is workspace f32
+ * [batch*t*hq]. */
 int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o, int ldo,
                     const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk, int lddk, void* dv,
                     int lddv, float* delta, int batch, int t, int hq, int hk, int head_dim, int window,
-                    float rope_theta, void* stream);
+                    float rope_theta, const float* rope_table, void* stream);
 
 /* ------------------------------------------------------------------ optimizer */
 /* FP64 sum of squares of a flat f32 buffer into `partials` (f64, sj_sumsq_partials(n) entries):

@@ -30,7 +30,8 @@ SIGNATURES = {
     "sj_rmsnorm_fwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
     "sj_rmsnorm_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_int, c_int, c_void_p]),
-    "sj_embedding_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "sj_rmsnorm_workspace": (c_size_t, [c_int, c_int]),
+    "sj_embedding_fwd":(c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "sj_embedding_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "sj_rope": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p]),
     "sj_swiglu_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
@@ -47,7 +48,8 @@ SIGNATURES = {
                                 c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "sj_attn_gqa_bwd": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                 c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
-                                c_int, c_int, c_int, c_float, c_void_p]),
+                                c_int, c_int, c_int, c_float, c_void_p, c_void_p]),
+    "sj_rope_table": (c_int, [c_void_p, c_int, c_int, c_int, c_float, c_void_p]),
     "sj_sumsq_partials": (c_int, [c_size_t]),
     "sj_grad_sumsq": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p]),
     "sj_optim_prepare": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_float, c_float, c_int, c_int, c_float, c_float,

@@ -28,6 +28,7 @@ struct AttnParams {
   int t, hq, hk, window;
   float scale;       // head_dim^-1/2
   float rope_log_theta;  // > 0: apply the inverse RoPE rotation to dq / dk before the store
+  const float2* rope_tab;  // optional (cos, sin) table [t][32]; preferred over rope_log_theta
 };
 
 // 64 x 64 bf16 tile, 128-byte rows, 16-byte chunks XOR-swizzled by (row & 7).
@@ -104,7 +105,7 @@ SJ_DEVICE void zero(float (&c)[8][4]) {
 // Store a warp's 16 x 64 C-layout tile (rows r0.., head columns) as bf16, optionally rotating the
 // (2i, 2i+1) pairs back by the RoPE angle of position (row mod t).
 SJ_DEVICE void store_rows(__nv_bfloat16* dst, int ld, const float (&c)[8][4], int r0, int t_limit, int pos_base,
-                          float rope_log_theta) {
+                          float rope_log_theta, const float2* rope_tab) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -115,10 +116,16 @@ SJ_DEVICE void store_rows(__nv_bfloat16* dst, int ld, const float (&c)[8][4], in
     for (int nt = 0; nt < 8; ++nt) {
       const int col = nt * 8 + 2 * tq;
       float a = c[nt][2 * half], b = c[nt][2 * half + 1];
-      if (rope_log_theta > 0.f) {
-        const float inv_freq = expf((-2.0f * static_cast<float>(col >> 1) / 64.0f) * rope_log_theta);
+      if (rope_tab != nullptr || rope_log_theta > 0.f) {
         float s, co;
-        sincosf(pos * inv_freq, &s, &co);
+        if (rope_tab != nullptr) {
+          const float2 cs = rope_tab[static_cast<size_t>(pos_base + r) * 32 + (col >> 1)];
+          co = cs.x;
+          s = cs.y;
+        } else {
+          const float inv_freq = expf((-2.0f * static_cast<float>(col >> 1) / 64.0f) * rope_log_theta);
+          sincosf(pos * inv_freq, &s, &co);
+        }
         const float na = a * co + b * s, nb = -a * s + b * co;  // inverse rotation
         a = na;
         b = nb;
@@ -232,7 +239,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const AttnParams
     o[nt][3] *= inv1;
   }
   __nv_bfloat16* og = p.out + static_cast<size_t>(b) * p.t * p.ldo + h * kAttnD;
-  store_rows(og, p.ldo, o, q0 + warp * 16, p.t, 0, 0.f);
+  store_rows(og, p.ldo, o, q0 + warp * 16, p.t, 0, 0.f, nullptr);
   if (tq == 0) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
@@ -326,7 +333,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dq_kernel(const AttnParams 
     mma_ab(dq, sf, smem_u32(sk[st]));
     __syncthreads();
   }
-  store_rows(p.dq + brow * p.lddq + h * kAttnD, p.lddq, dq, q0 + warp * 16, p.t, 0, p.rope_log_theta);
+  store_rows(p.dq + brow * p.lddq + h * kAttnD, p.lddq, dq, q0 + warp * 16, p.t, 0, p.rope_log_theta, p.rope_tab);
 }
 
 // dK, dV for one 64-key tile of kv head kvh, summed over the query group (hierarchy.py:73-104).
@@ -411,8 +418,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dkv_kernel(const AttnParams
     mma_ab(dk, sf, smem_u32(sq[st]));   // dK += dS^T Q
     __syncthreads();
   }
-  store_rows(p.dk + brow * p.lddk + kvh * kAttnD, p.lddk, dk, k0 + warp * 16, p.t, 0, p.rope_log_theta);
-  store_rows(p.dv + brow * p.lddv + kvh * kAttnD, p.lddv, dv, k0 + warp * 16, p.t, 0, 0.f);
+  store_rows(p.dk + brow * p.lddk + kvh * kAttnD, p.lddk, dk, k0 + warp * 16, p.t, 0, p.rope_log_theta, p.rope_tab);
+  store_rows(p.dv + brow * p.lddv + kvh * kAttnD, p.lddv, dv, k0 + warp * 16, p.t, 0, 0.f, nullptr);
 }
 
 static int configure_attention() {
@@ -473,7 +480,8 @@ extern "C" int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, c
 extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o,
                                int ldo, const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk,
                                int lddk, void* dv, int lddv, float* delta, int batch, int t, int hq, int hk,
-                               int head_dim, int window, float rope_theta, void* stream) {
+                               int head_dim, int window, float rope_theta, const float* rope_table,
+                               void* stream) {
   int rc = check_common(batch, t, hq, hk, head_dim, window);
   if (rc) return rc;
   if ((rc = configure_attention())) return rc;
@@ -504,6 +512,9 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   p.window = window;
   p.scale = 0.125f;
   p.rope_log_theta = rope_theta > 0.f ? logf(rope_theta) : 0.f;
+  p.rope_tab = reinterpret_cast<const float2*>(rope_table);
+  if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7))
+    return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: rope table must be 8-byte aligned");
   cudaStream_t s = as_stream(stream);
   const int rows = batch * t;
   const long long warps = static_cast<long long>(rows) * hq;

@@ -73,6 +73,17 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
   y[base + 1] = f2bf(a * s + b * c);
 }
 
+__global__ void rope_table_kernel(float2* __restrict__ table, int t, int half, int offset, float log_theta,
+                                  float hd) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= t * half) return;
+  const int pos = i / half, pair = i % half;
+  const float angle = static_cast<float>(pos + offset) * expf((-2.0f * static_cast<float>(pair) / hd) * log_theta);
+  float s, c;
+  sincosf(angle, &s, &c);
+  table[i] = make_float2(c, s);
+}
+
 // ---------------------------------------------------------------- SwiGLU backward (kernels.py:95-101)
 // gu: per row, blocks of 32 columns = 16 gate features then the same 16 up features.
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dh,
@@ -303,6 +314,18 @@ extern "C" int sj_rope(const void* x, void* y, int rows, int heads, int head_dim
       static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), rows, heads, head_dim, t, offset,
       logf(theta), inverse ? -1.0f : 1.0f);
   SJ_LAUNCH_CHECK("rope");
+  return SJ_OK;
+}
+
+extern "C" int sj_rope_table(float* table, int t, int head_dim, int offset, float theta, void* stream) {
+  if (!table || t <= 0 || head_dim <= 0 || head_dim % 2 || theta <= 0.f)
+    return fail(SJ_ERR_ARGUMENT, "sj_rope_table: bad arguments");
+  if (reinterpret_cast<uintptr_t>(table) & 7) return fail(SJ_ERR_ARGUMENT, "sj_rope_table: table must be 8-byte aligned");
+  const int n = t * (head_dim / 2);
+  rope_table_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(reinterpret_cast<float2*>(table), t,
+                                                                   head_dim / 2, offset, logf(theta),
+                                                                   static_cast<float>(head_dim));
+  SJ_LAUNCH_CHECK("rope_table");
   return SJ_OK;
 }
 

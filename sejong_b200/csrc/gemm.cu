@@ -292,17 +292,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint32_t hw[16];
           if (p.epilogue == SJ_EPI_ROPE) {
-            if (col0 < p.rope_cols) {
-              const float pos = static_cast<float>(row % p.rope_t);
+            if (col0 < p.rope_cols && row < p.M) {
+              const int pos = row % p.rope_t;
+              // col0 is a multiple of 64: the unit is one head, pair index j/2
+              const float4* tab = p.aux ? reinterpret_cast<const float4*>(
+                                              static_cast<const float2*>(p.aux) + static_cast<size_t>(pos) * 32)
+                                        : nullptr;
 #pragma unroll
-              for (int j = 0; j < 64; j += 2) {
-                const int pair = j >> 1;  // col0 is a multiple of 64: pair index within the head
-                const float inv_freq = expf((-2.0f * static_cast<float>(pair) / 64.0f) * p.rope_log_theta);
-                float s, co;
-                sincosf(pos * inv_freq, &s, &co);
-                const float a = v[j], b = v[j + 1];
-                v[j] = a * co - b * s;
-                v[j + 1] = a * s + b * co;
+              for (int j = 0; j < 64; j += 4) {
+                float c0, s0, c1, s1;
+                if (tab) {
+                  const float4 cs = tab[j >> 2];  // pairs j/2 and j/2+1: (cos, sin, cos, sin)
+                  c0 = cs.x; s0 = cs.y; c1 = cs.z; s1 = cs.w;
+                } else {
+                  const float fpos = static_cast<float>(pos);
+                  sincosf(fpos * expf((-2.0f * static_cast<float>(j >> 1) / 64.0f) * p.rope_log_theta), &s0, &c0);
+                  sincosf(fpos * expf((-2.0f * static_cast<float>((j >> 1) + 1) / 64.0f) * p.rope_log_theta), &s1,
+                          &c1);
+                }
+                const float a0 = v[j], b0 = v[j + 1], a1 = v[j + 2], b1 = v[j + 3];
+                v[j] = a0 * c0 - b0 * s0;
+                v[j + 1] = a0 * s0 + b0 * c0;
+                v[j + 2] = a1 * c1 - b1 * s1;
+                v[j + 3] = a1 * s1 + b1 * c1;
               }
             }
           } else if (swiglu) {
@@ -480,8 +492,10 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
         return fail(SJ_ERR_ARGUMENT, "sj_gemm: SWIGLU needs bf16 C, an aligned aux and N %% 64 == 0");
       break;
     case SJ_EPI_ROPE:
-      if (c_dtype != SJ_BF16 || rope_t <= 0 || (rope_cols % 64) || rope_theta <= 0.f)
-        return fail(SJ_ERR_ARGUMENT, "sj_gemm: ROPE needs bf16 C, rope_t > 0, rope_cols %% 64 == 0");
+      if (c_dtype != SJ_BF16 || rope_t <= 0 || (rope_cols % 64) || (rope_theta <= 0.f && !aux) ||
+          (aux && !aligned16(aux)))
+        return fail(SJ_ERR_ARGUMENT,
+                    "sj_gemm: ROPE needs bf16 C, rope_t > 0, rope_cols %% 64 == 0 and a table or theta");
       break;
     default:
       return fail(SJ_ERR_ARGUMENT, "sj_gemm: unknown epilogue %d", epilogue);

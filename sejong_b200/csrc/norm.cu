@@ -10,7 +10,7 @@ namespace sj {
 
 constexpr int kNormMaxVec = 4;  // 4 x 8 elements per lane: d <= 1024
 constexpr int kNormWarps = 8;
-constexpr int kNormRowsPerCta = 128;
+constexpr int kNormRowsPerCta = 32;
 
 template <typename T>
 SJ_DEVICE void load8(const T* p, float (&v)[8]);
@@ -84,21 +84,29 @@ __global__ void __launch_bounds__(kNormWarps * 32)
   for (int r = blockIdx.x * kNormRowsPerCta + warp; r < min(rows, (blockIdx.x + 1) * kNormRowsPerCta);
        r += kNormWarps) {
     const size_t base = static_cast<size_t>(r) * d;
-    float xv[VEC][8], gv[VEC][8];
+    float xv[VEC][8], gv[VEC][8], o[VEC][8];
     float dot = 0.f;
     const float inv = inv_rms[r];
+    // all loads of the row are issued before the reduction: one memory round trip per row
 #pragma unroll
     for (int i = 0; i < VEC; ++i) {
       const int col = (lane + 32 * i) * 8;
       if (col < d) {
         load8<T>(x + base + col, xv[i]);
-        float dzv[8];
-        load8<float>(dz + base + col, dzv);
+        load8<float>(dz + base + col, gv[i]);
+        load8<float>(dres + base + col, o[i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int col = (lane + 32 * i) * 8;
+      if (col < d) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          gv[i][j] = dzv[j] * w[col + j];
+          const float dzv = gv[i][j];
+          gv[i][j] = dzv * w[col + j];
           dot += gv[i][j] * xv[i][j];
-          dw_acc[i][j] += dzv[j] * xv[i][j] * inv;
+          dw_acc[i][j] += dzv * xv[i][j] * inv;
         }
       }
     }
@@ -108,14 +116,13 @@ __global__ void __launch_bounds__(kNormWarps * 32)
     for (int i = 0; i < VEC; ++i) {
       const int col = (lane + 32 * i) * 8;
       if (col < d) {
-        float o[8];
-        load8<float>(dres + base + col, o);
+        float (&oi)[8] = o[i];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] += inv * (gv[i][j] - xv[i][j] * coef);
+        for (int j = 0; j < 8; ++j) oi[j] += inv * (gv[i][j] - xv[i][j] * coef);
         float4* dst = reinterpret_cast<float4*>(dres + base + col);
-        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
-        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
-        if (dres_bf16) store8_bf16(dres_bf16 + base + col, o);
+        dst[0] = make_float4(oi[0], oi[1], oi[2], oi[3]);
+        dst[1] = make_float4(oi[4], oi[5], oi[6], oi[7]);
+        if (dres_bf16) store8_bf16(dres_bf16 + base + col, oi);
       }
     }
   }
@@ -216,6 +223,11 @@ extern "C" int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* 
   return SJ_OK;
 }
 
+extern "C" size_t sj_rmsnorm_workspace(int rows, int d) {
+  if (rows <= 0 || d <= 0) return 0;
+  return static_cast<size_t>((rows + sj::kNormRowsPerCta - 1) / sj::kNormRowsPerCta) * static_cast<size_t>(d);
+}
+
 extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz,
                               float* dres, void* dres_bf16, float* dw, float* partials, int rows, int d,
                               void* stream) {
@@ -224,6 +236,8 @@ extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const 
     return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd: bad d=%d", d);
   if (!x || !w || !inv_rms || !dz || !dres || !dw || !partials)
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: null pointer");
+  if (!aligned16(x) || !aligned16(dz) || !aligned16(dres) || (dres_bf16 && !aligned16(dres_bf16)))
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: rows must be 16-byte aligned");
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
   cudaStream_t s = as_stream(stream);
   if (x_dtype == SJ_BF16)

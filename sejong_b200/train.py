@@ -87,7 +87,7 @@ class _StageRun:
         self.do = e(n, d)
         self.dqkv = e(n, cq)
         self.delta = e(n * stage.heads, dt=f32)
-        self.partials = e(((n + 63) // 64) * d, dt=f32)
+        self.partials = e(_lib.load().sj_rmsnorm_workspace(n, d), dt=f32)
 
 
 class ByteTrainer:
@@ -151,7 +151,7 @@ class ByteTrainer:
             self.dpool = e(np_, de, dt=torch.float32)
             self.dy32 = e(self.rows, dg, dt=torch.float32)
             self.dyb = e(self.rows, dg)
-            self.top_partials = e(((self.rows + 63) // 64) * max(dg, de, dd), dt=torch.float32)
+            self.top_partials = e(self.lib.sj_rmsnorm_workspace(self.rows, max(dg, de, dd)), dt=torch.float32)
             top_width = dg
         self.hf, self.invF = e(self.rows, top_width), e(self.rows, dt=torch.float32)
         self.logits = e(self.rows, VOCAB_PAD, dt=torch.float32)
@@ -159,7 +159,14 @@ class ByteTrainer:
         self.dhead = e(self.rows, top_width, dt=torch.float32)
         self.dheadb = e(self.rows, top_width)
         if h is None:
-            self.top_partials = e(((self.rows + 63) // 64) * top_width, dt=torch.float32)
+            self.top_partials = e(self.lib.sj_rmsnorm_workspace(self.rows, top_width), dt=torch.float32)
+        # RoPE (cos, sin) tables, one per distinct stage sequence length, built once
+        self.rope_tables = {}
+        for run in self.runs.values():
+            if run.seq not in self.rope_tables:
+                tab = torch.empty(run.seq * HEAD_DIM, dtype=torch.float32, device=self.dev)
+                call("sj_rope_table", _ptr(tab), run.seq, HEAD_DIM, 0, float(config.rope_theta), self.stream)
+                self.rope_tables[run.seq] = tab
         self.graph = None
 
     # kernels each entry point launches (sj_zero is a memset, not a kernel)
@@ -209,7 +216,8 @@ class ByteTrainer:
         x, xn = run.x[i], run.x[i + 1]
         self._norm(x, f"{p}.attention_norm", a["z1"], a["inv1"], n, d)
         self._gemm(_ptr(a["z1"]), d, 0, self.wb_ptr(f"{p}.qkv"), cq, 0, _ptr(a["qkv"]), cq, SJ_BF16, n, cq, d,
-                   EPI_ROPE, rope_cols=(s.heads + s.kv_heads) * HEAD_DIM, rope_t=seq)
+                   EPI_ROPE, aux=_ptr(self.rope_tables[seq]), rope_cols=(s.heads + s.kv_heads) * HEAD_DIM,
+                   rope_t=seq)
         qkv = a["qkv"]
         self._call("sj_attn_gqa_fwd", _ptr(qkv), cq, _ptr(qkv, s.heads * HEAD_DIM), cq,
              _ptr(qkv, (s.heads + s.kv_heads) * HEAD_DIM), cq, _ptr(a["o"]), d, _ptr(a["lse"]), run.batch, seq,
@@ -245,7 +253,8 @@ class ByteTrainer:
         kq, vq = s.heads * HEAD_DIM, (s.heads + s.kv_heads) * HEAD_DIM
         self._call("sj_attn_gqa_bwd", _ptr(qkv), cq, _ptr(qkv, kq), cq, _ptr(qkv, vq), cq, _ptr(a["o"]), d, _ptr(a["lse"]),
              _ptr(run.do), d, _ptr(dqkv), cq, _ptr(dqkv, kq), cq, _ptr(dqkv, vq), cq, _ptr(run.delta), run.batch,
-             seq, s.heads, s.kv_heads, HEAD_DIM, s.window, float(self.c.rope_theta), self.stream)
+             seq, s.heads, s.kv_heads, HEAD_DIM, s.window, float(self.c.rope_theta), _ptr(self.rope_tables[seq]),
+             self.stream)
         self._gemm(_ptr(a["z1"]), d, 1, _ptr(dqkv), cq, 0, self.g_ptr(f"{p}.qkv"), cq, SJ_F32, d, cq, n, EPI_ACCUM)
         self._gemm(_ptr(dqkv), cq, 0, self.wb_ptr(f"{p}.qkv"), cq, 1, _ptr(run.dz), d, SJ_F32, n, d, cq)
         self._norm_bwd(run.x[i], f"{p}.attention_norm", a["inv1"], run.dz, dx, dxb, run.partials, n, d)

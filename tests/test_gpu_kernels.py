@@ -147,11 +147,15 @@ def test_gemm_rope_epilogue():
     cq = (hq + 2 * hk) * 64
     x, w = bf(randn(m, k)), bf(randn(k, cq, scale=0.1))
     c = gemm(x, 0, w, 0, m, cq, k, c_dtype=torch.bfloat16, epi=4, rope_cols=(hq + hk) * 64, rope_t=t, theta=10000.0)
+    table = torch.empty(t * 64, device=DEV)
+    call("sj_rope_table", ptr(table), t, 64, 0, 10000.0, stream())
+    c_tab = gemm(x, 0, w, 0, m, cq, k, c_dtype=torch.bfloat16, epi=4, aux=table, rope_cols=(hq + hk) * 64, rope_t=t)
     y = (x.float() @ w.float()).double().cpu()
     q = ops.rope(y[:, :hq * 64], t, 0, hq, 10000.0)
     kk = ops.rope(y[:, hq * 64:(hq + hk) * 64], t, 0, hk, 10000.0)
     ref = torch.cat([q, kk, y[:, (hq + hk) * 64:]], dim=1)
     assert rel(c, ref) < 1e-2
+    assert rel(c_tab, ref) < 1e-2
 
 
 def test_gemm_rejects_bad_arguments():
@@ -180,7 +184,8 @@ def test_rmsnorm_forward_backward(rows, d, x_f32):
     dres = dres0.clone()
     dres_b = torch.empty(rows, d, dtype=torch.bfloat16, device=DEV)
     dw = torch.zeros(d, device=DEV)
-    partials = torch.empty(((rows + 63) // 64) * d, device=DEV)
+    from sejong_b200 import _lib
+    partials = torch.empty(_lib.load().sj_rmsnorm_workspace(rows, d), device=DEV)
     call("sj_rmsnorm_bwd", ptr(x), xdt, ptr(w), ptr(inv), ptr(dz), ptr(dres), ptr(dres_b), ptr(dw), ptr(partials),
          rows, d, stream())
     torch.cuda.synchronize()
@@ -216,7 +221,7 @@ def test_attention_forward_backward(b, t, hq, hk, window):
     delta = torch.empty(n * hq, dtype=torch.float32, device=DEV)
     call("sj_attn_gqa_bwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), ptr(do),
          hq * d, ptr(dqkv), cq, ptr(dqkv, ko), cq, ptr(dqkv, vo), cq, ptr(delta), b, t, hq, hk, d, window, 0.0,
-         stream())
+         0, stream())
     torch.cuda.synchronize()
     check_device_error()
     assert rel(dqkv[:, :ko], q.grad) < 2e-2
@@ -234,18 +239,34 @@ def test_attention_backward_inverse_rope():
     call("sj_attn_gqa_fwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), b, t, hq, hk,
          d, 0, stream())
     do = bf(randn(n, hq * d))
+    table = torch.empty(t * 64, device=DEV)
+    call("sj_rope_table", ptr(table), t, 64, 0, 10000.0, stream())
     outs = []
-    for theta in (0.0, 10000.0):
+    for theta, tab in ((0.0, 0), (10000.0, 0), (0.0, ptr(table))):
         dqkv = torch.zeros(n, cq, dtype=torch.bfloat16, device=DEV)
         delta = torch.empty(n * hq, device=DEV)
         call("sj_attn_gqa_bwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), ptr(do),
              hq * d, ptr(dqkv), cq, ptr(dqkv, ko), cq, ptr(dqkv, vo), cq, ptr(delta), b, t, hq, hk, d, 0, theta,
-             stream())
+             tab, stream())
         outs.append(dqkv.double().cpu())
-    plain, rotated = outs
-    assert rel(rotated[:, :ko], ops.rope(plain[:, :ko], t, 0, hq, 10000.0, inverse=True)) < 2e-2
-    assert rel(rotated[:, ko:vo], ops.rope(plain[:, ko:vo], t, 0, hk, 10000.0, inverse=True)) < 2e-2
-    assert rel(rotated[:, vo:], plain[:, vo:]) == 0.0
+    plain = outs[0]
+    for rotated in outs[1:]:
+        assert rel(rotated[:, :ko], ops.rope(plain[:, :ko], t, 0, hq, 10000.0, inverse=True)) < 2e-2
+        assert rel(rotated[:, ko:vo], ops.rope(plain[:, ko:vo], t, 0, hk, 10000.0, inverse=True)) < 2e-2
+        assert rel(rotated[:, vo:], plain[:, vo:]) == 0.0
+
+
+def test_rope_table_matches_reference_formula():
+    t = 300
+    table = torch.empty(t * 64, device=DEV)
+    call("sj_rope_table", ptr(table), t, 64, 0, 10000.0, stream())
+    torch.cuda.synchronize()
+    tab = table.reshape(t, 32, 2).double().cpu()
+    pos = torch.arange(t, dtype=torch.float64)[:, None]
+    pair = torch.arange(32, dtype=torch.float64)[None, :]
+    angle = pos * torch.exp((-2.0 * pair / 64) * np.log(10000.0))
+    assert float((tab[..., 0] - torch.cos(angle)).abs().max()) < 5e-4
+    assert float((tab[..., 1] - torch.sin(angle)).abs().max()) < 5e-4
 
 
 # ------------------------------------------------------------------------------------- elementwise
