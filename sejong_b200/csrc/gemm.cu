@@ -40,10 +40,11 @@ struct GemmParams {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpilogueWarps = 8;  // two per TMEM lane quarter, alternating 128-byte column units
+constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kSmemLimit = 232448;          // 227 KB: the sm_100 per-block opt-in maximum
-constexpr int kStagingC = 4 * 2 * 4096;      // 4 epilogue warps x 2 buffers x (32 rows x 128 B)
-constexpr int kStagingH = 4 * 2 * 2048;      // SwiGLU h output: 4 x 2 x (32 rows x 64 B)
+constexpr int kStagingC = kEpilogueWarps * 4096;  // one 32 rows x 128 B slab per epilogue warp
+constexpr int kStagingH = kEpilogueWarps * 2048;  // SwiGLU h output: 32 rows x 64 B per warp
 constexpr int kBarrierBytes = 256;
 
 template <int BN>
@@ -67,7 +68,7 @@ SJ_DEVICE void tma_reduce_add_2d(const CUtensorMap* map, const void* smem, int x
                : "memory");
 }
 SJ_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-SJ_DEVICE void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+SJ_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 SJ_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 SJ_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], kEpilogueWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -217,9 +218,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(drain, 0, nullptr, SJ_DEV_GEMM_DRAIN_WAIT);
     }
   } else {
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
-    uint8_t* my_c = staging_c + quarter * 2 * 4096;
-    uint8_t* my_h = staging_h + quarter * 2 * 2048;
+    const int quarter = warp & 3;       // TMEM lanes [32*quarter, 32*quarter+32) belong to this warp
+    const int ew = warp - 2;            // epilogue warp 0..7
+    const int half = ew >> 2;           // takes column units c with c % 2 == half
+    uint8_t* my_c = staging_c + ew * 4096;  // one 32 x 128 B slab per warp
+    uint8_t* my_h = staging_h + ew * 2048;
     int local = 0, unit = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const int mb = (tile % tiles_mn) / p.n_tiles;
@@ -233,7 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
       if (p.c_f32) {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           const int col0 = nb * BN + c * 32;
           if (col0 >= p.N) break;
           uint32_t r[32];
@@ -258,8 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (col0 + j < p.N) r[j] = __float_as_uint(__uint_as_float(r[j]) + res[j]);
             }
           }
-          uint8_t* sbuf = my_c + (unit & 1) * 4096;
-          if (lane == 0) bulk_wait_read1();
+          uint8_t* sbuf = my_c;
+          if (lane == 0) bulk_wait_read0();  // this warp's previous slab has been read out
           __syncwarp();
           stage_row128(sbuf, lane, r);
           fence_async_smem();
@@ -277,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = half; c < BN / 64; c += 2) {
           const int col0 = nb * BN + c * 64;
           if (col0 >= p.N) break;
           uint32_t r[32], r2[32];
@@ -329,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int e = 0; e < 2; ++e) {
                   const float g = round_bf16(v[32 * half + j + e]);
                   const float u = round_bf16(v[32 * half + 16 + j + e]);
-                  hv[e] = g / (1.0f + __expf(-g)) * u;
+                  hv[e] = __fdividef(g, 1.0f + __expf(-g)) * u;
                 }
                 hw[8 * half + (j >> 1)] = pack_bf16x2(hv[0], hv[1]);
               }
@@ -361,9 +364,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t w[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-          uint8_t* sbuf = my_c + (unit & 1) * 4096;
-          uint8_t* hbuf = my_h + (unit & 1) * 2048;
-          if (lane == 0) bulk_wait_read1();
+          uint8_t* sbuf = my_c;
+          uint8_t* hbuf = my_h;
+          if (lane == 0) bulk_wait_read0();  // this warp's previous slabs have been read out
           __syncwarp();
           stage_row128(sbuf, lane, w);
           if (swiglu) stage_row64(hbuf, lane, hw);
