@@ -213,25 +213,19 @@ def run_ours(args):
     import torch
     import torch.distributed as dist
 
+    from sejong_b200 import distributed
     from sejong_b200 import model as pm
     from sejong_b200.train import ByteTrainer, TrainConfig, corpus_batch, synthetic_corpus_tokens
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rank, world, local, pg = distributed.init_from_env("nccl", timeout_s=300)
     torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-        pg = dist.group.WORLD
     cfg = pm.config_c3()
     tc = TrainConfig(sequence=args.seq, batch=args.batch, warmup_steps=0, steps=10000)
     trainer = ByteTrainer(cfg, tc, device=local, process_group=pg)
     rows = tc.batch * tc.sequence
     total = args.warmup + args.steps
-    toks = synthetic_corpus_tokens(1000 + rank, 1 << 22)
-    st = ctypes.c_uint64(123 + rank)
+    toks = synthetic_corpus_tokens(distributed.rank_seed(1000, rank), 1 << 22)
+    st = ctypes.c_uint64(distributed.rank_seed(123, rank))
     host_ids = torch.empty(total, rows, dtype=torch.int32).pin_memory()
     host_tg = torch.empty(total, rows, dtype=torch.int32).pin_memory()
     for i in range(total):

@@ -32,7 +32,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, distributed
 from ._lib import (EPI_ACCUM, EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call)
 from .model import HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage
 
@@ -309,10 +309,9 @@ class ByteTrainer:
         self._norm(top, "final_norm", self.hf, self.invF, n, top_width)
         self._gemm(_ptr(self.hf), top_width, 0, self.wb_ptr("output"), VOCAB_PAD, 0, _ptr(self.logits), VOCAB_PAD,
                    SJ_F32, n, VOCAB, top_width)
-        scale = 1.0 / (n * self.world)
         self._call("sj_cross_entropy", _ptr(self.logits), VOCAB_PAD, _ptr(self.targets), n, VOCAB,
-             float(self.tc.loss_scale * scale), 0, _ptr(self.dlogits), VOCAB_PAD, _ptr(self.loss_sum), scale,
-             self.stream)
+                   distributed.ce_seed(n, self.world, self.tc.loss_scale), 0, _ptr(self.dlogits), VOCAB_PAD,
+                   _ptr(self.loss_sum), distributed.ce_seed(n, self.world), self.stream)
         return top, top_width
 
     def _backward(self, top, top_width):
@@ -383,8 +382,7 @@ class ByteTrainer:
         """Data-parallel exchange: sum of the per-rank gradients (each seeded with 1/global rows, so
         the sum is the global-batch mean gradient) and of the loss, over NCCL."""
         if self.world > 1:
-            torch.distributed.all_reduce(self.g, group=self.pg)
-            torch.distributed.all_reduce(self.loss_sum, group=self.pg)
+            distributed.exchange(self.g, self.loss_sum, self.pg)
 
     def forward_backward(self):
         """Loss (into self.loss_sum) and gradients (into self.g) for the staged batch."""
