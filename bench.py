@@ -41,8 +41,8 @@ CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ = 1, 1024
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=8, help="per-GPU batch")
     ap.add_argument("--seq", type=int, default=4096)
@@ -254,17 +254,17 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    clocks = ClockSampler(local)  # sampling starts before warm-up so it is running in the timed region
+    clocks.start()
     for i in range(args.warmup):
         trainer.ids.copy_(host_ids[i], non_blocking=True)
         trainer.targets.copy_(host_tg[i], non_blocking=True)
         trainer.replay()
         loss_host[i].copy_(trainer.loss_sum[0], non_blocking=True)
     barrier()
+    time.sleep(0.3)
 
-    clocks = ClockSampler(local)
-    clocks.start()
     # device-resident inputs
-    launches_before = trainer.launches
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(stream)

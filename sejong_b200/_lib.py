@@ -50,6 +50,7 @@ SIGNATURES = {
                                 c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
                                 c_int, c_int, c_int, c_float, c_void_p, c_void_p]),
     "sj_rope_table": (c_int, [c_void_p, c_int, c_int, c_int, c_float, c_void_p]),
+    "sj_attn_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
     "sj_sumsq_partials": (c_int, [c_size_t]),
     "sj_grad_sumsq": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p]),
     "sj_optim_prepare": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_float, c_float, c_int, c_int, c_float, c_float,

@@ -6,7 +6,9 @@
 // every query; here a CTA owns a 64-query (or 64-key) tile, K/V (or Q/dO) tiles are staged once in
 // swizzled shared memory with cp.async double buffering and shared by the CTA's four warps, and the
 // products run on bf16 mma.sync tensor-core tiles with f32 accumulation and an online softmax.
-// dK/dV sum over the query group inside the CTA (no atomics); dQ is a separate pass.
+// dQ is one pass over key tiles; dK/dV is one CTA per (key tile, query head) so the causal
+// critical path is a single head long, and for grouped heads a small kernel sums the group's f32
+// partials (no atomics) and applies the inverse RoPE.
 #include "common.cuh"
 #include "internal.h"
 
@@ -141,11 +143,12 @@ constexpr int kFwdSmem = 5 * kTileElems * 2;
 constexpr int kDqSmem = 6 * kTileElems * 2;
 constexpr int kDkvSmem = 6 * kTileElems * 2 + 4 * kAttnTile * 4;
 
-__global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_fwd_kernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t attn_smem[];
+  // smem: Q tile, then K stages 0/1, then V stages 0/1 (stage st at + st * kTileElems)
   __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(attn_smem);
-  __nv_bfloat16* sk[2] = {sq + kTileElems, sq + 2 * kTileElems};
-  __nv_bfloat16* sv[2] = {sq + 3 * kTileElems, sq + 4 * kTileElems};
+  __nv_bfloat16* sk0 = sq + kTileElems;
+  __nv_bfloat16* sv0 = sq + 3 * kTileElems;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.hq / p.hk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
@@ -157,8 +160,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const AttnParams
   const int kb_hi = min((q0 + kAttnTile - 1) / kAttnTile, (p.t - 1) / kAttnTile);
 
   load_tile_async(sq, qg, p.ldq, q0, p.t);
-  load_tile_async(sk[0], kg, p.ldk, kb_lo * kAttnTile, p.t);
-  load_tile_async(sv[0], vg, p.ldv, kb_lo * kAttnTile, p.t);
+  load_tile_async(sk0, kg, p.ldk, kb_lo * kAttnTile, p.t);
+  load_tile_async(sv0, vg, p.ldv, kb_lo * kAttnTile, p.t);
   cp_async_commit();
 
   const float sl2 = p.scale * kLog2e;
@@ -171,8 +174,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const AttnParams
   for (int kb = kb_lo; kb <= kb_hi; ++kb) {
     const int st = (kb - kb_lo) & 1;
     if (kb < kb_hi) {
-      load_tile_async(sk[st ^ 1], kg, p.ldk, (kb + 1) * kAttnTile, p.t);
-      load_tile_async(sv[st ^ 1], vg, p.ldv, (kb + 1) * kAttnTile, p.t);
+      load_tile_async(sk0 + (st ^ 1) * kTileElems, kg, p.ldk, (kb + 1) * kAttnTile, p.t);
+      load_tile_async(sv0 + (st ^ 1) * kTileElems, vg, p.ldv, (kb + 1) * kAttnTile, p.t);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -182,7 +185,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const AttnParams
     if (kb == kb_lo) load_a_frags(qf, smem_u32(sq), warp * 16);
     float s[8][4];
     zero(s);
-    mma_abt(s, qf, smem_u32(sk[st]));
+    mma_abt(s, qf, smem_u32(sk0 + st * kTileElems));
     float mx[2] = {m[0], m[1]};
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_fwd_kernel(const AttnParams
     }
     uint32_t pf[4][4];
     c_to_a_frags(pf, s);
-    mma_ab(o, pf, smem_u32(sv[st]));
+    mma_ab(o, pf, smem_u32(sv0 + st * kTileElems));
     __syncthreads();
   }
 #pragma unroll
@@ -264,12 +267,13 @@ __global__ void attn_delta_kernel(const AttnParams p, int rows) {
 }
 
 // dQ for one 64-query tile of head h (hierarchy.py:42-70).
-__global__ void __launch_bounds__(kAttnThreads) attn_dq_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_dq_kernel(const AttnParams p) {
   extern __shared__ __align__(128) uint8_t attn_smem[];
+  // smem: Q, dO, then K stages 0/1, then V stages 0/1
   __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(attn_smem);
   __nv_bfloat16* sdo = sq + kTileElems;
-  __nv_bfloat16* sk[2] = {sq + 2 * kTileElems, sq + 3 * kTileElems};
-  __nv_bfloat16* sv[2] = {sq + 4 * kTileElems, sq + 5 * kTileElems};
+  __nv_bfloat16* sk0 = sq + 2 * kTileElems;
+  __nv_bfloat16* sv0 = sq + 4 * kTileElems;
   const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int kvh = h / (p.hq / p.hk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
@@ -282,8 +286,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dq_kernel(const AttnParams 
 
   load_tile_async(sq, p.q + brow * p.ldq + h * kAttnD, p.ldq, q0, p.t);
   load_tile_async(sdo, p.dout + brow * p.lddo + h * kAttnD, p.lddo, q0, p.t);
-  load_tile_async(sk[0], kg, p.ldk, kb_lo * kAttnTile, p.t);
-  load_tile_async(sv[0], vg, p.ldv, kb_lo * kAttnTile, p.t);
+  load_tile_async(sk0, kg, p.ldk, kb_lo * kAttnTile, p.t);
+  load_tile_async(sv0, vg, p.ldv, kb_lo * kAttnTile, p.t);
   cp_async_commit();
 
   const int row_lo = q0 + warp * 16 + g;
@@ -301,8 +305,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dq_kernel(const AttnParams 
   for (int kb = kb_lo; kb <= kb_hi; ++kb) {
     const int st = (kb - kb_lo) & 1;
     if (kb < kb_hi) {
-      load_tile_async(sk[st ^ 1], kg, p.ldk, (kb + 1) * kAttnTile, p.t);
-      load_tile_async(sv[st ^ 1], vg, p.ldv, (kb + 1) * kAttnTile, p.t);
+      load_tile_async(sk0 + (st ^ 1) * kTileElems, kg, p.ldk, (kb + 1) * kAttnTile, p.t);
+      load_tile_async(sv0 + (st ^ 1) * kTileElems, vg, p.ldv, (kb + 1) * kAttnTile, p.t);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
@@ -316,8 +320,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dq_kernel(const AttnParams 
     float s[8][4], dp[8][4];
     zero(s);
     zero(dp);
-    mma_abt(s, qf, smem_u32(sk[st]));
-    mma_abt(dp, df, smem_u32(sv[st]));
+    mma_abt(s, qf, smem_u32(sk0 + st * kTileElems));
+    mma_abt(dp, df, smem_u32(sv0 + st * kTileElems));
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -330,47 +334,51 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dq_kernel(const AttnParams 
       }
     uint32_t sf[4][4];
     c_to_a_frags(sf, s);
-    mma_ab(dq, sf, smem_u32(sk[st]));
+    mma_ab(dq, sf, smem_u32(sk0 + st * kTileElems));
     __syncthreads();
   }
   store_rows(p.dq + brow * p.lddq + h * kAttnD, p.lddq, dq, q0 + warp * 16, p.t, 0, p.rope_log_theta, p.rope_tab);
 }
 
-// dK, dV for one 64-key tile of kv head kvh, summed over the query group (hierarchy.py:73-104).
-__global__ void __launch_bounds__(kAttnThreads) attn_dkv_kernel(const AttnParams p) {
+// dK, dV of one 64-key tile against ONE query head h (hierarchy.py:73-104 sums the query group in
+// one program; here each query head is its own CTA so the causal critical path is one head long).
+// With a single query head per kv head the result is stored directly (bf16, inverse RoPE on dK);
+// otherwise the f32 partial goes to part_dk / part_dv [rows, hq*64] and attn_dkv_reduce_kernel
+// sums the group.
+__global__ void __launch_bounds__(kAttnThreads, 3) attn_dkv_kernel(const AttnParams p, float* part_dk,
+                                                                    float* part_dv) {
   extern __shared__ __align__(128) uint8_t attn_smem[];
+  // smem: K, V, then Q stages 0/1, dO stages 0/1, LSE stages 0/1, Delta stages 0/1
   __nv_bfloat16* skk = reinterpret_cast<__nv_bfloat16*>(attn_smem);
   __nv_bfloat16* svv = skk + kTileElems;
-  __nv_bfloat16* sq[2] = {skk + 2 * kTileElems, skk + 3 * kTileElems};
-  __nv_bfloat16* sdo[2] = {skk + 4 * kTileElems, skk + 5 * kTileElems};
-  float* slse_base = reinterpret_cast<float*>(skk + 6 * kTileElems);
-  float* slse[2] = {slse_base, slse_base + kAttnTile};
-  float* sdl[2] = {slse_base + 2 * kAttnTile, slse_base + 3 * kAttnTile};
-  const int kb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  __nv_bfloat16* sq0 = skk + 2 * kTileElems;
+  __nv_bfloat16* sdo0 = skk + 4 * kTileElems;
+  float* slse0 = reinterpret_cast<float*>(skk + 6 * kTileElems);
+  float* sdl0 = slse0 + 2 * kAttnTile;
+  const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int group = p.hq / p.hk;
+  const int kvh = h / group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
   const int k0 = kb * kAttnTile;
   const size_t brow = static_cast<size_t>(b) * p.t;
   const int nqb = (p.t + kAttnTile - 1) / kAttnTile;
   const int qb_lo = k0 / kAttnTile;
   const int qb_hi = p.window > 0 ? min(nqb - 1, (k0 + kAttnTile - 1 + p.window - 1) / kAttnTile) : nqb - 1;
-  const int per_head = qb_hi - qb_lo + 1;
-  const int total = per_head * group;
+  const __nv_bfloat16* qg = p.q + brow * p.ldq + h * kAttnD;
+  const __nv_bfloat16* dog = p.dout + brow * p.lddo + h * kAttnD;
 
   load_tile_async(skk, p.k + brow * p.ldk + kvh * kAttnD, p.ldk, k0, p.t);
   load_tile_async(svv, p.v + brow * p.ldv + kvh * kAttnD, p.ldv, k0, p.t);
-  auto issue = [&](int it, int st) {
-    const int h = kvh * group + it / per_head;
-    const int qb = qb_lo + it % per_head;
-    load_tile_async(sq[st], p.q + brow * p.ldq + h * kAttnD, p.ldq, qb * kAttnTile, p.t);
-    load_tile_async(sdo[st], p.dout + brow * p.lddo + h * kAttnD, p.lddo, qb * kAttnTile, p.t);
+  auto issue = [&](int qb, int st) {
+    load_tile_async(sq0 + st * kTileElems, qg, p.ldq, qb * kAttnTile, p.t);
+    load_tile_async(sdo0 + st * kTileElems, dog, p.lddo, qb * kAttnTile, p.t);
     for (int i = threadIdx.x; i < kAttnTile; i += kAttnThreads) {
       const int r = min(qb * kAttnTile + i, p.t - 1);
-      slse[st][i] = p.lse_in[(brow + r) * p.hq + h] * kLog2e;
-      sdl[st][i] = p.delta[(brow + r) * p.hq + h];
+      slse0[st * kAttnTile + i] = p.lse_in[(brow + r) * p.hq + h] * kLog2e;
+      sdl0[st * kAttnTile + i] = p.delta[(brow + r) * p.hq + h];
     }
   };
-  issue(0, 0);
+  issue(qb_lo, 0);
   cp_async_commit();
 
   const float sl2 = p.scale * kLog2e;
@@ -379,26 +387,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dkv_kernel(const AttnParams
   float dk[8][4], dv[8][4];
   zero(dk);
   zero(dv);
-  for (int it = 0; it < total; ++it) {
-    const int st = it & 1;
-    if (it + 1 < total) {
-      issue(it + 1, st ^ 1);
+  for (int qb = qb_lo; qb <= qb_hi; ++qb) {
+    const int st = (qb - qb_lo) & 1;
+    if (qb < qb_hi) {
+      issue(qb + 1, st ^ 1);
       cp_async_commit();
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
-    if (it == 0) {
+    if (qb == qb_lo) {
       load_a_frags(kf, smem_u32(skk), warp * 16);
       load_a_frags(vf, smem_u32(svv), warp * 16);
     }
-    const int qb = qb_lo + it % per_head;
-    float s[8][4], dp[8][4];
+    const float* slse = slse0 + st * kAttnTile;
+    const float* sdl = sdl0 + st * kAttnTile;
+    const uint32_t q_tile = smem_u32(sq0 + st * kTileElems);
+    const uint32_t do_tile = smem_u32(sdo0 + st * kTileElems);
+    float s[8][4];
     zero(s);
-    zero(dp);
-    mma_abt(s, kf, smem_u32(sq[st]));    // S^T = K Q^T   [keys x queries]
-    mma_abt(dp, vf, smem_u32(sdo[st]));  // dP^T = V dO^T
+    mma_abt(s, kf, q_tile);  // S^T = K Q^T   [keys x queries]
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
@@ -407,19 +416,91 @@ __global__ void __launch_bounds__(kAttnThreads) attn_dkv_kernel(const AttnParams
         const int qi = nt * 8 + 2 * tq + (e & 1);
         const int qpos = qb * kAttnTile + qi;
         const bool ok = qpos >= kpos && qpos < p.t && kpos < p.t && (p.window <= 0 || qpos - kpos < p.window);
-        const float pr = ok ? exp2f(s[nt][e] * sl2 - slse[st][qi]) : 0.f;
-        s[nt][e] = pr;                                             // P^T
-        dp[nt][e] = pr * (dp[nt][e] - sdl[st][qi]) * p.scale;      // dS^T
+        s[nt][e] = ok ? exp2f(s[nt][e] * sl2 - slse[qi]) : 0.f;  // P^T
       }
-    uint32_t pf[4][4], sf[4][4];
-    c_to_a_frags(pf, s);
-    c_to_a_frags(sf, dp);
-    mma_ab(dv, pf, smem_u32(sdo[st]));  // dV += P^T dO
-    mma_ab(dk, sf, smem_u32(sq[st]));   // dK += dS^T Q
+    {
+      uint32_t pf[4][4];
+      c_to_a_frags(pf, s);
+      mma_ab(dv, pf, do_tile);  // dV += P^T dO
+    }
+    float dp[8][4];
+    zero(dp);
+    mma_abt(dp, vf, do_tile);  // dP^T = V dO^T
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qi = nt * 8 + 2 * tq + (e & 1);
+        dp[nt][e] = s[nt][e] * (dp[nt][e] - sdl[qi]) * p.scale;  // dS^T
+      }
+    {
+      uint32_t sf[4][4];
+      c_to_a_frags(sf, dp);
+      mma_ab(dk, sf, q_tile);  // dK += dS^T Q
+    }
     __syncthreads();
   }
-  store_rows(p.dk + brow * p.lddk + kvh * kAttnD, p.lddk, dk, k0 + warp * 16, p.t, 0, p.rope_log_theta, p.rope_tab);
-  store_rows(p.dv + brow * p.lddv + kvh * kAttnD, p.lddv, dv, k0 + warp * 16, p.t, 0, 0.f, nullptr);
+  if (group == 1) {
+    store_rows(p.dk + brow * p.lddk + kvh * kAttnD, p.lddk, dk, k0 + warp * 16, p.t, 0, p.rope_log_theta,
+               p.rope_tab);
+    store_rows(p.dv + brow * p.lddv + kvh * kAttnD, p.lddv, dv, k0 + warp * 16, p.t, 0, 0.f, nullptr);
+    return;
+  }
+  // f32 partials of this query head: [rows, hq*64]
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int r = k0 + warp * 16 + g + half * 8;
+    if (r >= p.t) continue;
+    float* pk = part_dk + (brow + r) * (static_cast<size_t>(p.hq) * kAttnD) + h * kAttnD;
+    float* pv = part_dv + (brow + r) * (static_cast<size_t>(p.hq) * kAttnD) + h * kAttnD;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int col = nt * 8 + 2 * tq;
+      *reinterpret_cast<float2*>(pk + col) = make_float2(dk[nt][2 * half], dk[nt][2 * half + 1]);
+      *reinterpret_cast<float2*>(pv + col) = make_float2(dv[nt][2 * half], dv[nt][2 * half + 1]);
+    }
+  }
+}
+
+// Sum the query-group partials of dK / dV, apply the inverse RoPE to dK, store bf16.
+// One thread per (row, kv head, column pair).
+__global__ void attn_dkv_reduce_kernel(const AttnParams p, const float* __restrict__ part_dk,
+                                       const float* __restrict__ part_dv, int rows) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int pairs = p.hk * (kAttnD / 2);
+  if (i >= static_cast<size_t>(rows) * pairs) return;
+  const int row = static_cast<int>(i / pairs);
+  const int kvh = static_cast<int>(i % pairs) / (kAttnD / 2);
+  const int col = (static_cast<int>(i % pairs) % (kAttnD / 2)) * 2;
+  const int group = p.hq / p.hk;
+  float2 k = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
+  const size_t base = static_cast<size_t>(row) * p.hq * kAttnD;
+  for (int j = 0; j < group; ++j) {
+    const int h = kvh * group + j;
+    const float2 a = *reinterpret_cast<const float2*>(part_dk + base + h * kAttnD + col);
+    const float2 c = *reinterpret_cast<const float2*>(part_dv + base + h * kAttnD + col);
+    k.x += a.x;
+    k.y += a.y;
+    v.x += c.x;
+    v.y += c.y;
+  }
+  if (p.rope_tab != nullptr || p.rope_log_theta > 0.f) {
+    const int pos = row % p.t;
+    float s, co;
+    if (p.rope_tab != nullptr) {
+      const float2 cs = p.rope_tab[static_cast<size_t>(pos) * 32 + (col >> 1)];
+      co = cs.x;
+      s = cs.y;
+    } else {
+      sincosf(static_cast<float>(pos) * expf((-2.0f * static_cast<float>(col >> 1) / 64.0f) * p.rope_log_theta), &s,
+              &co);
+    }
+    const float na = k.x * co + k.y * s, nb = -k.x * s + k.y * co;
+    k.x = na;
+    k.y = nb;
+  }
+  *reinterpret_cast<uint32_t*>(p.dk + static_cast<size_t>(row) * p.lddk + kvh * kAttnD + col) = pack_bf16x2(k.x, k.y);
+  *reinterpret_cast<uint32_t*>(p.dv + static_cast<size_t>(row) * p.lddv + kvh * kAttnD + col) = pack_bf16x2(v.x, v.y);
 }
 
 static int configure_attention() {
@@ -447,6 +528,12 @@ static int check_common(int batch, int t, int hq, int hk, int head_dim, int wind
 }  // namespace sj
 
 using namespace sj;
+
+extern "C" size_t sj_attn_workspace(int batch, int t, int hq, int hk) {
+  if (batch <= 0 || t <= 0 || hq <= 0 || hk <= 0) return 0;
+  const size_t rows = static_cast<size_t>(batch) * t;
+  return rows * hq + (hq != hk ? 2 * rows * hq * kAttnD : 0);
+}
 
 extern "C" int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, void* o,
                                int ldo, float* lse, int batch, int t, int hq, int hk, int head_dim, int window,
@@ -479,14 +566,14 @@ extern "C" int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, c
 
 extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o,
                                int ldo, const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk,
-                               int lddk, void* dv, int lddv, float* delta, int batch, int t, int hq, int hk,
-                               int head_dim, int window, float rope_theta, const float* rope_table,
-                               void* stream) {
+                               int lddk, void* dv, int lddv, float* workspace, int batch, int t, int hq, int hk,
+                               int head_dim, int window, float rope_theta, const float* rope_table, void* stream) {
   int rc = check_common(batch, t, hq, hk, head_dim, window);
   if (rc) return rc;
   if ((rc = configure_attention())) return rc;
   if ((ldq | ldk | ldv | ldo | lddo | lddq | lddk | lddv) % 8)
     return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: strides must be multiples of 8");
+  if (!workspace || !aligned16(workspace)) return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: workspace must be aligned");
   AttnParams p{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = static_cast<const __nv_bfloat16*>(k);
@@ -497,7 +584,6 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   p.dk = static_cast<__nv_bfloat16*>(dk);
   p.dv = static_cast<__nv_bfloat16*>(dv);
   p.lse_in = lse;
-  p.delta = delta;
   p.ldq = ldq;
   p.ldk = ldk;
   p.ldv = ldv;
@@ -515,14 +601,24 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   p.rope_tab = reinterpret_cast<const float2*>(rope_table);
   if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7))
     return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: rope table must be 8-byte aligned");
-  cudaStream_t s = as_stream(stream);
   const int rows = batch * t;
+  // workspace: delta [rows*hq], then (GQA only) f32 dK / dV partials [rows, hq*64] each
+  p.delta = workspace;
+  float* part_dk = workspace + ((static_cast<size_t>(rows) * hq + 3) / 4) * 4;
+  float* part_dv = part_dk + static_cast<size_t>(rows) * hq * kAttnD;
+  cudaStream_t s = as_stream(stream);
   const long long warps = static_cast<long long>(rows) * hq;
   attn_delta_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(p, rows);
   SJ_LAUNCH_CHECK("attn_delta");
   attn_dq_kernel<<<dim3((t + kAttnTile - 1) / kAttnTile, hq, batch), kAttnThreads, kDqSmem, s>>>(p);
   SJ_LAUNCH_CHECK("attn_dq");
-  attn_dkv_kernel<<<dim3((t + kAttnTile - 1) / kAttnTile, hk, batch), kAttnThreads, kDkvSmem, s>>>(p);
+  attn_dkv_kernel<<<dim3((t + kAttnTile - 1) / kAttnTile, hq, batch), kAttnThreads, kDkvSmem, s>>>(p, part_dk,
+                                                                                                  part_dv);
   SJ_LAUNCH_CHECK("attn_dkv");
+  if (hq != hk) {
+    const size_t n = static_cast<size_t>(rows) * hk * (kAttnD / 2);
+    attn_dkv_reduce_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(p, part_dk, part_dv, rows);
+    SJ_LAUNCH_CHECK("attn_dkv_reduce");
+  }
   return SJ_OK;
 }

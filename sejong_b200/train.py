@@ -86,7 +86,7 @@ class _StageRun:
         self.dgu = e(n, 2 * f)
         self.do = e(n, d)
         self.dqkv = e(n, cq)
-        self.delta = e(n * stage.heads, dt=f32)
+        self.delta = e(_lib.load().sj_attn_workspace(batch, seq, stage.heads, stage.kv_heads), dt=f32)
         self.partials = e(_lib.load().sj_rmsnorm_workspace(n, d), dt=f32)
 
 

@@ -218,7 +218,8 @@ def test_attention_forward_backward(b, t, hq, hk, window):
     do = bf(randn(n, hq * d))
     (ro * do.double().cpu()).sum().backward()
     dqkv = torch.zeros(n, cq, dtype=torch.bfloat16, device=DEV)
-    delta = torch.empty(n * hq, dtype=torch.float32, device=DEV)
+    from sejong_b200 import _lib
+    delta = torch.empty(_lib.load().sj_attn_workspace(b, t, hq, hk), dtype=torch.float32, device=DEV)
     call("sj_attn_gqa_bwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), ptr(do),
          hq * d, ptr(dqkv), cq, ptr(dqkv, ko), cq, ptr(dqkv, vo), cq, ptr(delta), b, t, hq, hk, d, window, 0.0,
          0, stream())
@@ -244,7 +245,8 @@ def test_attention_backward_inverse_rope():
     outs = []
     for theta, tab in ((0.0, 0), (10000.0, 0), (0.0, ptr(table))):
         dqkv = torch.zeros(n, cq, dtype=torch.bfloat16, device=DEV)
-        delta = torch.empty(n * hq, device=DEV)
+        from sejong_b200 import _lib
+        delta = torch.empty(_lib.load().sj_attn_workspace(b, t, hq, hk), device=DEV)
         call("sj_attn_gqa_bwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), ptr(do),
              hq * d, ptr(dqkv), cq, ptr(dqkv, ko), cq, ptr(dqkv, vo), cq, ptr(delta), b, t, hq, hk, d, 0, theta,
              tab, stream())
