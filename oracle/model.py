@@ -195,18 +195,30 @@ def initialize(c):
     return params
 
 
+# Every parameter matmul goes through `mm`, in the reference's node-creation order, so that a
+# recorder (param_vjp.py) can replay the tape's backward visit order (graph.rs:567-913).
+MATMUL_HOOK = None
+
+
+def mm(x, p, name):
+    y = x @ p[name]
+    if MATMUL_HOOK is not None:
+        MATMUL_HOOK(name, x, y)
+    return y
+
+
 def _block(p, prefix, s, x, seq, theta, eps):
     z = ops.rmsnorm(x, p[f"{prefix}.attention_norm"], eps)
-    q = z @ p[f"{prefix}.query"]
-    k = z @ p[f"{prefix}.key"]
-    v = z @ p[f"{prefix}.value"]
+    q = mm(z, p, f"{prefix}.query")
+    k = mm(z, p, f"{prefix}.key")
+    v = mm(z, p, f"{prefix}.value")
     q = ops.rope(q, seq, 0, s.heads, theta)
     k = ops.rope(k, seq, 0, s.kv_heads, theta)
     a, _ = ops.grouped_attention(q, k, v, seq, s.heads, s.kv_heads, s.window)
-    x = x + a @ p[f"{prefix}.attention_output"]
+    x = x + mm(a, p, f"{prefix}.attention_output")
     z = ops.rmsnorm(x, p[f"{prefix}.ffn_norm"], eps)
     if s.experts is not None:
-        logits = z @ p[f"{prefix}.router"]
+        logits = mm(z, p, f"{prefix}.router")
         gates, ids = ops.route_topk(logits, s.experts.top_k)
         update = torch.zeros_like(z)
         for e in range(s.experts.count):
@@ -214,12 +226,12 @@ def _block(p, prefix, s, x, seq, theta, eps):
             if rows.numel() == 0:
                 continue
             xe = z[rows]
-            he = ops.swiglu(xe @ p[f"{prefix}.experts.{e}.gate"], xe @ p[f"{prefix}.experts.{e}.up"])
-            ye = he @ p[f"{prefix}.experts.{e}.down"]
+            he = ops.swiglu(mm(xe, p, f"{prefix}.experts.{e}.gate"), mm(xe, p, f"{prefix}.experts.{e}.up"))
+            ye = mm(he, p, f"{prefix}.experts.{e}.down")
             update = update.index_add(0, rows, ye * gates[rows, slot][:, None])
     else:
-        h = ops.swiglu(z @ p[f"{prefix}.gate"], z @ p[f"{prefix}.up"])
-        update = h @ p[f"{prefix}.down"]
+        h = ops.swiglu(mm(z, p, f"{prefix}.gate"), mm(z, p, f"{prefix}.up"))
+        update = mm(h, p, f"{prefix}.down")
     return x + update
 
 
@@ -240,17 +252,17 @@ def hidden(p, c, ids, seq):
     x = _blocks(p, local_stage(c, True), x, seq, c)
     x = ops.rmsnorm(x, p["encoder_norm"], eps)
     pooled = ops.patch_pool(x, seq, h.patch_size)
-    z = pooled @ p["encoder_to_global"]
+    z = mm(pooled, p, "encoder_to_global")
     patches = -(-seq // h.patch_size)
     z = _blocks(p, global_stage(c), z, patches, c)
     z = ops.rmsnorm(z, p["global_norm"], eps)
-    z = z @ p["global_to_decoder"]
-    bos = p["global_bos"] @ p["global_to_decoder"]
+    z = mm(z, p, "global_to_decoder")
+    bos = mm(p["global_bos"], p, "global_to_decoder")
     z = ops.patch_broadcast(z, bos, seq, h.patch_size)
-    x = x @ p["encoder_to_decoder"] + z
+    x = mm(x, p, "encoder_to_decoder") + z
     x = _blocks(p, local_stage(c, False), x, seq, c)
     x = ops.rmsnorm(x, p["decoder_norm"], eps)
-    x = x @ p["output_projection"]
+    x = mm(x, p, "output_projection")
     return ops.rmsnorm(x, p["final_norm"], eps)
 
 
@@ -283,7 +295,7 @@ def loss_and_grads(params, c, ids, targets, seq, dtype=torch.float64, scale=1.0,
     ids = torch.as_tensor(np.asarray(ids, dtype=np.int64))
     targets = torch.as_tensor(np.asarray(targets, dtype=np.int64))
     h = hidden(p, c, ids, seq)
-    logits = h @ p["output"]
+    logits = mm(h, p, "output")
     per_row = ops.cross_entropy(logits, targets)
     loss = per_row.mean()
     (loss * scale).backward()

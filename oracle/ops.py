@@ -64,7 +64,7 @@ def rope(x, t, offset, heads, theta, inverse=False):
     pos = (torch.arange(n, dtype=torch.float64) % t + offset)[:, None, None]
     pair = torch.arange(d // 2, dtype=torch.float64)[None, None, :]
     angle = pos * torch.exp((-2.0 * pair / d) * math.log(theta))
-    cos, sin = torch.cos(angle), torch.sin(angle)
+    cos, sin = torch.cos(angle).to(x.dtype), torch.sin(angle).to(x.dtype)
     if inverse:
         sin = -sin
     xv = x.reshape(n, heads, d // 2, 2)
