@@ -127,6 +127,17 @@ int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* i
 size_t sj_rmsnorm_workspace(int rows, int d);
 int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz, float* dres,
                    void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream);
+/* No counterpart in the reference: an addition for callers that cannot allocate device memory
+ * (a plugin interface that passes only the op's tensors, or a process whose device memory is held
+ * by another allocator).  Same arguments and results as sj_rmsnorm_bwd without `partials`: the
+ * partials live in a fixed 4 MiB array inside the library's device image, so the call allocates
+ * nothing.  Limit: sj_rmsnorm_workspace(rows, d) <= sj_rmsnorm_noalloc_limit() floats, else
+ * SJ_ERR_CAPACITY.  The first call on each device looks the array up (and loads the library's
+ * device code there if needed): make it before any stream capture.  Calls that overlap in time on
+ * one device share the array and race: serialise them. */
+size_t sj_rmsnorm_noalloc_limit(void);
+int sj_rmsnorm_bwd_noalloc(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz,
+                           float* dres, void* dres_bf16, float* dw, int rows, int d, void* stream);
 /* Engine::embedding (lib.rs:650-665; kernels.py:41-45): y[i,:] = w[ids[i],:]; w bf16, y bf16 or f32
  * (y_dtype; f32 starts an f32 residual stream).  Ids outside [0, vocab) are an error recorded in the
  * device error word (row left zero). */

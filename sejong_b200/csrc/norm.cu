@@ -3,6 +3,8 @@
 // rmsnorm_backward_partial/_reduce (crates/sejong-gpu/src/norm_ops.rs:14-134); the backward is
 // fused with the residual-gradient accumulation the tape performs with separate `add` launches
 // (crates/sejong-gpu/src/graph.rs:503-513).
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -249,5 +251,84 @@ extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const 
   SJ_LAUNCH_CHECK("rmsnorm_bwd");
   column_reduce_add_kernel<<<(d + 31) / 32, 256, 0, s>>>(partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd reduce");
+  return SJ_OK;
+}
+
+// ------------------------------------------------------------------ RMSNorm backward without a workspace
+// Some callers cannot hand over device memory for the dw partials: a plugin whose interface
+// passes only the tensors of the op, or a process whose device memory is all reserved by
+// another allocator so that a cudaMalloc here would fail (and a cudaFree would stall the whole
+// device).  sj_rmsnorm_bwd_noalloc keeps the partials in a fixed array that lives in the
+// library's own device image instead, so the call itself allocates nothing.
+//
+// Limit: ceil(rows / 32) * d <= kNoAllocPartials floats (4 MiB per GPU, held by every GPU that
+// loads the library until the process exits), e.g. 32768 rows at d = 1024 or 131072 at d = 256.
+// Larger shapes are rejected with SJ_ERR_CAPACITY.  The array is shared by all calls on a device,
+// so two calls that overlap in time on the same device (two streams, two host threads) race
+// on it; serialise them.  Nothing in it has to start at zero: every CTA of the backward kernel
+// writes its full partial row before the column reduction reads it.
+namespace sj {
+
+constexpr size_t kNoAllocPartials = size_t(1) << 20;
+constexpr int kNoAllocMaxDevices = 64;
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
+
+static std::mutex g_noalloc_mutex;
+static float* g_noalloc_address[kNoAllocMaxDevices];
+
+// Device address of g_noalloc_partials on the current device, looked up once per device.  The
+// first lookup loads the library's device image on that device if it is not loaded yet.
+static int noalloc_partials(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_check(e, "sj_rmsnorm_bwd_noalloc: cudaGetDevice");
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: device %d beyond the %d supported", dev,
+                kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_address[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+    if (e != cudaSuccess) return cuda_check(e, "sj_rmsnorm_bwd_noalloc: cudaGetSymbolAddress");
+    if (!p) return fail(SJ_ERR_CUDA, "sj_rmsnorm_bwd_noalloc: null scratch address");
+    g_noalloc_address[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_address[dev];
+  return SJ_OK;
+}
+
+}  // namespace sj
+
+extern "C" size_t sj_rmsnorm_noalloc_limit(void) { return sj::kNoAllocPartials; }
+
+extern "C" int sj_rmsnorm_bwd_noalloc(const void* x, int x_dtype, const float* w, const float* inv_rms,
+                                      const float* dz, float* dres, void* dres_bf16, float* dw, int rows, int d,
+                                      void* stream) {
+  using namespace sj;
+  if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
+    return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd_noalloc: bad d=%d", d);
+  const size_t need = sj_rmsnorm_workspace(rows, d);
+  if (need > kNoAllocPartials)
+    return fail(SJ_ERR_CAPACITY,
+                "sj_rmsnorm_bwd_noalloc: rows=%d d=%d needs %zu partial floats, above the static limit of %zu",
+                rows, d, need, kNoAllocPartials);
+  if (!x || !w || !inv_rms || !dz || !dres || !dw)
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: null pointer");
+  if (!aligned16(x) || !aligned16(dz) || !aligned16(dres) || (dres_bf16 && !aligned16(dres_bf16)))
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: rows must be 16-byte aligned");
+  if (x_dtype != SJ_BF16 && x_dtype != SJ_F32)
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: x must be bf16 or f32");
+  float* partials = nullptr;
+  const int status = noalloc_partials(&partials);
+  if (status != SJ_OK) return status;
+  const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
+  cudaStream_t s = as_stream(stream);
+  if (x_dtype == SJ_BF16)
+    dispatch_norm_bwd<__nv_bfloat16>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
+  else
+    dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
+  SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc");
+  column_reduce_add_kernel<<<(d + 31) / 32, 256, 0, s>>>(partials, groups, d, dw);
+  SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc reduce");
   return SJ_OK;
 }
