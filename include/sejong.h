@@ -216,6 +216,36 @@ int sj_adamw(float* w, const float* g, float* m, float* v, void* w_bf16, size_t 
 int sj_sgd(float* w, const float* g, void* w_bf16, size_t n, size_t n_decay, const float* hyper, float weight_decay,
            void* stream);
 
+/* ------------------------------------------------------------------ parameter VJP (low-rank + selected rows) */
+/* The index draw of the parameter_indices kernel (python/sejong_kernels/ops/parameter.py:25-62) as
+ * launched by ParameterVjp::prepare (crates/sejong-gpu/src/parameter_vjp.rs:186-214): a SplitMix64
+ * generator seeded with one next_u64 of `rng_state` (device memory, advanced in place) draws a
+ * partial Fisher-Yates of r of the b donor columns, then of s of the nb feature blocks of `group`
+ * rows.  columns [r]; rows [s*group] (feature index, -1 past a); row_map [a] (position in rows or -1).
+ * scratch: b + nb ints.  Zero sizes skip the corresponding draw, as the reference's do. */
+int sj_param_indices(uint64_t* rng_state, int a, int b, int nb, int s, int r, int group, int32_t* scratch,
+                     int32_t* columns, int32_t* rows, int32_t* row_map, void* stream);
+/* The same draw on the host from an explicit seed (the reference kernel's own inputs). */
+int sj_param_indices_host(uint64_t seed, int a, int b, int nb, int s, int r, int group, int32_t* columns,
+                          int32_t* rows, int32_t* row_map);
+/* Orthonormal basis q [n, r] f32 of the selected donor columns Y[:, columns] with Y = x w (x bf16
+ * [n, a], row stride ldx; w bf16 with row stride ldw, pointing at the donor's first column;
+ * interleave > 0 selects the second half of a weight interleaved in blocks of `interleave`
+ * columns): the CGS2 with small-norm cutoff `eps` of parameter.py:65-129 / parameter_vjp.rs:216-258.
+ * workspace: sj_param_basis_workspace(n, r) bytes, 8-byte aligned.  r <= 32. */
+size_t sj_param_basis_workspace(int n, int r);
+int sj_param_basis(const void* x, int ldx, int n, int a, const void* w, int ldw, int interleave, const int32_t* columns,
+                   int r, float eps, float* q, void* workspace, void* stream);
+/* The prepare kernel (parameter.py:131-191, parameter_vjp.rs:260-290): left = x^T q [a, r] f32 and
+ * E [(r + k), n] bf16 = [q^T ; (x - q left^T)[:, rows]^T * inverse] (zero rows where rows[i] < 0),
+ * inverse = NB/S in f32.  E is the A operand of the coefficient GEMM (right; tail) = E dY. */
+int sj_param_prepare(const void* x, int ldx, int n, int a, const float* q, int r, const int32_t* rows, int k,
+                     float inverse, float* left, void* e, void* stream);
+/* The factored gradient (parameter.py:204-244): g[i, j] (+)= sum_k left[i, k] coeff[k, j] +
+ * coeff[r + row_map[i], j] (when row_map[i] >= 0), j < b; coeff rows [0, r) = right, [r, r+k) = tail. */
+int sj_param_materialize(const float* left, const float* coeff, int ldc, const int32_t* row_map, int a, int b, int r,
+                         float* g, int ldg, int accumulate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

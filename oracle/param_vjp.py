@@ -193,15 +193,24 @@ class VjpState:
                 self.selections[a] = selection
         q, columns = basis
         rows, row_map = selection
-        left = x.T @ q
-        k = selected * cfg.block_rows
-        e = np.zeros((rank + k, n))
-        e[:rank] = q.T
         inverse = float(np.float32(blocks) / np.float32(selected))
-        for pos, row in enumerate(rows):
-            if row >= 0:
-                e[rank + pos] = (x[:, row] - q @ left[row]) * inverse
+        left, e = prepare_factors(x, q, rows, inverse)
         return Prepared(q, left, e, row_map, rows, columns)
+
+
+def prepare_factors(x, q, rows, inverse):
+    """parameter_prepare (parameter.py:131-166): left = X^T Q and
+    E = [Q^T ; (X - Q left^T)[:, rows] * inverse] (zero rows for padded entries rows[i] < 0)."""
+    x = np.asarray(x, dtype=np.float64)
+    q = np.asarray(q, dtype=np.float64)
+    rank = q.shape[1]
+    left = x.T @ q
+    e = np.zeros((rank + len(rows), x.shape[0]))
+    e[:rank] = q.T
+    for pos, row in enumerate(rows):
+        if row >= 0:
+            e[rank + pos] = (x[:, row] - q @ left[row]) * inverse
+    return left, e
 
 
 def factored_gradient(prep, dy, scale=1.0):

@@ -28,11 +28,12 @@ weights and moments, FP64 loss and gradient norm.
 import ctypes
 import math
 from dataclasses import dataclass
+from typing import Optional
 
 import numpy as np
 import torch
 
-from . import _lib, distributed
+from . import _lib, distributed, param_vjp
 from ._lib import (EPI_ACCUM, EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call)
 from .model import HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage
 
@@ -55,6 +56,9 @@ class TrainConfig:
     clip_enabled: bool = True
     loss_scale: float = 1.0
     seed: int = 123
+    # weight gradients through the parameter VJP (low-rank factors + selected rows), as the
+    # reference's control-variate trainer does (crates/sejong-train/src/control_variate.rs)
+    parameter_vjp: Optional[param_vjp.VjpConfig] = None
 
 
 def _ptr(t, offset_elems=0):
@@ -168,10 +172,13 @@ class ByteTrainer:
                 call("sj_rope_table", _ptr(tab), run.seq, HEAD_DIM, 0, float(config.rope_theta), self.stream)
                 self.rope_tables[run.seq] = tab
         self.graph = None
+        self.vjp = None
+        if train.parameter_vjp is not None:
+            self._init_vjp(train.parameter_vjp)
 
     # kernels each entry point launches (sj_zero is a memset, not a kernel)
     KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 3,
-               "sj_zero": 0}
+               "sj_zero": 0, "sj_param_basis": 4, "sj_param_prepare": 2}
 
     def _call(self, name, *args):
         call(name, *args)
@@ -208,6 +215,100 @@ class ByteTrainer:
     def _zero(self, t):
         self._call("sj_zero", _ptr(t), t.numel() * t.element_size(), self.stream)
 
+    # ------------------------------------------------------------------ parameter VJP
+    def _init_vjp(self, cfg):
+        """Plan and buffers of the parameter VJP (crates/sejong-gpu/src/parameter_vjp.rs:133-321).
+
+        The generator state lives on the device and advances there, so the step stays free of
+        host round trips; bases are kept per (rows, rank) and selections per width, as the
+        reference shares them within one backward pass."""
+        self.vjp = param_vjp.plan(self.c, self.tc.batch, self.tc.sequence, cfg)
+        dev, i32, f32 = self.dev, torch.int32, torch.float32
+        # with data parallelism every rank draws its own basis and selection from its own X; the
+        # sum of the ranks' factored gradients (the all-reduce) applies every rank's terms
+        rank = torch.distributed.get_rank(self.pg) if self.pg is not None else 0
+        seed = distributed.rank_seed(cfg.seed, rank)
+        self.vjp_rng = torch.from_numpy(np.array([seed], dtype=np.uint64).view(np.int64)).to(dev)
+        self.vjp_q, self.vjp_columns, self.vjp_rows, self.vjp_map = {}, {}, {}, {}
+        scratch = basis_ws = left = e = coeff = 1
+        for g in self.vjp.groups.values():
+            donor = g.members[g.donor].width
+            self.vjp_q.setdefault(g.basis_key, torch.empty(g.rows, g.rank, dtype=f32, device=dev))
+            self.vjp_columns.setdefault(g.basis_key, torch.zeros(g.rank, dtype=i32, device=dev))
+            self.vjp_rows.setdefault(g.features, torch.zeros(g.k, dtype=i32, device=dev))
+            self.vjp_map.setdefault(g.features, torch.zeros(g.features, dtype=i32, device=dev))
+            scratch = max(scratch, donor + g.blocks)
+            basis_ws = max(basis_ws, self.lib.sj_param_basis_workspace(g.rows, g.rank))
+            left = max(left, g.features * g.rank)
+            e = max(e, (g.rank + g.k) * g.rows)
+            coeff = max(coeff, (g.rank + g.k) * sum(m.width for m in g.members))
+        self.vjp_scratch = torch.zeros(scratch, dtype=i32, device=dev)
+        self.vjp_ws = torch.empty((basis_ws + 7) // 8, dtype=torch.float64, device=dev)
+        self.vjp_left = torch.empty(left, dtype=f32, device=dev)
+        self.vjp_e = torch.empty(e, dtype=torch.bfloat16, device=dev)
+        self.vjp_coeff = torch.empty(coeff, dtype=f32, device=dev)
+
+    def vjp_rng_state(self):
+        """The device generator state as the reference Rng's u64."""
+        return int(self.vjp_rng.cpu().numpy().view(np.uint64)[0])
+
+    def _member_layout(self, g, fused):
+        """(column offset, width, interleave) of each member inside the fused weight `fused`:
+        `*.qkv` holds query | key | value; `*.gate_up` interleaves gate and up in 16-column blocks."""
+        if fused.endswith(".gate_up"):
+            return [(0, m.width, 16) for m in g.members]
+        out, col = [], 0
+        for m in g.members:
+            out.append((col, m.width, 0))
+            col += m.width
+        return out
+
+    def _weight_grad(self, key, x, dy, gname):
+        """dW += X^T dY for the fused weight `gname` (X [n, a] bf16, dY [n, width] bf16): a dense
+        TN GEMM, or, for a group the plan compresses, the parameter VJP of its active members."""
+        n, a = x.shape
+        width = dy.shape[1]
+        g = self.vjp.groups.get(key) if self.vjp is not None else None
+        if g is None:
+            self._gemm(_ptr(x), a, 1, _ptr(dy), width, 0, self.g_ptr(gname), width, SJ_F32, a, width, n, EPI_ACCUM)
+            return
+        layout = self._member_layout(g, gname)
+        wname = gname
+        r, k = g.rank, g.k
+        cols, q = self.vjp_columns[g.basis_key], self.vjp_q[g.basis_key]
+        rows, row_map = self.vjp_rows[a], self.vjp_map[a]
+        if g.draw:
+            donor_width = g.members[g.donor].width
+            self._call("sj_param_indices", _ptr(self.vjp_rng), a if g.new_selection else 0,
+                       donor_width if g.new_basis else 0, g.blocks if g.new_selection else 0,
+                       g.selected if g.new_selection else 0, r if g.new_basis else 0, g.block_rows,
+                       _ptr(self.vjp_scratch), _ptr(cols), _ptr(rows), _ptr(row_map), self.stream)
+        if g.new_basis:
+            off, _, interleave = layout[g.donor]
+            if interleave:
+                assert g.donor == len(g.members) - 1, "an interleaved donor must be the second half"
+            self._call("sj_param_basis", _ptr(x), a, n, a, _ptr(self.wb, self.layout[wname].offset + off), width,
+                       interleave, _ptr(cols), r, param_vjp.basis_eps(n, r), _ptr(q), _ptr(self.vjp_ws), self.stream)
+        self._call("sj_param_prepare", _ptr(x), a, n, a, _ptr(q), r, _ptr(rows), k, g.inverse, _ptr(self.vjp_left),
+                   _ptr(self.vjp_e), self.stream)
+        # (right ; tail) = E dY over all columns of the fused weight
+        coeff = self.vjp_coeff[:(r + k) * width]
+        self._zero(coeff)
+        self._gemm(_ptr(self.vjp_e), n, 0, _ptr(dy), width, 0, _ptr(coeff), width, SJ_F32, r + k, width, n, EPI_ACCUM)
+        interleaved = layout[0][2] > 0
+        if interleaved:
+            assert len(g.active) in (0, len(g.members)), "gate and up share one decision (equal widths)"
+            spans = [(0, width, True)]
+        else:
+            spans = [(off, w, i in g.active) for i, (off, w, _) in enumerate(layout)]
+        for off, w, compressed in spans:
+            if compressed:
+                self._call("sj_param_materialize", _ptr(self.vjp_left), _ptr(coeff, off), width, _ptr(row_map), a, w,
+                           r, self.g_ptr(gname) + off * 4, width, 1, self.stream)
+            else:
+                self._gemm(_ptr(x), a, 1, _ptr(dy, off), width, 0, self.g_ptr(gname) + off * 4, width, SJ_F32, a, w,
+                           n, EPI_ACCUM)
+
     # ------------------------------------------------------------------ blocks
     def _block_fwd(self, run, i):
         s, a = run.stage, run.layers[i]
@@ -240,8 +341,7 @@ class ByteTrainer:
         self._gemm(_ptr(a["h"]), f, 1, _ptr(dxb), d, 0, self.g_ptr(f"{p}.down"), d, SJ_F32, f, d, n, EPI_ACCUM)
         self._gemm(_ptr(dxb), d, 0, self.wb_ptr(f"{p}.down"), d, 1, _ptr(run.dh), f, SJ_BF16, n, f, d)
         self._call("sj_swiglu_bwd", _ptr(a["gu"]), _ptr(run.dh), _ptr(run.dgu), n, f, self.stream)
-        self._gemm(_ptr(a["z2"]), d, 1, _ptr(run.dgu), 2 * f, 0, self.g_ptr(f"{p}.gate_up"), 2 * f, SJ_F32, d, 2 * f,
-                   n, EPI_ACCUM)
+        self._weight_grad(f"{p}.z2", a["z2"], run.dgu, f"{p}.gate_up")
         self._gemm(_ptr(run.dgu), 2 * f, 0, self.wb_ptr(f"{p}.gate_up"), 2 * f, 1, _ptr(run.dz), d, SJ_F32, n, d,
                    2 * f)
         self._norm_bwd(a["x1"], f"{p}.ffn_norm", a["inv2"], run.dz, dx, dxb, run.partials, n, d)
@@ -255,7 +355,7 @@ class ByteTrainer:
              _ptr(run.do), d, _ptr(dqkv), cq, _ptr(dqkv, kq), cq, _ptr(dqkv, vq), cq, _ptr(run.delta), run.batch,
              seq, s.heads, s.kv_heads, HEAD_DIM, s.window, float(self.c.rope_theta), _ptr(self.rope_tables[seq]),
              self.stream)
-        self._gemm(_ptr(a["z1"]), d, 1, _ptr(dqkv), cq, 0, self.g_ptr(f"{p}.qkv"), cq, SJ_F32, d, cq, n, EPI_ACCUM)
+        self._weight_grad(f"{p}.z1", a["z1"], dqkv, f"{p}.qkv")
         self._gemm(_ptr(dqkv), cq, 0, self.wb_ptr(f"{p}.qkv"), cq, 1, _ptr(run.dz), d, SJ_F32, n, d, cq)
         self._norm_bwd(run.x[i], f"{p}.attention_norm", a["inv1"], run.dz, dx, dxb, run.partials, n, d)
 

@@ -263,6 +263,59 @@ def parameter_index_cases():
                                GROUP=group, BLOCK=512)
     save("parameter_indices", columns=columns, rows=rows, map=row_map,
          shape=np.array([a, bcols, nb, s, r, group], dtype=np.int64), seed=np.uint64(seed))
+    # the hierarchical model's two preparations (local d256 / FFN 768, global d768 / FFN 2048), a
+    # basis-only and a selection-only draw (the zero sizes of a reused basis or selection)
+    cases = [(256, 768, 8, 2, 16, 32), (768, 2048, 24, 6, 16, 32), (0, 300, 0, 0, 16, 32), (200, 0, 7, 2, 0, 32)]
+    for idx, (a, bcols, nb, s, r, group) in enumerate(cases):
+        seed = (0x9E3779B97F4A7C15 * (idx + 3)) & 0xFFFFFFFFFFFFFFFF
+        scratch = torch.empty(max(bcols + nb, 1), dtype=torch.int32)
+        columns = torch.full((max(r, 1),), -7, dtype=torch.int32)
+        rows = torch.full((max(s * group, 1),), -7, dtype=torch.int32)
+        row_map = torch.full((max(a, 1),), -7, dtype=torch.int32)
+        lo = np.int64(seed & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
+        hi = np.int64(seed >> 32).astype(np.uint32).view(np.int32)
+        PV.parameter_indices[(1,)](scratch, columns, rows, row_map, a, bcols, nb, s, r, int(lo), int(hi),
+                                   GROUP=group, BLOCK=512)
+        save(f"parameter_indices_{idx}", columns=columns[:r], rows=rows[:s * group], map=row_map[:a],
+             shape=np.array([a, bcols, nb, s, r, group], dtype=np.int64), seed=np.uint64(seed))
+
+
+def parameter_basis_cases():
+    # CGS2 of selected donor columns: the register form (small N) and the streaming form; the
+    # streaming case selects a column twice so the small-norm cutoff zeroes one basis column
+    for tag, n, bcols, cols in (("register", 40, 20, [3, 17, 0, 9, 11, 5]),
+                                ("streaming", 300, 37, [4, 30, 12, 4, 7, 21, 0, 36, 15, 2, 8, 25, 33, 19, 1, 28])):
+        y = randn(n, bcols)
+        columns = torch.tensor(cols, dtype=torch.int32)
+        r = len(cols)
+        q = torch.full((n, r), float("nan"))
+        operations = n * (4.0 * r + 1.0)
+        roundoff = operations * (np.finfo(np.float32).eps / 2.0)
+        eps = float(np.float32(roundoff / (1.0 - roundoff)))
+        if tag == "register":
+            PV.parameter_basis_register[(1,)](y, columns, q, n, bcols, eps, R=r, NR=npow2(n), NC=npow2(r))
+        else:
+            PV.parameter_basis[(1,)](y, columns, q, n, bcols, eps, R=r, BR=16, BC=32)
+        save(f"parameter_basis_{tag}", y=y, columns=columns, q=q, eps=np.float32(eps))
+
+
+def parameter_prepare_cases():
+    # left = X^T Q and E = [Q^T ; (X - Q left^T)[:, rows] * INVERSE] with the rows of a draw
+    n, m, r, group, nb, s = 96, 70, 5, 16, 5, 2
+    x = randn(n, m)
+    q = torch.linalg.qr(randn(n, r, dtype=torch.float64))[0].float().contiguous()  # QR returns column-major
+    rows = [16 * 3 + o for o in range(16)] + [16 * 4 + o for o in range(16)]
+    row_map = torch.full((m,), -1, dtype=torch.int32)
+    for pos, row in enumerate(rows):
+        if row < m:
+            row_map[row] = pos
+    k = s * group
+    inverse = float(np.float32(nb) / np.float32(s))
+    a_out = torch.full((m, r), float("nan"))
+    e = torch.zeros(r + k, n)
+    PV.parameter_prepare[(-(-m // 16),)](x, q, a_out, row_map, e, m, n, k, r, inverse, BM=16, BN=32, BK=32)
+    save("parameter_prepare", x=x, q=q, map=row_map, left=a_out, e=e,
+         shape=np.array([n, m, r, k], dtype=np.int64), inverse=np.float32(inverse))
 
 
 def main():
@@ -273,7 +326,9 @@ def main():
     hierarchy_cases()
     projection_cases()
     parameter_index_cases()
-    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_kernels.npz")
+    parameter_basis_cases()
+    parameter_prepare_cases()
+    path =os.path.join(os.path.dirname(os.path.abspath(__file__)), "reference_kernels.npz")
     np.savez_compressed(path, **OUT)
     print(f"wrote {len(OUT)} arrays to {path}")
 

@@ -225,3 +225,47 @@ def test_rng_pinned_by_parameter_indices():
             idx = blocks[i] * group + o
             rows.append(idx if idx < a else -1)
     assert rows == list(g(p, "rows"))
+
+
+@pytest.mark.parametrize("case", ["parameter_indices"] + [f"parameter_indices_{i}" for i in range(4)])
+def test_param_vjp_indices_pinned(case):
+    """oracle.param_vjp.parameter_indices reproduces the reference kernel (parameter.py:25-62) bit for
+    bit, including the zero-size draws of a reused basis or selection."""
+    from oracle import param_vjp as pv
+    a, bcols, nb, s, r, group = (int(v) for v in g(case, "shape"))
+    columns, rows, row_map = pv.parameter_indices(int(g(case, "seed")), a, bcols, nb, s, r, group)
+    assert list(columns) == list(g(case, "columns"))
+    assert list(rows) == list(g(case, "rows"))
+    assert list(row_map) == list(g(case, "map"))
+
+
+@pytest.mark.parametrize("tag", ["register", "streaming"])
+def test_param_vjp_basis_pinned(tag):
+    """oracle.param_vjp.basis_cgs2 (FP64) matches the reference's f32 CGS2 (parameter.py:65-129),
+    including the column the small-norm cutoff zeroes."""
+    from oracle import param_vjp as pv
+    p = f"parameter_basis_{tag}"
+    y, cols = g(p, "y"), g(p, "columns")
+    n, r = y.shape[0], len(cols)
+    eps = pv.basis_eps(n, r)
+    assert np.float32(eps) == g(p, "eps")
+    q = pv.basis_cgs2(y[:, cols], eps)
+    ref = g(p, "q")
+    zero = np.all(ref == 0, axis=0)
+    assert list(np.all(q == 0, axis=0)) == list(zero)
+    close(q, ref, 2e-5)
+
+
+def test_param_vjp_prepare_pinned():
+    """oracle.param_vjp.prepare_factors matches parameter_prepare (parameter.py:131-166)."""
+    from oracle import param_vjp as pv
+    p = "parameter_prepare"
+    n, m, r, k = (int(v) for v in g(p, "shape"))
+    row_map = g(p, "map")
+    rows = np.full(k, -1)
+    for row, pos in enumerate(row_map):
+        if pos >= 0:
+            rows[pos] = row
+    left, e = pv.prepare_factors(g(p, "x"), g(p, "q"), rows, float(g(p, "inverse")))
+    close(left, g(p, "left"), 1e-5)
+    close(e, g(p, "e"), 1e-5)
