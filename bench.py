@@ -34,8 +34,15 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "train_bytes_per_s"
+WORKLOADS = {"c3": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
+             "c4": "C4 hierarchical byte model, fwd + input VJP + parameter VJP (rank 16, fraction 0.25) + "
+                   "compact SGD lr 1e-2 (BASELINE configs[3])"}
 UNIT = "bytes/s"
 CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ = 1, 1024
+# DRAM bytes (read + write) of all GEMM launches of one C3 step, from the ncu launch list of
+# `python bench.py --steps 1 --warmup 3 --no-cpu-baseline --no-kernel-timing` summarised in
+# profiles/c3_step_launch_list.txt (ncu flushes caches between launches: an upper bound)
+NCU_GEMM_DRAM_BYTES_PER_STEP = {"c3": 5.5066e9}
 
 
 def parse():
@@ -46,6 +53,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=8, help="per-GPU batch")
     ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--config", choices=["c3", "c4"], default="c3",
+                    help="c3: AdamW (BASELINE configs[2]); c4: parameter-VJP SGD (configs[3])")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--kernel-report", default=None, help="write per-call kernel timings (JSON) to this path")
@@ -107,12 +116,14 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU restatement (oracle) timing
-def cpu_step_rate(steps, warmup, threads=None):
-    """bytes/s of the oracle's fp32 CPU training step on the bounded C3 sample."""
+def cpu_step_rate(steps, warmup, threads=None, config="c3"):
+    """bytes/s of the oracle's fp32 CPU training step on the bounded sample of C3 (AdamW) or C4
+    (parameter-VJP SGD)."""
     import numpy as np
     import torch
 
     from oracle import model as omodel
+    from oracle import param_vjp as opv
     from oracle.corpus import synthetic_corpus
     from oracle.rng import Rng
     if threads:
@@ -122,13 +133,20 @@ def cpu_step_rate(steps, warmup, threads=None):
     corp = synthetic_corpus(1000, 1 << 20)
     rng = Rng(123)
     state = omodel.AdamState()
-    tc = omodel.TrainConfig(sequence=CPU_SAMPLE_SEQ, batch=CPU_SAMPLE_BATCH)
+    tc = omodel.TrainConfig(sequence=CPU_SAMPLE_SEQ, batch=CPU_SAMPLE_BATCH,
+                            learning_rate=1e-2 if config == "c4" else 3e-4)
+    vcfg = opv.VjpConfig()
+    vrng = Rng(vcfg.seed)
     times = []
     for i in range(warmup + steps):
         ids, tg = corp.batch(rng, CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ)
         t0 = time.perf_counter()
-        loss, grads = omodel.loss_and_grads(params, c, ids, tg, CPU_SAMPLE_SEQ, dtype=torch.float32)
-        params, _ = omodel.adam_update(params, grads, state, tc)
+        if config == "c4":
+            _, grads, _ = opv.vjp_gradients(params, c, ids, tg, CPU_SAMPLE_SEQ, vcfg, vrng)
+            params, _ = opv.sgd_update(params, grads, tc, i)
+        else:
+            loss, grads = omodel.loss_and_grads(params, c, ids, tg, CPU_SAMPLE_SEQ, dtype=torch.float32)
+            params, _ = omodel.adam_update(params, grads, state, tc)
         params = {k: np.asarray(v, dtype=np.float32) for k, v in params.items()}
         if i >= warmup:
             times.append(time.perf_counter() - t0)
@@ -136,7 +154,10 @@ def cpu_step_rate(steps, warmup, threads=None):
     return CPU_SAMPLE_BATCH * CPU_SAMPLE_SEQ / sec, sec, torch.get_num_threads()
 
 
-def cpu_sample_text(steps):
+def cpu_sample_text(steps, config="c3"):
+    if config == "c4":
+        return (f"C4 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
+                f"FP64 CPU fwd + input VJP + parameter VJP + compact SGD, mean of {steps} steps")
     return (f"C3 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
             f"fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps")
 
@@ -146,15 +167,15 @@ def run_reference(args):
     if rank != 0:
         return
     steps, warmup = max(1, min(args.steps, 10)), max(0, min(args.warmup, 2))
-    rate, sec, cores = cpu_step_rate(steps, warmup)
+    rate, sec, cores = cpu_step_rate(steps, warmup, config=args.config)
     line = {"metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
             "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic Zipf(1.1) bytes, random-init N(0,0.02) weights",
-            "config": {"workload": "C3 hierarchical byte model fwd+bwd+AdamW (bounded CPU sample)",
+            "config": {"workload": WORKLOADS[args.config] + " (bounded CPU sample)",
                        "per_gpu_batch": CPU_SAMPLE_BATCH, "seq_len": CPU_SAMPLE_SEQ, "parallelism": "none"},
             "impl": "reference",
             "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": cpu_sample_text(steps)},
+                             "sample": cpu_sample_text(steps, args.config)},
             "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference has no CPU execution path (Engine::new needs HIP) and its Rust host cannot "
                     "be built in this image; this arm times the CPU restatement of its step in oracle/"}
@@ -220,7 +241,12 @@ def run_ours(args):
     rank, world, local, pg = distributed.init_from_env("nccl", timeout_s=300)
     torch.cuda.set_device(local)
     cfg = pm.config_c3()
-    tc = TrainConfig(sequence=args.seq, batch=args.batch, warmup_steps=0, steps=10000)
+    if args.config == "c4":
+        from sejong_b200.param_vjp import VjpConfig
+        tc = TrainConfig(sequence=args.seq, batch=args.batch, optimizer="sgd", learning_rate=1e-2, warmup_steps=0,
+                         steps=10000, parameter_vjp=VjpConfig())
+    else:
+        tc = TrainConfig(sequence=args.seq, batch=args.batch, warmup_steps=0, steps=10000)
     trainer = ByteTrainer(cfg, tc, device=local, process_group=pg)
     rows = tc.batch * tc.sequence
     total = args.warmup + args.steps
@@ -292,7 +318,7 @@ def run_ours(args):
     losses = loss_host.numpy()
     assert np.all(np.isfinite(losses)), "non-finite loss"
 
-    per_step_launches = sum(trainer.KERNELS.get(n, 1) for n in _call_names(trainer))
+    per_step_launches = sum(trainer.kernels_of(n, a) for n, a in _call_names(trainer))
     fam = {} if args.no_kernel_timing else kernel_timing(trainer, args.kernel_report if rank == 0 else None)
     if world > 1:
         trainer.release_graphs()
@@ -317,12 +343,14 @@ def run_ours(args):
             roofline = {"bound": "tensor", "kernel": "gemm_tcgen05 (all GEMMs of one step)",
                         "achieved": achieved, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": achieved / pk["bf16_sustained"], "peak_source": pk["source"] + " sustained bf16",
-                        "traffic": None, "launches": g["calls"], "ms_per_step": g["ms"]}
+                        "traffic": NCU_GEMM_DRAM_BYTES_PER_STEP.get(args.config),
+                        "traffic_unit": "bytes per step, all GEMM launches (ncu, cold cache)",
+                        "launches": g["calls"], "ms_per_step": g["ms"]}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: Zipf(1.1) bytes from the reference Rng (seed 1000+rank); random-init N(0,0.02) weights",
-        "config": {"workload": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
+        "config": {"workload": WORKLOADS[args.config],
                    "model": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
                    "global_batch": tc.batch * world, "per_gpu_batch": tc.batch, "seq_len": tc.sequence,
                    "parallelism": f"dp{world}", "l2": "per-step working set of several GB > 126 MB L2; no flush"},
@@ -338,19 +366,19 @@ def run_ours(args):
     if fam:
         line["kernel_ms_per_step"] = {k.replace("sj_", ""): round(v["ms"], 4) for k, v in sorted(fam.items())}
     if world == 1 and not args.no_cpu_baseline:
-        rate, _, cores = cpu_step_rate(2, 1)
+        rate, _, cores = cpu_step_rate(2, 1, config=args.config)
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-                                "sample": cpu_sample_text(2)}
+                                "sample": cpu_sample_text(2, args.config)}
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
 def _call_names(trainer):
-    """Names of the C-ABI calls one step makes (recorded without launching anything)."""
+    """(name, arguments) of the C-ABI calls one step makes (recorded without launching anything)."""
     names = []
     original = trainer._call
-    trainer._call = lambda name, *a: names.append(name)
+    trainer._call = lambda name, *a: names.append((name, a))
     try:
         trainer.step()
     finally:

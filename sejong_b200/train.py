@@ -180,9 +180,16 @@ class ByteTrainer:
     KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 3,
                "sj_zero": 0, "sj_param_basis": 4, "sj_param_prepare": 2}
 
+    @classmethod
+    def kernels_of(cls, name, args):
+        """Kernel launches one C-ABI call makes (the GQA backward adds a group reduction)."""
+        if name == "sj_attn_gqa_bwd":
+            return 3 + (1 if args[20] != args[21] else 0)
+        return cls.KERNELS.get(name, 1)
+
     def _call(self, name, *args):
         call(name, *args)
-        self.launches += self.KERNELS.get(name, 1)
+        self.launches += self.kernels_of(name, args)
 
     # ------------------------------------------------------------------ parameter pointers
     def wb_ptr(self, name):
@@ -598,7 +605,19 @@ class ByteTrainer:
             lin += 2 * b * t * h.encoder_width * h.decoder_width    # encoder_to_decoder
             lin += 2 * b * t * h.decoder_width * c.width            # output_projection
             lin += 2 * b * t * c.width * VOCAB                      # head
-        return 3 * lin + 3 * att  # fwd + (dX + dW) for linear; fwd (4) + bwd (8) for attention
+        total = 3 * lin + 3 * att  # fwd + (dX + dW) for linear; fwd (4) + bwd (8) for attention
+        if self.vjp is not None:
+            # executed work of the parameter VJP instead of the dense dW of each compressed group:
+            # basis (donor columns 2nar, once per (rows, rank)), prepare (left 2nar, residual rows
+            # 2nkr), coefficients 2(r+k)nB, factored gradient 2aBr
+            for g in self.vjp.groups.values():
+                n, a, r, k = g.rows, g.features, g.rank, g.k
+                width = sum(m.width for m in g.members)
+                active = sum(g.members[i].width for i in g.active)
+                total -= 2 * n * a * active
+                total += 2 * n * a * r * (2 if g.new_basis else 1) + 2 * n * k * r
+                total += 2 * (r + k) * n * width + 2 * a * active * r
+        return total
 
 
 def synthetic_corpus_tokens(seed, length, s=1.1):
