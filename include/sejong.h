@@ -222,9 +222,10 @@ int sj_sgd(float* w, const float* g, void* w_bf16, size_t n, size_t n_decay, con
  * generator seeded with one next_u64 of `rng_state` (device memory, advanced in place) draws a
  * partial Fisher-Yates of r of the b donor columns, then of s of the nb feature blocks of `group`
  * rows.  columns [r]; rows [s*group] (feature index, -1 past a); row_map [a] (position in rows or -1).
- * scratch: b + nb ints.  Zero sizes skip the corresponding draw, as the reference's do. */
-int sj_param_indices(uint64_t* rng_state, int a, int b, int nb, int s, int r, int group, int32_t* scratch,
-                     int32_t* columns, int32_t* rows, int32_t* row_map, void* stream);
+ * The reference kernel's permutation scratch lives in shared memory (b + nb + s <= 12288).  Zero
+ * sizes skip the corresponding draw, as the reference's do. */
+int sj_param_indices(uint64_t* rng_state, int a, int b, int nb, int s, int r, int group, int32_t* columns,
+                     int32_t* rows, int32_t* row_map, void* stream);
 /* The same draw on the host from an explicit seed (the reference kernel's own inputs). */
 int sj_param_indices_host(uint64_t seed, int a, int b, int nb, int s, int r, int group, int32_t* columns,
                           int32_t* rows, int32_t* row_map);
@@ -232,8 +233,8 @@ int sj_param_indices_host(uint64_t seed, int a, int b, int nb, int s, int r, int
  * [n, a], row stride ldx; w bf16 with row stride ldw, pointing at the donor's first column;
  * interleave > 0 selects the second half of a weight interleaved in blocks of `interleave`
  * columns): the CGS2 with small-norm cutoff `eps` of parameter.py:65-129 / parameter_vjp.rs:216-258.
- * workspace: sj_param_basis_workspace(n, r) bytes, 8-byte aligned.  r <= 32. */
-size_t sj_param_basis_workspace(int n, int r);
+ * workspace: sj_param_basis_workspace(n, a, r) bytes, 16-byte aligned.  r <= 32, a % 8 == 0. */
+size_t sj_param_basis_workspace(int n, int a, int r);
 int sj_param_basis(const void* x, int ldx, int n, int a, const void* w, int ldw, int interleave, const int32_t* columns,
                    int r, float eps, float* q, void* workspace, void* stream);
 /* The prepare kernel (parameter.py:131-191, parameter_vjp.rs:260-290): left = x^T q [a, r] f32 and

@@ -62,10 +62,10 @@ SIGNATURES = {
                          c_float, c_float, c_float, c_void_p]),
     "sj_sgd": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_void_p, c_float, c_void_p]),
     "sj_param_indices": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p,
-                                 c_void_p, c_void_p]),
+                                 c_void_p]),
     "sj_param_indices_host": (c_int, [c_u64, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                       c_void_p]),
-    "sj_param_basis_workspace": (c_size_t, [c_int, c_int]),
+    "sj_param_basis_workspace": (c_size_t, [c_int, c_int, c_int]),
     "sj_param_basis": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_float,
                                c_void_p, c_void_p, c_void_p]),
     "sj_param_prepare": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_float, c_void_p,

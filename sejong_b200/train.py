@@ -237,19 +237,17 @@ class ByteTrainer:
         seed = distributed.rank_seed(cfg.seed, rank)
         self.vjp_rng = torch.from_numpy(np.array([seed], dtype=np.uint64).view(np.int64)).to(dev)
         self.vjp_q, self.vjp_columns, self.vjp_rows, self.vjp_map = {}, {}, {}, {}
-        scratch = basis_ws = left = e = coeff = 1
+        basis_ws = left = e = coeff = 1
         for g in self.vjp.groups.values():
             donor = g.members[g.donor].width
             self.vjp_q.setdefault(g.basis_key, torch.empty(g.rows, g.rank, dtype=f32, device=dev))
             self.vjp_columns.setdefault(g.basis_key, torch.zeros(g.rank, dtype=i32, device=dev))
             self.vjp_rows.setdefault(g.features, torch.zeros(g.k, dtype=i32, device=dev))
             self.vjp_map.setdefault(g.features, torch.zeros(g.features, dtype=i32, device=dev))
-            scratch = max(scratch, donor + g.blocks)
-            basis_ws = max(basis_ws, self.lib.sj_param_basis_workspace(g.rows, g.rank))
+            basis_ws = max(basis_ws, self.lib.sj_param_basis_workspace(g.rows, g.features, g.rank))
             left = max(left, g.features * g.rank)
             e = max(e, (g.rank + g.k) * g.rows)
             coeff = max(coeff, (g.rank + g.k) * sum(m.width for m in g.members))
-        self.vjp_scratch = torch.zeros(scratch, dtype=i32, device=dev)
         self.vjp_ws = torch.empty((basis_ws + 7) // 8, dtype=torch.float64, device=dev)
         self.vjp_left = torch.empty(left, dtype=f32, device=dev)
         self.vjp_e = torch.empty(e, dtype=torch.bfloat16, device=dev)
@@ -289,7 +287,7 @@ class ByteTrainer:
             self._call("sj_param_indices", _ptr(self.vjp_rng), a if g.new_selection else 0,
                        donor_width if g.new_basis else 0, g.blocks if g.new_selection else 0,
                        g.selected if g.new_selection else 0, r if g.new_basis else 0, g.block_rows,
-                       _ptr(self.vjp_scratch), _ptr(cols), _ptr(rows), _ptr(row_map), self.stream)
+                       _ptr(cols), _ptr(rows), _ptr(row_map), self.stream)
         if g.new_basis:
             off, _, interleave = layout[g.donor]
             if interleave:
@@ -307,7 +305,13 @@ class ByteTrainer:
             assert len(g.active) in (0, len(g.members)), "gate and up share one decision (equal widths)"
             spans = [(0, width, True)]
         else:
-            spans = [(off, w, i in g.active) for i, (off, w, _) in enumerate(layout)]
+            spans = []
+            for i, (off, w, _) in enumerate(layout):
+                compressed = i in g.active
+                if spans and spans[-1][2] == compressed and spans[-1][0] + spans[-1][1] == off:
+                    spans[-1] = (spans[-1][0], spans[-1][1] + w, compressed)   # one launch per contiguous run
+                else:
+                    spans.append((off, w, compressed))
         for off, w, compressed in spans:
             if compressed:
                 self._call("sj_param_materialize", _ptr(self.vjp_left), _ptr(coeff, off), width, _ptr(row_map), a, w,

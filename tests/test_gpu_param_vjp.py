@@ -69,12 +69,10 @@ def test_device_indices(a, b, nb, s, r, group):
     state = 0x0123456789ABCDEF ^ (a * 1000003 + b)
     rng = u64_tensor(state)
     i32 = torch.int32
-    scratch = torch.zeros(max(b + nb, 1), dtype=i32, device=DEV)
     columns = torch.full((max(r, 1),), -7, dtype=i32, device=DEV)
     rows = torch.full((max(s * group, 1),), -7, dtype=i32, device=DEV)
     row_map = torch.full((max(a, 1),), -7, dtype=i32, device=DEV)
-    call("sj_param_indices", ptr(rng), a, b, nb, s, r, group, ptr(scratch), ptr(columns), ptr(rows), ptr(row_map),
-         stream())
+    call("sj_param_indices", ptr(rng), a, b, nb, s, r, group, ptr(columns), ptr(rows), ptr(row_map), stream())
     torch.cuda.synchronize()
     host = Rng(state)
     seed = host.next_u64()
@@ -101,7 +99,7 @@ def test_basis(n, a, ldw, offset, interleave, cols):
     columns = torch.tensor(cols, dtype=torch.int32, device=DEV)
     q = torch.empty(n, r, dtype=torch.float32, device=DEV)
     from sejong_b200 import _lib
-    ws = torch.empty((_lib.load().sj_param_basis_workspace(n, r) + 7) // 8, dtype=torch.float64, device=DEV)
+    ws = torch.empty((_lib.load().sj_param_basis_workspace(n, a, r) + 7) // 8, dtype=torch.float64, device=DEV)
     eps = opv.basis_eps(n, r)
     call("sj_param_basis", ptr(xd), a, n, a, ptr(wd, offset), ldw, interleave, ptr(columns), r, eps, ptr(q), ptr(ws),
          stream())
