@@ -127,6 +127,29 @@ def test_gemm_residual_epilogue():
     assert rel(c32, res32 + a.float() @ b.float()) < 1e-5
 
 
+@pytest.mark.parametrize("epi", [0, 2])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_gemm_f32_strided_store_residual(epi, in_place):
+    """f32 STORE / RESIDUAL products with a strided C holding stale values, the residual in place or
+    in its own buffer: columns past N stay untouched."""
+    if epi == 0 and in_place:
+        pytest.skip("in place applies to the residual only")
+    m, n, k, ldc = 4096, 768, 2048, 776
+    a, b = bf(randn(m, k, scale=0.1)), bf(randn(k, n, scale=0.1))
+    c = randn(m, ldc) * 100.0   # stale contents must not leak into a STORE
+    res = c if in_place else randn(m, ldc)
+    res0 = res[:, :n].clone()
+    pad0 = c[:, n:].clone()
+    from sejong_b200._lib import SJ_F32
+    call("sj_gemm", ptr(a), k, 0, ptr(b), n, 0, ptr(c), ldc, SJ_F32, m, n, k, epi, 1.0,
+         ptr(res) if epi == 2 else 0, ldc if epi == 2 else 0, 0, 0, 0.0, 0, stream())
+    torch.cuda.synchronize()
+    check_device_error()
+    ref = a.float() @ b.float() + (res0 if epi == 2 else 0)
+    assert rel(c[:, :n], ref) < 1e-5
+    assert torch.equal(c[:, n:], pad0)   # columns past N untouched
+
+
 def test_gemm_swiglu_epilogue():
     from sejong_b200.model import _interleave_cols
     m, k, f = 512, 256, 768
