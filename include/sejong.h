@@ -52,6 +52,7 @@ enum {
   SJ_DEV_GEMM_MMA_WAIT = 102,
   SJ_DEV_GEMM_EPILOGUE_WAIT = 103,
   SJ_DEV_GEMM_DRAIN_WAIT = 104,
+  SJ_DEV_ATTN_WAIT = 105,
   SJ_DEV_BAD_INDEX = 110
 };
 

@@ -1,6 +1,7 @@
-// Causal grouped-query attention with an optional sliding window, forward and backward, head dim 64.
+// Causal grouped-query attention with an optional sliding window, backward, head dim 64 (the forward
+// is the tcgen05 kernel of attention_fwd.cu).
 //
-// Restates python/sejong_kernels/ops/hierarchy.py:7-104 (hierarchy_attention, _dq, _dkv): query
+// Restates python/sejong_kernels/ops/hierarchy.py:42-104 (hierarchy_attention _dq, _dkv): query
 // (b, t, h) attends keys s of kv head h / (HQ/HK) with max(0, t+1-W) <= s <= t, scale 64^-1/2,
 // LSE in natural log.  The reference launches one program per (row, head) and re-reads K/V for
 // every query; here a CTA owns a 64-query (or 64-key) tile, K/V (or Q/dO) tiles are staged once in
@@ -139,118 +140,8 @@ SJ_DEVICE void store_rows(__nv_bfloat16* dst, int ld, const float (&c)[8][4], in
 
 // ------------------------------------------------------------------------------------ forward
 constexpr int kTileElems = kAttnTile * kAttnD;
-constexpr int kFwdSmem = 5 * kTileElems * 2;
 constexpr int kDqSmem = 6 * kTileElems * 2;
 constexpr int kDkvSmem = 6 * kTileElems * 2 + 4 * kAttnTile * 4;
-
-__global__ void __launch_bounds__(kAttnThreads, 3) attn_fwd_kernel(const AttnParams p) {
-  extern __shared__ __align__(128) uint8_t attn_smem[];
-  // smem: Q tile, then K stages 0/1, then V stages 0/1 (stage st at + st * kTileElems)
-  __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(attn_smem);
-  __nv_bfloat16* sk0 = sq + kTileElems;
-  __nv_bfloat16* sv0 = sq + 3 * kTileElems;
-  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / (p.hq / p.hk);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
-  const int q0 = qb * kAttnTile;
-  const __nv_bfloat16* qg = p.q + static_cast<size_t>(b) * p.t * p.ldq + h * kAttnD;
-  const __nv_bfloat16* kg = p.k + static_cast<size_t>(b) * p.t * p.ldk + kvh * kAttnD;
-  const __nv_bfloat16* vg = p.v + static_cast<size_t>(b) * p.t * p.ldv + kvh * kAttnD;
-  const int kb_lo = p.window > 0 ? max(0, q0 - p.window + 1) / kAttnTile : 0;
-  const int kb_hi = min((q0 + kAttnTile - 1) / kAttnTile, (p.t - 1) / kAttnTile);
-
-  load_tile_async(sq, qg, p.ldq, q0, p.t);
-  load_tile_async(sk0, kg, p.ldk, kb_lo * kAttnTile, p.t);
-  load_tile_async(sv0, vg, p.ldv, kb_lo * kAttnTile, p.t);
-  cp_async_commit();
-
-  const float sl2 = p.scale * kLog2e;
-  uint32_t qf[4][4];
-  float o[8][4];
-  zero(o);
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  const int row_lo = q0 + warp * 16 + g;  // rows row_lo and row_lo + 8
-
-  for (int kb = kb_lo; kb <= kb_hi; ++kb) {
-    const int st = (kb - kb_lo) & 1;
-    if (kb < kb_hi) {
-      load_tile_async(sk0 + (st ^ 1) * kTileElems, kg, p.ldk, (kb + 1) * kAttnTile, p.t);
-      load_tile_async(sv0 + (st ^ 1) * kTileElems, vg, p.ldv, (kb + 1) * kAttnTile, p.t);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    if (kb == kb_lo) load_a_frags(qf, smem_u32(sq), warp * 16);
-    float s[8][4];
-    zero(s);
-    mma_abt(s, qf, smem_u32(sk0 + st * kTileElems));
-    float mx[2] = {m[0], m[1]};
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int qpos = row_lo + (e >> 1) * 8;
-        const int kpos = kb * kAttnTile + nt * 8 + 2 * tq + (e & 1);
-        const bool ok = kpos <= qpos && kpos < p.t && (p.window <= 0 || qpos - kpos < p.window);
-        s[nt][e] = ok ? s[nt][e] * sl2 : -INFINITY;
-        mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
-      }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
-      mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
-    }
-    float alpha[2], base[2];
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      base[i] = mx[i] == -INFINITY ? 0.f : mx[i];
-      alpha[i] = exp2f(m[i] - base[i]);
-      m[i] = mx[i];
-      l[i] *= alpha[i];
-    }
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float pe = exp2f(s[nt][e] - base[e >> 1]);
-        s[nt][e] = pe;
-        l[e >> 1] += pe;
-      }
-      o[nt][0] *= alpha[0];
-      o[nt][1] *= alpha[0];
-      o[nt][2] *= alpha[1];
-      o[nt][3] *= alpha[1];
-    }
-    uint32_t pf[4][4];
-    c_to_a_frags(pf, s);
-    mma_ab(o, pf, smem_u32(sv0 + st * kTileElems));
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
-    l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
-  }
-  const float inv0 = 1.f / l[0], inv1 = 1.f / l[1];
-#pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    o[nt][0] *= inv0;
-    o[nt][1] *= inv0;
-    o[nt][2] *= inv1;
-    o[nt][3] *= inv1;
-  }
-  __nv_bfloat16* og = p.out + static_cast<size_t>(b) * p.t * p.ldo + h * kAttnD;
-  store_rows(og, p.ldo, o, q0 + warp * 16, p.t, 0, 0.f, nullptr);
-  if (tq == 0) {
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int r = row_lo + 8 * i;
-      if (r < p.t) p.lse_out[(static_cast<size_t>(b) * p.t + r) * p.hq + h] = (m[i] + log2f(l[i])) * kLn2;
-    }
-  }
-}
 
 // ------------------------------------------------------------------------------------ backward
 // Delta[row*hq + h] = sum_d dO * O (hierarchy.py:53-57).
@@ -508,9 +399,7 @@ static int configure_attention() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured == dev) return SJ_OK;
-  cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attn_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem);
+  cudaError_t e = cudaFuncSetAttribute(attn_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDkvSmem);
   if (e != cudaSuccess) return cuda_check(e, "attention shared-memory attribute");
@@ -533,35 +422,6 @@ extern "C" size_t sj_attn_workspace(int batch, int t, int hq, int hk) {
   if (batch <= 0 || t <= 0 || hq <= 0 || hk <= 0) return 0;
   const size_t rows = static_cast<size_t>(batch) * t;
   return rows * hq + (hq != hk ? 2 * rows * hq * kAttnD : 0);
-}
-
-extern "C" int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, void* o,
-                               int ldo, float* lse, int batch, int t, int hq, int hk, int head_dim, int window,
-                               void* stream) {
-  int rc = check_common(batch, t, hq, hk, head_dim, window);
-  if (rc) return rc;
-  if ((rc = configure_attention())) return rc;
-  if ((ldq | ldk | ldv | ldo) % 8 || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
-    return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_fwd: 16-byte aligned rows required");
-  AttnParams p{};
-  p.q = static_cast<const __nv_bfloat16*>(q);
-  p.k = static_cast<const __nv_bfloat16*>(k);
-  p.v = static_cast<const __nv_bfloat16*>(v);
-  p.out = static_cast<__nv_bfloat16*>(o);
-  p.lse_out = lse;
-  p.ldq = ldq;
-  p.ldk = ldk;
-  p.ldv = ldv;
-  p.ldo = ldo;
-  p.t = t;
-  p.hq = hq;
-  p.hk = hk;
-  p.window = window;
-  p.scale = 0.125f;
-  dim3 grid((t + kAttnTile - 1) / kAttnTile, hq, batch);
-  attn_fwd_kernel<<<grid, kAttnThreads, kFwdSmem, as_stream(stream)>>>(p);
-  SJ_LAUNCH_CHECK("attn_fwd");
-  return SJ_OK;
 }
 
 extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o,

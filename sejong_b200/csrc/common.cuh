@@ -103,6 +103,36 @@ SJ_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, in
   }
 }
 
+// Non-blocking probe of the phase with the given parity.
+SJ_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait by polling (no suspension between probes): for latency-critical hand-offs inside a
+// pipeline whose waits are short, where the wake-up delay of a suspended try_wait would dominate.
+SJ_DEVICE bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (globaltimer() - start > kWaitLimitNs) {
+      record_error(code);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 SJ_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -111,6 +141,8 @@ SJ_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// Make this thread's generic-proxy shared-memory writes visible to the async proxy (TMA, tcgen05.mma).
+SJ_DEVICE void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 SJ_DEVICE void tma_prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

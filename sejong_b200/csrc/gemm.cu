@@ -432,8 +432,8 @@ static int make_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype
   return SJ_OK;
 }
 
-static int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
-                    uint32_t box_inner, uint32_t box_outer) {
+int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+             uint32_t box_outer) {
   return make_map(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld, box_inner, box_outer,
                   CU_TENSOR_MAP_SWIZZLE_128B);
 }

@@ -1,5 +1,6 @@
 // Host-side helpers shared by the C-ABI translation units (not part of the ABI).
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -18,6 +19,10 @@ int cuda_check(cudaError_t e, const char* what);
 int sm_count();
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// 2-D bf16 TMA map with 128-byte swizzle: `inner` contiguous elements per row, `outer` rows, row
+// stride `ld` elements, box box_inner x box_outer (gemm.cu).
+int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+             uint32_t box_outer);
 
 }  // namespace sj
 
