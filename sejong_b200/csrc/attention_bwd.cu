@@ -1,0 +1,586 @@
+// Causal grouped-query attention backward on the 5th-generation tensor cores, head dim 64, optional
+// sliding window.
+//
+// Restates python/sejong_kernels/ops/hierarchy.py:42-104 (the dQ and dK/dV programs): with
+// P = exp(S scale - LSE) and dS = P (dP - Delta) scale, dV = P^T dO, dK = dS^T Q, dQ = dS K; the
+// inverse RoPE rotation of the tape's backward (crates/sejong-gpu/src/graph.rs:879-882) is applied
+// to dQ and dK on the way out.
+//
+// Persistent: one CTA per SM walks work items (batch, kv head, 128-key tile).  An item visits every
+// query head of its group and every query tile its keys are visible to, so dK and dV of the kv head
+// accumulate in TMEM across the whole group and are written once (no partials).  14 warps:
+//   warp 0      TMA: the item's K and V tiles (double-buffered by item), and per step the Q and dO
+//               tiles and the step's 128 LSE and Delta values (2-deep ring; the delta kernel lays
+//               both out per head, contiguous over the sequence).
+//   warp 1      TMEM owner and MMA issuer, per step g:
+//                 S^T_g = K Q_g^T and dP^T_g = V dO_g^T (M128 N128 K64) into TMEM,
+//                 then, once P^T_g and dS^T_g are in shared memory,
+//                 dV += P^T_g dO_g, dK += dS^T_g Q_g (M128 N64 K128, accumulated in TMEM) and
+//                 dQ_g = dS_g K (the dS^T buffer read as an MN-major operand).
+//               S^T_{g+1} / dP^T_{g+1} are issued before waiting for P^T_g, so the two overlap.
+//   warps 2-9   elementwise: thread <-> key row (TMEM lane), two threads per row, 64 query columns
+//               each: P^T and dS^T in bf16 into K-major 128-byte-swizzled shared memory.
+//   warps 10-13 dQ: thread <-> query row, adds dQ_g into an f32 accumulator [rows, hq*64] with
+//               vector reductions (attn_dq_finish_kernel applies the inverse RoPE and writes bf16);
+//               at the end of an item, dK (inverse RoPE) and dV out of TMEM to global bf16.
+// Every wait is bounded (SJ_DEV_ATTN_WAIT in the device error word).
+#include <algorithm>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace sj {
+
+namespace {
+
+constexpr int kBT = 128;                          // keys per item, queries per step
+constexpr int kBD = 64;                           // head dim
+constexpr int kEwWarps = 8;
+constexpr int kDqWarps = 4;
+constexpr int kBwdThreads = 32 * (2 + kEwWarps + kDqWarps);
+constexpr int kTile = kBT * kBD * 2;              // 16 KB: 128 rows x 128 B
+// shared memory: K0 K1 | V0 V1 | Q0 Q1 | dO0 dO1 | P^T | dS^T | LSE/Delta ring | barriers
+constexpr int kOffKb = 0;
+constexpr int kOffVb = kOffKb + 2 * kTile;
+constexpr int kOffQb = kOffVb + 2 * kTile;
+constexpr int kOffDOb = kOffQb + 2 * kTile;
+constexpr int kOffPt = kOffDOb + 2 * kTile;       // 32 KB: two 64-query halves
+constexpr int kOffDSt = kOffPt + 2 * kTile;       // 32 KB
+constexpr int kOffLd = kOffDSt + 2 * kTile;       // [2 slots][LSE*log2e 128 | Delta 128] f32
+constexpr int kOffBarB = kOffLd + 2 * 2 * kBT * 4;
+constexpr int kSmemBwd = kOffBarB + 512 + 1024;
+constexpr uint32_t kTmemColsB = 512;
+constexpr uint32_t kColSt = 0, kColDPt = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
+constexpr float kLog2eB = 1.4426950408889634f;
+
+struct BwdParams {
+  int t, hq, hk, window, batch, nkt, items;
+  float scale, scale_log2;
+  const float* lse_t;    // [hq][batch][tpad]: LSE * log2(e), per head contiguous over the sequence
+  const float* delta_t;  // [hq][batch][tpad]: Delta
+  int tpad;              // t rounded up to 128
+  float* dq_acc;         // [rows, hq * 64] f32, zeroed
+  __nv_bfloat16 *dk, *dv;
+  int lddk, lddv;
+  const float2* rope_tab;  // [t][32] (cos, sin) or null
+  float rope_log_theta;    // > 0 when no table: angles evaluated inline
+};
+
+SJ_DEVICE float ex2b(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Item -> (batch, kv head, key tile) and its query range per head: heaviest first (the first key
+// tiles see the most causal query tiles).
+struct BItem {
+  int b, kvh, kt, k0, qt_lo, nq;
+};
+SJ_DEVICE BItem decode_bitem(const BwdParams& p, int item) {
+  BItem it;
+  const int bk = p.batch * p.hk;
+  const int rest = item % bk;
+  it.kt = item / bk;
+  it.b = rest / p.hk;
+  it.kvh = rest % p.hk;
+  it.k0 = it.kt * kBT;
+  const int nqt = (p.t + kBT - 1) / kBT;
+  it.qt_lo = it.kt;
+  const int qt_hi = p.window > 0 ? min(nqt - 1, (it.k0 + kBT - 1 + p.window - 1) / kBT) : nqt - 1;
+  it.nq = qt_hi - it.qt_lo + 1;
+  return it;
+}
+
+// (cos, sin) of the RoPE angle of position pos, pair i (head dim 64).
+SJ_DEVICE float2 rope_cs(const float2* tab, float log_theta, int pos, int i) {
+  if (tab != nullptr) return tab[static_cast<size_t>(pos) * 32 + i];
+  float s, c;
+  sincosf(static_cast<float>(pos) * expf((-2.0f * static_cast<float>(i) / 64.0f) * log_theta), &s, &c);
+  return make_float2(c, s);
+}
+
+// 1-D bulk copy global -> shared completing on an mbarrier (16-byte aligned, size a multiple of 16).
+SJ_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+SJ_DEVICE void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
+                       const BwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBarB);
+  uint64_t* kv_full = bars;          // 2
+  uint64_t* kv_empty = bars + 2;     // 2
+  uint64_t* qd_full = bars + 4;      // 2
+  uint64_t* qd_empty = bars + 6;     // 2
+  uint64_t* sp_full = bars + 8;      // 1: S^T, dP^T in TMEM
+  uint64_t* sp_empty = bars + 9;     // 1: elementwise warps have them in registers
+  uint64_t* ps_full = bars + 10;     // 1: P^T, dS^T in shared memory
+  uint64_t* ps_empty = bars + 11;    // 1: their MMAs are done
+  uint64_t* dq_full = bars + 12;     // 1
+  uint64_t* dq_empty = bars + 13;    // 1
+  uint64_t* acc_full = bars + 14;    // 1: an item's dK / dV complete in TMEM
+  uint64_t* acc_empty = bars + 15;   // 1: read out
+  uint64_t* drain = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* ldbuf = reinterpret_cast<float*>(smem + kOffLd);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = p.hq / p.hk;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(sp_full, 1);
+    mbar_init(sp_empty, kEwWarps);
+    mbar_init(ps_full, kEwWarps);
+    mbar_init(ps_empty, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, kDqWarps);
+    mbar_init(acc_full, 1);
+    mbar_init(acc_empty, kDqWarps);  // the dQ warps read dK / dV out
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&map_q);
+    tma_prefetch_map(&map_k);
+    tma_prefetch_map(&map_v);
+    tma_prefetch_map(&map_do);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemColsB);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (whole warp)
+    int n = 0, g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++n) {
+      const BItem it = decode_bitem(p, item);
+      const int row_base = it.b * p.t;
+      const int ks = n & 1;
+      if (lane == 0) {
+        ok = mbar_wait(&kv_empty[ks], ((n >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
+        if (ok) {
+          mbar_arrive_expect_tx(&kv_full[ks], 2 * kTile);
+          tma_load_2d(smem + kOffKb + ks * kTile, &map_k, &kv_full[ks], it.kvh * kBD, row_base + it.k0);
+          tma_load_2d(smem + kOffVb + ks * kTile, &map_v, &kv_full[ks], it.kvh * kBD, row_base + it.k0);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      for (int hh = 0; hh < group && ok; ++hh) {
+        const int h = it.kvh * group + hh;
+        for (int j = 0; j < it.nq && ok; ++j, ++g) {
+          const int st = g & 1;
+          const int q0 = (it.qt_lo + j) * kBT;
+          if (lane == 0) ok = mbar_wait(&qd_empty[st], ((g >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) {
+            ++g;
+            break;
+          }
+          if (lane == 0) {
+            // Q, dO tiles and the step's 128 LSE*log2(e) and Delta values (one contiguous run each)
+            float* lsl = ldbuf + st * 2 * kBT;
+            const size_t run = (static_cast<size_t>(h) * p.batch + it.b) * p.tpad + q0;
+            mbar_arrive_expect_tx(&qd_full[st], 2 * kTile + 2 * kBT * 4);
+            tma_load_2d(smem + kOffQb + st * kTile, &map_q, &qd_full[st], h * kBD, row_base + q0);
+            tma_load_2d(smem + kOffDOb + st * kTile, &map_do, &qd_full[st], h * kBD, row_base + q0);
+            bulk_load(lsl, p.lse_t + run, kBT * 4, &qd_full[st]);
+            bulk_load(lsl + kBT, p.delta_t + run, kBT * 4, &qd_full[st]);
+          }
+        }
+      }
+    }
+    if (lane == 0) {
+      for (int i = max(0, n - 2); i < n; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1, nullptr, SJ_DEV_ATTN_WAIT);
+      for (int i = max(0, g - 2); i < g; ++i) mbar_wait(&qd_full[i & 1], (i >> 1) & 1, nullptr, SJ_DEV_ATTN_WAIT);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (one thread)
+    if (lane == 0) {
+      constexpr uint32_t kIdS = umma_idesc_bf16(kBT, kBT, 0, 0);   // K-major A, K-major B
+      constexpr uint32_t kIdAcc = umma_idesc_bf16(kBT, kBD, 0, 1);  // K-major A, MN-major B
+      constexpr uint32_t kIdDq = umma_idesc_bf16(kBT, kBD, 1, 1);   // MN-major A, MN-major B
+      // the second half of a step: dV, dK (accumulated) and dQ from P^T / dS^T of step i
+      int pend_i = -1, pend_ks = 0, pend_first = 0, pend_last = 0, pend_n = 0;
+      bool ok = true;
+      auto issue_acc = [&]() -> bool {
+        const int i = pend_i;
+        const int st = i & 1;
+        if (!mbar_wait(ps_full, i & 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        if (!mbar_wait(dq_empty, (i & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        if (pend_first && !mbar_wait(acc_empty, (pend_n & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        tc_fence_after();
+        const uint32_t pt = smem_u32(smem + kOffPt), dst = smem_u32(smem + kOffDSt);
+        const uint32_t qa = smem_u32(smem + kOffQb + st * kTile), da = smem_u32(smem + kOffDOb + st * kTile);
+        const uint32_t ka = smem_u32(smem + kOffKb + pend_ks * kTile);
+#pragma unroll
+        for (int kk = 0; kk < kBT / 16; ++kk) {
+          const uint32_t kmaj = (kk >> 2) * kTile + (kk & 3) * 32;  // K-major step inside a 128 x 128 tile
+          const uint32_t acc = (pend_first && kk == 0) ? 0u : 1u;
+          umma_f16(tmem + kColDV, umma_desc(pt + kmaj, 16, 1024), umma_desc(da + kk * 2048, 8192, 1024), kIdAcc, acc);
+          umma_f16(tmem + kColDK, umma_desc(dst + kmaj, 16, 1024), umma_desc(qa + kk * 2048, 8192, 1024), kIdAcc,
+                   acc);
+          umma_f16(tmem + kColDQ, umma_desc(dst + kk * 2048, kTile, 1024), umma_desc(ka + kk * 2048, 8192, 1024),
+                   kIdDq, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(ps_empty);
+        umma_commit(dq_full);
+        umma_commit(&qd_empty[st]);
+        if (pend_last) {
+          umma_commit(acc_full);
+          umma_commit(&kv_empty[pend_ks]);
+        }
+        pend_i = -1;
+        return true;
+      };
+      int n = 0, g = 0;
+      for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++n) {
+        const BItem it = decode_bitem(p, item);
+        const int ks = n & 1;
+        if (!mbar_wait(&kv_full[ks], (n >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
+        const uint32_t ka = smem_u32(smem + kOffKb + ks * kTile), va = smem_u32(smem + kOffVb + ks * kTile);
+        const int steps = group * it.nq;
+        for (int s = 0; s < steps && ok; ++s, ++g) {
+          const int st = g & 1;
+          if (!mbar_wait(&qd_full[st], (g >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT) ||
+              !mbar_wait(sp_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t qa = smem_u32(smem + kOffQb + st * kTile), da = smem_u32(smem + kOffDOb + st * kTile);
+#pragma unroll
+          for (int kk = 0; kk < kBD / 16; ++kk) {
+            umma_f16(tmem + kColSt, umma_desc(ka + kk * 32, 16, 1024), umma_desc(qa + kk * 32, 16, 1024), kIdS,
+                     kk > 0 ? 1u : 0u);
+            umma_f16(tmem + kColDPt, umma_desc(va + kk * 32, 16, 1024), umma_desc(da + kk * 32, 16, 1024), kIdS,
+                     kk > 0 ? 1u : 0u);
+          }
+          umma_commit(sp_full);
+          if (pend_i >= 0 && !issue_acc()) {
+            ok = false;
+            break;
+          }
+          pend_i = g;
+          pend_ks = ks;
+          pend_first = s == 0;
+          pend_last = s == steps - 1;
+          pend_n = n;
+        }
+      }
+      if (ok && pend_i >= 0) issue_acc();
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, SJ_DEV_ATTN_WAIT);
+    }
+  } else if (warp < 2 + kEwWarps) {
+    // ---------------------------------------------------------------- elementwise warps
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;  // key row of the tile
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    int n = 0, g = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < p.items && alive; item += gridDim.x, ++n) {
+      const BItem it = decode_bitem(p, item);
+      const int kpos = it.k0 + r;
+      const int steps = group * it.nq;
+      for (int s = 0; s < steps && alive; ++s, ++g) {
+        const int st = g & 1;
+        const int q0 = (it.qt_lo + s % it.nq) * kBT;
+        if (!mbar_wait(&qd_full[st], (g >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT) ||
+            !mbar_wait(sp_full, g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        const float* lsl = ldbuf + st * 2 * kBT + half * 64;
+        const float* dls = lsl + kBT;
+        // visible queries of this key row in this half's columns: [lo, hi]
+        const int cbase = q0 + half * 64;
+        const bool full_tile =
+            q0 >= it.k0 + kBT - 1 && q0 + kBT <= p.t && it.k0 + kBT <= p.t &&
+            (p.window <= 0 || q0 + kBT - 1 - it.k0 < p.window);
+        int lo = 0, hi = 63;
+        if (!full_tile) {
+          lo = kpos - cbase;
+          hi = min(p.window > 0 ? kpos + p.window - 1 : p.t - 1, p.t - 1) - cbase;
+          if (kpos >= p.t) hi = -1;
+        }
+        // P^T and dS^T may overwrite the buffers once the previous step's MMAs have read them
+        if (!mbar_wait(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+          alive = false;
+          break;
+        }
+        uint8_t* pt = smem + kOffPt + half * kTile;
+        uint8_t* dst = smem + kOffDSt + half * kTile;
+        // this thread's 64 query columns of S^T and dP^T, in two chunks of 32
+#pragma unroll
+        for (int chunk = 0; chunk < 2; ++chunk) {
+          uint32_t sv[32], dv[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + kColSt + half * 64 + chunk * 32, sv);
+          tmem_ld_32x32b_x32(tmem + lane_off + kColDPt + half * 64 + chunk * 32, dv);
+          tmem_wait_ld();
+          if (chunk == 1) {  // S^T / dP^T are in registers: the next step's products may start
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sp_empty);
+          }
+          float pv[32], d[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int cc = chunk * 32 + c;
+            const bool valid = cc >= lo && cc <= hi;  // (LSE / Delta past the sequence end are not data)
+            const float pr = valid ? ex2b(fmaf(__uint_as_float(sv[c]), p.scale_log2, -lsl[cc])) : 0.f;
+            pv[c] = pr;                                                              // P^T
+            d[c] = valid ? pr * (__uint_as_float(dv[c]) - dls[cc]) * p.scale : 0.f;  // dS^T
+          }
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            const int c8 = chunk * 4 + q8;
+            const int off = r * 128 + ((c8 ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(pt + off) =
+                make_uint4(pack_bf16x2(pv[8 * q8], pv[8 * q8 + 1]), pack_bf16x2(pv[8 * q8 + 2], pv[8 * q8 + 3]),
+                           pack_bf16x2(pv[8 * q8 + 4], pv[8 * q8 + 5]), pack_bf16x2(pv[8 * q8 + 6], pv[8 * q8 + 7]));
+            *reinterpret_cast<uint4*>(dst + off) =
+                make_uint4(pack_bf16x2(d[8 * q8], d[8 * q8 + 1]), pack_bf16x2(d[8 * q8 + 2], d[8 * q8 + 3]),
+                           pack_bf16x2(d[8 * q8 + 4], d[8 * q8 + 5]), pack_bf16x2(d[8 * q8 + 6], d[8 * q8 + 7]));
+          }
+        }
+        fence_proxy_async_shared();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ps_full);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- dQ warps
+    // thread <-> row of the tile: a query row for dQ_g, a key row for the item's dK / dV
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    int n = 0, g = 0;
+    bool alive = true;
+    for (int item = blockIdx.x; item < p.items && alive; item += gridDim.x, ++n) {
+      const BItem it = decode_bitem(p, item);
+      const int steps = group * it.nq;
+      for (int s = 0; s < steps; ++s, ++g) {
+        const int h = it.kvh * group + s / it.nq;
+        const int qpos = (it.qt_lo + s % it.nq) * kBT + r;
+        if (!mbar_wait(dq_full, g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        float* dst = p.dq_acc + (static_cast<size_t>(it.b) * p.t + min(qpos, p.t - 1)) * (static_cast<size_t>(p.hq) * kBD) +
+                     h * kBD;
+#pragma unroll
+        for (int hc = 0; hc < 2; ++hc) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + kColDQ + hc * 32, v);
+          tmem_wait_ld();
+          if (qpos < p.t) {
+#pragma unroll
+            for (int c = 0; c < 32; c += 4)
+              red_add_v4(dst + hc * 32 + c, __uint_as_float(v[c]), __uint_as_float(v[c + 1]),
+                         __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+      }
+      if (!alive) break;
+      // the item's dK (inverse RoPE) and dV rows, off the elementwise warps' path
+      if (!mbar_wait(acc_full, n & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
+      tc_fence_after();
+      const int kpos = it.k0 + r;
+      const size_t row = static_cast<size_t>(it.b) * p.t + min(kpos, p.t - 1);
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {  // dK cols 0-31, 32-63, then dV cols 0-31, 32-63
+        const bool is_k = part < 2;
+        const int c0 = (part & 1) * 32;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + (is_k ? kColDK : kColDV) + c0, v);
+        tmem_wait_ld();
+        if (part == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty);
+        }
+        if (kpos < p.t) {
+          uint32_t w[16];
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float a = __uint_as_float(v[c]), b = __uint_as_float(v[c + 1]);
+            if (is_k && (p.rope_tab != nullptr || p.rope_log_theta > 0.f)) {
+              const float2 cs = rope_cs(p.rope_tab, p.rope_log_theta, kpos, (c0 + c) >> 1);
+              const float na = a * cs.x + b * cs.y, nb = -a * cs.y + b * cs.x;  // inverse rotation
+              a = na;
+              b = nb;
+            }
+            w[c >> 1] = pack_bf16x2(a, b);
+          }
+          uint4* out = reinterpret_cast<uint4*>((is_k ? p.dk + row * p.lddk : p.dv + row * p.lddv) + it.kvh * kBD + c0);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) out[c4] = make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemColsB);
+  }
+}
+
+// Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57), one warp each, written with the LSE
+// (times log2 e) transposed to [head][batch][tpad] so that a step's 128 values are one contiguous run.
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int ldo, const __nv_bfloat16* __restrict__ dout,
+                                  int lddo, const float* __restrict__ lse, float* __restrict__ delta_t,
+                                  float* __restrict__ lse_t, int rows, int t, int tpad, int hq) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (w >= rows * hq) return;
+  const int row = w / hq, h = w % hq;
+  const float2 a = unpack_bf16x2(
+      *reinterpret_cast<const uint32_t*>(dout + static_cast<size_t>(row) * lddo + h * kBD + 2 * lane));
+  const float2 c =
+      unpack_bf16x2(*reinterpret_cast<const uint32_t*>(o + static_cast<size_t>(row) * ldo + h * kBD + 2 * lane));
+  const float s = warp_sum(a.x * c.x + a.y * c.y);
+  if (lane == 0) {
+    const int b = row / t, pos = row % t;
+    const size_t dst = (static_cast<size_t>(h) * (rows / t) + b) * tpad + pos;
+    delta_t[dst] = s;
+    lse_t[dst] = lse[w] * kLog2eB;
+  }
+}
+
+// dq = bf16(inverse RoPE(dq_acc)), one thread per (row, head, column pair).
+__global__ void attn_dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int lddq,
+                                      int rows, int t, int hq, const float2* __restrict__ tab, float log_theta) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t pairs = static_cast<size_t>(rows) * hq * (kBD / 2);
+  if (i >= pairs) return;
+  const int row = static_cast<int>(i / (hq * (kBD / 2)));
+  const int rem = static_cast<int>(i % (hq * (kBD / 2)));
+  const int h = rem / (kBD / 2), pr = rem % (kBD / 2);
+  const float2 v = *reinterpret_cast<const float2*>(acc + i * 2);
+  float a = v.x, b = v.y;
+  if (tab != nullptr || log_theta > 0.f) {
+    const float2 cs = rope_cs(tab, log_theta, row % t, pr);
+    const float na = a * cs.x + b * cs.y, nb = -a * cs.y + b * cs.x;
+    a = na;
+    b = nb;
+  }
+  *reinterpret_cast<uint32_t*>(dq + static_cast<size_t>(row) * lddq + h * kBD + 2 * pr) = pack_bf16x2(a, b);
+}
+
+}  // namespace sj
+
+using namespace sj;
+
+extern "C" size_t sj_attn_workspace(int batch, int t, int hq, int hk) {
+  if (batch <= 0 || t <= 0 || hq <= 0 || hk <= 0) return 0;
+  const size_t rows = static_cast<size_t>(batch) * t;
+  const size_t tpad = static_cast<size_t>((t + kBT - 1) / kBT) * kBT;
+  // the f32 dQ accumulator [rows, hq*64], then Delta and LSE*log2(e) transposed, [hq][batch][tpad] each
+  return rows * hq * kBD + 2 * static_cast<size_t>(hq) * batch * tpad;
+}
+
+extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o,
+                               int ldo, const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk,
+                               int lddk, void* dv, int lddv, float* workspace, int batch, int t, int hq, int hk,
+                               int head_dim, int window, float rope_theta, const float* rope_table, void* stream) {
+  if (head_dim != kBD) return fail(SJ_ERR_UNSUPPORTED, "attention: head_dim %d (this build: 64)", head_dim);
+  if (batch <= 0 || t <= 0 || hq <= 0 || hk <= 0 || hq % hk || window < 0)
+    return fail(SJ_ERR_SHAPE, "attention: bad shape batch=%d t=%d hq=%d hk=%d window=%d", batch, t, hq, hk, window);
+  if ((ldq | ldk | ldv | ldo | lddo | lddq | lddk | lddv) % 8)
+    return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: strides must be multiples of 8");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dout) || !aligned16(dk) || !aligned16(dv))
+    return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: 16-byte aligned operands required");
+  if (!workspace || !aligned16(workspace)) return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: workspace must be aligned");
+  if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7))
+    return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: rope table must be 8-byte aligned");
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBwd);
+    if (e != cudaSuccess) return cuda_check(e, "attention backward shared-memory attribute");
+    configured_device = dev;
+  }
+  cudaStream_t s = as_stream(stream);
+  const size_t rows = static_cast<size_t>(batch) * t;
+  const int tpad = ((t + kBT - 1) / kBT) * kBT;
+  float* dq_acc = workspace;
+  float* delta_t = dq_acc + rows * hq * kBD;
+  float* lse_t = delta_t + static_cast<size_t>(hq) * batch * tpad;
+  cudaError_t e = cudaMemsetAsync(dq_acc, 0, rows * hq * kBD * sizeof(float), s);
+  if (e != cudaSuccess) return cuda_check(e, "sj_attn_gqa_bwd: clearing the dQ accumulator");
+  const long long warps = static_cast<long long>(rows) * hq;
+  attn_delta_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo, lse, delta_t, lse_t,
+      static_cast<int>(rows), t, tpad, hq);
+  SJ_LAUNCH_CHECK("attn_delta");
+  CUtensorMap maps[4];
+  int rc = bf16_map(&maps[0], q, static_cast<uint64_t>(hq) * kBD, rows, ldq, kBD, kBT);
+  if (!rc) rc = bf16_map(&maps[1], k, static_cast<uint64_t>(hk) * kBD, rows, ldk, kBD, kBT);
+  if (!rc) rc = bf16_map(&maps[2], v, static_cast<uint64_t>(hk) * kBD, rows, ldv, kBD, kBT);
+  if (!rc) rc = bf16_map(&maps[3], dout, static_cast<uint64_t>(hq) * kBD, rows, lddo, kBD, kBT);
+  if (rc) return rc;
+  BwdParams p;
+  p.t = t;
+  p.hq = hq;
+  p.hk = hk;
+  p.window = window;
+  p.batch = batch;
+  p.nkt = (t + kBT - 1) / kBT;
+  p.items = batch * hk * p.nkt;
+  p.scale = 0.125f;
+  p.scale_log2 = 0.125f * kLog2eB;
+  p.lse_t = lse_t;
+  p.delta_t = delta_t;
+  p.tpad = tpad;
+  p.dq_acc = dq_acc;
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.lddk = lddk;
+  p.lddv = lddv;
+  p.rope_tab = reinterpret_cast<const float2*>(rope_table);
+  p.rope_log_theta = rope_table ? 0.f : (rope_theta > 0.f ? logf(rope_theta) : 0.f);
+  const int grid = std::min(p.items, sm_count());
+  attn_bwd_tc_kernel<<<grid, kBwdThreads, kSmemBwd, s>>>(maps[0], maps[1], maps[2], maps[3], p);
+  SJ_LAUNCH_CHECK("attn_bwd_tc");
+  const size_t pairs = rows * hq * (kBD / 2);
+  attn_dq_finish_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256, 0, s>>>(
+      dq_acc, static_cast<__nv_bfloat16*>(dq), lddq, static_cast<int>(rows), t, hq, p.rope_tab, p.rope_log_theta);
+  SJ_LAUNCH_CHECK("attn_dq_finish");
+  return SJ_OK;
+}
