@@ -52,7 +52,7 @@ struct GemmCfg {
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;  // 256 or 512: powers of two
+  static constexpr int TMEM_COLS = BN == 128 ? 256 : 512;  // two accumulators, rounded to a power of two
 };
 
 SJ_DEVICE void tma_store_2d(const CUtensorMap* map, const void* smem, int x, int y) {
@@ -508,32 +508,43 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   const int sms = sm_count();
   const int m_tiles = (m + kBM - 1) / kBM;
   const int kb_total = (k + kBK - 1) / kBK;
-  // N = 256 tiles: measured on B200, a 128 x 256 UMMA tile runs 1.3-1.8x faster per FLOP than
-  // 128 x 128 on every shape of the training step, even where it leaves SMs without a tile
-  const int bn = n > 128 ? 256 : 128;
-  const int n_tiles = (n + bn - 1) / bn;
-  int splits = 1;
-  if (epilogue == SJ_EPI_ACCUM) {
-    if (split_k > 0) {
-      splits = split_k;
-    } else {
-      // the split count (at least 4 k-blocks per split) whose work units fill the last wave of
-      // CTAs best; ties go to fewer splits (less reduce-add traffic)
-      const int tiles = m_tiles * n_tiles;
-      const int max_splits = std::max(1, std::min(kb_total / 4, 4 * sms / std::max(tiles, 1) + 1));
-      double best = -1.0;
-      for (int sp = 1; sp <= max_splits; ++sp) {
-        const int units = tiles * sp;
-        const int waves = (units + sms - 1) / sms;
-        const double fill = static_cast<double>(units) / (static_cast<double>(waves) * sms);
-        if (fill > best + 0.02) {
-          best = fill;
+  // Tile width and split count from a cost model fitted to B200 measurements of the step's shapes:
+  // time ~ (units per CTA) x (k-blocks per unit + epilogue) x (cost per k-block of the tile width).
+  // Per FLOP a 128 x 256 tile is the most efficient (x1.0), 128 x 192 costs 0.83 of its k-block
+  // time for 0.75 of its work, 128 x 128 costs 0.88 for half of it; 192 wins where 256 leaves
+  // SMs idle (N = 768, 1280 outputs of 4096 rows).  Split-K (ACCUM only) shortens units at the
+  // price of a reduce-add epilogue each.
+  int bn = 128, splits = 1;
+  {
+    const int candidates[3] = {128, 192, 256};
+    const double weight[3] = {0.88, 0.83, 1.0};
+    const double epi_blocks = 3.0;
+    double best = 1e30;
+    for (int ci = 0; ci < 3; ++ci) {
+      const int cbn = candidates[ci];
+      if ((n > 128) != (cbn > 128)) continue;  // N <= 128: one 128-wide tile; wider N: 192 or 256
+      const int tiles = m_tiles * ((n + cbn - 1) / cbn);
+      int sp_lo = 1, sp_hi = 1;
+      if (epilogue == SJ_EPI_ACCUM) {
+        if (split_k > 0) {
+          sp_lo = sp_hi = std::min(split_k, kb_total);
+        } else {
+          sp_hi = std::max(1, std::min(kb_total / 4, 4 * sms / std::max(tiles, 1) + 1));
+        }
+      }
+      for (int sp = sp_lo; sp <= sp_hi; ++sp) {
+        const int kb_unit = (kb_total + sp - 1) / sp;
+        const int waves = (tiles * sp + sms - 1) / sms;
+        const double cost = waves * (kb_unit + epi_blocks) * weight[ci];
+        if (cost < best - 1e-9) {
+          best = cost;
+          bn = cbn;
           splits = sp;
         }
       }
     }
-    splits = std::max(1, std::min(splits, kb_total));
   }
+  const int n_tiles = (n + bn - 1) / bn;
   const int kb_per_split = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per_split - 1) / kb_per_split;  // no empty split
 
@@ -593,5 +604,6 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   const bool a_mn = a_trans != 0;   // A stored [K, M]
   const bool b_mn = b_trans == 0;   // B stored [K, N]
   if (bn == 256) return dispatch_majors<256>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
+  if (bn == 192) return dispatch_majors<192>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
   return dispatch_majors<128>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
 }

@@ -219,6 +219,49 @@ def test_rmsnorm_forward_backward(rows, d, x_f32):
 
 
 # ------------------------------------------------------------------------------------- attention
+@pytest.mark.parametrize("b,t,hq,hk,window", [(8, 1024, 4, 4, 128), (20, 512, 6, 2, 0)])
+def test_attention_more_items_than_sms(b, t, hq, hk, window):
+    """The persistent forward and backward walk several work items per CTA (here 256 or more items
+    on 148 SMs): outputs and gradients against an fp32 torch reference on the GPU, and no expired
+    wait in the device error word."""
+    d = 64
+    n = b * t
+    cq = (hq + 2 * hk) * d
+    qkv = bf(randn(n, cq))
+    ko, vo = hq * d, (hq + hk) * d
+    o = torch.empty(n, hq * d, dtype=torch.bfloat16, device=DEV)
+    lse = torch.empty(n * hq, dtype=torch.float32, device=DEV)
+    call("sj_attn_gqa_fwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), b, t, hq, hk,
+         d, window, stream())
+    do = bf(randn(n, hq * d))
+    dqkv = torch.zeros(n, cq, dtype=torch.bfloat16, device=DEV)
+    from sejong_b200 import _lib
+    ws = torch.empty(_lib.load().sj_attn_workspace(b, t, hq, hk), dtype=torch.float32, device=DEV)
+    call("sj_attn_gqa_bwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), ptr(do),
+         hq * d, ptr(dqkv), cq, ptr(dqkv, ko), cq, ptr(dqkv, vo), cq, ptr(ws), b, t, hq, hk, d, window, 0.0, 0, stream())
+    torch.cuda.synchronize()
+    check_device_error()
+    # fp32 reference on the GPU
+    q = qkv[:, :ko].float().reshape(b, t, hq, d).permute(0, 2, 1, 3).requires_grad_()
+    k = qkv[:, ko:vo].float().reshape(b, t, hk, d).permute(0, 2, 1, 3).requires_grad_()
+    v = qkv[:, vo:].float().reshape(b, t, hk, d).permute(0, 2, 1, 3).requires_grad_()
+    kk, vv = k.repeat_interleave(hq // hk, dim=1), v.repeat_interleave(hq // hk, dim=1)
+    s = q @ kk.transpose(-1, -2) * d ** -0.5
+    pos = torch.arange(t, device=DEV)
+    allowed = pos[None, :] <= pos[:, None]
+    if window:
+        allowed &= pos[None, :] > pos[:, None] - window
+    s = s.masked_fill(~allowed, float("-inf"))
+    ro = torch.softmax(s, dim=-1) @ vv
+    rlse = torch.logsumexp(s, dim=-1)
+    (ro * do.float().reshape(b, t, hq, d).permute(0, 2, 1, 3)).sum().backward()
+    assert rel(o, ro.permute(0, 2, 1, 3).reshape(n, hq * d).detach()) < 2e-2
+    assert float((lse - rlse.permute(0, 2, 1).reshape(-1)).abs().max()) < 2e-2
+    assert rel(dqkv[:, :ko], q.grad.permute(0, 2, 1, 3).reshape(n, ko)) < 2e-2
+    assert rel(dqkv[:, ko:vo], k.grad.permute(0, 2, 1, 3).reshape(n, hk * d)) < 2e-2
+    assert rel(dqkv[:, vo:], v.grad.permute(0, 2, 1, 3).reshape(n, hk * d)) < 2e-2
+
+
 @pytest.mark.parametrize("b,t,hq,hk,window", [(2, 128, 4, 2, 0), (1, 200, 4, 4, 0), (2, 256, 4, 4, 64),
                                               (1, 300, 6, 2, 100), (2, 512, 12, 4, 0), (1, 4096, 4, 4, 128)])
 def test_attention_forward_backward(b, t, hq, hk, window):
