@@ -67,6 +67,11 @@ SJ_DEVICE void tma_reduce_add_2d(const CUtensorMap* map, const void* smem, int x
                "r"(smem_u32(smem)), "r"(x), "r"(y)
                : "memory");
 }
+SJ_DEVICE float tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 SJ_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 SJ_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 SJ_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -332,7 +337,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int e = 0; e < 2; ++e) {
                   const float g = round_bf16(v[32 * half + j + e]);
                   const float u = round_bf16(v[32 * half + 16 + j + e]);
-                  hv[e] = __fdividef(g, 1.0f + __expf(-g)) * u;
+                  // silu(g) = g sigmoid(g) = g (1/2 + tanh(g/2) / 2): one special-function op
+                  hv[e] = g * fmaf(0.5f, tanh_approx(0.5f * g), 0.5f) * u;
                 }
                 hw[8 * half + (j >> 1)] = pack_bf16x2(hv[0], hv[1]);
               }
