@@ -85,6 +85,17 @@ SJ_DEVICE void stage_row128(uint8_t* buf, int lane, const uint32_t (&w)[32]) {
     *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) =
         make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
 }
+// Half `hb` (chunks 4 hb .. 4 hb + 3) of row `lane` of a 32 x 128-byte SWIZZLE_128B slab.
+SJ_DEVICE void stage_half128(uint8_t* buf, int lane, int hb, const uint32_t (&w)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(buf + lane * 128 + (((4 * hb + j) ^ (lane & 7)) << 4)) =
+        make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+// Chunk j of row `lane` of a 32 x 64-byte SWIZZLE_64B slab: r*64 + ((j ^ ((r >> 1) & 3)) * 16).
+SJ_DEVICE void stage_chunk64(uint8_t* buf, int lane, int j, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) = make_uint4(a, b, c, d);
+}
 // Row `lane` of a 32 x 64-byte slab in the SWIZZLE_64B layout: chunk j of row r at
 // r*64 + ((j ^ ((r >> 1) & 3)) * 16).
 SJ_DEVICE void stage_row64(uint8_t* buf, int lane, const uint32_t (&w)[16]) {
@@ -228,164 +239,207 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;           // takes column units c with c % 2 == half
     uint8_t* my_c = staging_c + ew * 4096;  // one 32 x 128 B slab per warp
     uint8_t* my_h = staging_h + ew * 2048;
-    int local = 0, unit = 0;
+    const bool residual = p.epilogue == SJ_EPI_RESIDUAL;
+    const bool rope = p.epilogue == SJ_EPI_ROPE;
+    int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const int mb = (tile % tiles_mn) / p.n_tiles;
       const int nb = tile % p.n_tiles;
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
-      if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, SJ_DEV_GEMM_EPILOGUE_WAIT)) break;
-      tc_fence_after();
       const int r0 = mb * kBM + quarter * 32;
       const int row = r0 + lane;
+      const bool row_ok = row < p.M;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      // Operands of the epilogue that come from global memory (residual rows, the RoPE table row of
+      // this lane's position) are read into `pre` before the accumulator is ready, so that their
+      // latency overlaps this tile's main loop instead of following each TMEM read.
+      uint32_t pre[64];
       if (p.c_f32) {
-#pragma unroll 1
-        for (int c = half; c < BN / 32; c += 2) {
+        // f32 units are 32 columns; the warp's i-th unit (c = half + 2i) uses pre[32 (i & 1) ...],
+        // refilled with unit i + 2 once unit i has consumed it.
+        constexpr int kUnits = BN / 64;
+        auto load_res = [&](int c, int slot) {
           const int col0 = nb * BN + c * 32;
-          if (col0 >= p.N) break;
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + c * 32, r);
-          tmem_wait_ld();
+          if (!residual || !row_ok || col0 >= p.N) return;
+          const float* res = static_cast<const float*>(p.aux) + static_cast<size_t>(row) * p.ld_aux + col0;
+          if (col0 + 32 <= p.N) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * p.alpha);
-          if (p.epilogue == SJ_EPI_RESIDUAL && row < p.M) {
-            const float* res = static_cast<const float*>(p.aux) + static_cast<size_t>(row) * p.ld_aux + col0;
-            if (col0 + 32 <= p.N) {
+            for (int j = 0; j < 8; ++j) {
+              const uint4 q = reinterpret_cast<const uint4*>(res)[j];
+              pre[32 * slot + 4 * j] = q.x;
+              pre[32 * slot + 4 * j + 1] = q.y;
+              pre[32 * slot + 4 * j + 2] = q.z;
+              pre[32 * slot + 4 * j + 3] = q.w;
+            }
+          } else {
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 a4 = reinterpret_cast<const float4*>(res)[j];
-                r[4 * j + 0] = __float_as_uint(__uint_as_float(r[4 * j + 0]) + a4.x);
-                r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) + a4.y);
-                r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) + a4.z);
-                r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) + a4.w);
-              }
-            } else {
+            for (int j = 0; j < 32; ++j) pre[32 * slot + j] = col0 + j < p.N ? __float_as_uint(res[j]) : 0u;
+          }
+        };
+        load_res(half, 0);
+        if (kUnits > 1) load_res(half + 2, 1);
+        if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, SJ_DEV_GEMM_EPILOGUE_WAIT)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < kUnits; ++i) {
+          const int c = half + 2 * i;
+          const int col0 = nb * BN + c * 32;
+          if (col0 < p.N) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(taddr + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * p.alpha);
+            if (residual && row_ok) {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.N) r[j] = __float_as_uint(__uint_as_float(r[j]) + res[j]);
+                r[j] = __float_as_uint(__uint_as_float(r[j]) + __uint_as_float(pre[32 * (i & 1) + j]));
+            }
+            if (i + 2 < kUnits) load_res(c + 4, i & 1);
+            uint8_t* sbuf = my_c;
+            if (lane == 0) bulk_wait_read0();  // this warp's previous slab has been read out
+            __syncwarp();
+            stage_row128(sbuf, lane, r);
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (r0 < p.M) {  // boxes are clipped at M and N; a slab wholly past M is not issued
+                if (p.epilogue == SJ_EPI_ACCUM)
+                  tma_reduce_add_2d(&map_c, sbuf, col0, r0);
+                else
+                  tma_store_2d(&map_c, sbuf, col0, r0);
+              }
+              bulk_commit();
             }
           }
-          uint8_t* sbuf = my_c;
-          if (lane == 0) bulk_wait_read0();  // this warp's previous slab has been read out
-          __syncwarp();
-          stage_row128(sbuf, lane, r);
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (r0 < p.M) {  // boxes are clipped at M and N; a slab wholly past M is not issued
-              if (p.epilogue == SJ_EPI_ACCUM)
-                tma_reduce_add_2d(&map_c, sbuf, col0, r0);
-              else
-                tma_store_2d(&map_c, sbuf, col0, r0);
-            }
-            bulk_commit();
-          }
-          ++unit;
         }
       } else {
-#pragma unroll 1
-        for (int c = half; c < BN / 64; c += 2) {
+        // bf16 units are 64 columns (one RoPE head); a warp has at most two per tile (c = half,
+        // half + 2).  Residual: unit i in pre[32 i ...] (64 bf16).  RoPE: the (cos, sin) pairs of this
+        // row's position, pre[0..63], shared by every head of the tile.
+        constexpr int kUnits = (BN / 64 + 1) / 2;
+        const bool rope_tab = rope && row_ok && nb * BN < p.rope_cols;
+        if (rope_tab && !p.aux) {  // no table given: (cos, sin) of pos * theta^(-2i/64), i = 0..31
+          const float fpos = static_cast<float>(row % p.rope_t);
+#pragma unroll
+          for (int j = 0; j < 64; j += 2) {
+            float sn, cs;
+            sincosf(fpos * expf((-2.0f * static_cast<float>(j >> 1) / 64.0f) * p.rope_log_theta), &sn, &cs);
+            pre[j] = __float_as_uint(cs);
+            pre[j + 1] = __float_as_uint(sn);
+          }
+        } else if (rope_tab) {
+          const uint4* tab = reinterpret_cast<const uint4*>(static_cast<const float*>(p.aux) +
+                                                            static_cast<size_t>(row % p.rope_t) * 64);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const uint4 q = tab[j];
+            pre[4 * j] = q.x;
+            pre[4 * j + 1] = q.y;
+            pre[4 * j + 2] = q.z;
+            pre[4 * j + 3] = q.w;
+          }
+        } else if (residual && row_ok) {
+#pragma unroll
+          for (int i = 0; i < kUnits; ++i) {
+            const int col0 = nb * BN + (half + 2 * i) * 64;
+            if (half + 2 * i < BN / 64 && col0 < p.N) {
+              const __nv_bfloat16* res =
+                  static_cast<const __nv_bfloat16*>(p.aux) + static_cast<size_t>(row) * p.ld_aux + col0;
+              if (col0 + 64 <= p.N) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const uint4 q = reinterpret_cast<const uint4*>(res)[j];
+                  pre[32 * i + 4 * j] = q.x;
+                  pre[32 * i + 4 * j + 1] = q.y;
+                  pre[32 * i + 4 * j + 2] = q.z;
+                  pre[32 * i + 4 * j + 3] = q.w;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  const float lo = col0 + 2 * j < p.N ? bf2f(res[2 * j]) : 0.f;
+                  const float hi = col0 + 2 * j + 1 < p.N ? bf2f(res[2 * j + 1]) : 0.f;
+                  pre[32 * i + j] = pack_bf16x2(lo, hi);
+                }
+              }
+            }
+          }
+        }
+        if (!mbar_wait(&acc_full[buf], use & 1u, abort_flag, SJ_DEV_GEMM_EPILOGUE_WAIT)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int i = 0; i < kUnits; ++i) {
+          const int c = half + 2 * i;
           const int col0 = nb * BN + c * 64;
-          if (col0 >= p.N) break;
-          uint32_t r[32], r2[32];
-          tmem_ld_32x32b_x32(taddr + c * 64, r);
-          tmem_ld_32x32b_x32(taddr + c * 64 + 32, r2);
-          tmem_wait_ld();
-          float v[64];
+          if (c < BN / 64 && col0 < p.N) {
+            uint8_t* sbuf = my_c;
+            uint8_t* hbuf = my_h;
+            if (lane == 0) bulk_wait_read0();  // this warp's previous slabs have been read out
+            __syncwarp();
+            // two halves of 32 columns: (RoPE pairs, SwiGLU gate|up blocks and residual all stay
+            // within a half)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            v[j] = __uint_as_float(r[j]) * p.alpha;
-            v[32 + j] = __uint_as_float(r2[j]) * p.alpha;
-          }
-          uint32_t hw[16];
-          if (p.epilogue == SJ_EPI_ROPE) {
-            if (col0 < p.rope_cols && row < p.M) {
-              const int pos = row % p.rope_t;
-              // col0 is a multiple of 64: the unit is one head, pair index j/2
-              const float4* tab = p.aux ? reinterpret_cast<const float4*>(
-                                              static_cast<const float2*>(p.aux) + static_cast<size_t>(pos) * 32)
-                                        : nullptr;
+            for (int hb = 0; hb < 2; ++hb) {
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(taddr + c * 64 + 32 * hb, r);
+              tmem_wait_ld();
+              float v[32];
 #pragma unroll
-              for (int j = 0; j < 64; j += 4) {
-                float c0, s0, c1, s1;
-                if (tab) {
-                  const float4 cs = tab[j >> 2];  // pairs j/2 and j/2+1: (cos, sin, cos, sin)
-                  c0 = cs.x; s0 = cs.y; c1 = cs.z; s1 = cs.w;
-                } else {
-                  const float fpos = static_cast<float>(pos);
-                  sincosf(fpos * expf((-2.0f * static_cast<float>(j >> 1) / 64.0f) * p.rope_log_theta), &s0, &c0);
-                  sincosf(fpos * expf((-2.0f * static_cast<float>((j >> 1) + 1) / 64.0f) * p.rope_log_theta), &s1,
-                          &c1);
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+              uint32_t w[16];
+              if (swiglu) {
+                // columns come as blocks of 16 gate then the same 16 up features; g and u are
+                // rounded to bf16 before h = silu(g) * u (projection.py:464-470)
+                uint32_t hw[8];
+#pragma unroll
+                for (int j = 0; j < 16; j += 2) {
+                  float hv[2];
+#pragma unroll
+                  for (int e = 0; e < 2; ++e) {
+                    const float g = round_bf16(v[j + e]);
+                    const float u = round_bf16(v[16 + j + e]);
+                    // silu(g) = g sigmoid(g) = g (1/2 + tanh(g/2) / 2): one special-function op
+                    hv[e] = g * fmaf(0.5f, tanh_approx(0.5f * g), 0.5f) * u;
+                  }
+                  hw[j >> 1] = pack_bf16x2(hv[0], hv[1]);
                 }
-                const float a0 = v[j], b0 = v[j + 1], a1 = v[j + 2], b1 = v[j + 3];
-                v[j] = a0 * c0 - b0 * s0;
-                v[j + 1] = a0 * s0 + b0 * c0;
-                v[j + 2] = a1 * c1 - b1 * s1;
-                v[j + 3] = a1 * s1 + b1 * c1;
-              }
-            }
-          } else if (swiglu) {
-            // columns come as blocks of 16 gate then the same 16 up features; g and u are rounded to
-            // bf16 before h = silu(g) * u (projection.py:464-470)
+                stage_chunk64(hbuf, lane, 2 * hb, hw[0], hw[1], hw[2], hw[3]);
+                stage_chunk64(hbuf, lane, 2 * hb + 1, hw[4], hw[5], hw[6], hw[7]);
+              } else if (rope) {
+                if (col0 < p.rope_cols && row_ok) {
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 2) {
-                float hv[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                  const float g = round_bf16(v[32 * half + j + e]);
-                  const float u = round_bf16(v[32 * half + 16 + j + e]);
-                  // silu(g) = g sigmoid(g) = g (1/2 + tanh(g/2) / 2): one special-function op
-                  hv[e] = g * fmaf(0.5f, tanh_approx(0.5f * g), 0.5f) * u;
+                  for (int j = 0; j < 32; j += 2) {  // pair (32 hb + j) / 2 of the row's (cos, sin)
+                    const float cs = __uint_as_float(pre[32 * hb + j]);
+                    const float sn = __uint_as_float(pre[32 * hb + j + 1]);
+                    const float a = v[j], b = v[j + 1];
+                    v[j] = a * cs - b * sn;
+                    v[j + 1] = a * sn + b * cs;
+                  }
                 }
-                hw[8 * half + (j >> 1)] = pack_bf16x2(hv[0], hv[1]);
+              } else if (residual && row_ok) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float2 a = unpack_bf16x2(pre[32 * i + 16 * hb + j]);
+                  v[2 * j] += a.x;
+                  v[2 * j + 1] += a.y;
+                }
               }
+#pragma unroll
+              for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+              stage_half128(sbuf, lane, hb, w);
             }
-          } else if (p.epilogue == SJ_EPI_RESIDUAL && row < p.M) {
-            const __nv_bfloat16* res =
-                static_cast<const __nv_bfloat16*>(p.aux) + static_cast<size_t>(row) * p.ld_aux + col0;
-            if (col0 + 64 <= p.N) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const uint4 w4 = reinterpret_cast<const uint4*>(res)[j];
-                const float2 a = unpack_bf16x2(w4.x), b = unpack_bf16x2(w4.y), cc = unpack_bf16x2(w4.z),
-                             d = unpack_bf16x2(w4.w);
-                v[8 * j + 0] += a.x;
-                v[8 * j + 1] += a.y;
-                v[8 * j + 2] += b.x;
-                v[8 * j + 3] += b.y;
-                v[8 * j + 4] += cc.x;
-                v[8 * j + 5] += cc.y;
-                v[8 * j + 6] += d.x;
-                v[8 * j + 7] += d.y;
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (r0 < p.M) {
+                tma_store_2d(&map_c, sbuf, col0, r0);
+                if (swiglu) tma_store_2d(&map_h, hbuf, col0 / 2, r0);
               }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 64; ++j)
-                if (col0 + j < p.N) v[j] += bf2f(res[j]);
+              bulk_commit();
             }
           }
-          uint32_t w[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) w[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-          uint8_t* sbuf = my_c;
-          uint8_t* hbuf = my_h;
-          if (lane == 0) bulk_wait_read0();  // this warp's previous slabs have been read out
-          __syncwarp();
-          stage_row128(sbuf, lane, w);
-          if (swiglu) stage_row64(hbuf, lane, hw);
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (r0 < p.M) {
-              tma_store_2d(&map_c, sbuf, col0, r0);
-              if (swiglu) tma_store_2d(&map_h, hbuf, col0 / 2, r0);
-            }
-            bulk_commit();
-          }
-          ++unit;
         }
       }
       tc_fence_before();
@@ -514,30 +568,26 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   const int sms = sm_count();
   const int m_tiles = (m + kBM - 1) / kBM;
   const int kb_total = (k + kBK - 1) / kBK;
-  // Tile width and split count from a cost model fitted to B200 measurements of the step's shapes:
-  // time ~ (units per CTA) x (k-blocks per unit + epilogue) x (cost per k-block of the tile width).
-  // Per FLOP a 128 x 256 tile is the most efficient (x1.0), 128 x 192 costs 0.83 of its k-block
-  // time for 0.75 of its work, 128 x 128 costs 0.88 for half of it; 192 wins where 256 leaves
-  // SMs idle (N = 768, 1280 outputs of 4096 rows).  Split-K (ACCUM only) shortens units at the
-  // price of a reduce-add epilogue each.
+  // Tile width and split count from cost models fitted to B200 measurements of the step's shapes.
+  // Per FLOP a 128 x 256 tile is the most efficient (cost x1.0 per k-block), 128 x 192 costs 0.83
+  // of its k-block time for 0.75 of its work, 128 x 128 about 0.8-0.88 for half of it.
   int bn = 128, splits = 1;
-  {
-    const int candidates[3] = {128, 192, 256};
+  const int candidates[3] = {128, 192, 256};
+  if (epilogue == SJ_EPI_ACCUM) {
+    // Weight gradients: time ~ waves x (k-blocks per unit + epilogue) x (k-block cost); split-K
+    // shortens units at the price of a reduce-add epilogue each.  N <= 128: one 128-wide tile.
     const double weight[3] = {0.88, 0.83, 1.0};
     const double epi_blocks = 3.0;
     double best = 1e30;
     for (int ci = 0; ci < 3; ++ci) {
       const int cbn = candidates[ci];
-      if ((n > 128) != (cbn > 128)) continue;  // N <= 128: one 128-wide tile; wider N: 192 or 256
+      if ((n > 128) != (cbn > 128)) continue;
       const int tiles = m_tiles * ((n + cbn - 1) / cbn);
       int sp_lo = 1, sp_hi = 1;
-      if (epilogue == SJ_EPI_ACCUM) {
-        if (split_k > 0) {
-          sp_lo = sp_hi = std::min(split_k, kb_total);
-        } else {
-          sp_hi = std::max(1, std::min(kb_total / 4, 4 * sms / std::max(tiles, 1) + 1));
-        }
-      }
+      if (split_k > 0)
+        sp_lo = sp_hi = std::min(split_k, kb_total);
+      else
+        sp_hi = std::max(1, std::min(kb_total / 4, 4 * sms / std::max(tiles, 1) + 1));
       for (int sp = sp_lo; sp <= sp_hi; ++sp) {
         const int kb_unit = (kb_total + sp - 1) / sp;
         const int waves = (tiles * sp + sms - 1) / sms;
@@ -547,6 +597,31 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
           bn = cbn;
           splits = sp;
         }
+      }
+    }
+  } else {
+    // A CTA overlaps the epilogue of one tile with the main loop of the next, so a CTA with t tiles
+    // takes about t x max(ML, EP) + min(ML, EP): ML = k-blocks x k-block cost of the width, EP = the
+    // epilogue's traffic in the same unit, (BN / 256) per byte that one output column moves per row
+    // (C, plus the residual read or the SwiGLU h), and for RoPE a table row per tile shared by
+    // its BN / 64 heads.
+    const double weight[3] = {0.8, 0.83, 1.0};
+    const int c_bytes = c_dtype == SJ_F32 ? 4 : 2;
+    const double col_bytes = epilogue == SJ_EPI_RESIDUAL ? 2.0 * c_bytes
+                             : epilogue == SJ_EPI_SWIGLU ? 3.0
+                                                         : static_cast<double>(c_bytes);
+    double best = 1e30;
+    for (int ci = 0; ci < 3; ++ci) {
+      const int cbn = candidates[ci];
+      if (n <= 128 && cbn > 128) continue;
+      const int tiles = m_tiles * ((n + cbn - 1) / cbn);
+      const int per_cta = (tiles + sms - 1) / sms;
+      const double ml = kb_total * weight[ci];
+      const double ep = (cbn / 256.0) * col_bytes + (epilogue == SJ_EPI_ROPE ? 2.0 * 256.0 / cbn : 0.0);
+      const double cost = per_cta * std::max(ml, ep) + std::min(ml, ep);
+      if (cost < best - 1e-9) {
+        best = cost;
+        bn = cbn;
       }
     }
   }
