@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // operands may come from the previous kernel
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -463,9 +464,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
 // Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57), one warp each, written with the LSE
 // (times log2 e) transposed to [head][batch][tpad] so that a step's 128 values are one contiguous run.
-__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int ldo, const __nv_bfloat16* __restrict__ dout,
-                                  int lddo, const float* __restrict__ lse, float* __restrict__ delta_t,
-                                  float* __restrict__ lse_t, int rows, int t, int tpad, int hq) {
+__global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dout,
+                                  int lddo, const float* lse, float* delta_t,
+                                  float* lse_t, int rows, int t, int tpad, int hq) {
+  pdl_wait();
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (w >= rows * hq) return;
   const int row = w / hq, h = w % hq;
@@ -483,8 +485,9 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, int ldo, 
 }
 
 // dq = bf16(inverse RoPE(dq_acc)), one thread per (row, head, column pair).
-__global__ void attn_dq_finish_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int lddq,
-                                      int rows, int t, int hq, const float2* __restrict__ tab, float log_theta) {
+__global__ void attn_dq_finish_kernel(const float* acc, __nv_bfloat16* dq, int lddq,
+                                      int rows, int t, int hq, const float2* tab, float log_theta) {
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t pairs = static_cast<size_t>(rows) * hq * (kBD / 2);
   if (i >= pairs) return;
@@ -542,10 +545,10 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   float* dq_acc = workspace;
   float* delta_t = dq_acc + rows * hq * kBD;
   float* lse_t = delta_t + static_cast<size_t>(hq) * batch * tpad;
-  cudaError_t e = cudaMemsetAsync(dq_acc, 0, rows * hq * kBD * sizeof(float), s);
-  if (e != cudaSuccess) return cuda_check(e, "sj_attn_gqa_bwd: clearing the dQ accumulator");
+  const int zs = zero_async(dq_acc, rows * hq * kBD * sizeof(float), s);
+  if (zs != SJ_OK) return zs;
   const long long warps = static_cast<long long>(rows) * hq;
-  attn_delta_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s>>>(
+  launch(attn_delta_kernel, static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s, 
       static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo, lse, delta_t, lse_t,
       static_cast<int>(rows), t, tpad, hq);
   SJ_LAUNCH_CHECK("attn_delta");
@@ -576,10 +579,10 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   p.rope_tab = reinterpret_cast<const float2*>(rope_table);
   p.rope_log_theta = rope_table ? 0.f : (rope_theta > 0.f ? logf(rope_theta) : 0.f);
   const int grid = std::min(p.items, sm_count());
-  attn_bwd_tc_kernel<<<grid, kBwdThreads, kSmemBwd, s>>>(maps[0], maps[1], maps[2], maps[3], p);
+  launch(attn_bwd_tc_kernel, grid, kBwdThreads, kSmemBwd, s, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("attn_bwd_tc");
   const size_t pairs = rows * hq * (kBD / 2);
-  attn_dq_finish_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256, 0, s>>>(
+  launch(attn_dq_finish_kernel, static_cast<unsigned>((pairs + 255) / 256), 256, 0, s, 
       dq_acc, static_cast<__nv_bfloat16*>(dq), lddq, static_cast<int>(rows), t, hq, p.rope_tab, p.rope_log_theta);
   SJ_LAUNCH_CHECK("attn_dq_finish");
   return SJ_OK;

@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // operands may come from the previous kernel
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
@@ -465,7 +466,7 @@ extern "C" int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, c
   p.ldo = ldo;
   p.lse = lse;
   const int grid = std::min(p.items, sm_count());
-  attn_fwd_tc_kernel<<<grid, kThreadsTc, kSmemFwd, as_stream(stream)>>>(maps[0], maps[1], maps[2], p);
+  launch(attn_fwd_tc_kernel, grid, kThreadsTc, kSmemFwd, as_stream(stream), maps[0], maps[1], maps[2], p);
   SJ_LAUNCH_CHECK("attn_fwd_tc");
   return SJ_OK;
 }

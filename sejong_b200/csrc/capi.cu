@@ -3,6 +3,7 @@
 // which must be bit-exact with the reference.
 #include <cmath>
 #include <cstring>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -29,6 +30,14 @@ int fail(int code, const char* fmt, ...) {
 int cuda_check(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return SJ_OK;
   return fail(SJ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("SJ_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 int sm_count() {
@@ -92,7 +101,7 @@ int sj_device_error(int* code, int clear, void* stream) {
 int sj_zero(void* ptr, size_t bytes, void* stream) {
   if (bytes == 0) return SJ_OK;
   if (!ptr) return sj::fail(SJ_ERR_ARGUMENT, "sj_zero: null pointer");
-  return sj::cuda_check(cudaMemsetAsync(ptr, 0, bytes, sj::as_stream(stream)), "sj_zero");
+  return sj::zero_async(ptr, bytes, sj::as_stream(stream));
 }
 
 // ---------------------------------------------------------------- Rng (crates/sejong-core/src/lib.rs:591-623)

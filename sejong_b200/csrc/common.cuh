@@ -61,6 +61,18 @@ SJ_DEVICE float warp_max(float v) {
   return v;
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels are launched with programmatic stream serialization (sj::launch), so the launch of one
+// is processed while its predecessor in the stream drains.  pdl_wait() blocks until the
+// predecessor grid has completed and its memory operations are visible; every kernel calls it
+// before its first global-memory access (and before any early return, so that its own completion
+// still implies its predecessor's).  No kernel triggers its dependents early: measured on the
+// training step, CTAs of the next kernel resident and waiting beside a running kernel cost more
+// than the launch latency they hide.  Kernel pointer parameters carry no __restrict__: a const
+// __restrict__ pointer lets the compiler use read-only loads that it may schedule before the
+// wait, which would read the predecessor's output before it is complete.
+SJ_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---------------------------------------------------------------- mbarrier
 SJ_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");

@@ -1,16 +1,45 @@
 // Bandwidth-bound kernels of the step: embedding gather / scatter, RoPE, SwiGLU backward,
 // hierarchy patch pooling and broadcast, casts and adds.  All use 16-byte vector accesses along
 // the contiguous feature dimension.
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
 namespace sj {
 
+// ---------------------------------------------------------------- zero fill
+// Bytes [0, head) and the `tail` bytes after the 16-byte-aligned middle are written one by one, the
+// n16 vectors of the middle with 16-byte stores.  Used instead of a memset node so that every
+// operation of the library on a stream is a kernel that orders itself with pdl_wait.
+__global__ void zero_kernel(uint8_t* p, size_t head, size_t n16, size_t tail) {
+  pdl_wait();
+  const size_t tid = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  if (tid < head) p[tid] = 0;
+  uint4* v = reinterpret_cast<uint4*>(p + head);
+  for (size_t i = tid; i < n16; i += stride) v[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid < tail) p[head + 16 * n16 + tid] = 0;
+}
+
+int zero_async(void* ptr, size_t bytes, cudaStream_t stream) {
+  if (bytes == 0) return SJ_OK;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(ptr);
+  const size_t head = std::min(bytes, static_cast<size_t>((16 - (addr & 15u)) & 15u));
+  const size_t n16 = (bytes - head) / 16;
+  const size_t tail = bytes - head - 16 * n16;
+  const size_t blocks = std::min<size_t>((n16 + 255) / 256 + 1, static_cast<size_t>(sm_count()) * 8);
+  launch(zero_kernel, static_cast<unsigned>(blocks), 256, 0, stream, static_cast<uint8_t*>(ptr), head, n16, tail);
+  SJ_LAUNCH_CHECK("zero");
+  return SJ_OK;
+}
+
 // ---------------------------------------------------------------- embedding (kernels.py:41-52)
 // One thread per 8 columns (one 16-byte bf16 vector of the weight row).
 template <bool F32_OUT>
-__global__ void embedding_fwd_kernel(const uint4* __restrict__ w, const int32_t* __restrict__ ids, void* __restrict__ y,
+__global__ void embedding_fwd_kernel(const uint4* w, const int32_t* ids, void* y,
                                      int n, int vec_per_row, int vocab) {
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<size_t>(n) * vec_per_row) return;
   const int row = static_cast<int>(i / vec_per_row), c = static_cast<int>(i % vec_per_row);
@@ -34,8 +63,9 @@ __global__ void embedding_fwd_kernel(const uint4* __restrict__ w, const int32_t*
 // (vocab row, column) per CTA; avoids per-element global atomics on frequent bytes.
 constexpr int kEmbRows = 2048;
 __global__ void __launch_bounds__(256)
-    embedding_bwd_kernel(const float* __restrict__ dy, const int32_t* __restrict__ ids, float* __restrict__ dw, int n,
+    embedding_bwd_kernel(const float* dy, const int32_t* ids, float* dw, int n,
                          int d, int vocab) {
+  pdl_wait();
   extern __shared__ float acc[];  // [vocab][32]
   const int col = blockIdx.y * 32 + (threadIdx.x & 31);
   for (int i = threadIdx.x; i < vocab * 32; i += blockDim.x) acc[i] = 0.f;
@@ -55,8 +85,9 @@ __global__ void __launch_bounds__(256)
 }
 
 // ---------------------------------------------------------------- RoPE (kernels.py:103-113)
-__global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int rows, int heads,
+__global__ void rope_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int rows, int heads,
                             int hd, int t, int offset, float log_theta, float sign) {
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t pairs_per_row = static_cast<size_t>(heads) * (hd / 2);
   if (i >= static_cast<size_t>(rows) * pairs_per_row) return;
@@ -73,8 +104,9 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
   y[base + 1] = f2bf(a * s + b * c);
 }
 
-__global__ void rope_table_kernel(float2* __restrict__ table, int t, int half, int offset, float log_theta,
+__global__ void rope_table_kernel(float2* table, int t, int half, int offset, float log_theta,
                                   float hd) {
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= t * half) return;
   const int pos = i / half, pair = i % half;
@@ -86,8 +118,9 @@ __global__ void rope_table_kernel(float2* __restrict__ table, int t, int half, i
 
 // ---------------------------------------------------------------- SwiGLU backward (kernels.py:95-101)
 // gu: per row, blocks of 32 columns = 16 gate features then the same 16 up features.
-__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __nv_bfloat16* __restrict__ dh,
-                                  __nv_bfloat16* __restrict__ dgu, int rows, int f) {
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* gu, const __nv_bfloat16* dh,
+                                  __nv_bfloat16* dgu, int rows, int f) {
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // one per 8 features
   const int groups = f / 8;
   if (i >= static_cast<size_t>(rows) * groups) return;
@@ -112,8 +145,9 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, const __
 }
 
 // ---------------------------------------------------------------- hierarchy (hierarchy.py:107-172)
-__global__ void patch_pool_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int batch,
+__global__ void patch_pool_fwd_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, int batch,
                                       int t, int d, int patch) {
+  pdl_wait();
   const int patches = (t + patch - 1) / patch;
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // one per 8 columns
   const int vec = d / 8;
@@ -141,8 +175,9 @@ __global__ void patch_pool_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_
   *reinterpret_cast<uint4*>(y + static_cast<size_t>(prow) * d + c) = o;
 }
 
-__global__ void patch_pool_bwd_kernel(const float* __restrict__ dy, float* __restrict__ dx, int batch, int t, int d,
+__global__ void patch_pool_bwd_kernel(const float* dy, float* dx, int batch, int t, int d,
                                       int patch) {
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // one per 4 columns
   const int vec = d / 4;
   if (i >= static_cast<size_t>(batch) * t * vec) return;
@@ -161,8 +196,9 @@ __global__ void patch_pool_bwd_kernel(const float* __restrict__ dy, float* __res
 }
 
 template <bool F32_OUT>
-__global__ void patch_broadcast_fwd_kernel(const __nv_bfloat16* __restrict__ z, const __nv_bfloat16* __restrict__ bos,
-                                           void* __restrict__ yv, int add, int batch, int t, int d, int patch) {
+__global__ void patch_broadcast_fwd_kernel(const __nv_bfloat16* z, const __nv_bfloat16* bos,
+                                           void* yv, int add, int batch, int t, int d, int patch) {
+  pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // one per 8 columns
   const int vec = d / 8;
   if (i >= static_cast<size_t>(batch) * t * vec) return;
@@ -202,9 +238,10 @@ __global__ void patch_broadcast_fwd_kernel(const __nv_bfloat16* __restrict__ z, 
 }
 
 // dz[b,p,:] = sum_{k<P} dy[b, (p+1)P + k, :]  (bf16 out); blocks past the body reduce dbos.
-__global__ void patch_broadcast_bwd_kernel(const float* __restrict__ dy, __nv_bfloat16* __restrict__ dz,
-                                           __nv_bfloat16* __restrict__ dbos, int batch, int t, int d, int patch,
+__global__ void patch_broadcast_bwd_kernel(const float* dy, __nv_bfloat16* dz,
+                                           __nv_bfloat16* dbos, int batch, int t, int d, int patch,
                                            int body_threads) {
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int patches = (t + patch - 1) / patch;
   if (i < body_threads) {
@@ -228,34 +265,39 @@ __global__ void patch_broadcast_bwd_kernel(const float* __restrict__ dy, __nv_bf
 
 // ---------------------------------------------------------------- cast / add
 template <typename S, typename D>
-__global__ void cast_kernel(const S* __restrict__ x, D* __restrict__ y, size_t n);
+__global__ void cast_kernel(const S* x, D* y, size_t n);
 template <>
-__global__ void cast_kernel<float, __nv_bfloat16>(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, size_t n) {
+__global__ void cast_kernel<float, __nv_bfloat16>(const float* x, __nv_bfloat16* y, size_t n) {
+  pdl_wait();
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     y[i] = f2bf(x[i]);
 }
 template <>
-__global__ void cast_kernel<__nv_bfloat16, float>(const __nv_bfloat16* __restrict__ x, float* __restrict__ y, size_t n) {
+__global__ void cast_kernel<__nv_bfloat16, float>(const __nv_bfloat16* x, float* y, size_t n) {
+  pdl_wait();
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     y[i] = bf2f(x[i]);
 }
 template <>
-__global__ void cast_kernel<float, double>(const float* __restrict__ x, double* __restrict__ y, size_t n) {
+__global__ void cast_kernel<float, double>(const float* x, double* y, size_t n) {
+  pdl_wait();
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     y[i] = static_cast<double>(x[i]);
 }
 template <>
-__global__ void cast_kernel<double, float>(const double* __restrict__ x, float* __restrict__ y, size_t n) {
+__global__ void cast_kernel<double, float>(const double* x, float* y, size_t n) {
+  pdl_wait();
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
     y[i] = static_cast<float>(x[i]);
 }
 
 template <typename T>
-__global__ void add_kernel(const T* __restrict__ x, const T* __restrict__ z, T* __restrict__ y, size_t n, float alpha) {
+__global__ void add_kernel(const T* x, const T* z, T* y, size_t n, float alpha) {
+  pdl_wait();
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     if constexpr (sizeof(T) == 2)
@@ -284,9 +326,9 @@ extern "C" int sj_embedding_fwd(const void* w, const int32_t* ids, void* y, int 
   const size_t total = static_cast<size_t>(n) * vpr;
   const unsigned grid = static_cast<unsigned>((total + 255) / 256);
   if (y_dtype == SJ_BF16)
-    embedding_fwd_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const uint4*>(w), ids, y, n, vpr, vocab);
+    launch(embedding_fwd_kernel<false>, grid, 256, 0, as_stream(stream), static_cast<const uint4*>(w), ids, y, n, vpr, vocab);
   else if (y_dtype == SJ_F32)
-    embedding_fwd_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(static_cast<const uint4*>(w), ids, y, n, vpr, vocab);
+    launch(embedding_fwd_kernel<true>, grid, 256, 0, as_stream(stream), static_cast<const uint4*>(w), ids, y, n, vpr, vocab);
   else
     return fail(SJ_ERR_ARGUMENT, "sj_embedding_fwd: y must be bf16 or f32");
   SJ_LAUNCH_CHECK("embedding_fwd");
@@ -300,7 +342,7 @@ extern "C" int sj_embedding_bwd(const float* dy, const int32_t* ids, float* dw, 
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(embedding_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   }
-  embedding_bwd_kernel<<<grid, 256, smem, as_stream(stream)>>>(dy, ids, dw, n, d, vocab);
+  launch(embedding_bwd_kernel, grid, 256, smem, as_stream(stream), dy, ids, dw, n, d, vocab);
   SJ_LAUNCH_CHECK("embedding_bwd");
   return SJ_OK;
 }
@@ -310,7 +352,7 @@ extern "C" int sj_rope(const void* x, void* y, int rows, int heads, int head_dim
   if (rows <= 0 || heads <= 0 || head_dim <= 0 || head_dim % 2 || t <= 0)
     return fail(SJ_ERR_SHAPE, "sj_rope: bad shape");
   const size_t pairs = static_cast<size_t>(rows) * heads * (head_dim / 2);
-  rope_kernel<<<static_cast<unsigned>((pairs + 255) / 256), 256, 0, as_stream(stream)>>>(
+  launch(rope_kernel, static_cast<unsigned>((pairs + 255) / 256), 256, 0, as_stream(stream), 
       static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), rows, heads, head_dim, t, offset,
       logf(theta), inverse ? -1.0f : 1.0f);
   SJ_LAUNCH_CHECK("rope");
@@ -322,7 +364,7 @@ extern "C" int sj_rope_table(float* table, int t, int head_dim, int offset, floa
     return fail(SJ_ERR_ARGUMENT, "sj_rope_table: bad arguments");
   if (reinterpret_cast<uintptr_t>(table) & 7) return fail(SJ_ERR_ARGUMENT, "sj_rope_table: table must be 8-byte aligned");
   const int n = t * (head_dim / 2);
-  rope_table_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(reinterpret_cast<float2*>(table), t,
+  launch(rope_table_kernel, (n + 255) / 256, 256, 0, as_stream(stream), reinterpret_cast<float2*>(table), t,
                                                                    head_dim / 2, offset, logf(theta),
                                                                    static_cast<float>(head_dim));
   SJ_LAUNCH_CHECK("rope_table");
@@ -334,7 +376,7 @@ extern "C" int sj_swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows
   if (!aligned16(gu) || !aligned16(dh) || !aligned16(dgu))
     return fail(SJ_ERR_ARGUMENT, "sj_swiglu_bwd: 16-byte alignment required");
   const size_t threads = static_cast<size_t>(rows) * (f / 8);
-  swiglu_bwd_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+  launch(swiglu_bwd_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream), 
       static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(dh), static_cast<__nv_bfloat16*>(dgu),
       rows, f);
   SJ_LAUNCH_CHECK("swiglu_bwd");
@@ -345,7 +387,7 @@ extern "C" int sj_patch_pool_fwd(const void* x, void* y, int batch, int t, int d
   if (batch <= 0 || t <= 0 || d % 8 || patch <= 0) return fail(SJ_ERR_SHAPE, "sj_patch_pool_fwd: bad shape");
   const int patches = (t + patch - 1) / patch;
   const size_t threads = static_cast<size_t>(batch) * patches * (d / 8);
-  patch_pool_fwd_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(
+  launch(patch_pool_fwd_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream), 
       static_cast<const __nv_bfloat16*>(x), static_cast<__nv_bfloat16*>(y), batch, t, d, patch);
   SJ_LAUNCH_CHECK("patch_pool_fwd");
   return SJ_OK;
@@ -354,7 +396,7 @@ extern "C" int sj_patch_pool_fwd(const void* x, void* y, int batch, int t, int d
 extern "C" int sj_patch_pool_bwd(const float* dy, float* dx, int batch, int t, int d, int patch, void* stream) {
   if (batch <= 0 || t <= 0 || d % 4 || patch <= 0) return fail(SJ_ERR_SHAPE, "sj_patch_pool_bwd: bad shape");
   const size_t threads = static_cast<size_t>(batch) * t * (d / 4);
-  patch_pool_bwd_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream)>>>(dy, dx, batch, t,
+  launch(patch_pool_bwd_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream), dy, dx, batch, t,
                                                                                                     d, patch);
   SJ_LAUNCH_CHECK("patch_pool_bwd");
   return SJ_OK;
@@ -368,9 +410,9 @@ extern "C" int sj_patch_broadcast_fwd(const void* z, const void* bos, void* y, i
   const auto* zz = static_cast<const __nv_bfloat16*>(z);
   const auto* bb = static_cast<const __nv_bfloat16*>(bos);
   if (y_dtype == SJ_BF16)
-    patch_broadcast_fwd_kernel<false><<<grid, 256, 0, as_stream(stream)>>>(zz, bb, y, add, batch, t, d, patch);
+    launch(patch_broadcast_fwd_kernel<false>, grid, 256, 0, as_stream(stream), zz, bb, y, add, batch, t, d, patch);
   else if (y_dtype == SJ_F32)
-    patch_broadcast_fwd_kernel<true><<<grid, 256, 0, as_stream(stream)>>>(zz, bb, y, add, batch, t, d, patch);
+    launch(patch_broadcast_fwd_kernel<true>, grid, 256, 0, as_stream(stream), zz, bb, y, add, batch, t, d, patch);
   else
     return fail(SJ_ERR_ARGUMENT, "sj_patch_broadcast_fwd: y must be bf16 or f32");
   SJ_LAUNCH_CHECK("patch_broadcast_fwd");
@@ -383,7 +425,7 @@ extern "C" int sj_patch_broadcast_bwd(const float* dy, void* dz, void* dbos, int
   const int patches = (t + patch - 1) / patch;
   const int body = batch * patches * d;
   const int total = body + d;
-  patch_broadcast_bwd_kernel<<<(total + 255) / 256, 256, 0, as_stream(stream)>>>(
+  launch(patch_broadcast_bwd_kernel, (total + 255) / 256, 256, 0, as_stream(stream), 
       dy, static_cast<__nv_bfloat16*>(dz), static_cast<__nv_bfloat16*>(dbos), batch, t, d, patch, body);
   SJ_LAUNCH_CHECK("patch_broadcast_bwd");
   return SJ_OK;
@@ -394,13 +436,13 @@ extern "C" int sj_cast(const void* x, int x_dtype, void* y, int y_dtype, size_t 
   cudaStream_t s = as_stream(stream);
   const int g = grid_for(n, 256);
   if (x_dtype == SJ_F32 && y_dtype == SJ_BF16)
-    cast_kernel<float, __nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const float*>(x), static_cast<__nv_bfloat16*>(y), n);
+    launch(cast_kernel<float, __nv_bfloat16>, g, 256, 0, s, static_cast<const float*>(x), static_cast<__nv_bfloat16*>(y), n);
   else if (x_dtype == SJ_BF16 && y_dtype == SJ_F32)
-    cast_kernel<__nv_bfloat16, float><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x), static_cast<float*>(y), n);
+    launch(cast_kernel<__nv_bfloat16, float>, g, 256, 0, s, static_cast<const __nv_bfloat16*>(x), static_cast<float*>(y), n);
   else if (x_dtype == SJ_F32 && y_dtype == SJ_F64)
-    cast_kernel<float, double><<<g, 256, 0, s>>>(static_cast<const float*>(x), static_cast<double*>(y), n);
+    launch(cast_kernel<float, double>, g, 256, 0, s, static_cast<const float*>(x), static_cast<double*>(y), n);
   else if (x_dtype == SJ_F64 && y_dtype == SJ_F32)
-    cast_kernel<double, float><<<g, 256, 0, s>>>(static_cast<const double*>(x), static_cast<float*>(y), n);
+    launch(cast_kernel<double, float>, g, 256, 0, s, static_cast<const double*>(x), static_cast<float*>(y), n);
   else
     return fail(SJ_ERR_UNSUPPORTED, "sj_cast: %d -> %d not supported", x_dtype, y_dtype);
   SJ_LAUNCH_CHECK("cast");
@@ -412,10 +454,10 @@ extern "C" int sj_add(const void* x, const void* z, void* y, size_t n, float alp
   cudaStream_t s = as_stream(stream);
   const int g = grid_for(n, 256);
   if (dtype == SJ_F32)
-    add_kernel<float><<<g, 256, 0, s>>>(static_cast<const float*>(x), static_cast<const float*>(z),
+    launch(add_kernel<float>, g, 256, 0, s, static_cast<const float*>(x), static_cast<const float*>(z),
                                          static_cast<float*>(y), n, alpha);
   else if (dtype == SJ_BF16)
-    add_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+    launch(add_kernel<__nv_bfloat16>, g, 256, 0, s, static_cast<const __nv_bfloat16*>(x),
                                                  static_cast<const __nv_bfloat16*>(z), static_cast<__nv_bfloat16*>(y),
                                                  n, alpha);
   else

@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // operands may come from the previous kernel
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = tiles_mn * p.splits;
   // work unit -> (split, m tile, n tile); the split index is slowest so that concurrently running
@@ -509,7 +510,7 @@ static int launch_gemm(const CUtensorMap* maps, const GemmParams& p, int grid, i
     if (e != cudaSuccess) return cuda_check(e, "gemm shared-memory attribute");
     configured_device = dev;
   }
-  kernel<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], p);
+  launch(kernel, grid, kThreads, smem, stream, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("gemm launch");
   return SJ_OK;
 }

@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "sejong.h"
 
@@ -23,6 +24,36 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // stride `ld` elements, box box_inner x box_outer (gemm.cu).
 int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
              uint32_t box_outer);
+
+// Zero `bytes` bytes at `ptr` on `stream` with a kernel (elementwise.cu).
+int zero_async(void* ptr, size_t bytes, cudaStream_t stream);
+
+// Whether kernels are launched with programmatic stream serialization (default on; SJ_PDL=0 in the
+// environment turns it off, read once per process).
+bool pdl_enabled();
+
+// kernel<<<grid, block, smem, stream>>>(args...) with programmatic stream serialization: the kernel
+// may begin while the previous kernel of the stream finishes, and waits for it (pdl_wait) before
+// touching global memory.  Errors are left for SJ_LAUNCH_CHECK (cudaGetLastError).
+template <typename... KArgs, typename... Args>
+inline void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                   Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // arguments converted to the parameter types, as <<<...>>> would (const parameters included)
+  [&](KArgs... coerced) {
+    void* pargs[] = {const_cast<void*>(static_cast<const void*>(&coerced))...};
+    cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kernel), pargs);
+  }(std::forward<Args>(args)...);
+}
 
 }  // namespace sj
 

@@ -8,10 +8,11 @@ namespace sj {
 
 // ---------------------------------------------------------------- cross entropy
 // One warp per row.  kernels.py:176-191 (forward, backward), kernels.py:254-262 (loss_summary).
-__global__ void cross_entropy_kernel(const float* __restrict__ logits, int ld, const int32_t* __restrict__ targets,
-                                     int rows, int vocab, float seed, float* __restrict__ loss_rows,
-                                     __nv_bfloat16* __restrict__ dlogits, int ld_d, double* __restrict__ loss_sum,
+__global__ void cross_entropy_kernel(const float* logits, int ld, const int32_t* targets,
+                                     int rows, int vocab, float seed, float* loss_rows,
+                                     __nv_bfloat16* dlogits, int ld_d, double* loss_sum,
                                      double weight) {
+  pdl_wait();
   __shared__ double block_sum[8];
   const int warp_in_block = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_in_block;
@@ -52,7 +53,8 @@ __global__ void cross_entropy_kernel(const float* __restrict__ logits, int ld, c
 
 // ---------------------------------------------------------------- gradient norm (kernels.py:265-287)
 constexpr int kSumsqThreads = 256;
-__global__ void grad_sumsq_kernel(const float* __restrict__ g, size_t n, double* __restrict__ partials) {
+__global__ void grad_sumsq_kernel(const float* g, size_t n, double* partials) {
+  pdl_wait();
   __shared__ double red[kSumsqThreads / 32];
   double acc = 0.0;
   const size_t n4 = n / 4;
@@ -76,9 +78,10 @@ __global__ void grad_sumsq_kernel(const float* __restrict__ g, size_t n, double*
 }
 
 // hyper layout: [0] lr, [1] 1/(1-b1^t), [2] 1/(1-b2^t), [3] gradient scale, [4] norm, [5] step
-__global__ void optim_prepare_kernel(const double* __restrict__ partials, int n_partials, double* state, float* hyper,
+__global__ void optim_prepare_kernel(const double* partials, int n_partials, double* state, float* hyper,
                                      float learning_rate, float min_learning_rate, int warmup_steps, int total_steps,
                                      float beta1, float beta2, float clip_norm, int clip_enabled, float loss_scale) {
+  pdl_wait();
   __shared__ double red[32];
   double acc = 0.0;
   for (int i = threadIdx.x; i < n_partials; i += blockDim.x) acc += partials[i];
@@ -112,9 +115,10 @@ __global__ void optim_prepare_kernel(const double* __restrict__ partials, int n_
 }
 
 // kernels.py:193-202 per element; decay on [0, n_decay).
-__global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g, float* __restrict__ m,
-                             float* __restrict__ v, __nv_bfloat16* __restrict__ wb, size_t n, size_t n_decay,
-                             const float* __restrict__ hyper, float beta1, float beta2, float eps, float wd) {
+__global__ void adamw_kernel(float* w, const float* g, float* m,
+                             float* v, __nv_bfloat16* wb, size_t n, size_t n_decay,
+                             const float* hyper, float beta1, float beta2, float eps, float wd) {
+  pdl_wait();
   const float lr = hyper[0], inv_b1 = hyper[1], inv_b2 = hyper[2], scale = hyper[3];
   const size_t n4 = n / 4;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < (n + 3) / 4;
@@ -162,8 +166,9 @@ __global__ void adamw_kernel(float* __restrict__ w, const float* __restrict__ g,
   }
 }
 
-__global__ void sgd_kernel(float* __restrict__ w, const float* __restrict__ g, __nv_bfloat16* __restrict__ wb,
-                           size_t n, size_t n_decay, const float* __restrict__ hyper, float wd) {
+__global__ void sgd_kernel(float* w, const float* g, __nv_bfloat16* wb,
+                           size_t n, size_t n_decay, const float* hyper, float wd) {
+  pdl_wait();
   const float lr = hyper[0], scale = hyper[3];
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -183,7 +188,7 @@ extern "C" int sj_cross_entropy(const float* logits, int ld, const int32_t* targ
   if (rows <= 0 || vocab <= 0 || ld < vocab || (dlogits && ld_d < vocab))
     return fail(SJ_ERR_SHAPE, "sj_cross_entropy: bad shape");
   const int warps = 8;
-  cross_entropy_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, as_stream(stream)>>>(
+  launch(cross_entropy_kernel, (rows + warps - 1) / warps, warps * 32, 0, as_stream(stream), 
       logits, ld, targets, rows, vocab, seed, loss_rows, static_cast<__nv_bfloat16*>(dlogits), ld_d, loss_sum, weight);
   SJ_LAUNCH_CHECK("cross_entropy");
   return SJ_OK;
@@ -197,7 +202,7 @@ extern "C" int sj_sumsq_partials(size_t n) {
 
 extern "C" int sj_grad_sumsq(const float* g, size_t n, double* partials, void* stream) {
   if (!aligned16(g)) return fail(SJ_ERR_ARGUMENT, "sj_grad_sumsq: gradient buffer must be 16-byte aligned");
-  grad_sumsq_kernel<<<sj_sumsq_partials(n), kSumsqThreads, 0, as_stream(stream)>>>(g, n, partials);
+  launch(grad_sumsq_kernel, sj_sumsq_partials(n), kSumsqThreads, 0, as_stream(stream), g, n, partials);
   SJ_LAUNCH_CHECK("grad_sumsq");
   return SJ_OK;
 }
@@ -207,7 +212,7 @@ extern "C" int sj_optim_prepare(const double* partials, int n_partials, double* 
                                 float beta1, float beta2, float clip_norm, int clip_enabled, float loss_scale,
                                 void* stream) {
   if (n_partials <= 0 || !partials || !state || !hyper) return fail(SJ_ERR_ARGUMENT, "sj_optim_prepare: bad argument");
-  optim_prepare_kernel<<<1, 256, 0, as_stream(stream)>>>(partials, n_partials, state, hyper, learning_rate,
+  launch(optim_prepare_kernel, 1, 256, 0, as_stream(stream), partials, n_partials, state, hyper, learning_rate,
                                                         min_learning_rate, warmup_steps, total_steps, beta1, beta2,
                                                         clip_norm, clip_enabled, loss_scale);
   SJ_LAUNCH_CHECK("optim_prepare");
@@ -223,7 +228,7 @@ extern "C" int sj_adamw(float* w, const float* g, float* m, float* v, void* w_bf
   const size_t cap = static_cast<size_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  adamw_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+  launch(adamw_kernel, static_cast<unsigned>(blocks), 256, 0, as_stream(stream), 
       w, g, m, v, static_cast<__nv_bfloat16*>(w_bf16), n, n_decay, hyper, beta1, beta2, eps, weight_decay);
   SJ_LAUNCH_CHECK("adamw");
   return SJ_OK;
@@ -235,7 +240,7 @@ extern "C" int sj_sgd(float* w, const float* g, void* w_bf16, size_t n, size_t n
   const size_t cap = static_cast<size_t>(sm_count()) * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
-  sgd_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(w, g, static_cast<__nv_bfloat16*>(w_bf16),
+  launch(sgd_kernel, static_cast<unsigned>(blocks), 256, 0, as_stream(stream), w, g, static_cast<__nv_bfloat16*>(w_bf16),
                                                                           n, n_decay, hyper, weight_decay);
   SJ_LAUNCH_CHECK("sgd");
   return SJ_OK;

@@ -37,8 +37,9 @@ SJ_DEVICE void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
 }
 
 template <typename T, int VEC>
-__global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restrict__ w, __nv_bfloat16* __restrict__ y,
-                                   float* __restrict__ inv_rms, int rows, int d, float eps) {
+__global__ void rmsnorm_fwd_kernel(const T* x, const float* w, __nv_bfloat16* y,
+                                   float* inv_rms, int rows, int d, float eps) {
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -72,9 +73,10 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const float* __restr
 // One CTA = kNormWarps warps over kNormRowsPerCta rows; per-CTA dw partial row in `partials`.
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kNormWarps * 32)
-    rmsnorm_bwd_kernel(const T* __restrict__ x, const float* __restrict__ w,
-                       const float* __restrict__ inv_rms, const float* __restrict__ dz, float* __restrict__ dres,
-                       __nv_bfloat16* __restrict__ dres_bf16, float* __restrict__ partials, int rows, int d) {
+    rmsnorm_bwd_kernel(const T* x, const float* w,
+                       const float* inv_rms, const float* dz, float* dres,
+                       __nv_bfloat16* dres_bf16, float* partials, int rows, int d) {
+  pdl_wait();
   __shared__ float red[kNormWarps][VEC * 256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float dw_acc[VEC][8];
@@ -146,8 +148,9 @@ __global__ void __launch_bounds__(kNormWarps * 32)
 
 // out[col] += sum over groups of partials[g][col]: 32 columns per CTA, the 8 warps split the
 // groups, coalesced 128-byte row reads, one shared-memory reduction.
-__global__ void __launch_bounds__(256) column_reduce_add_kernel(const float* __restrict__ partials, int groups, int d,
-                                                               float* __restrict__ out) {
+__global__ void __launch_bounds__(256) column_reduce_add_kernel(const float* partials, int groups, int d,
+                                                               float* out) {
+  pdl_wait();
   __shared__ float red[8][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
@@ -172,7 +175,7 @@ template <typename T, int VEC>
 static void launch_norm_fwd(const void* x, const float* w, void* y, float* inv, int rows, int d, float eps,
                             cudaStream_t s) {
   const int threads = 256, warps = threads / 32;
-  rmsnorm_fwd_kernel<T, VEC><<<(rows + warps - 1) / warps, threads, 0, s>>>(
+  launch(rmsnorm_fwd_kernel<T, VEC>, (rows + warps - 1) / warps, threads, 0, s, 
       static_cast<const T*>(x), w, static_cast<__nv_bfloat16*>(y), inv, rows, d, eps);
 }
 
@@ -180,7 +183,7 @@ template <typename T, int VEC>
 static void launch_norm_bwd(const void* x, const float* w, const float* inv, const float* dz, float* dres,
                             void* dres_b, float* partials, int rows, int d, cudaStream_t s) {
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
-  rmsnorm_bwd_kernel<T, VEC><<<groups, kNormWarps * 32, 0, s>>>(static_cast<const T*>(x), w, inv, dz, dres,
+  launch(rmsnorm_bwd_kernel<T, VEC>, groups, kNormWarps * 32, 0, s, static_cast<const T*>(x), w, inv, dz, dres,
                                                                  static_cast<__nv_bfloat16*>(dres_b), partials, rows, d);
 }
 
@@ -249,7 +252,7 @@ extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const 
   else
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: x must be bf16 or f32");
   SJ_LAUNCH_CHECK("rmsnorm_bwd");
-  column_reduce_add_kernel<<<(d + 31) / 32, 256, 0, s>>>(partials, groups, d, dw);
+  launch(column_reduce_add_kernel, (d + 31) / 32, 256, 0, s, partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd reduce");
   return SJ_OK;
 }
@@ -328,7 +331,7 @@ extern "C" int sj_rmsnorm_bwd_noalloc(const void* x, int x_dtype, const float* w
   else
     dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
   SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc");
-  column_reduce_add_kernel<<<(d + 31) / 32, 256, 0, s>>>(partials, groups, d, dw);
+  launch(column_reduce_add_kernel, (d + 31) / 32, 256, 0, s, partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc reduce");
   return SJ_OK;
 }

@@ -52,6 +52,7 @@ SJ_DEVICE uint64_t splitmix_index(uint64_t& state, uint64_t size) {
 __global__ void __launch_bounds__(256) param_indices_kernel(unsigned long long* rng_state, int a, int b, int nb,
                                                             int s, int r, int group, int32_t* columns,
                                                             int32_t* rows, int32_t* row_map) {
+  pdl_wait();
   extern __shared__ int32_t scratch[];  // [b + nb] permutation, then [s] chosen blocks
   int32_t* chosen = scratch + b + nb;
   for (int i = threadIdx.x; i < b + nb; i += blockDim.x) scratch[i] = i < b ? i : i - b;
@@ -91,8 +92,9 @@ SJ_DEVICE int member_column(int c, int interleave) {
 }
 
 // wsel[f, j] = w[f, column j] in f32: the r donor columns of the weight, gathered once.
-__global__ void param_wsel_kernel(const __nv_bfloat16* __restrict__ w, int ldw, int interleave,
-                                  const int32_t* __restrict__ columns, int a, int r, float* __restrict__ wsel) {
+__global__ void param_wsel_kernel(const __nv_bfloat16* w, int ldw, int interleave,
+                                  const int32_t* columns, int a, int r, float* wsel) {
+  pdl_wait();
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= a * r) return;
   const int f = idx / r, j = idx % r;
@@ -104,9 +106,10 @@ __global__ void param_wsel_kernel(const __nv_bfloat16* __restrict__ w, int ldw, 
 // then the CTA's 64 x R tile adds its R x R Gram contribution.
 constexpr int kYsRows = 64;
 template <int R>
-__global__ void __launch_bounds__(256) param_ys_gram_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int n,
-                                                            int a, const float* __restrict__ wsel_g, int r,
-                                                            float* __restrict__ ys, double* __restrict__ gram) {
+__global__ void __launch_bounds__(256) param_ys_gram_kernel(const __nv_bfloat16* x, int ldx, int n,
+                                                            int a, const float* wsel_g, int r,
+                                                            float* ys, double* gram) {
+  pdl_wait();
   extern __shared__ __align__(16) float smem[];
   float* wsel = smem;                        // [a][R] (columns >= r zero)
   float* part = smem + a * R;                // [8][kYsRows][R]
@@ -181,8 +184,9 @@ SJ_DEVICE double shfl_d(double v, int src) { return __shfl_sync(0xffffffffu, v, 
 // the Gram matrix and row k of T; lane i also keeps column i of T.  For the current column, u
 // starts as e_c; each pass takes all projections coef_i = q_i . v = t_i^T (G u) from the same v and
 // then subtracts them (classical Gram-Schmidt), twice; |v|^2 = u^T G u.  t[k * r + c] on output.
-__global__ void __launch_bounds__(32) param_cgs2_kernel(const double* __restrict__ gram, int r, float eps,
-                                                        double* __restrict__ t) {
+__global__ void __launch_bounds__(32) param_cgs2_kernel(const double* gram, int r, float eps,
+                                                        double* t) {
+  pdl_wait();
   const int lane = threadIdx.x;
   double grow[kMaxRank], trow[kMaxRank], tcol[kMaxRank];
 #pragma unroll
@@ -238,9 +242,10 @@ __global__ void __launch_bounds__(32) param_cgs2_kernel(const double* __restrict
 
 // q = ys T (T upper triangular), thread per row.
 template <int R>
-__global__ void __launch_bounds__(256) param_apply_t_kernel(const float* __restrict__ ys,
-                                                            const double* __restrict__ t, int n, int r,
-                                                            float* __restrict__ q) {
+__global__ void __launch_bounds__(256) param_apply_t_kernel(const float* ys,
+                                                            const double* t, int n, int r,
+                                                            float* q) {
+  pdl_wait();
   __shared__ float ts[R * R];
   for (int i = threadIdx.x; i < R * R; i += blockDim.x) {
     const int k = i / R, j = i % R;
@@ -270,9 +275,10 @@ __global__ void __launch_bounds__(256) param_apply_t_kernel(const float* __restr
 template <int R>
 constexpr int left_tokens() { return R <= 16 ? 256 : 128; }  // keeps q + partial sums within 48 KB
 template <int R>
-__global__ void __launch_bounds__(256) param_left_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int n, int a,
-                                                         const float* __restrict__ q, int r,
-                                                         float* __restrict__ left) {
+__global__ void __launch_bounds__(256) param_left_kernel(const __nv_bfloat16* x, int ldx, int n, int a,
+                                                         const float* q, int r,
+                                                         float* left) {
+  pdl_wait();
   constexpr int kTokens = left_tokens<R>();
   __shared__ __align__(16) float qs[kTokens * R];
   __shared__ float red[8][32][R];
@@ -339,11 +345,12 @@ __global__ void __launch_bounds__(256) param_left_kernel(const __nv_bfloat16* __
 // (x[:, rows[pos]] - q left[rows[pos]]^T) * inverse (zero where rows[pos] < 0); the last y-slice
 // writes rows [0, r) = q^T.  Thread per token; the slice's left rows sit in shared memory.
 template <int R>
-__global__ void __launch_bounds__(128) param_e_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int n,
-                                                      const float* __restrict__ q, int r,
-                                                      const float* __restrict__ left,
-                                                      const int32_t* __restrict__ rows, int k, float inverse,
-                                                      __nv_bfloat16* __restrict__ e) {
+__global__ void __launch_bounds__(128) param_e_kernel(const __nv_bfloat16* x, int ldx, int n,
+                                                      const float* q, int r,
+                                                      const float* left,
+                                                      const int32_t* rows, int k, float inverse,
+                                                      __nv_bfloat16* e) {
+  pdl_wait();
   __shared__ __align__(16) float ls[32][R];
   __shared__ int rs[32];
   __shared__ int contiguous;
@@ -425,11 +432,12 @@ __global__ void __launch_bounds__(128) param_e_kernel(const __nv_bfloat16* __res
 // 128 columns: each thread keeps its column's r coefficients in registers and walks the rows.
 constexpr int kMatRows = 8;
 template <int R>
-__global__ void __launch_bounds__(128) param_materialize_kernel(const float* __restrict__ left,
-                                                                const float* __restrict__ coeff, int ldc,
-                                                                const int32_t* __restrict__ row_map, int a, int b,
-                                                                int r, float* __restrict__ g, int ldg,
+__global__ void __launch_bounds__(128) param_materialize_kernel(const float* left,
+                                                                const float* coeff, int ldc,
+                                                                const int32_t* row_map, int a, int b,
+                                                                int r, float* g, int ldg,
                                                                 int accumulate) {
+  pdl_wait();
   __shared__ float ls[kMatRows][R];
   __shared__ int ms[kMatRows];
   const int i0 = blockIdx.y * kMatRows;
@@ -504,7 +512,7 @@ extern "C" int sj_param_indices(uint64_t* rng_state, int a, int b, int nb, int s
     return fail(SJ_ERR_ARGUMENT, "sj_param_indices: null output");
   const size_t smem = (static_cast<size_t>(b) + nb + s) * sizeof(int32_t);
   if (smem > 48 * 1024) return fail(SJ_ERR_SHAPE, "sj_param_indices: b + nb + s = %zu above 12288", smem / 4);
-  param_indices_kernel<<<1, 256, smem, as_stream(stream)>>>(reinterpret_cast<unsigned long long*>(rng_state), a, b,
+  launch(param_indices_kernel, 1, 256, smem, as_stream(stream), reinterpret_cast<unsigned long long*>(rng_state), a, b,
                                                             nb, s, r, group, columns, rows, row_map);
   SJ_LAUNCH_CHECK("param_indices");
   return SJ_OK;
@@ -544,15 +552,15 @@ int launch_basis(const __nv_bfloat16* x, int ldx, int n, int a, const __nv_bfloa
   }
   const size_t smem = (static_cast<size_t>(a) * R + 8 * kYsRows * R) * sizeof(float);
   if (smem > 200 * 1024) return fail(SJ_ERR_SHAPE, "sj_param_basis: a = %d too wide for rank %d", a, r);
-  cudaError_t e = cudaMemsetAsync(ws.gram, 0, sizeof(double) * r * r, s);
-  if (e != cudaSuccess) return cuda_check(e, "param_basis memset");
-  param_wsel_kernel<<<(a * r + 255) / 256, 256, 0, s>>>(w, ldw, interleave, columns, a, r, ws.wsel);
+  const int zs = zero_async(ws.gram, sizeof(double) * r * r, s);
+  if (zs != SJ_OK) return zs;
+  launch(param_wsel_kernel, (a * r + 255) / 256, 256, 0, s, w, ldw, interleave, columns, a, r, ws.wsel);
   SJ_LAUNCH_CHECK("param_wsel");
-  param_ys_gram_kernel<R><<<(n + kYsRows - 1) / kYsRows, 256, smem, s>>>(x, ldx, n, a, ws.wsel, r, ws.ys, ws.gram);
+  launch(param_ys_gram_kernel<R>, (n + kYsRows - 1) / kYsRows, 256, smem, s, x, ldx, n, a, ws.wsel, r, ws.ys, ws.gram);
   SJ_LAUNCH_CHECK("param_ys_gram");
-  param_cgs2_kernel<<<1, 32, 0, s>>>(ws.gram, r, eps, ws.t);
+  launch(param_cgs2_kernel, 1, 32, 0, s, ws.gram, r, eps, ws.t);
   SJ_LAUNCH_CHECK("param_cgs2");
-  param_apply_t_kernel<R><<<(n + 255) / 256, 256, 0, s>>>(ws.ys, ws.t, n, r, q);
+  launch(param_apply_t_kernel<R>, (n + 255) / 256, 256, 0, s, ws.ys, ws.t, n, r, q);
   SJ_LAUNCH_CHECK("param_apply_t");
   return SJ_OK;
 }
@@ -583,13 +591,13 @@ namespace {
 template <int R>
 int launch_prepare(const __nv_bfloat16* x, int ldx, int n, int a, const float* q, int r, const int32_t* rows, int k,
                    float inverse, float* left, __nv_bfloat16* e, cudaStream_t s) {
-  cudaError_t err = cudaMemsetAsync(left, 0, sizeof(float) * a * r, s);
-  if (err != cudaSuccess) return cuda_check(err, "param_prepare memset");
+  const int zs = zero_async(left, sizeof(float) * a * r, s);
+  if (zs != SJ_OK) return zs;
   const dim3 grid_left((n + left_tokens<R>() - 1) / left_tokens<R>(), (a + 63) / 64);
-  param_left_kernel<R><<<grid_left, 256, 0, s>>>(x, ldx, n, a, q, r, left);
+  launch(param_left_kernel<R>, grid_left, 256, 0, s, x, ldx, n, a, q, r, left);
   SJ_LAUNCH_CHECK("param_left");
   const dim3 grid_e((n + 127) / 128, (k + 31) / 32 + 1);
-  param_e_kernel<R><<<grid_e, 128, 0, s>>>(x, ldx, n, q, r, left, rows, k, inverse, e);
+  launch(param_e_kernel<R>, grid_e, 128, 0, s, x, ldx, n, q, r, left, rows, k, inverse, e);
   SJ_LAUNCH_CHECK("param_e");
   return SJ_OK;
 }
@@ -598,7 +606,7 @@ template <int R>
 int launch_materialize(const float* left, const float* coeff, int ldc, const int32_t* row_map, int a, int b, int r,
                        float* g, int ldg, int accumulate, cudaStream_t s) {
   const dim3 grid((b + 127) / 128, (a + kMatRows - 1) / kMatRows);
-  param_materialize_kernel<R><<<grid, 128, 0, s>>>(left, coeff, ldc, row_map, a, b, r, g, ldg, accumulate);
+  launch(param_materialize_kernel<R>, grid, 128, 0, s, left, coeff, ldc, row_map, a, b, r, g, ldg, accumulate);
   SJ_LAUNCH_CHECK("param_materialize");
   return SJ_OK;
 }

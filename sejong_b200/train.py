@@ -176,15 +176,13 @@ class ByteTrainer:
         if train.parameter_vjp is not None:
             self._init_vjp(train.parameter_vjp)
 
-    # kernels each entry point launches (sj_zero is a memset, not a kernel)
-    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 3,
-               "sj_zero": 0, "sj_param_basis": 4, "sj_param_prepare": 2}
+    # kernels each entry point launches (zero fills are kernels too)
+    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 4,
+               "sj_zero": 1, "sj_param_basis": 5, "sj_param_prepare": 3}
 
     @classmethod
     def kernels_of(cls, name, args):
-        """Kernel launches one C-ABI call makes (the GQA backward adds a group reduction)."""
-        if name == "sj_attn_gqa_bwd":
-            return 3 + (1 if args[20] != args[21] else 0)
+        """Kernel launches one C-ABI call makes."""
         return cls.KERNELS.get(name, 1)
 
     def _call(self, name, *args):

@@ -139,3 +139,41 @@ def test_flat_layout_round_trip():
         assert (e.offset < lay.n_decay) == e.decay
         assert e.offset % pm.ALIGN == 0
     assert lay.total >= pm.parameter_count(c)
+
+
+def _kernel_bodies():
+    """(file, kernel name, body) of every __global__ definition under sejong_b200/csrc."""
+    csrc = os.path.join(ROOT, "sejong_b200", "csrc")
+    out = []
+    for name in sorted(os.listdir(csrc)):
+        if not name.endswith(".cu"):
+            continue
+        text = open(os.path.join(csrc, name)).read()
+        for m in re.finditer(r"__global__", text):
+            brace, semi = text.index("{", m.start()), text.find(";", m.start())
+            if semi != -1 and semi < brace:
+                continue  # a declaration
+            depth, i = 1, brace + 1
+            while depth:
+                depth += {"{": 1, "}": -1}.get(text[i], 0)
+                i += 1
+            header = " ".join(text[m.start():brace].split())
+            out.append((name, header[:80], text[brace:i]))
+    return out
+
+
+def test_kernels_order_themselves_after_their_predecessor():
+    """Every kernel is launched with programmatic stream serialization, so each must execute
+    griddepcontrol.wait (pdl_wait) before touching global memory; pointer parameters carry no
+    __restrict__ (read-only loads could be scheduled before the wait), and the library issues no
+    memset nodes between its kernels."""
+    bodies = _kernel_bodies()
+    assert len(bodies) > 30
+    for name, header, body in bodies:
+        assert "pdl_wait();" in body, f"{name}: {header} does not call pdl_wait()"
+    csrc = os.path.join(ROOT, "sejong_b200", "csrc")
+    for name in os.listdir(csrc):
+        code = re.sub(r"//.*", "", open(os.path.join(csrc, name)).read())
+        assert "__restrict__" not in code, f"{name} uses __restrict__"
+        assert "<<<" not in code, f"{name} launches without sj::launch"
+        assert "cudaMemsetAsync" not in code, f"{name} issues a memset node"
