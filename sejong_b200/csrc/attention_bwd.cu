@@ -8,7 +8,7 @@
 //
 // Persistent: one CTA per SM walks work items (batch, kv head, 128-key tile).  An item visits every
 // query head of its group and every query tile its keys are visible to, so dK and dV of the kv head
-// accumulate in TMEM across the whole group and are written once (no partials).  14 warps:
+// accumulate in TMEM across the whole group and are written once (no partials).  10 warps:
 //   warp 0      TMA: the item's K and V tiles (double-buffered by item), and per step the Q and dO
 //               tiles and the step's 128 LSE and Delta values (2-deep ring; the delta kernel lays
 //               both out per head, contiguous over the sequence).
@@ -16,13 +16,16 @@
 //                 S^T_g = K Q_g^T and dP^T_g = V dO_g^T (M128 N128 K64) into TMEM,
 //                 then, once P^T_g and dS^T_g are in shared memory,
 //                 dV += P^T_g dO_g, dK += dS^T_g Q_g (M128 N64 K128, accumulated in TMEM) and
-//                 dQ_g = dS_g K (the dS^T buffer read as an MN-major operand).
+//                 dQ_g = dS_g K (the dS^T buffer read as an MN-major operand) into one of two TMEM
+//                 buffers.
 //               S^T_{g+1} / dP^T_{g+1} are issued before waiting for P^T_g, so the two overlap.
 //   warps 2-9   elementwise: thread <-> key row (TMEM lane), two threads per row, 64 query columns
-//               each: P^T and dS^T in bf16 into K-major 128-byte-swizzled shared memory.
-//   warps 10-13 dQ: thread <-> query row, adds dQ_g into an f32 accumulator [rows, hq*64] with
-//               vector reductions (attn_dq_finish_kernel applies the inverse RoPE and writes bf16);
-//               at the end of an item, dK (inverse RoPE) and dV out of TMEM to global bf16.
+//               each: P^T and dS^T computed from TMEM while the previous step's MMAs still read the
+//               shared-memory buffers, then stored in bf16 into K-major 128-byte-swizzled shared
+//               memory; after handing them over, the previous step's dQ goes into an f32
+//               accumulator [rows, hq*64] with vector reductions (attn_dq_finish_kernel applies the
+//               inverse RoPE and writes bf16) and, at the end of an item, dK (inverse RoPE) and dV
+//               go out of TMEM to global bf16.
 // Every wait is bounded (SJ_DEV_ATTN_WAIT in the device error word).
 #include <algorithm>
 
@@ -36,8 +39,7 @@ namespace {
 constexpr int kBT = 128;                          // keys per item, queries per step
 constexpr int kBD = 64;                           // head dim
 constexpr int kEwWarps = 8;
-constexpr int kDqWarps = 4;
-constexpr int kBwdThreads = 32 * (2 + kEwWarps + kDqWarps);
+constexpr int kBwdThreads = 32 * (2 + kEwWarps);
 constexpr int kTile = kBT * kBD * 2;              // 16 KB: 128 rows x 128 B
 // shared memory: K0 K1 | V0 V1 | Q0 Q1 | dO0 dO1 | P^T | dS^T | LSE/Delta ring | barriers
 constexpr int kOffKb = 0;
@@ -50,7 +52,7 @@ constexpr int kOffLd = kOffDSt + 2 * kTile;       // [2 slots][LSE*log2e 128 | D
 constexpr int kOffBarB = kOffLd + 2 * 2 * kBT * 4;
 constexpr int kSmemBwd = kOffBarB + 512 + 1024;
 constexpr uint32_t kTmemColsB = 512;
-constexpr uint32_t kColSt = 0, kColDPt = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
+constexpr uint32_t kColSt = 0, kColDPt = 128, kColDV = 256, kColDK = 320, kColDQ = 384;  // dQ: 2 x 64
 constexpr float kLog2eB = 1.4426950408889634f;
 
 struct BwdParams {
@@ -130,12 +132,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* sp_empty = bars + 9;     // 1: elementwise warps have them in registers
   uint64_t* ps_full = bars + 10;     // 1: P^T, dS^T in shared memory
   uint64_t* ps_empty = bars + 11;    // 1: their MMAs are done
-  uint64_t* dq_full = bars + 12;     // 1
-  uint64_t* dq_empty = bars + 13;    // 1
-  uint64_t* acc_full = bars + 14;    // 1: an item's dK / dV complete in TMEM
-  uint64_t* acc_empty = bars + 15;   // 1: read out
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* dq_empty = bars + 12;    // 2: dQ_g (TMEM buffer g & 1) read out
+  uint64_t* acc_empty = bars + 14;   // 1: an item's dK / dV read out
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* ldbuf = reinterpret_cast<float*>(smem + kOffLd);
 
@@ -153,10 +153,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(sp_empty, kEwWarps);
     mbar_init(ps_full, kEwWarps);
     mbar_init(ps_empty, 1);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_empty, kDqWarps);
-    mbar_init(acc_full, 1);
-    mbar_init(acc_empty, kDqWarps);  // the dQ warps read dK / dV out
+    for (int i = 0; i < 2; ++i) mbar_init(&dq_empty[i], kEwWarps);
+    mbar_init(acc_empty, kEwWarps);  // the elementwise warps read dK / dV out
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -233,7 +231,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int i = pend_i;
         const int st = i & 1;
         if (!mbar_wait(ps_full, i & 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
-        if (!mbar_wait(dq_empty, (i & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        const int qb = i & 1;  // dQ buffer
+        if (!mbar_wait(&dq_empty[qb], ((i >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
         if (pend_first && !mbar_wait(acc_empty, (pend_n & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
         tc_fence_after();
         const uint32_t pt = smem_u32(smem + kOffPt), dst = smem_u32(smem + kOffDSt);
@@ -246,16 +245,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           umma_f16(tmem + kColDV, umma_desc(pt + kmaj, 16, 1024), umma_desc(da + kk * 2048, 8192, 1024), kIdAcc, acc);
           umma_f16(tmem + kColDK, umma_desc(dst + kmaj, 16, 1024), umma_desc(qa + kk * 2048, 8192, 1024), kIdAcc,
                    acc);
-          umma_f16(tmem + kColDQ, umma_desc(dst + kk * 2048, kTile, 1024), umma_desc(ka + kk * 2048, 8192, 1024),
-                   kIdDq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + kColDQ + qb * kBD, umma_desc(dst + kk * 2048, kTile, 1024),
+                   umma_desc(ka + kk * 2048, 8192, 1024), kIdDq, kk > 0 ? 1u : 0u);
         }
-        umma_commit(ps_empty);
-        umma_commit(dq_full);
+        umma_commit(ps_empty);  // also: dQ_i, and at an item's last step dK / dV, complete in TMEM
         umma_commit(&qd_empty[st]);
-        if (pend_last) {
-          umma_commit(acc_full);
-          umma_commit(&kv_empty[pend_ks]);
-        }
+        if (pend_last) umma_commit(&kv_empty[pend_ks]);
         pend_i = -1;
         return true;
       };
@@ -298,12 +293,72 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       umma_commit(drain);
       mbar_wait(drain, 0, nullptr, SJ_DEV_ATTN_WAIT);
     }
-  } else if (warp < 2 + kEwWarps) {
+  } else {
     // ---------------------------------------------------------------- elementwise warps
+    // thread <-> TMEM lane r: a key row for P^T / dS^T and dK / dV, a query row for dQ; half
+    // selects 64 of the 128 query columns (P^T, dS^T) or 32 of the 64 head columns (dQ, dK, dV)
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int r = quarter * 32 + lane;  // key row of the tile
+    const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    // step whose dQ (and, at an item's end, dK / dV) is still to be read out of TMEM
+    int pend_g = -1, pend_h = 0, pend_qpos = 0, pend_last = 0;
+    BItem pend_it{};
+    // dQ_g: f32 vector reductions into the accumulator (attn_dq_finish_kernel writes bf16); at the
+    // item's last step also its dK (inverse RoPE) and dV rows, then the TMEM is released
+    auto read_out = [&]() {
+      const int qb = pend_g & 1;
+      {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + kColDQ + qb * kBD + half * 32, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_empty[qb]);
+        if (pend_qpos < p.t) {
+          float* dst = p.dq_acc + (static_cast<size_t>(pend_it.b) * p.t + pend_qpos) * (static_cast<size_t>(p.hq) * kBD) +
+                       pend_h * kBD + half * 32;
+#pragma unroll
+          for (int c = 0; c < 32; c += 4)
+            red_add_v4(dst + c, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
+                       __uint_as_float(v[c + 3]));
+        }
+      }
+      if (!pend_last) return;
+      const int kpos = pend_it.k0 + r;
+      const size_t row = static_cast<size_t>(pend_it.b) * p.t + min(kpos, p.t - 1);
+      const int c0 = half * 32;
+      uint32_t vk[32], vv[32];
+      tmem_ld_32x32b_x32(tmem + lane_off + kColDK + c0, vk);
+      tmem_ld_32x32b_x32(tmem + lane_off + kColDV + c0, vv);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
+      if (kpos < p.t) {
+        const bool rope = p.rope_tab != nullptr || p.rope_log_theta > 0.f;
+        uint32_t w[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float a = __uint_as_float(vk[c]), b = __uint_as_float(vk[c + 1]);
+          if (rope) {
+            const float2 cs = rope_cs(p.rope_tab, p.rope_log_theta, kpos, (c0 + c) >> 1);
+            const float na = a * cs.x + b * cs.y, nb = -a * cs.y + b * cs.x;  // inverse rotation
+            a = na;
+            b = nb;
+          }
+          w[c >> 1] = pack_bf16x2(a, b);
+        }
+        uint4* out = reinterpret_cast<uint4*>(p.dk + row * p.lddk + pend_it.kvh * kBD + c0);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) out[c4] = make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) w[c >> 1] = pack_bf16x2(__uint_as_float(vv[c]), __uint_as_float(vv[c + 1]));
+        out = reinterpret_cast<uint4*>(p.dv + row * p.lddv + pend_it.kvh * kBD + c0);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) out[c4] = make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]);
+      }
+    };
     int n = 0, g = 0;
     bool alive = true;
     for (int item = blockIdx.x; item < p.items && alive; item += gridDim.x, ++n) {
@@ -332,125 +387,65 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           hi = min(p.window > 0 ? kpos + p.window - 1 : p.t - 1, p.t - 1) - cbase;
           if (kpos >= p.t) hi = -1;
         }
-        // P^T and dS^T may overwrite the buffers once the previous step's MMAs have read them
-        if (!mbar_wait(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
-          alive = false;
-          break;
-        }
-        uint8_t* pt = smem + kOffPt + half * kTile;
-        uint8_t* dst = smem + kOffDSt + half * kTile;
-        // this thread's 64 query columns of S^T and dP^T, in two chunks of 32
+        // this thread's 64 query columns of S^T and dP^T, in four chunks of 16: P^T and dS^T are
+        // computed and packed to bf16 while the previous step's MMAs may still read the buffers
+        uint32_t pw[32], dw[32];
 #pragma unroll
-        for (int chunk = 0; chunk < 2; ++chunk) {
-          uint32_t sv[32], dv[32];
-          tmem_ld_32x32b_x32(tmem + lane_off + kColSt + half * 64 + chunk * 32, sv);
-          tmem_ld_32x32b_x32(tmem + lane_off + kColDPt + half * 64 + chunk * 32, dv);
+        for (int chunk = 0; chunk < 4; ++chunk) {
+          uint32_t sv[16], dv[16];
+          tmem_ld_32x32b_x16(tmem + lane_off + kColSt + half * 64 + chunk * 16, sv);
+          tmem_ld_32x32b_x16(tmem + lane_off + kColDPt + half * 64 + chunk * 16, dv);
           tmem_wait_ld();
-          if (chunk == 1) {  // S^T / dP^T are in registers: the next step's products may start
+          if (chunk == 3) {  // S^T / dP^T are in registers: the next step's products may start
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(sp_empty);
           }
-          float pv[32], d[32];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int cc = chunk * 32 + c;
-            const bool valid = cc >= lo && cc <= hi;  // (LSE / Delta past the sequence end are not data)
-            const float pr = valid ? ex2b(fmaf(__uint_as_float(sv[c]), p.scale_log2, -lsl[cc])) : 0.f;
-            pv[c] = pr;                                                              // P^T
-            d[c] = valid ? pr * (__uint_as_float(dv[c]) - dls[cc]) * p.scale : 0.f;  // dS^T
-          }
+          for (int c = 0; c < 16; c += 2) {
+            float pr[2], ds[2];
 #pragma unroll
-          for (int q8 = 0; q8 < 4; ++q8) {
-            const int c8 = chunk * 4 + q8;
-            const int off = r * 128 + ((c8 ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4*>(pt + off) =
-                make_uint4(pack_bf16x2(pv[8 * q8], pv[8 * q8 + 1]), pack_bf16x2(pv[8 * q8 + 2], pv[8 * q8 + 3]),
-                           pack_bf16x2(pv[8 * q8 + 4], pv[8 * q8 + 5]), pack_bf16x2(pv[8 * q8 + 6], pv[8 * q8 + 7]));
-            *reinterpret_cast<uint4*>(dst + off) =
-                make_uint4(pack_bf16x2(d[8 * q8], d[8 * q8 + 1]), pack_bf16x2(d[8 * q8 + 2], d[8 * q8 + 3]),
-                           pack_bf16x2(d[8 * q8 + 4], d[8 * q8 + 5]), pack_bf16x2(d[8 * q8 + 6], d[8 * q8 + 7]));
+            for (int e = 0; e < 2; ++e) {
+              const int cc = chunk * 16 + c + e;
+              const bool valid = cc >= lo && cc <= hi;  // (LSE / Delta past the sequence end are not data)
+              pr[e] = valid ? ex2b(fmaf(__uint_as_float(sv[c + e]), p.scale_log2, -lsl[cc])) : 0.f;   // P^T
+              ds[e] = valid ? pr[e] * (__uint_as_float(dv[c + e]) - dls[cc]) * p.scale : 0.f;        // dS^T
+            }
+            pw[chunk * 8 + (c >> 1)] = pack_bf16x2(pr[0], pr[1]);
+            dw[chunk * 8 + (c >> 1)] = pack_bf16x2(ds[0], ds[1]);
           }
+        }
+        // P^T and dS^T may overwrite the buffers once the previous step's MMAs have read them
+        // (which also completes that step's dQ and, at an item's end, its dK / dV)
+        if (!mbar_wait(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+          alive = false;
+          break;
+        }
+        tc_fence_after();
+        uint8_t* pt = smem + kOffPt + half * kTile;
+        uint8_t* dst = smem + kOffDSt + half * kTile;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const int off = r * 128 + ((c8 ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pw[4 * c8], pw[4 * c8 + 1], pw[4 * c8 + 2], pw[4 * c8 + 3]);
+          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dw[4 * c8], dw[4 * c8 + 1], dw[4 * c8 + 2], dw[4 * c8 + 3]);
         }
         fence_proxy_async_shared();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(ps_full);
+        if (pend_g >= 0) read_out();
+        pend_g = g;
+        pend_it = it;
+        pend_h = it.kvh * group + s / it.nq;
+        pend_qpos = q0 + r;
+        pend_last = s == steps - 1;
       }
     }
-  } else {
-    // ---------------------------------------------------------------- dQ warps
-    // thread <-> row of the tile: a query row for dQ_g, a key row for the item's dK / dV
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    int n = 0, g = 0;
-    bool alive = true;
-    for (int item = blockIdx.x; item < p.items && alive; item += gridDim.x, ++n) {
-      const BItem it = decode_bitem(p, item);
-      const int steps = group * it.nq;
-      for (int s = 0; s < steps; ++s, ++g) {
-        const int h = it.kvh * group + s / it.nq;
-        const int qpos = (it.qt_lo + s % it.nq) * kBT + r;
-        if (!mbar_wait(dq_full, g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        float* dst = p.dq_acc + (static_cast<size_t>(it.b) * p.t + min(qpos, p.t - 1)) * (static_cast<size_t>(p.hq) * kBD) +
-                     h * kBD;
-#pragma unroll
-        for (int hc = 0; hc < 2; ++hc) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem + lane_off + kColDQ + hc * 32, v);
-          tmem_wait_ld();
-          if (qpos < p.t) {
-#pragma unroll
-            for (int c = 0; c < 32; c += 4)
-              red_add_v4(dst + hc * 32 + c, __uint_as_float(v[c]), __uint_as_float(v[c + 1]),
-                         __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3]));
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dq_empty);
-      }
-      if (!alive) break;
-      // the item's dK (inverse RoPE) and dV rows, off the elementwise warps' path
-      if (!mbar_wait(acc_full, n & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
+    // the last step's products
+    if (alive && pend_g >= 0 && mbar_wait(ps_empty, pend_g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
       tc_fence_after();
-      const int kpos = it.k0 + r;
-      const size_t row = static_cast<size_t>(it.b) * p.t + min(kpos, p.t - 1);
-#pragma unroll
-      for (int part = 0; part < 4; ++part) {  // dK cols 0-31, 32-63, then dV cols 0-31, 32-63
-        const bool is_k = part < 2;
-        const int c0 = (part & 1) * 32;
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + (is_k ? kColDK : kColDV) + c0, v);
-        tmem_wait_ld();
-        if (part == 3) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(acc_empty);
-        }
-        if (kpos < p.t) {
-          uint32_t w[16];
-#pragma unroll
-          for (int c = 0; c < 32; c += 2) {
-            float a = __uint_as_float(v[c]), b = __uint_as_float(v[c + 1]);
-            if (is_k && (p.rope_tab != nullptr || p.rope_log_theta > 0.f)) {
-              const float2 cs = rope_cs(p.rope_tab, p.rope_log_theta, kpos, (c0 + c) >> 1);
-              const float na = a * cs.x + b * cs.y, nb = -a * cs.y + b * cs.x;  // inverse rotation
-              a = na;
-              b = nb;
-            }
-            w[c >> 1] = pack_bf16x2(a, b);
-          }
-          uint4* out = reinterpret_cast<uint4*>((is_k ? p.dk + row * p.lddk : p.dv + row * p.lddv) + it.kvh * kBD + c0);
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) out[c4] = make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]);
-        }
-      }
+      read_out();
     }
   }
 
