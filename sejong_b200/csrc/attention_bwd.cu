@@ -41,16 +41,22 @@ constexpr int kBD = 64;                           // head dim
 constexpr int kEwWarps = 8;
 constexpr int kBwdThreads = 32 * (2 + kEwWarps);
 constexpr int kTile = kBT * kBD * 2;              // 16 KB: 128 rows x 128 B
-// shared memory: K0 K1 | V0 V1 | Q0 Q1 | dO0 dO1 | P^T | dS^T | LSE/Delta ring | barriers
+// shared memory: K | V | Q ring | dO ring | P^T | dS^T | LSE/Delta ring | barriers
+// K, V tiles per item: two, because the MMA thread issues an item's last dV / dK / dQ after the
+// next item's first S^T / dP^T, which need that item's K and V already loaded.
+constexpr int kKvStages = 2;
+constexpr int kQdStages = 2;                     // Q, dO tiles (and LSE, Delta) per step
 constexpr int kOffKb = 0;
-constexpr int kOffVb = kOffKb + 2 * kTile;
-constexpr int kOffQb = kOffVb + 2 * kTile;
-constexpr int kOffDOb = kOffQb + 2 * kTile;
-constexpr int kOffPt = kOffDOb + 2 * kTile;       // 32 KB: two 64-query halves
-constexpr int kOffDSt = kOffPt + 2 * kTile;       // 32 KB
-constexpr int kOffLd = kOffDSt + 2 * kTile;       // [2 slots][LSE*log2e 128 | Delta 128] f32
-constexpr int kOffBarB = kOffLd + 2 * 2 * kBT * 4;
+constexpr int kOffVb = kOffKb + kKvStages * kTile;
+constexpr int kOffQb = kOffVb + kKvStages * kTile;
+constexpr int kOffDOb = kOffQb + kQdStages * kTile;
+constexpr int kOffPt = kOffDOb + kQdStages * kTile;  // 32 KB: two 64-query halves
+constexpr int kOffDSt = kOffPt + 2 * kTile;          // 32 KB
+constexpr int kOffLd = kOffDSt + 2 * kTile;          // [kQdStages][LSE*log2e 128 | Delta 128] f32
+constexpr int kOffBarB = kOffLd + kQdStages * 2 * kBT * 4;
 constexpr int kSmemBwd = kOffBarB + 512 + 1024;
+static_assert(kSmemBwd <= 232448, "attention backward shared memory above the 227 KB per-CTA limit");
+static_assert(kKvStages == 2 && kQdStages <= 4, "K/V double buffer; barrier slots");
 constexpr uint32_t kTmemColsB = 512;
 constexpr uint32_t kColSt = 0, kColDPt = 128, kColDV = 256, kColDK = 320, kColDQ = 384;  // dQ: 2 x 64
 constexpr float kLog2eB = 1.4426950408889634f;
@@ -124,18 +130,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBarB);
-  uint64_t* kv_full = bars;          // 2
-  uint64_t* kv_empty = bars + 2;     // 2
-  uint64_t* qd_full = bars + 4;      // 2
-  uint64_t* qd_empty = bars + 6;     // 2
-  uint64_t* sp_full = bars + 8;      // 1: S^T, dP^T in TMEM
-  uint64_t* sp_empty = bars + 9;     // 1: elementwise warps have them in registers
-  uint64_t* ps_full = bars + 10;     // 1: P^T, dS^T in shared memory
-  uint64_t* ps_empty = bars + 11;    // 1: their MMAs are done
-  uint64_t* dq_empty = bars + 12;    // 2: dQ_g (TMEM buffer g & 1) read out
-  uint64_t* acc_empty = bars + 14;   // 1: an item's dK / dV read out
-  uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* kv_full = bars;          // kKvStages (<= 2)
+  uint64_t* kv_empty = bars + 2;     // kKvStages
+  uint64_t* qd_full = bars + 4;      // kQdStages (<= 4)
+  uint64_t* qd_empty = bars + 8;     // kQdStages
+  uint64_t* sp_full = bars + 12;     // 1: S^T, dP^T in TMEM
+  uint64_t* sp_empty = bars + 13;    // 1: elementwise warps have them in registers
+  uint64_t* ps_full = bars + 14;     // 1: P^T, dS^T in shared memory
+  uint64_t* ps_empty = bars + 15;    // 1: their MMAs are done
+  uint64_t* dq_empty = bars + 16;    // 2: dQ_g (TMEM buffer g & 1) read out
+  uint64_t* acc_empty = bars + 18;   // 1: an item's dK / dV read out
+  uint64_t* drain = bars + 19;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* ldbuf = reinterpret_cast<float*>(smem + kOffLd);
 
@@ -143,9 +149,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int group = p.hq / p.hk;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKvStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < kQdStages; ++i) {
       mbar_init(&qd_full[i], 1);
       mbar_init(&qd_empty[i], 1);
     }
@@ -180,9 +188,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++n) {
       const BItem it = decode_bitem(p, item);
       const int row_base = it.b * p.t;
-      const int ks = n & 1;
+      const int ks = n % kKvStages;
       if (lane == 0) {
-        ok = mbar_wait(&kv_empty[ks], ((n >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
+        ok = mbar_wait_sleep(&kv_empty[ks], ((n / kKvStages) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
         if (ok) {
           mbar_arrive_expect_tx(&kv_full[ks], 2 * kTile);
           tma_load_2d(smem + kOffKb + ks * kTile, &map_k, &kv_full[ks], it.kvh * kBD, row_base + it.k0);
@@ -193,9 +201,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int hh = 0; hh < group && ok; ++hh) {
         const int h = it.kvh * group + hh;
         for (int j = 0; j < it.nq && ok; ++j, ++g) {
-          const int st = g & 1;
+          const int st = g % kQdStages;
           const int q0 = (it.qt_lo + j) * kBT;
-          if (lane == 0) ok = mbar_wait(&qd_empty[st], ((g >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
+          if (lane == 0) ok = mbar_wait_sleep(&qd_empty[st], ((g / kQdStages) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) {
             ++g;
@@ -215,8 +223,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     if (lane == 0) {
-      for (int i = max(0, n - 2); i < n; ++i) mbar_wait(&kv_full[i & 1], (i >> 1) & 1, nullptr, SJ_DEV_ATTN_WAIT);
-      for (int i = max(0, g - 2); i < g; ++i) mbar_wait(&qd_full[i & 1], (i >> 1) & 1, nullptr, SJ_DEV_ATTN_WAIT);
+      for (int i = max(0, n - kKvStages); i < n; ++i)
+        mbar_wait_sleep(&kv_full[i % kKvStages], (i / kKvStages) & 1, nullptr, SJ_DEV_ATTN_WAIT);
+      for (int i = max(0, g - kQdStages); i < g; ++i)
+        mbar_wait_sleep(&qd_full[i % kQdStages], (i / kQdStages) & 1, nullptr, SJ_DEV_ATTN_WAIT);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (one thread)
@@ -229,24 +239,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       bool ok = true;
       auto issue_acc = [&]() -> bool {
         const int i = pend_i;
-        const int st = i & 1;
-        if (!mbar_wait(ps_full, i & 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        const int st = i % kQdStages;
+        if (!mbar_wait_sleep(ps_full, i & 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
         const int qb = i & 1;  // dQ buffer
-        if (!mbar_wait(&dq_empty[qb], ((i >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
-        if (pend_first && !mbar_wait(acc_empty, (pend_n & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        if (!mbar_wait_sleep(&dq_empty[qb], ((i >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        if (pend_first && !mbar_wait_sleep(acc_empty, (pend_n & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
         tc_fence_after();
-        const uint32_t pt = smem_u32(smem + kOffPt), dst = smem_u32(smem + kOffDSt);
-        const uint32_t qa = smem_u32(smem + kOffQb + st * kTile), da = smem_u32(smem + kOffDOb + st * kTile);
-        const uint32_t ka = smem_u32(smem + kOffKb + pend_ks * kTile);
+        // descriptors of the k = 0 slices; a k step adds its byte offset / 16 to the start-address
+        // field (all of shared memory is below 256 KB, so the 14-bit field does not carry)
+        const uint64_t d_pt = umma_desc(smem_u32(smem + kOffPt), 16, 1024);
+        const uint64_t d_dst = umma_desc(smem_u32(smem + kOffDSt), 16, 1024);
+        const uint64_t d_dst_mn = umma_desc(smem_u32(smem + kOffDSt), kTile, 1024);
+        const uint64_t d_q = umma_desc(smem_u32(smem + kOffQb + st * kTile), 8192, 1024);
+        const uint64_t d_do = umma_desc(smem_u32(smem + kOffDOb + st * kTile), 8192, 1024);
+        const uint64_t d_k = umma_desc(smem_u32(smem + kOffKb + pend_ks * kTile), 8192, 1024);
 #pragma unroll
         for (int kk = 0; kk < kBT / 16; ++kk) {
-          const uint32_t kmaj = (kk >> 2) * kTile + (kk & 3) * 32;  // K-major step inside a 128 x 128 tile
+          const uint64_t kmaj = ((kk >> 2) * kTile + (kk & 3) * 32) >> 4;  // K-major step in a 128 x 128 tile
+          const uint64_t mn = (kk * 2048) >> 4;                              // MN-major step
           const uint32_t acc = (pend_first && kk == 0) ? 0u : 1u;
-          umma_f16(tmem + kColDV, umma_desc(pt + kmaj, 16, 1024), umma_desc(da + kk * 2048, 8192, 1024), kIdAcc, acc);
-          umma_f16(tmem + kColDK, umma_desc(dst + kmaj, 16, 1024), umma_desc(qa + kk * 2048, 8192, 1024), kIdAcc,
-                   acc);
-          umma_f16(tmem + kColDQ + qb * kBD, umma_desc(dst + kk * 2048, kTile, 1024),
-                   umma_desc(ka + kk * 2048, 8192, 1024), kIdDq, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + kColDV, d_pt + kmaj, d_do + mn, kIdAcc, acc);
+          umma_f16(tmem + kColDK, d_dst + kmaj, d_q + mn, kIdAcc, acc);
+          umma_f16(tmem + kColDQ + qb * kBD, d_dst_mn + mn, d_k + mn, kIdDq, kk > 0 ? 1u : 0u);
         }
         umma_commit(ps_empty);  // also: dQ_i, and at an item's last step dK / dV, complete in TMEM
         umma_commit(&qd_empty[st]);
@@ -257,25 +271,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int n = 0, g = 0;
       for (int item = blockIdx.x; item < p.items && ok; item += gridDim.x, ++n) {
         const BItem it = decode_bitem(p, item);
-        const int ks = n & 1;
-        if (!mbar_wait(&kv_full[ks], (n >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
+        const int ks = n % kKvStages;
+        if (!mbar_wait_sleep(&kv_full[ks], (n / kKvStages) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
         const uint32_t ka = smem_u32(smem + kOffKb + ks * kTile), va = smem_u32(smem + kOffVb + ks * kTile);
         const int steps = group * it.nq;
         for (int s = 0; s < steps && ok; ++s, ++g) {
-          const int st = g & 1;
-          if (!mbar_wait(&qd_full[st], (g >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT) ||
-              !mbar_wait(sp_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+          const int st = g % kQdStages;
+          if (!mbar_wait_sleep(&qd_full[st], (g / kQdStages) & 1, abort_flag, SJ_DEV_ATTN_WAIT) ||
+              !mbar_wait_sleep(sp_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t qa = smem_u32(smem + kOffQb + st * kTile), da = smem_u32(smem + kOffDOb + st * kTile);
+          const uint64_t d_k = umma_desc(ka, 16, 1024), d_v = umma_desc(va, 16, 1024);
+          const uint64_t d_q = umma_desc(smem_u32(smem + kOffQb + st * kTile), 16, 1024);
+          const uint64_t d_do = umma_desc(smem_u32(smem + kOffDOb + st * kTile), 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < kBD / 16; ++kk) {
-            umma_f16(tmem + kColSt, umma_desc(ka + kk * 32, 16, 1024), umma_desc(qa + kk * 32, 16, 1024), kIdS,
-                     kk > 0 ? 1u : 0u);
-            umma_f16(tmem + kColDPt, umma_desc(va + kk * 32, 16, 1024), umma_desc(da + kk * 32, 16, 1024), kIdS,
-                     kk > 0 ? 1u : 0u);
+            const uint64_t step = (kk * 32) >> 4;
+            umma_f16(tmem + kColSt, d_k + step, d_q + step, kIdS, kk > 0 ? 1u : 0u);
+            umma_f16(tmem + kColDPt, d_v + step, d_do + step, kIdS, kk > 0 ? 1u : 0u);
           }
           umma_commit(sp_full);
           if (pend_i >= 0 && !issue_acc()) {
@@ -291,7 +306,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       if (ok && pend_i >= 0) issue_acc();
       umma_commit(drain);
-      mbar_wait(drain, 0, nullptr, SJ_DEV_ATTN_WAIT);
+      mbar_wait_sleep(drain, 0, nullptr, SJ_DEV_ATTN_WAIT);
     }
   } else {
     // ---------------------------------------------------------------- elementwise warps
@@ -366,10 +381,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const int kpos = it.k0 + r;
       const int steps = group * it.nq;
       for (int s = 0; s < steps && alive; ++s, ++g) {
-        const int st = g & 1;
+        const int st = g % kQdStages;
         const int q0 = (it.qt_lo + s % it.nq) * kBT;
-        if (!mbar_wait(&qd_full[st], (g >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT) ||
-            !mbar_wait(sp_full, g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+        if (!mbar_wait_sleep(&qd_full[st], (g / kQdStages) & 1, abort_flag, SJ_DEV_ATTN_WAIT) ||
+            !mbar_wait_sleep(sp_full, g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
           alive = false;
           break;
         }
@@ -387,37 +402,42 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           hi = min(p.window > 0 ? kpos + p.window - 1 : p.t - 1, p.t - 1) - cbase;
           if (kpos >= p.t) hi = -1;
         }
-        // this thread's 64 query columns of S^T and dP^T, in four chunks of 16: P^T and dS^T are
+        // this thread's 64 query columns of S^T and dP^T, in two chunks of 32: P^T and dS^T are
         // computed and packed to bf16 while the previous step's MMAs may still read the buffers
         uint32_t pw[32], dw[32];
 #pragma unroll
-        for (int chunk = 0; chunk < 4; ++chunk) {
-          uint32_t sv[16], dv[16];
-          tmem_ld_32x32b_x16(tmem + lane_off + kColSt + half * 64 + chunk * 16, sv);
-          tmem_ld_32x32b_x16(tmem + lane_off + kColDPt + half * 64 + chunk * 16, dv);
+        for (int chunk = 0; chunk < 2; ++chunk) {
+          uint32_t sv[32], dv[32];
+          tmem_ld_32x32b_x32(tmem + lane_off + kColSt + half * 64 + chunk * 32, sv);
+          tmem_ld_32x32b_x32(tmem + lane_off + kColDPt + half * 64 + chunk * 32, dv);
           tmem_wait_ld();
-          if (chunk == 3) {  // S^T / dP^T are in registers: the next step's products may start
+          if (chunk == 1) {  // S^T / dP^T are in registers: the next step's products may start
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(sp_empty);
           }
 #pragma unroll
-          for (int c = 0; c < 16; c += 2) {
-            float pr[2], ds[2];
+          for (int c = 0; c < 32; c += 4) {
+            const int cc = chunk * 32 + c;
+            const float4 l4 = *reinterpret_cast<const float4*>(lsl + cc);
+            const float4 d4 = *reinterpret_cast<const float4*>(dls + cc);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dlv[4] = {d4.x, d4.y, d4.z, d4.w};
+            float pr[4], ds[4];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int cc = chunk * 16 + c + e;
-              const bool valid = cc >= lo && cc <= hi;  // (LSE / Delta past the sequence end are not data)
-              pr[e] = valid ? ex2b(fmaf(__uint_as_float(sv[c + e]), p.scale_log2, -lsl[cc])) : 0.f;   // P^T
-              ds[e] = valid ? pr[e] * (__uint_as_float(dv[c + e]) - dls[cc]) * p.scale : 0.f;        // dS^T
+            for (int e = 0; e < 4; ++e) {
+              const bool valid = cc + e >= lo && cc + e <= hi;  // (LSE / Delta past the sequence end are not data)
+              pr[e] = valid ? ex2b(fmaf(__uint_as_float(sv[c + e]), p.scale_log2, -lv[e])) : 0.f;  // P^T
+              ds[e] = valid ? pr[e] * (__uint_as_float(dv[c + e]) - dlv[e]) * p.scale : 0.f;       // dS^T
             }
-            pw[chunk * 8 + (c >> 1)] = pack_bf16x2(pr[0], pr[1]);
-            dw[chunk * 8 + (c >> 1)] = pack_bf16x2(ds[0], ds[1]);
+            pw[chunk * 16 + (c >> 1)] = pack_bf16x2(pr[0], pr[1]);
+            pw[chunk * 16 + (c >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
+            dw[chunk * 16 + (c >> 1)] = pack_bf16x2(ds[0], ds[1]);
+            dw[chunk * 16 + (c >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
           }
         }
         // P^T and dS^T may overwrite the buffers once the previous step's MMAs have read them
         // (which also completes that step's dQ and, at an item's end, its dK / dV)
-        if (!mbar_wait(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+        if (!mbar_wait_sleep(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
           alive = false;
           break;
         }
@@ -443,7 +463,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     // the last step's products
-    if (alive && pend_g >= 0 && mbar_wait(ps_empty, pend_g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+    if (alive && pend_g >= 0 && mbar_wait_sleep(ps_empty, pend_g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
       tc_fence_after();
       read_out();
     }

@@ -115,6 +115,34 @@ SJ_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, in
   }
 }
 
+// Bounded wait that lets the waiting thread sleep: try_wait with a suspend-time hint returns when the
+// phase completes or after about `hint_ns`, so a warp that waits long (a producer or MMA thread
+// sharing its scheduler with compute warps) does not spend issue slots polling.
+SJ_DEVICE bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+SJ_DEVICE bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+  if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+  const uint64_t start = globaltimer();
+  while (true) {
+    if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
+    if (abort != nullptr && *abort) return false;
+    if (globaltimer() - start > kWaitLimitNs) {
+      record_error(code);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+}
+
 // Non-blocking probe of the phase with the given parity.
 SJ_DEVICE bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
