@@ -8,7 +8,7 @@
 //
 // Persistent: one CTA per SM walks work items (batch, kv head, 128-key tile).  An item visits every
 // query head of its group and every query tile its keys are visible to, so dK and dV of the kv head
-// accumulate in TMEM across the whole group and are written once (no partials).  10 warps:
+// accumulate in TMEM across the whole group and are written once (no partials).  18 warps:
 //   warp 0      TMA: the item's K and V tiles (double-buffered by item), and per step the Q and dO
 //               tiles and the step's 128 LSE and Delta values (2-deep ring; the delta kernel lays
 //               both out per head, contiguous over the sequence).
@@ -19,7 +19,7 @@
 //                 dQ_g = dS_g K (the dS^T buffer read as an MN-major operand) into one of two TMEM
 //                 buffers.
 //               S^T_{g+1} / dP^T_{g+1} are issued before waiting for P^T_g, so the two overlap.
-//   warps 2-9   elementwise: thread <-> key row (TMEM lane), two threads per row, 64 query columns
+//   warps 2-17  elementwise: thread <-> key row (TMEM lane), four threads per row, 32 query columns
 //               each: P^T and dS^T computed from TMEM while the previous step's MMAs still read the
 //               shared-memory buffers, then stored in bf16 into K-major 128-byte-swizzled shared
 //               memory; after handing them over, the previous step's dQ goes into an f32
@@ -38,7 +38,10 @@ namespace {
 
 constexpr int kBT = 128;                          // keys per item, queries per step
 constexpr int kBD = 64;                           // head dim
-constexpr int kEwWarps = 8;
+constexpr int kEwWarps = 16;                     // 4 per TMEM lane quarter
+constexpr int kEwCols = kBT / (kEwWarps / 4);    // 32 query columns of P^T / dS^T per thread
+constexpr int kEwHead = kBD / (kEwWarps / 4);    // 16 head columns of dQ / dK / dV per thread
+static_assert(kEwCols == 32 && kEwHead == 16, "elementwise mapping");
 constexpr int kBwdThreads = 32 * (2 + kEwWarps);
 constexpr int kTile = kBT * kBD * 2;              // 16 KB: 128 rows x 128 B
 // shared memory: K | V | Q ring | dO ring | P^T | dS^T | LSE/Delta ring | barriers
@@ -310,10 +313,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- elementwise warps
-    // thread <-> TMEM lane r: a key row for P^T / dS^T and dK / dV, a query row for dQ; half
-    // selects 64 of the 128 query columns (P^T, dS^T) or 32 of the 64 head columns (dQ, dK, dV)
+    // thread <-> TMEM lane r: a key row for P^T / dS^T and dK / dV, a query row for dQ; part selects
+    // 32 of the 128 query columns (P^T, dS^T) and 16 of the 64 head columns (dQ, dK, dV)
     const int quarter = warp & 3;
-    const int half = (warp - 2) >> 2;
+    const int part = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     // step whose dQ (and, at an item's end, dK / dV) is still to be read out of TMEM
@@ -323,18 +326,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // item's last step also its dK (inverse RoPE) and dV rows, then the TMEM is released
     auto read_out = [&]() {
       const int qb = pend_g & 1;
+      const int c0 = part * kEwHead;
       {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kColDQ + qb * kBD + half * 32, v);
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(tmem + lane_off + kColDQ + qb * kBD + c0, v);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&dq_empty[qb]);
         if (pend_qpos < p.t) {
           float* dst = p.dq_acc + (static_cast<size_t>(pend_it.b) * p.t + pend_qpos) * (static_cast<size_t>(p.hq) * kBD) +
-                       pend_h * kBD + half * 32;
+                       pend_h * kBD + c0;
 #pragma unroll
-          for (int c = 0; c < 32; c += 4)
+          for (int c = 0; c < 16; c += 4)
             red_add_v4(dst + c, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
                        __uint_as_float(v[c + 3]));
         }
@@ -342,19 +346,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!pend_last) return;
       const int kpos = pend_it.k0 + r;
       const size_t row = static_cast<size_t>(pend_it.b) * p.t + min(kpos, p.t - 1);
-      const int c0 = half * 32;
-      uint32_t vk[32], vv[32];
-      tmem_ld_32x32b_x32(tmem + lane_off + kColDK + c0, vk);
-      tmem_ld_32x32b_x32(tmem + lane_off + kColDV + c0, vv);
+      uint32_t vk[16], vv[16];
+      tmem_ld_32x32b_x16(tmem + lane_off + kColDK + c0, vk);
+      tmem_ld_32x32b_x16(tmem + lane_off + kColDV + c0, vv);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
       if (kpos < p.t) {
         const bool rope = p.rope_tab != nullptr || p.rope_log_theta > 0.f;
-        uint32_t w[16];
+        uint32_t w[8];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < 16; c += 2) {
           float a = __uint_as_float(vk[c]), b = __uint_as_float(vk[c + 1]);
           if (rope) {
             const float2 cs = rope_cs(p.rope_tab, p.rope_log_theta, kpos, (c0 + c) >> 1);
@@ -365,13 +368,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           w[c >> 1] = pack_bf16x2(a, b);
         }
         uint4* out = reinterpret_cast<uint4*>(p.dk + row * p.lddk + pend_it.kvh * kBD + c0);
+        out[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        out[1] = make_uint4(w[4], w[5], w[6], w[7]);
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) out[c4] = make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]);
-#pragma unroll
-        for (int c = 0; c < 32; c += 2) w[c >> 1] = pack_bf16x2(__uint_as_float(vv[c]), __uint_as_float(vv[c + 1]));
+        for (int c = 0; c < 16; c += 2) w[c >> 1] = pack_bf16x2(__uint_as_float(vv[c]), __uint_as_float(vv[c + 1]));
         out = reinterpret_cast<uint4*>(p.dv + row * p.lddv + pend_it.kvh * kBD + c0);
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) out[c4] = make_uint4(w[4 * c4], w[4 * c4 + 1], w[4 * c4 + 2], w[4 * c4 + 3]);
+        out[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        out[1] = make_uint4(w[4], w[5], w[6], w[7]);
       }
     };
     int n = 0, g = 0;
@@ -389,27 +392,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         tc_fence_after();
-        const float* lsl = ldbuf + st * 2 * kBT + half * 64;
+        const float* lsl = ldbuf + st * 2 * kBT + part * kEwCols;
         const float* dls = lsl + kBT;
-        // visible queries of this key row in this half's columns: [lo, hi]
-        const int cbase = q0 + half * 64;
+        // visible queries of this key row in this part's columns: [lo, hi]
+        const int cbase = q0 + part * kEwCols;
         const bool full_tile =
             q0 >= it.k0 + kBT - 1 && q0 + kBT <= p.t && it.k0 + kBT <= p.t &&
             (p.window <= 0 || q0 + kBT - 1 - it.k0 < p.window);
-        int lo = 0, hi = 63;
+        int lo = 0, hi = kEwCols - 1;
         if (!full_tile) {
           lo = kpos - cbase;
           hi = min(p.window > 0 ? kpos + p.window - 1 : p.t - 1, p.t - 1) - cbase;
           if (kpos >= p.t) hi = -1;
         }
-        // this thread's 64 query columns of S^T and dP^T, in two chunks of 32: P^T and dS^T are
-        // computed and packed to bf16 while the previous step's MMAs may still read the buffers
-        uint32_t pw[32], dw[32];
+        // this thread's 32 query columns of S^T and dP^T: P^T and dS^T are computed and packed to
+        // bf16 while the previous step's MMAs may still read the buffers
+        uint32_t pw[16], dw[16];
 #pragma unroll
         for (int chunk = 0; chunk < 2; ++chunk) {
-          uint32_t sv[32], dv[32];
-          tmem_ld_32x32b_x32(tmem + lane_off + kColSt + half * 64 + chunk * 32, sv);
-          tmem_ld_32x32b_x32(tmem + lane_off + kColDPt + half * 64 + chunk * 32, dv);
+          uint32_t sv[16], dv[16];
+          tmem_ld_32x32b_x16(tmem + lane_off + kColSt + part * kEwCols + chunk * 16, sv);
+          tmem_ld_32x32b_x16(tmem + lane_off + kColDPt + part * kEwCols + chunk * 16, dv);
           tmem_wait_ld();
           if (chunk == 1) {  // S^T / dP^T are in registers: the next step's products may start
             tc_fence_before();
@@ -417,8 +420,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             if (lane == 0) mbar_arrive(sp_empty);
           }
 #pragma unroll
-          for (int c = 0; c < 32; c += 4) {
-            const int cc = chunk * 32 + c;
+          for (int c = 0; c < 16; c += 4) {
+            const int cc = chunk * 16 + c;
             const float4 l4 = *reinterpret_cast<const float4*>(lsl + cc);
             const float4 d4 = *reinterpret_cast<const float4*>(dls + cc);
             const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dlv[4] = {d4.x, d4.y, d4.z, d4.w};
@@ -429,10 +432,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               pr[e] = valid ? ex2b(fmaf(__uint_as_float(sv[c + e]), p.scale_log2, -lv[e])) : 0.f;  // P^T
               ds[e] = valid ? pr[e] * (__uint_as_float(dv[c + e]) - dlv[e]) * p.scale : 0.f;       // dS^T
             }
-            pw[chunk * 16 + (c >> 1)] = pack_bf16x2(pr[0], pr[1]);
-            pw[chunk * 16 + (c >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
-            dw[chunk * 16 + (c >> 1)] = pack_bf16x2(ds[0], ds[1]);
-            dw[chunk * 16 + (c >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
+            pw[cc >> 1] = pack_bf16x2(pr[0], pr[1]);
+            pw[(cc >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
+            dw[cc >> 1] = pack_bf16x2(ds[0], ds[1]);
+            dw[(cc >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
           }
         }
         // P^T and dS^T may overwrite the buffers once the previous step's MMAs have read them
@@ -442,13 +445,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
         tc_fence_after();
-        uint8_t* pt = smem + kOffPt + half * kTile;
-        uint8_t* dst = smem + kOffDSt + half * kTile;
+        // columns [32 part, 32 part + 32): 64-query half part / 2, 16-byte chunks 4 (part & 1) ..
+        uint8_t* pt = smem + kOffPt + (part >> 1) * kTile;
+        uint8_t* dst = smem + kOffDSt + (part >> 1) * kTile;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
+        for (int j = 0; j < 4; ++j) {
+          const int c8 = (part & 1) * 4 + j;
           const int off = r * 128 + ((c8 ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pw[4 * c8], pw[4 * c8 + 1], pw[4 * c8 + 2], pw[4 * c8 + 3]);
-          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dw[4 * c8], dw[4 * c8 + 1], dw[4 * c8 + 2], dw[4 * c8 + 3]);
+          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pw[4 * j], pw[4 * j + 1], pw[4 * j + 2], pw[4 * j + 3]);
+          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dw[4 * j], dw[4 * j + 1], dw[4 * j + 2], dw[4 * j + 3]);
         }
         fence_proxy_async_shared();
         tc_fence_before();
