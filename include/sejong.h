@@ -183,9 +183,10 @@ int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, const void* 
 /* Engine::attention_grouped_backward (hierarchy_ops.rs:74-147; hierarchy.py:42-104).
  * do bf16 (lddo); dq/dk/dv bf16 with their own strides; when rope_table (an sj_rope_table of t
  * positions) is given, or else rope_theta > 0, the inverse rotation of Engine::rope(.., inverse=true)
- * (graph.rs:879-882) is applied to dq and dk before the store.  `workspace` is 16-byte aligned f32
- * scratch of sj_attn_workspace(batch, t, hq, hk) elements (Delta, and for hq != hk the per-query-head
- * dK/dV partials). */
+ * (graph.rs:879-882) is applied to dq and dk before the store.  All operands 16-byte aligned, row
+ * strides multiples of 8 elements.  `workspace` is 16-byte aligned f32 scratch of
+ * sj_attn_workspace(batch, t, hq, hk) elements: the f32 dQ accumulator [batch*t, hq*64], then Delta
+ * and LSE*log2(e) laid out [hq][batch][t rounded up to 128]. */
 size_t sj_attn_workspace(int batch, int t, int hq, int hk);
 int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o, int ldo,
                     const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk, int lddk, void* dv,

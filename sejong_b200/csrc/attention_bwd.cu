@@ -482,47 +482,64 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-// Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57), one warp each, written with the LSE
-// (times log2 e) transposed to [head][batch][tpad] so that a step's 128 values are one contiguous run.
-__global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dout,
-                                  int lddo, const float* lse, float* delta_t,
-                                  float* lse_t, int rows, int t, int tpad, int hq) {
-  pdl_wait();
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  if (w >= rows * hq) return;
-  const int row = w / hq, h = w % hq;
-  const float2 a = unpack_bf16x2(
-      *reinterpret_cast<const uint32_t*>(dout + static_cast<size_t>(row) * lddo + h * kBD + 2 * lane));
-  const float2 c =
-      unpack_bf16x2(*reinterpret_cast<const uint32_t*>(o + static_cast<size_t>(row) * ldo + h * kBD + 2 * lane));
-  const float s = warp_sum(a.x * c.x + a.y * c.y);
-  if (lane == 0) {
-    const int b = row / t, pos = row % t;
-    const size_t dst = (static_cast<size_t>(h) * (rows / t) + b) * tpad + pos;
-    delta_t[dst] = s;
-    lse_t[dst] = lse[w] * kLog2eB;
-  }
-}
-
-// dq = bf16(inverse RoPE(dq_acc)), one thread per (row, head, column pair).
-__global__ void attn_dq_finish_kernel(const float* acc, __nv_bfloat16* dq, int lddq,
-                                      int rows, int t, int hq, const float2* tab, float log_theta) {
+// Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57) and the LSE times log2(e), both written
+// transposed to [head][batch][tpad] so that a step's 128 values are one contiguous run; the same
+// thread zeroes the (row, head) slice of the f32 dQ accumulator.  Thread <-> (head, row), rows
+// fastest, so the transposed stores are coalesced.
+__global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dout, int lddo,
+                                  const float* lse, float* delta_t, float* lse_t, float* dq_acc, int rows, int t,
+                                  int tpad, int hq) {
   pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const size_t pairs = static_cast<size_t>(rows) * hq * (kBD / 2);
-  if (i >= pairs) return;
-  const int row = static_cast<int>(i / (hq * (kBD / 2)));
-  const int rem = static_cast<int>(i % (hq * (kBD / 2)));
-  const int h = rem / (kBD / 2), pr = rem % (kBD / 2);
-  const float2 v = *reinterpret_cast<const float2*>(acc + i * 2);
-  float a = v.x, b = v.y;
-  if (tab != nullptr || log_theta > 0.f) {
-    const float2 cs = rope_cs(tab, log_theta, row % t, pr);
-    const float na = a * cs.x + b * cs.y, nb = -a * cs.y + b * cs.x;
-    a = na;
-    b = nb;
+  if (i >= static_cast<size_t>(rows) * hq) return;
+  const int h = static_cast<int>(i / rows), row = static_cast<int>(i % rows);
+  const uint4* a = reinterpret_cast<const uint4*>(dout + static_cast<size_t>(row) * lddo + h * kBD);
+  const uint4* c = reinterpret_cast<const uint4*>(o + static_cast<size_t>(row) * ldo + h * kBD);
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < kBD / 8; ++j) {
+    const uint4 x = a[j], y = c[j];
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 u = unpack_bf16x2(xs[e]), v = unpack_bf16x2(ys[e]);
+      acc = fmaf(u.x, v.x, fmaf(u.y, v.y, acc));
+    }
   }
-  *reinterpret_cast<uint32_t*>(dq + static_cast<size_t>(row) * lddq + h * kBD + 2 * pr) = pack_bf16x2(a, b);
+  const int b = row / t, pos = row % t;
+  const size_t dst = (static_cast<size_t>(h) * (rows / t) + b) * tpad + pos;
+  delta_t[dst] = acc;
+  lse_t[dst] = lse[static_cast<size_t>(row) * hq + h] * kLog2eB;
+  float4* z = reinterpret_cast<float4*>(dq_acc + (static_cast<size_t>(row) * hq + h) * kBD);
+#pragma unroll
+  for (int j = 0; j < kBD / 4; ++j) z[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
+// dq = bf16(inverse RoPE(dq_acc)), one thread per (row, head, 4 column pairs).
+__global__ void attn_dq_finish_kernel(const float* acc, __nv_bfloat16* dq, int lddq, int rows, int t, int hq,
+                                      const float2* tab, float log_theta) {
+  pdl_wait();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  constexpr int kQuads = kBD / 8;
+  if (i >= static_cast<size_t>(rows) * hq * kQuads) return;
+  const int row = static_cast<int>(i / (hq * kQuads));
+  const int rem = static_cast<int>(i % (hq * kQuads));
+  const int h = rem / kQuads, q4 = rem % kQuads;
+  const float4* src = reinterpret_cast<const float4*>(acc + i * 8);
+  const float4 v0 = src[0], v1 = src[1];
+  float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  if (tab != nullptr || log_theta > 0.f) {
+    const int pos = row % t;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 cs = rope_cs(tab, log_theta, pos, 4 * q4 + e);
+      const float a = x[2 * e], b = x[2 * e + 1];
+      x[2 * e] = a * cs.x + b * cs.y;
+      x[2 * e + 1] = -a * cs.y + b * cs.x;
+    }
+  }
+  *reinterpret_cast<uint4*>(dq + static_cast<size_t>(row) * lddq + h * kBD + 8 * q4) =
+      make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
 }
 
 }  // namespace sj
@@ -546,7 +563,8 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
     return fail(SJ_ERR_SHAPE, "attention: bad shape batch=%d t=%d hq=%d hk=%d window=%d", batch, t, hq, hk, window);
   if ((ldq | ldk | ldv | ldo | lddo | lddq | lddk | lddv) % 8)
     return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: strides must be multiples of 8");
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(dout) || !aligned16(dk) || !aligned16(dv))
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(dout) || !aligned16(dq) ||
+      !aligned16(dk) || !aligned16(dv))
     return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: 16-byte aligned operands required");
   if (!workspace || !aligned16(workspace)) return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: workspace must be aligned");
   if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7))
@@ -565,12 +583,10 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   float* dq_acc = workspace;
   float* delta_t = dq_acc + rows * hq * kBD;
   float* lse_t = delta_t + static_cast<size_t>(hq) * batch * tpad;
-  const int zs = zero_async(dq_acc, rows * hq * kBD * sizeof(float), s);
-  if (zs != SJ_OK) return zs;
-  const long long warps = static_cast<long long>(rows) * hq;
-  launch(attn_delta_kernel, static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, s, 
-      static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo, lse, delta_t, lse_t,
-      static_cast<int>(rows), t, tpad, hq);
+  const size_t row_heads = rows * hq;
+  launch(attn_delta_kernel, static_cast<unsigned>((row_heads + 255) / 256), 256, 0, s,
+         static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo, lse, delta_t, lse_t,
+         dq_acc, static_cast<int>(rows), t, tpad, hq);
   SJ_LAUNCH_CHECK("attn_delta");
   CUtensorMap maps[4];
   int rc = bf16_map(&maps[0], q, static_cast<uint64_t>(hq) * kBD, rows, ldq, kBD, kBT);
@@ -601,8 +617,8 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   const int grid = std::min(p.items, sm_count());
   launch(attn_bwd_tc_kernel, grid, kBwdThreads, kSmemBwd, s, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("attn_bwd_tc");
-  const size_t pairs = rows * hq * (kBD / 2);
-  launch(attn_dq_finish_kernel, static_cast<unsigned>((pairs + 255) / 256), 256, 0, s, 
+  const size_t quads = rows * hq * (kBD / 8);
+  launch(attn_dq_finish_kernel, static_cast<unsigned>((quads + 255) / 256), 256, 0, s,
       dq_acc, static_cast<__nv_bfloat16*>(dq), lddq, static_cast<int>(rows), t, hq, p.rope_tab, p.rope_log_theta);
   SJ_LAUNCH_CHECK("attn_dq_finish");
   return SJ_OK;

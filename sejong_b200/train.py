@@ -177,7 +177,7 @@ class ByteTrainer:
             self._init_vjp(train.parameter_vjp)
 
     # kernels each entry point launches (zero fills are kernels too)
-    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 4,
+    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 3,
                "sj_zero": 1, "sj_param_basis": 5, "sj_param_prepare": 3}
 
     @classmethod
