@@ -35,7 +35,7 @@ import torch
 
 from . import _lib, distributed, param_vjp
 from ._lib import (EPI_ACCUM, EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call)
-from .model import HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage
+from .model import HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage, reference_layout
 
 
 @dataclass
@@ -522,6 +522,49 @@ class ByteTrainer:
         """Copy a batch (host or device int32 tensors) into the step's input buffers."""
         self.ids.copy_(torch.as_tensor(ids, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
         self.targets.copy_(torch.as_tensor(targets, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
+
+    # ------------------------------------------------------------------ artifacts
+    def save_checkpoint(self, directory, data_fingerprint=None, rng_state=None):
+        """save_training (crates/sejong-train/src/lib.rs:472-491): the FP32 master weights under the
+        reference's parameter names, the AdamW moments as m.<name> / v.<name>, the optimizer step
+        (the device optimizer state) and the training config, written atomically."""
+        from . import checkpoint
+        torch.cuda.synchronize(self.dev)
+        params = self.layout.unpack(self.w.cpu().numpy())
+        optimizer = None
+        if self.tc.optimizer == "adamw":
+            optimizer = {}
+            for prefix, buf in (("m", self.m), ("v", self.v)):
+                for name, value in self.layout.unpack(buf.cpu().numpy()).items():
+                    optimizer[f"{prefix}.{name}"] = value
+        step = int(self.opt_state[0].item())
+        return checkpoint.save(directory, self.c, params, step, optimizer, checkpoint.train_config_json(self.tc),
+                               data_fingerprint, rng_state)
+
+    def load_checkpoint(self, directory):
+        """Resume from an artifact directory (Model::load, crates/sejong-model/src/lib.rs:134-170):
+        weights, moments when present, and the optimizer step.  The artifact's model must have this
+        trainer's parameter layout.  Returns the manifest."""
+        from . import checkpoint
+        config, params, manifest, optimizer = checkpoint.load(directory, self.c.init_std)
+        if reference_layout(config) != reference_layout(self.c):
+            raise checkpoint.ArtifactError("artifact model layout differs from this trainer's")
+        torch.cuda.synchronize(self.dev)
+        self.w.copy_(torch.from_numpy(self.layout.pack(params)).to(self.dev))
+        if optimizer is not None:
+            for prefix, buf in (("m", self.m), ("v", self.v)):
+                named = {k[len(prefix) + 1:]: v for k, v in optimizer.items() if k.startswith(prefix + ".")}
+                if set(named) != set(params):
+                    raise checkpoint.ArtifactError(f"optimizer state {prefix} does not cover every parameter")
+                buf.copy_(torch.from_numpy(self.layout.pack(named)).to(self.dev))
+        else:
+            self.m.zero_()
+            self.v.zero_()
+        self.opt_state[0] = float(manifest["step"])
+        call("sj_cast", _ptr(self.w), SJ_F32, _ptr(self.wb), SJ_BF16, self.layout.total,
+             torch.cuda.current_stream(self.dev).cuda_stream)
+        torch.cuda.synchronize(self.dev)
+        return manifest
 
     def capture(self):
         """Capture the step as CUDA graphs (replayed by `replay`).
