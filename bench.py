@@ -22,6 +22,7 @@ on a bounded sample of the same workload (rank 0, N = 1 only).
 its Rust/HIP host cannot be built here).
 """
 import argparse
+import ctypes
 import json
 import os
 import subprocess
@@ -53,8 +54,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=8, help="per-GPU batch")
     ap.add_argument("--seq", type=int, default=4096)
-    ap.add_argument("--config", choices=["c3", "c4"], default="c3",
-                    help="c3: AdamW (BASELINE configs[2]); c4: parameter-VJP SGD (configs[3])")
+    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c3",
+                    help="c3: AdamW (BASELINE configs[2]); c4: parameter-VJP SGD (configs[3]); "
+                         "c2: MiniLM encoder forward (configs[1])")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--kernel-report", default=None, help="write per-call kernel timings (JSON) to this path")
@@ -386,9 +388,223 @@ def _call_names(trainer):
     return names
 
 
+# ---------------------------------------------------------------- C2: MiniLM encoder forward
+C2_BATCH = 64
+C2_CPU_SEQS = 64
+C2_CPU_PASSES = 3
+C2_METRIC, C2_UNIT = "encoder_tokens_per_s", "tokens/s"
+C2_WORKLOAD = ("C2 MiniLM-L6-shaped BERT encoder forward (BASELINE configs[1]): batch 64, lengths uniform "
+               "16..128, d384 x 6 layers, 12 heads, FFN 1536 GELU, post-LN")
+
+
+def c2_cpu_rate(threads=None):
+    """Valid tokens/s of the CPU restatement (oracle/bert.py, fp32 torch, per unpadded sequence as the
+    reference runs it) on one C2 batch, mean of C2_CPU_PASSES passes."""
+    import torch
+
+    from oracle import bert as obert
+    from sejong_b200 import bert
+    if threads:
+        torch.set_num_threads(threads)
+    c = bert.MiniLMConfig()
+    params = bert.initialize(c)
+    seqs = bert.synthetic_batch(3000, C2_BATCH)[:C2_CPU_SEQS]
+    obert.COMPUTE = torch.float32
+    try:
+        obert.hidden(params, seqs[0], c.layers, c.heads)  # warm-up
+        t0 = time.perf_counter()
+        for _ in range(C2_CPU_PASSES):
+            for sq in seqs:
+                obert.hidden(params, sq, c.layers, c.heads)
+        sec = (time.perf_counter() - t0) / C2_CPU_PASSES
+    finally:
+        obert.COMPUTE = torch.float64
+    tokens = sum(len(sq) for sq in seqs)
+    return tokens / sec, sec, tokens, torch.get_num_threads()
+
+
+def run_c2_reference(args):
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    rate, sec, tokens, cores = c2_cpu_rate()
+    sample = (f"one C2 batch ({C2_CPU_SEQS} sequences, {tokens} tokens), fp32 torch CPU, one sequence at a time, "
+              f"mean of {C2_CPU_PASSES} passes")
+    line = {"metric": C2_METRIC, "value": rate, "unit": C2_UNIT, "n_gpus": args.gpus, "steps": 1, "warmup": 1,
+            "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic ids per BASELINE C2, random-init N(0,0.02) weights",
+            "config": {"workload": C2_WORKLOAD + " (bounded CPU sample)", "parallelism": "none"},
+            "impl": "reference",
+            "cpu_baseline": {"value": rate, "unit": C2_UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": rate, "unit": C2_UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's BERT runs on HIP only; this arm times the CPU restatement in oracle/bert.py"}
+    print(json.dumps(line), flush=True)
+
+
+def run_c2(args):
+    """MiniLM forward over batches of 64 packed sequences, one CUDA graph per batch; `value` with the
+    batches resident in HBM, `e2e` with each batch's ids copied from pinned host memory and its hidden
+    states [rows, 384] f32 read back; replicas on N GPUs (no collective)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from sejong_b200 import bert, distributed
+    rank, world, local, pg = distributed.init_from_env("nccl", timeout_s=300)
+    torch.cuda.set_device(local)
+    c = bert.MiniLMConfig()
+    m = bert.MiniLM(c, device=local)
+    total = args.warmup + args.steps
+    cap = C2_BATCH * 128
+    packed = [bert.pack(bert.synthetic_batch(distributed.rank_seed(3000, rank) + i, C2_BATCH)) for i in range(total)]
+    rows = [len(ids) for ids, _ in packed]
+    host_ids = torch.zeros(total, cap, dtype=torch.int32).pin_memory()
+    host_cu = torch.zeros(total, C2_BATCH + 1, dtype=torch.int32).pin_memory()
+    for i, (ids, cu) in enumerate(packed):
+        host_ids[i, :len(ids)] = torch.from_numpy(ids)
+        host_cu[i] = torch.from_numpy(cu)
+    dev_ids, dev_cu = host_ids.to(m.dev), host_cu.to(m.dev)
+    host_out = torch.empty(cap, c.hidden, dtype=torch.float32).pin_memory()
+    m.reserve(cap)
+    m.forward(dev_ids[0, :rows[0]], dev_cu[0])  # eager first pass: kernel attributes, checks the path runs
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(m.dev)
+    s.wait_stream(torch.cuda.current_stream(m.dev))
+    graphs = []
+    launches0 = m.launches
+    with torch.cuda.stream(s):
+        for i in range(total):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                m.forward(dev_ids[i, :rows[i]], dev_cu[i], stream=s.cuda_stream)
+            graphs.append(g)
+    per_forward = (m.launches - launches0) // total
+    torch.cuda.current_stream(m.dev).wait_stream(s)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=m.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    for i in range(args.warmup):
+        graphs[i].replay()
+    barrier()
+    time.sleep(0.3)
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.warmup, total):
+        graphs[i].replay()
+    t1.record(stream)
+    barrier()
+    dev_ms = max_over_ranks(t0.elapsed_time(t1))
+    h2d = d2h = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for i in range(args.warmup, total):
+        dev_ids[i, :rows[i]].copy_(host_ids[i, :rows[i]], non_blocking=True)
+        dev_cu[i].copy_(host_cu[i], non_blocking=True)
+        graphs[i].replay()
+        host_out[:rows[i]].copy_(m.x[:rows[i]], non_blocking=True)
+        h2d += rows[i] * 4 + (C2_BATCH + 1) * 4
+        d2h += rows[i] * c.hidden * 4
+    e1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    clk = clocks.stop()
+    code = ctypes.c_int(0)
+    from sejong_b200._lib import call
+    call("sj_device_error", ctypes.byref(code), 0, None)
+    assert code.value == 0, f"device error {code.value} during the benchmark"
+    assert torch.isfinite(host_out[:rows[-1]]).all(), "non-finite hidden states"
+
+    # GEMM family: one eager forward with CUDA events around each GEMM call
+    gemm = {"ms": 0.0, "flops": 0.0, "calls": 0}
+    original = m._call
+    recs = []
+
+    def timed(name, *a):
+        if name != "sj_gemm_bias":
+            return original(name, *a)
+        e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_s.record(stream)
+        original(name, *a)
+        e_e.record(stream)
+        recs.append((e_s, e_e, 2.0 * a[9] * a[10] * a[11]))
+
+    torch.cuda.synchronize()
+    torch.cuda._sleep(100_000_000)
+    m._call = timed
+    try:
+        m.forward(dev_ids[0, :rows[0]], dev_cu[0])
+    finally:
+        m._call = original
+    torch.cuda.synchronize()
+    for e_s, e_e, fl in recs:
+        gemm["ms"] += e_s.elapsed_time(e_e)
+        gemm["flops"] += fl
+        gemm["calls"] += 1
+    for g in graphs:
+        g.reset()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    K = args.steps
+    tokens = sum(rows[args.warmup:]) * world
+    pk = peaks()
+    flops = sum(m.flops(packed[i][1]) for i in range(args.warmup, total)) / K
+    ms = dev_ms / K
+    achieved = gemm["flops"] / (gemm["ms"] / 1e3) / 1e12
+    line = {
+        "metric": C2_METRIC, "value": tokens / (dev_ms / 1e3), "unit": C2_UNIT, "n_gpus": world, "steps": K,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic ids per BASELINE C2 (reference Rng, seed 3000+rank+step); random-init N(0,0.02) weights",
+        "config": {"workload": C2_WORKLOAD, "global_batch": C2_BATCH * world, "per_gpu_batch": C2_BATCH,
+                   "seq_len": 128, "mean_tokens_per_step": sum(rows[args.warmup:]) / K, "parallelism": f"replicas{world}",
+                   "l2": "weights and activations of one forward fit in L2 across replays; no flush"},
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": C2_UNIT, "h2d_bytes_per_step": h2d // K,
+                "d2h_bytes_per_step": d2h // K},
+        "gpu_launches": per_forward * K,
+        "roofline": {"bound": "tensor", "kernel": "gemm_tcgen05 with bias epilogues (all GEMMs of one forward)",
+                     "achieved": achieved, "peak": pk["bf16"], "unit": "TFLOP/s", "frac": achieved / pk["bf16"],
+                     "peak_source": pk["source"] + " bf16 (burst)", "traffic": None, "launches": gemm["calls"],
+                     "ms_per_step": gemm["ms"]},
+        "tensor_frac_of_step": flops / (ms / 1e3) / (pk["bf16"] * 1e12),
+        "step_tflop": flops / 1e12,
+    }
+    if clk:
+        line["clocks"] = clk
+    if world == 1 and not args.no_cpu_baseline:
+        rate, _, ctoks, cores = c2_cpu_rate()
+        line["cpu_baseline"] = {"value": rate, "unit": C2_UNIT, "cores": cores, "kind": "port",
+                                "sample": f"one C2 batch ({C2_CPU_SEQS} sequences, {ctoks} tokens), fp32 torch CPU "
+                                          f"restatement, one sequence at a time, mean of {C2_CPU_PASSES} passes"}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
-    if args.impl == "reference":
+    if args.config == "c2":
+        if args.impl == "reference":
+            run_c2_reference(args)
+        else:
+            run_c2(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -93,9 +93,13 @@ enum {
                           stride ld_aux) */
   SJ_EPI_SWIGLU = 3,   /* C = round(acc) (gate/up interleaved by 16 columns, bf16);
                           aux = silu(g)*u  [M, N/2] bf16 with row stride ld_aux */
-  SJ_EPI_ROPE = 4      /* C = RoPE(acc) on columns < rope_cols (head dim 64, pairs 2i,2i+1,
+  SJ_EPI_ROPE = 4,     /* C = RoPE(acc) on columns < rope_cols (head dim 64, pairs 2i,2i+1,
                           position = row mod rope_t), bf16; aux = the sj_rope_table of rope_t
                           positions (or null: angles evaluated inline from rope_theta) */
+  /* sj_gemm_bias only (f32 bias [N]): */
+  SJ_EPI_BIAS = 5,          /* C = alpha*acc + bias                        (C bf16 or f32) */
+  SJ_EPI_BIAS_GELU = 6,     /* C = gelu(alpha*acc + bias), erf GELU         (C bf16 or f32) */
+  SJ_EPI_BIAS_RESIDUAL = 7  /* C = aux + alpha*acc + bias (aux same dtype as C, row stride ld_aux) */
 };
 /* table[p*hd/2 + i] = (cos, sin) of (p + offset) * exp((-2 i / hd) * ln theta) for p < t, in f32 as
  * the reference's rope kernel evaluates it (python/sejong_kernels/ops/kernels.py:103-113).
@@ -114,6 +118,14 @@ int sj_rope_table(float* table, int t, int head_dim, int offset, float theta, vo
 int sj_gemm(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc, int c_dtype,
             int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux, int rope_cols, int rope_t,
             float rope_theta, int split_k, void* stream);
+/* sj_gemm with a bias epilogue: the reference's `linear` (x W^T then Engine::bias_add, crates/
+ * sejong-model/src/native/bert.rs:335-347; common.py:27-30), optionally followed by Engine::gelu
+ * (crates/sejong-gpu/src/lib.rs:985-994; kernels.py:227-232) or by the residual add of the post-LN
+ * block (bert.rs:393-406).  epilogue: SJ_EPI_BIAS, SJ_EPI_BIAS_GELU or SJ_EPI_BIAS_RESIDUAL; bias
+ * f32 [N], 16-byte aligned. */
+int sj_gemm_bias(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
+                 int c_dtype, int m, int n, int k, int epilogue, float alpha, const float* bias, void* aux,
+                 int ld_aux, void* stream);
 
 /* ------------------------------------------------------------------ normalisation, embedding, elementwise */
 /* Engine::norm / rmsnorm (crates/sejong-gpu/src/lib.rs:688-699; kernels.py:54-61).
@@ -192,6 +204,28 @@ int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* 
                     const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk, int lddk, void* dv,
                     int lddv, float* workspace, int batch, int t, int hq, int hk, int head_dim, int window,
                     float rope_theta, const float* rope_table, void* stream);
+
+/* ------------------------------------------------------------------ BERT encoder (MiniLM) forward */
+/* BertEncoder::hidden (crates/sejong-model/src/native/bert.rs:360-411) on a batch of sequences packed
+ * row after row: sequence s owns rows [cu_seqlens[s], cu_seqlens[s+1]), so nothing is padded and
+ * each sequence attends to its own keys only, as the reference's one-sequence-at-a-time loop does.
+ * Position of a row = its index inside its sequence; token types are 0. */
+/* x = LayerNorm(word[id] + position[pos] + type0) (bert.rs:364-385, common.py:6-14).  Tables f32
+ * row-major [vocab,d], [max_position,d], type0 [d]; x f32 [rows,d] and optional x_bf16 [rows,d].
+ * d a multiple of 128 up to 1024.  An id or position out of range is read as row 0 and raises
+ * SJ_DEV_BAD_INDEX in the device error word. */
+int sj_bert_embed(const int32_t* ids, const int32_t* cu_seqlens, int batch, const float* word, int vocab,
+                  const float* position, int max_position, const float* type0, const float* ln_w, const float* ln_b,
+                  float eps, float* x, void* x_bf16, int rows, int d, void* stream);
+/* Engine::layer_norm (crates/sejong-gpu/src/common_ops.rs:4-17; common.py:6-14): per row mean,
+ * centred variance, y = (x - mean) / sqrt(var + eps) * w + b.  x, y f32 [rows,d]; y_bf16 optional. */
+int sj_layernorm(const float* x, const float* w, const float* b, float eps, float* y, void* y_bf16, int rows, int d,
+                 void* stream);
+/* Engine::attention_mode(.., causal = false) (crates/sejong-gpu/src/lib.rs:771-815; kernels.py:115-136)
+ * per packed sequence: qkv bf16 rows [q | k | v] (heads*head_dim columns each, row stride ldqkv),
+ * out bf16 [rows, heads*head_dim] (ldo).  head_dim 32, sequences of at most 128 rows. */
+int sj_bert_attention(const void* qkv, int ldqkv, const int32_t* cu_seqlens, int batch, int max_len, int heads,
+                      int head_dim, void* out, int ldo, void* stream);
 
 /* ------------------------------------------------------------------ optimizer */
 /* FP64 sum of squares of a flat f32 buffer into `partials` (f64, sj_sumsq_partials(n) entries):

@@ -27,6 +27,12 @@ SIGNATURES = {
     "sj_corpus_batch": (c_int, [c_void_p, c_size_t, c_u64p, c_int, c_int, c_void_p, c_void_p]),
     "sj_gemm": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
                         c_int, c_float, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p]),
+    "sj_gemm_bias": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int,
+                             c_int, c_int, c_float, c_void_p, c_void_p, c_int, c_void_p]),
+    "sj_bert_embed": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                              c_void_p, c_float, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "sj_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "sj_bert_attention": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
     "sj_rmsnorm_fwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
     "sj_rmsnorm_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_int, c_int, c_void_p]),
@@ -77,7 +83,7 @@ SIGNATURES = {
 # status codes (include/sejong.h)
 SJ_OK, SJ_ERR_SHAPE, SJ_ERR_CAPACITY, SJ_ERR_CUDA, SJ_ERR_NCCL, SJ_ERR_TIMEOUT, SJ_ERR_ARGUMENT, SJ_ERR_UNSUPPORTED = range(8)
 SJ_F32, SJ_F64, SJ_F16, SJ_I32, SJ_BF16 = range(5)
-EPI_STORE, EPI_ACCUM, EPI_RESIDUAL, EPI_SWIGLU, EPI_ROPE = range(5)
+EPI_STORE, EPI_ACCUM, EPI_RESIDUAL, EPI_SWIGLU, EPI_ROPE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RESIDUAL = range(8)
 
 
 class SejongError(RuntimeError):

@@ -36,6 +36,7 @@ struct GemmParams {
   int ld_aux;
   int rope_cols, rope_t;
   float rope_log_theta;
+  const float* bias;  // [N] f32 (SJ_EPI_BIAS*), else null
 };
 
 constexpr int kBM = 128;
@@ -67,6 +68,8 @@ SJ_DEVICE void tma_reduce_add_2d(const CUtensorMap* map, const void* smem, int x
                "r"(smem_u32(smem)), "r"(x), "r"(y)
                : "memory");
 }
+// erf GELU, kernels.py:227-232: 0.5 x (1 + erf(x / sqrt 2))
+SJ_DEVICE float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f)); }
 SJ_DEVICE float tanh_approx(float x) {
   float y;
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -240,8 +243,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;           // takes column units c with c % 2 == half
     uint8_t* my_c = staging_c + ew * 4096;  // one 32 x 128 B slab per warp
     uint8_t* my_h = staging_h + ew * 2048;
-    const bool residual = p.epilogue == SJ_EPI_RESIDUAL;
+    const bool residual = p.epilogue == SJ_EPI_RESIDUAL || p.epilogue == SJ_EPI_BIAS_RESIDUAL;
     const bool rope = p.epilogue == SJ_EPI_ROPE;
+    const bool gelu = p.epilogue == SJ_EPI_BIAS_GELU;
+    const float* bias = p.bias;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const int mb = (tile % tiles_mn) / p.n_tiles;
@@ -292,6 +297,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * p.alpha);
+            if (bias != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float x = __uint_as_float(r[j]) + (col0 + j < p.N ? bias[col0 + j] : 0.f);
+                if (gelu) x = gelu_erf(x);
+                r[j] = __float_as_uint(x);
+              }
+            }
             if (residual && row_ok) {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
@@ -389,6 +402,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               float v[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+              if (bias != nullptr) {
+                const int cb = col0 + 32 * hb;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  v[j] += cb + j < p.N ? bias[cb + j] : 0.f;
+                  if (gelu) v[j] = gelu_erf(v[j]);
+                }
+              }
               uint32_t w[16];
               if (swiglu) {
                 // columns come as blocks of 16 gate then the same 16 up features; g and u are
@@ -526,10 +547,11 @@ static int dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap* maps, const 
 
 }  // namespace sj
 
-extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
-                       int c_dtype, int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux,
-                       int rope_cols, int rope_t, float rope_theta, int split_k, void* stream) {
-  using namespace sj;
+namespace sj {
+
+static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
+                     int c_dtype, int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux,
+                     int rope_cols, int rope_t, float rope_theta, int split_k, const float* bias, void* stream) {
   if (m <= 0 || n <= 0 || k <= 0) return fail(SJ_ERR_SHAPE, "sj_gemm: empty problem %dx%dx%d", m, n, k);
   if (!a || !b || !c) return fail(SJ_ERR_ARGUMENT, "sj_gemm: null operand");
   if (!aligned16(a) || !aligned16(b) || !aligned16(c))
@@ -560,6 +582,14 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
           (aux && !aligned16(aux)))
         return fail(SJ_ERR_ARGUMENT,
                     "sj_gemm: ROPE needs bf16 C, rope_t > 0, rope_cols %% 64 == 0 and a table or theta");
+      break;
+    case SJ_EPI_BIAS:
+    case SJ_EPI_BIAS_GELU:
+      if (!bias || !aligned16(bias)) return fail(SJ_ERR_ARGUMENT, "sj_gemm_bias: a 16-byte aligned bias is required");
+      break;
+    case SJ_EPI_BIAS_RESIDUAL:
+      if (!bias || !aligned16(bias) || !aux || !aligned16(aux) || (ld_aux % 8))
+        return fail(SJ_ERR_ARGUMENT, "sj_gemm_bias: BIAS_RESIDUAL needs an aligned bias and aux (same dtype as C)");
       break;
     default:
       return fail(SJ_ERR_ARGUMENT, "sj_gemm: unknown epilogue %d", epilogue);
@@ -608,7 +638,7 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
     // its BN / 64 heads.
     const double weight[3] = {0.8, 0.83, 1.0};
     const int c_bytes = c_dtype == SJ_F32 ? 4 : 2;
-    const double col_bytes = epilogue == SJ_EPI_RESIDUAL ? 2.0 * c_bytes
+    const double col_bytes = (epilogue == SJ_EPI_RESIDUAL || epilogue == SJ_EPI_BIAS_RESIDUAL) ? 2.0 * c_bytes
                              : epilogue == SJ_EPI_SWIGLU ? 3.0
                                                          : static_cast<double>(c_bytes);
     double best = 1e30;
@@ -681,6 +711,7 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   p.rope_cols = rope_cols;
   p.rope_t = rope_t > 0 ? rope_t : 1;
   p.rope_log_theta = rope_theta > 0.f ? logf(rope_theta) : 0.f;
+  p.bias = bias;
   const int total = m_tiles * n_tiles * splits;
   const int grid = std::min(total, sms);
   const bool a_mn = a_trans != 0;   // A stored [K, M]
@@ -688,4 +719,24 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
   if (bn == 256) return dispatch_majors<256>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
   if (bn == 192) return dispatch_majors<192>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
   return dispatch_majors<128>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
+}
+
+}  // namespace sj
+
+extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
+                       int c_dtype, int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux,
+                       int rope_cols, int rope_t, float rope_theta, int split_k, void* stream) {
+  if (epilogue >= SJ_EPI_BIAS && epilogue <= SJ_EPI_BIAS_RESIDUAL)
+    return sj::fail(SJ_ERR_ARGUMENT, "sj_gemm: bias epilogues go through sj_gemm_bias");
+  return sj::gemm_impl(a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epilogue, alpha, aux, ld_aux,
+                       rope_cols, rope_t, rope_theta, split_k, nullptr, stream);
+}
+
+extern "C" int sj_gemm_bias(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c,
+                            int ldc, int c_dtype, int m, int n, int k, int epilogue, float alpha, const float* bias,
+                            void* aux, int ld_aux, void* stream) {
+  if (epilogue < SJ_EPI_BIAS || epilogue > SJ_EPI_BIAS_RESIDUAL)
+    return sj::fail(SJ_ERR_ARGUMENT, "sj_gemm_bias: epilogue %d is not a bias epilogue", epilogue);
+  return sj::gemm_impl(a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epilogue, alpha, aux, ld_aux, 0,
+                       0, 0.f, 0, bias, stream);
 }
