@@ -205,6 +205,51 @@ int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* 
                     int lddv, float* workspace, int batch, int t, int hq, int hk, int head_dim, int window,
                     float rope_theta, const float* rope_table, void* stream);
 
+/* Grouped GEMM over device-side groups (the experts of an MoE layer in one launch, without reading
+ * the expert counts back to the host as Engine::expert_routes does, hierarchy_ops.rs:332-378).
+ * group_rows: device int32 [groups + 1] row offsets, each a multiple of 128 (sj_route_pack).
+ *   group_mode 1 (grouped rows): A [m, k] and C [m, n] are packed by group, m the row capacity (a
+ *     multiple of 128); rows [group_rows[g], group_rows[g+1]) use group g's B, stored as the g-th
+ *     block of b_group_rows rows of B (b_group_rows = k for B [k, n], n for b_trans B [n, k]).
+ *     Epilogue SJ_EPI_STORE or SJ_EPI_SWIGLU.
+ *   group_mode 2 (grouped reduction): C_g [m, n] += A_g^T B_g over the packed rows [group_rows[g],
+ *     group_rows[g+1]) of A (a_trans: stored [k, m]) and B ([k, n]); C_g is the g-th block of
+ *     c_group_rows rows of C (f32).  Epilogue SJ_EPI_ACCUM.
+ * groups <= 63. */
+int sj_gemm_grouped(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
+                    int c_dtype, int m, int n, int k, int epilogue, void* aux, int ld_aux, int groups,
+                    const int32_t* group_rows, int group_mode, int b_group_rows, int c_group_rows, void* stream);
+
+/* ------------------------------------------------------------------ mixture of experts */
+/* The MoE FFN of a block (crates/sejong-model/src/architecture.rs:229-241): router GEMM, then
+ *   sj_route_topk      Engine::route_topk (hierarchy_ops.rs:280-295; hierarchy.py:174-190): softmax over
+ *                      the experts; top-k by logit, lowest index on ties; gate = softmax probability.
+ *                      logits f32 [rows, ld]; ids int32 [rows, k]; gates f32 [rows, k].  experts <= 32.
+ *   sj_route_pack      Engine::expert_routes (hierarchy_ops.rs:332-378; hierarchy.py:211-225) on the
+ *                      device: group_rows [experts + 1] (each expert's packed rows padded to 128),
+ *                      pos [rows*k] (packed row of each routed slot row*k + j), row_slot [cap] (slot of
+ *                      each packed row, -1 for padding); inside an expert, slots in increasing order.
+ *                      cap >= sj_moe_capacity(rows, k, experts).
+ *   sj_moe_dispatch    A[r] = z[row_slot[r] / k] (bf16, 0 for padding): the per-expert gather.
+ *   sj_moe_combine     y = x + sum_j gates[:, j] out[pos[:, j]] (Engine::expert_combine,
+ *                      hierarchy_ops.rs:380-419, and the block's residual add); out bf16 [cap, d], x, y f32.
+ * and the backward: sj_moe_combine_bwd (Engine::expert_combine_backward, hierarchy_ops.rs:421-454:
+ * d_out[r] = gate * dy[t], d_gates[slot] = <out[r], dy[t]>), sj_route_topk_bwd (route_topk_backward,
+ * hierarchy_ops.rs:297-330: dlogits = p (dy_selected - sum gate dy), bf16 [rows, ldd]) and
+ * sj_moe_dispatch_bwd (dz[t] = sum_j dA[pos[t, j]], f32). */
+int sj_moe_capacity(int rows, int k, int experts);
+int sj_route_topk(const float* logits, int ld, int rows, int experts, int k, int32_t* ids, float* gates, void* stream);
+int sj_route_pack(const int32_t* ids, int rows, int experts, int k, int32_t* group_rows, int32_t* pos,
+                  int32_t* row_slot, int cap, void* stream);
+int sj_moe_dispatch(const void* z, int ldz, const int32_t* row_slot, int cap, int k, int d, void* a, void* stream);
+int sj_moe_combine(const void* out, const int32_t* pos, const float* gates, const float* x, float* y, int rows, int k,
+                   int d, void* stream);
+int sj_moe_combine_bwd(const void* out, const int32_t* row_slot, const float* gates, const float* dy, void* d_out,
+                       float* d_gates, int cap, int k, int d, void* stream);
+int sj_route_topk_bwd(const float* logits, int ld, const int32_t* ids, const float* gates, const float* d_gates,
+                      void* dlogits, int ldd, int rows, int experts, int k, void* stream);
+int sj_moe_dispatch_bwd(const float* da, const int32_t* pos, float* dz, int ldz, int rows, int k, int d, void* stream);
+
 /* ------------------------------------------------------------------ BERT encoder (MiniLM) forward */
 /* BertEncoder::hidden (crates/sejong-model/src/native/bert.rs:360-411) on a batch of sequences packed
  * row after row: sequence s owns rows [cu_seqlens[s], cu_seqlens[s+1]), so nothing is padded and

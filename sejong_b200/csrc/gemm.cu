@@ -37,6 +37,14 @@ struct GemmParams {
   int rope_cols, rope_t;
   float rope_log_theta;
   const float* bias;  // [N] f32 (SJ_EPI_BIAS*), else null
+  // Grouped products (one launch over all groups, e.g. the experts of an MoE layer); group_rows
+  // is a device array [groups + 1] of row offsets, each a multiple of 128:
+  //   group_mode 1 (grouped rows): the rows of A and C are packed by group; rows [group_rows[g],
+  //     group_rows[g+1]) use B rows offset by g * b_group_rows (B's stored outer dimension);
+  //   group_mode 2 (grouped reduction): C_g (rows offset by g * c_group_rows) = A_g^T B_g over
+  //     the reduction rows [group_rows[g], group_rows[g+1]).
+  const int* group_rows;
+  int groups, group_mode, b_group_rows, c_group_rows;
 };
 
 constexpr int kBM = 128;
@@ -46,7 +54,8 @@ constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kSmemLimit = 232448;          // 227 KB: the sm_100 per-block opt-in maximum
 constexpr int kStagingC = kEpilogueWarps * 4096;  // one 32 rows x 128 B slab per epilogue warp
 constexpr int kStagingH = kEpilogueWarps * 2048;  // SwiGLU h output: 32 rows x 64 B per warp
-constexpr int kBarrierBytes = 256;
+constexpr int kBarrierBytes = 512;  // barriers, then (grouped products) the group offsets
+constexpr int kMaxGroups = 63;
 
 template <int BN>
 struct GemmCfg {
@@ -108,6 +117,45 @@ SJ_DEVICE void stage_row64(uint8_t* buf, int lane, const uint32_t (&w)[16]) {
         make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
 }
 
+// One output tile: its rows / columns, reduction k-blocks, and the outer-coordinate offsets of B
+// and C (grouped products).
+struct Unit {
+  int mb, nb, kb_begin, kb_end, b_off, c_off;
+};
+SJ_DEVICE Unit unit_of(const GemmParams& p, const int* grp, int tile) {
+  Unit u;
+  const int tiles_mn = p.m_tiles * p.n_tiles;
+  if (p.group_mode == 2) {
+    const int g = tile / tiles_mn;
+    const int rest = tile % tiles_mn;
+    u.mb = rest / p.n_tiles;
+    u.nb = rest % p.n_tiles;
+    u.kb_begin = grp[g] / kBK;
+    u.kb_end = grp[g + 1] / kBK;
+    u.b_off = 0;
+    u.c_off = g * p.c_group_rows;
+  } else if (p.group_mode == 1) {
+    u.mb = tile / p.n_tiles;
+    u.nb = tile % p.n_tiles;
+    const int m0 = u.mb * kBM;
+    int g = 0;
+    while (g + 1 < p.groups && grp[g + 1] <= m0) ++g;
+    u.kb_begin = 0;
+    u.kb_end = p.kb_total;
+    u.b_off = g * p.b_group_rows;
+    u.c_off = 0;
+  } else {
+    const int ks = tile / tiles_mn;
+    u.mb = (tile % tiles_mn) / p.n_tiles;
+    u.nb = tile % p.n_tiles;
+    u.kb_begin = ks * p.kb_per_split;
+    u.kb_end = min(u.kb_begin + p.kb_per_split, p.kb_total);
+    u.b_off = 0;
+    u.c_off = 0;
+  }
+  return u;
+}
+
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -129,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* grp = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(full) + 256);  // [groups + 1]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -158,22 +207,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   pdl_wait();  // operands may come from the previous kernel
+  if (p.group_mode != 0) {
+    for (int i = threadIdx.x; i <= p.groups; i += blockDim.x) grp[i] = p.group_rows[i];
+    __syncthreads();
+  }
   const uint32_t tmem_base = *tmem_slot;
-  const int total_tiles = tiles_mn * p.splits;
   // work unit -> (split, m tile, n tile); the split index is slowest so that concurrently running
-  // CTAs share the K range of their A and B tiles in L2.
+  // CTAs share the K range of their A and B tiles in L2.  Grouped rows: the tile count follows
+  // the device-side group offsets.
+  const int total_tiles = p.group_mode == 1   ? (grp[p.groups] / kBM) * p.n_tiles
+                          : p.group_mode == 2 ? p.groups * tiles_mn
+                                              : tiles_mn * p.splits;
 
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
       for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
-        const int ks = tile / tiles_mn;
-        const int mb = (tile % tiles_mn) / p.n_tiles;
-        const int nb = tile % p.n_tiles;
-        const int m0 = mb * kBM, n0 = nb * BN;
-        const int kb_begin = ks * p.kb_per_split;
-        const int kb_end = min(kb_begin + p.kb_per_split, p.kb_total);
-        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        const Unit u = unit_of(p, grp, tile);
+        const int m0 = u.mb * kBM, n0 = u.nb * BN;
+        for (int kb = u.kb_begin; kb < u.kb_end; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t round = static_cast<uint32_t>(it / stages);
           if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag, SJ_DEV_GEMM_PRODUCER_WAIT)) break;
@@ -189,9 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (B_MN) {
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c) tma_load_2d(sb + c * 8192, &map_b, &full[s], n0 + 64 * c, k0);
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(sb + c * 8192, &map_b, &full[s], n0 + 64 * c, k0 + u.b_off);
           } else {
-            tma_load_2d(sb, &map_b, &full[s], k0, n0);
+            tma_load_2d(sb, &map_b, &full[s], k0, n0 + u.b_off);
           }
         }
       }
@@ -204,9 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0, local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++local) {
-        const int ks = tile / tiles_mn;
-        const int kb_begin = ks * p.kb_per_split;
-        const int kb_end = min(kb_begin + p.kb_per_split, p.kb_total);
+        const Unit u = unit_of(p, grp, tile);
+        const int kb_begin = u.kb_begin, kb_end = u.kb_end;
         const int buf = local & 1;
         const uint32_t use = static_cast<uint32_t>(local >> 1);
         if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, SJ_DEV_GEMM_MMA_WAIT)) break;
@@ -249,8 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* bias = p.bias;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
-      const int mb = (tile % tiles_mn) / p.n_tiles;
-      const int nb = tile % p.n_tiles;
+      const Unit u = unit_of(p, grp, tile);
+      const int mb = u.mb, nb = u.nb;
+      const bool empty_unit = u.kb_end <= u.kb_begin;  // a group without reduction rows adds nothing
+      const int c_off = u.c_off;
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
       const int r0 = mb * kBM + quarter * 32;
@@ -318,11 +372,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
-              if (r0 < p.M) {  // boxes are clipped at M and N; a slab wholly past M is not issued
+              if (r0 < p.M && !empty_unit) {  // boxes are clipped at M and N; a slab wholly past M is not issued
                 if (p.epilogue == SJ_EPI_ACCUM)
-                  tma_reduce_add_2d(&map_c, sbuf, col0, r0);
+                  tma_reduce_add_2d(&map_c, sbuf, col0, r0 + c_off);
                 else
-                  tma_store_2d(&map_c, sbuf, col0, r0);
+                  tma_store_2d(&map_c, sbuf, col0, r0 + c_off);
               }
               bulk_commit();
             }
@@ -549,9 +603,15 @@ static int dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap* maps, const 
 
 namespace sj {
 
+struct Grouping {
+  const int* rows = nullptr;  // device [groups + 1]
+  int groups = 0, mode = 0, b_rows = 0, c_rows = 0;
+};
+
 static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
                      int c_dtype, int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux,
-                     int rope_cols, int rope_t, float rope_theta, int split_k, const float* bias, void* stream) {
+                     int rope_cols, int rope_t, float rope_theta, int split_k, const float* bias, void* stream,
+                     const Grouping& grouping = Grouping()) {
   if (m <= 0 || n <= 0 || k <= 0) return fail(SJ_ERR_SHAPE, "sj_gemm: empty problem %dx%dx%d", m, n, k);
   if (!a || !b || !c) return fail(SJ_ERR_ARGUMENT, "sj_gemm: null operand");
   if (!aligned16(a) || !aligned16(b) || !aligned16(c))
@@ -656,6 +716,7 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
       }
     }
   }
+  if (grouping.mode != 0) splits = 1;
   const int n_tiles = (n + bn - 1) / bn;
   const int kb_per_split = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per_split - 1) / kb_per_split;  // no empty split
@@ -675,12 +736,16 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
     rc = bf16_map(&maps[0], a, static_cast<uint64_t>(m), static_cast<uint64_t>(k), lda, 64, 64);
   if (rc) return rc;
   if (b_trans)
-    rc = bf16_map(&maps[1], b, static_cast<uint64_t>(k), static_cast<uint64_t>(n), ldb, 64, static_cast<uint32_t>(bn));
+    rc = bf16_map(&maps[1], b, static_cast<uint64_t>(k),
+                  static_cast<uint64_t>(grouping.mode == 1 ? grouping.groups * grouping.b_rows : n), ldb, 64,
+                  static_cast<uint32_t>(bn));
   else
-    rc = bf16_map(&maps[1], b, static_cast<uint64_t>(n), static_cast<uint64_t>(k), ldb, 64, 64);
+    rc = bf16_map(&maps[1], b, static_cast<uint64_t>(n),
+                  static_cast<uint64_t>(grouping.mode == 1 ? grouping.groups * grouping.b_rows : k), ldb, 64, 64);
   if (rc) return rc;
   if (c_dtype == SJ_F32)
-    rc = make_map(&maps[2], c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, static_cast<uint64_t>(n), static_cast<uint64_t>(m),
+    rc = make_map(&maps[2], c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, static_cast<uint64_t>(n),
+                  static_cast<uint64_t>(grouping.mode == 2 ? grouping.groups * grouping.c_rows : m),
                   ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   else
     rc = make_map(&maps[2], c, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(m),
@@ -712,7 +777,12 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
   p.rope_t = rope_t > 0 ? rope_t : 1;
   p.rope_log_theta = rope_theta > 0.f ? logf(rope_theta) : 0.f;
   p.bias = bias;
-  const int total = m_tiles * n_tiles * splits;
+  p.group_rows = grouping.rows;
+  p.groups = grouping.groups;
+  p.group_mode = grouping.mode;
+  p.b_group_rows = grouping.b_rows;
+  p.c_group_rows = grouping.c_rows;
+  const int total = m_tiles * n_tiles * splits * (grouping.mode == 2 ? grouping.groups : 1);
   const int grid = std::min(total, sms);
   const bool a_mn = a_trans != 0;   // A stored [K, M]
   const bool b_mn = b_trans == 0;   // B stored [K, N]
@@ -730,6 +800,37 @@ extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int l
     return sj::fail(SJ_ERR_ARGUMENT, "sj_gemm: bias epilogues go through sj_gemm_bias");
   return sj::gemm_impl(a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epilogue, alpha, aux, ld_aux,
                        rope_cols, rope_t, rope_theta, split_k, nullptr, stream);
+}
+
+extern "C" int sj_gemm_grouped(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c,
+                               int ldc, int c_dtype, int m, int n, int k, int epilogue, void* aux, int ld_aux,
+                               int groups, const int32_t* group_rows, int group_mode, int b_group_rows,
+                               int c_group_rows, void* stream) {
+  using namespace sj;
+  if (groups <= 0 || groups > kMaxGroups || !group_rows)
+    return fail(SJ_ERR_ARGUMENT, "sj_gemm_grouped: 1..%d groups and their device row offsets required", kMaxGroups);
+  Grouping gp;
+  gp.rows = group_rows;
+  gp.groups = groups;
+  gp.mode = group_mode;
+  gp.b_rows = b_group_rows;
+  gp.c_rows = c_group_rows;
+  if (group_mode == 1) {
+    if (epilogue != SJ_EPI_STORE && epilogue != SJ_EPI_SWIGLU)
+      return fail(SJ_ERR_ARGUMENT, "sj_gemm_grouped: grouped rows take STORE or SWIGLU");
+    if (m % kBM) return fail(SJ_ERR_SHAPE, "sj_gemm_grouped: row capacity %d must be a multiple of 128", m);
+    if (b_group_rows != (b_trans ? n : k))
+      return fail(SJ_ERR_SHAPE, "sj_gemm_grouped: b_group_rows must be the stored rows of one group's B");
+  } else if (group_mode == 2) {
+    if (epilogue != SJ_EPI_ACCUM || c_dtype != SJ_F32 || !a_trans || b_trans)
+      return fail(SJ_ERR_ARGUMENT, "sj_gemm_grouped: grouped reduction is C_g += A_g^T B_g (f32 ACCUM)");
+    if (k % kBM) return fail(SJ_ERR_SHAPE, "sj_gemm_grouped: reduction capacity %d must be a multiple of 128", k);
+    if (c_group_rows < m) return fail(SJ_ERR_SHAPE, "sj_gemm_grouped: c_group_rows below the rows of one group's C");
+  } else {
+    return fail(SJ_ERR_ARGUMENT, "sj_gemm_grouped: group_mode must be 1 (rows) or 2 (reduction)");
+  }
+  return gemm_impl(a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epilogue, 1.0f, aux, ld_aux, 0, 0, 0.f,
+                   1, nullptr, stream, gp);
 }
 
 extern "C" int sj_gemm_bias(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c,

@@ -180,6 +180,11 @@ def _deinterleave_cols(gu):
     return x[:, :, 0, :].reshape(d, f2 // 2), x[:, :, 1, :].reshape(d, f2 // 2)
 
 
+def router_pad(experts):
+    """Columns of a router weight in the flat buffers: the expert count rounded up to 8."""
+    return (experts + 7) // 8 * 8
+
+
 class FlatLayout:
     """Placement of every (fused) parameter in the flat master / gradient / moment buffers."""
 
@@ -206,8 +211,27 @@ class FlatLayout:
                 fused_done.add(f"{p}.up")
             elif name == "output":
                 entries.append(("output", (shape[0], VOCAB_PAD), True, ("output",)))
+            elif name.endswith(".router"):  # columns padded to 8 (16-byte rows for TMA), padding zero
+                entries.append((name, (shape[0], router_pad(shape[1])), True, (name,)))
             else:
                 entries.append((name, shape, (not norm) and len(shape) > 1, (name,)))
+        # the experts of an MoE layer: all fused gate/up matrices, then all down matrices, each run
+        # contiguous, so that a grouped GEMM reads expert g's matrix as the g-th block of one stack
+        grouped = []
+        i = 0
+        while i < len(entries):
+            if ".experts." not in entries[i][0]:
+                grouped.append(entries[i])
+                i += 1
+                continue
+            layer = entries[i][0].split(".experts.")[0]
+            j = i
+            while j < len(entries) and entries[j][0].startswith(layer + ".experts."):
+                j += 1
+            run = entries[i:j]
+            grouped += [e for e in run if e[0].endswith(".gate_up")] + [e for e in run if e[0].endswith(".down")]
+            i = j
+        entries = grouped
         ordered = [e for e in entries if e[2]] + [e for e in entries if not e[2]]
         self.entries = {}
         off = 0
@@ -234,6 +258,9 @@ class FlatLayout:
             elif e.name == "output":
                 v = np.zeros(e.shape, dtype=np.float32)
                 v[:, :VOCAB] = params["output"]
+            elif e.name.endswith(".router"):
+                v = np.zeros(e.shape, dtype=np.float32)
+                v[:, :params[e.name].shape[1]] = params[e.name]
             else:
                 v = params[e.name]
             flat[e.offset:e.offset + e.size] = np.asarray(v, dtype=np.float32).reshape(-1)
@@ -258,6 +285,8 @@ class FlatLayout:
                 out[e.parts[1]] = u.copy()
             elif e.name == "output":
                 out["output"] = v[:, :VOCAB].copy()
+            elif e.name.endswith(".router"):
+                out[e.name] = v[:, :ref_shapes[e.name][1]].copy()
             else:
                 out[e.name] = v.copy()
         return out

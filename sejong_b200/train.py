@@ -35,7 +35,8 @@ import torch
 
 from . import _lib, distributed, param_vjp
 from ._lib import (EPI_ACCUM, EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call)
-from .model import HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage, reference_layout
+from .model import (HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage,
+                    reference_layout, router_pad)
 
 
 @dataclass
@@ -92,6 +93,22 @@ class _StageRun:
         self.dqkv = e(n, cq)
         self.delta = e(_lib.load().sj_attn_workspace(batch, seq, stage.heads, stage.kv_heads), dt=f32)
         self.partials = e(_lib.load().sj_rmsnorm_workspace(n, d), dt=f32)
+        self.moe = stage.experts is not None
+        if self.moe:
+            # MoE FFN (architecture.rs:229-241): routing and the expert rows packed per expert, each
+            # expert's segment padded to 128 rows (sj_route_pack); kept per layer for the backward
+            ex = stage.experts
+            cap = _lib.load().sj_moe_capacity(n, ex.top_k, ex.count)
+            fe, i32 = ex.ffn_width, torch.int32
+            self.cap = cap
+            for L in self.layers:
+                L.update(logits=e(n, router_pad(ex.count), dt=f32), ids=e(n, ex.top_k, dt=i32), gates=e(n, ex.top_k, dt=f32),
+                         group_rows=e(ex.count + 1, dt=i32), pos=e(n * ex.top_k, dt=i32), row_slot=e(cap, dt=i32),
+                         a=e(cap, d), gu=e(cap, 2 * fe), h=e(cap, fe), out=e(cap, d))
+            self.d_out, self.d_gates = e(cap, d), e(n * ex.top_k, dt=f32)
+            self.dh_packed, self.dgu_packed = e(cap, fe), e(cap, 2 * fe)
+            self.da = e(cap, d, dt=f32)
+            self.dlogits = e(n, router_pad(ex.count))
 
 
 class ByteTrainer:
@@ -335,6 +352,9 @@ class ByteTrainer:
         self._gemm(_ptr(a["o"]), d, 0, self.wb_ptr(f"{p}.attention_output"), d, 0, _ptr(a["x1"]), d, SJ_F32, n, d, d,
                    EPI_RESIDUAL, aux=_ptr(x), ld_aux=d)
         self._norm(a["x1"], f"{p}.ffn_norm", a["z2"], a["inv2"], n, d)
+        if run.moe:
+            self._moe_fwd(run, a, p, xn)
+            return
         self._gemm(_ptr(a["z2"]), d, 0, self.wb_ptr(f"{p}.gate_up"), 2 * f, 0, _ptr(a["gu"]), 2 * f, SJ_BF16, n,
                    2 * f, d, EPI_SWIGLU, aux=_ptr(a["h"]), ld_aux=f)
         self._gemm(_ptr(a["h"]), f, 0, self.wb_ptr(f"{p}.down"), d, 0, _ptr(xn), d, SJ_F32, n, d, f, EPI_RESIDUAL,
@@ -347,12 +367,15 @@ class ByteTrainer:
         p = f"{s.prefix}.{i}"
         dx, dxb = run.dx, run.dxb
         # FFN: down, SwiGLU, gate/up
-        self._gemm(_ptr(a["h"]), f, 1, _ptr(dxb), d, 0, self.g_ptr(f"{p}.down"), d, SJ_F32, f, d, n, EPI_ACCUM)
-        self._gemm(_ptr(dxb), d, 0, self.wb_ptr(f"{p}.down"), d, 1, _ptr(run.dh), f, SJ_BF16, n, f, d)
-        self._call("sj_swiglu_bwd", _ptr(a["gu"]), _ptr(run.dh), _ptr(run.dgu), n, f, self.stream)
-        self._weight_grad(f"{p}.z2", a["z2"], run.dgu, f"{p}.gate_up")
-        self._gemm(_ptr(run.dgu), 2 * f, 0, self.wb_ptr(f"{p}.gate_up"), 2 * f, 1, _ptr(run.dz), d, SJ_F32, n, d,
-                   2 * f)
+        if run.moe:
+            self._moe_bwd(run, a, p)
+        else:
+            self._gemm(_ptr(a["h"]), f, 1, _ptr(dxb), d, 0, self.g_ptr(f"{p}.down"), d, SJ_F32, f, d, n, EPI_ACCUM)
+            self._gemm(_ptr(dxb), d, 0, self.wb_ptr(f"{p}.down"), d, 1, _ptr(run.dh), f, SJ_BF16, n, f, d)
+            self._call("sj_swiglu_bwd", _ptr(a["gu"]), _ptr(run.dh), _ptr(run.dgu), n, f, self.stream)
+            self._weight_grad(f"{p}.z2", a["z2"], run.dgu, f"{p}.gate_up")
+            self._gemm(_ptr(run.dgu), 2 * f, 0, self.wb_ptr(f"{p}.gate_up"), 2 * f, 1, _ptr(run.dz), d, SJ_F32, n, d,
+                       2 * f)
         self._norm_bwd(a["x1"], f"{p}.ffn_norm", a["inv2"], run.dz, dx, dxb, run.partials, n, d)
         # attention: output projection, attention, QKV
         self._gemm(_ptr(a["o"]), d, 1, _ptr(dxb), d, 0, self.g_ptr(f"{p}.attention_output"), d, SJ_F32, d, d, n,
@@ -367,6 +390,58 @@ class ByteTrainer:
         self._weight_grad(f"{p}.z1", a["z1"], dqkv, f"{p}.qkv")
         self._gemm(_ptr(dqkv), cq, 0, self.wb_ptr(f"{p}.qkv"), cq, 1, _ptr(run.dz), d, SJ_F32, n, d, cq)
         self._norm_bwd(run.x[i], f"{p}.attention_norm", a["inv1"], run.dz, dx, dxb, run.partials, n, d)
+
+    # ------------------------------------------------------------------ mixture of experts
+    def _gemm_grouped(self, a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epi, groups, group_rows,
+                      mode, b_rows=0, c_rows=0, aux=0, ld_aux=0):
+        self._call("sj_gemm_grouped", a, lda, a_trans, b, ldb, b_trans, c, ldc, c_dtype, m, n, k, epi, aux, ld_aux,
+                   groups, group_rows, mode, b_rows, c_rows, self.stream)
+
+    def _moe_fwd(self, run, a, p, xn):
+        """The MoE FFN of a block (architecture.rs:229-241): router logits, top-k routing, the routed
+        rows packed per expert, one grouped GEMM per projection over all experts, and the gated
+        combine with the residual add into the block output `xn`."""
+        ex = run.stage.experts
+        n, d, fe, E, k, cap = run.rows, run.stage.width, ex.ffn_width, ex.count, ex.top_k, run.cap
+        gp = _ptr(a["group_rows"])
+        ep = router_pad(E)  # router columns (and logits) padded to 8; the padding is zero and ignored
+        self._gemm(_ptr(a["z2"]), d, 0, self.wb_ptr(f"{p}.router"), ep, 0, _ptr(a["logits"]), ep, SJ_F32, n, ep, d)
+        self._call("sj_route_topk", _ptr(a["logits"]), ep, n, E, k, _ptr(a["ids"]), _ptr(a["gates"]), self.stream)
+        self._call("sj_route_pack", _ptr(a["ids"]), n, E, k, gp, _ptr(a["pos"]), _ptr(a["row_slot"]), cap, self.stream)
+        self._call("sj_moe_dispatch", _ptr(a["z2"]), d, _ptr(a["row_slot"]), cap, k, d, _ptr(a["a"]), self.stream)
+        self._gemm_grouped(_ptr(a["a"]), d, 0, self.wb_ptr(f"{p}.experts.0.gate_up"), 2 * fe, 0, _ptr(a["gu"]), 2 * fe,
+                           SJ_BF16, cap, 2 * fe, d, EPI_SWIGLU, E, gp, 1, b_rows=d, aux=_ptr(a["h"]), ld_aux=fe)
+        self._gemm_grouped(_ptr(a["h"]), fe, 0, self.wb_ptr(f"{p}.experts.0.down"), d, 0, _ptr(a["out"]), d, SJ_BF16,
+                           cap, d, fe, EPI_STORE, E, gp, 1, b_rows=fe)
+        self._call("sj_moe_combine", _ptr(a["out"]), _ptr(a["pos"]), _ptr(a["gates"]), _ptr(a["x1"]), _ptr(xn), n, k,
+                   d, self.stream)
+
+    def _moe_bwd(self, run, a, p):
+        """Backward of _moe_fwd into run.dz (the gradient at the FFN norm's output), accumulating the
+        expert and router weight gradients (graph.rs:600-624 for the routing terms)."""
+        ex = run.stage.experts
+        n, d, fe, E, k, cap = run.rows, run.stage.width, ex.ffn_width, ex.count, ex.top_k, run.cap
+        gp = _ptr(a["group_rows"])
+        gate_up, down = f"{p}.experts.0.gate_up", f"{p}.experts.0.down"
+        self._call("sj_moe_combine_bwd", _ptr(a["out"]), _ptr(a["row_slot"]), _ptr(a["gates"]), _ptr(run.dx),
+                   _ptr(run.d_out), _ptr(run.d_gates), cap, k, d, self.stream)
+        self._gemm_grouped(_ptr(a["h"]), fe, 1, _ptr(run.d_out), d, 0, self.g_ptr(down), d, SJ_F32, fe, d, cap,
+                           EPI_ACCUM, E, gp, 2, c_rows=fe)
+        self._gemm_grouped(_ptr(run.d_out), d, 0, self.wb_ptr(down), d, 1, _ptr(run.dh_packed), fe, SJ_BF16, cap, fe,
+                           d, EPI_STORE, E, gp, 1, b_rows=fe)
+        self._call("sj_swiglu_bwd", _ptr(a["gu"]), _ptr(run.dh_packed), _ptr(run.dgu_packed), cap, fe, self.stream)
+        self._gemm_grouped(_ptr(a["a"]), d, 1, _ptr(run.dgu_packed), 2 * fe, 0, self.g_ptr(gate_up), 2 * fe, SJ_F32, d,
+                           2 * fe, cap, EPI_ACCUM, E, gp, 2, c_rows=d)
+        self._gemm_grouped(_ptr(run.dgu_packed), 2 * fe, 0, self.wb_ptr(gate_up), 2 * fe, 1, _ptr(run.da), d, SJ_F32,
+                           cap, d, 2 * fe, EPI_STORE, E, gp, 1, b_rows=d)
+        self._call("sj_moe_dispatch_bwd", _ptr(run.da), _ptr(a["pos"]), _ptr(run.dz), d, n, k, d, self.stream)
+        ep = router_pad(E)
+        self._call("sj_route_topk_bwd", _ptr(a["logits"]), ep, _ptr(a["ids"]), _ptr(a["gates"]), _ptr(run.d_gates),
+                   _ptr(run.dlogits), ep, n, E, k, self.stream)
+        self._gemm(_ptr(run.dlogits), ep, 0, self.wb_ptr(f"{p}.router"), ep, 1, _ptr(run.dz), d, SJ_F32, n, d, ep,
+                   EPI_ACCUM)
+        self._gemm(_ptr(a["z2"]), d, 1, _ptr(run.dlogits), ep, 0, self.g_ptr(f"{p}.router"), ep, SJ_F32, d, ep, n,
+                   EPI_ACCUM)
 
     def _stage_fwd(self, run):
         for i in range(run.stage.layers):
@@ -630,8 +705,13 @@ class ByteTrainer:
         def stage_cost(s, rows, seq):
             nonlocal lin, att
             d, kv = s.width, s.kv_heads * HEAD_DIM
-            per = d * d + 2 * d * kv + d * d + 3 * d * s.ffn
-            lin += 2 * rows * per * s.layers
+            if s.experts is None:
+                per = d * d + 2 * d * kv + d * d + 3 * d * s.ffn
+                lin += 2 * rows * per * s.layers
+            else:  # router for every row, the chosen experts' SwiGLU FFN for every routed row
+                e = s.experts
+                per = d * d + 2 * d * kv + d * d + d * e.count
+                lin += 2 * rows * per * s.layers + 2 * rows * e.top_k * 3 * d * e.ffn_width * s.layers
             w = s.window or seq
             pairs = sum(min(q + 1, w) for q in range(seq))
             att += 4 * (rows // seq) * s.heads * HEAD_DIM * pairs * s.layers

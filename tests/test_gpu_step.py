@@ -30,9 +30,10 @@ GRAD_TOL = 2e-2
 def oracle_config(c):
     h = c.hierarchy
     oh = None if h is None else omodel.HierarchyConfig(**h.__dict__)
+    ox = None if c.experts is None else omodel.ExpertConfig(c.experts.count, c.experts.top_k, c.experts.ffn_width)
     return omodel.ModelConfig(width=c.width, layers=c.layers, heads=c.heads, ffn_width=c.ffn_width,
                               kv_heads=c.kv_heads, rope_theta=c.rope_theta, norm_epsilon=c.norm_epsilon,
-                              hierarchy=oh, seed=c.seed, init_std=c.init_std, router_std=c.router_std)
+                              hierarchy=oh, experts=ox, seed=c.seed, init_std=c.init_std, router_std=c.router_std)
 
 
 def rel(a, b):
@@ -108,6 +109,14 @@ def test_step_parity_reference_init():
     """The reference's own fan-in initialisation (global_bos = 0) through the same path."""
     c, ids, tg = make_case("small_hierarchy", 2, 128, init_std=0.0)
     run_parity(c, ids, tg, 2, 128)
+
+
+def test_step_parity_moe():
+    """MoE FFN on the global stage (the C5 block): top-2 of 4 SwiGLU experts, grouped GEMMs over the
+    packed expert rows, router gradient through the softmax top-k."""
+    from sejong_b200 import model as pm
+    c, ids, tg = make_case("small_hierarchy", 2, 512, experts=pm.ExpertConfig(4, 2, 128))
+    run_parity(c, ids, tg, 2, 512)
 
 
 def test_graph_replay_matches_eager_and_loss_decreases():
