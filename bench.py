@@ -37,7 +37,14 @@ if ROOT not in sys.path:
 METRIC = "train_bytes_per_s"
 WORKLOADS = {"c3": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
              "c4": "C4 hierarchical byte model, fwd + input VJP + parameter VJP (rank 16, fraction 0.25) + "
-                   "compact SGD lr 1e-2 (BASELINE configs[3])"}
+                   "compact SGD lr 1e-2 (BASELINE configs[3])",
+             "c5": "C5 byte MoE model, fwd+bwd+AdamW, all 8 experts of a layer on each GPU (BASELINE configs[4]; "
+                   "the expert-parallel all-to-all is not built yet)"}
+MODELS = {"c3": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
+          "c4": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
+          "c5": "byte MoE model: local d256 2+2 layers W128, global d1024 x12 HQ16/HK4, 8 SwiGLU experts of 2816 "
+                "top-2 (router N(0,0.006))"}
+SHAPES = {"c3": (8, 4096), "c4": (8, 4096), "c5": (4, 8192)}  # per-GPU batch x bytes
 UNIT = "bytes/s"
 CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ = 1, 1024
 # DRAM bytes (read + write) of all GEMM launches of one C3 step, from the ncu launch list of
@@ -52,11 +59,11 @@ def parse():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=8, help="per-GPU batch")
-    ap.add_argument("--seq", type=int, default=4096)
-    ap.add_argument("--config", choices=["c2", "c3", "c4"], default="c3",
+    ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (default: the config's)")
+    ap.add_argument("--seq", type=int, default=None, help="bytes per row (default: the config's)")
+    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5"], default="c3",
                     help="c3: AdamW (BASELINE configs[2]); c4: parameter-VJP SGD (configs[3]); "
-                         "c2: MiniLM encoder forward (configs[1])")
+                         "c2: MiniLM encoder forward (configs[1]); c5: byte MoE (configs[4])")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
     ap.add_argument("--kernel-report", default=None, help="write per-call kernel timings (JSON) to this path")
@@ -130,7 +137,7 @@ def cpu_step_rate(steps, warmup, threads=None, config="c3"):
     from oracle.rng import Rng
     if threads:
         torch.set_num_threads(threads)
-    c = omodel.config_c3()
+    c = omodel.config_c5() if config == "c5" else omodel.config_c3()
     params = omodel.initialize(c)
     corp = synthetic_corpus(1000, 1 << 20)
     rng = Rng(123)
@@ -160,6 +167,9 @@ def cpu_sample_text(steps, config="c3"):
     if config == "c4":
         return (f"C4 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
                 f"FP64 CPU fwd + input VJP + parameter VJP + compact SGD, mean of {steps} steps")
+    if config == "c5":
+        return (f"C5 architecture (8 experts, top-2), batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 4 x 8192 "
+                f"on the GPU), fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps")
     return (f"C3 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
             f"fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps")
 
@@ -202,6 +212,9 @@ def kernel_timing(trainer, report=None):
         original(name, *a)
         e.record(stream)
         flops = 2.0 * a[9] * a[10] * a[11] if name == "sj_gemm" else 0.0
+        if name == "sj_gemm_grouped":  # algorithmic rows: the routed ones, not the padded capacity
+            routed = trainer.routed_rows()
+            flops = 2.0 * a[10] * (a[11] * routed if a[17] == 1 else a[9] * routed)
         info = {"m": a[9], "n": a[10], "k": a[11], "epi": a[12], "a_t": a[2], "b_t": a[5]} if name == "sj_gemm" else {}
         records.append((name, s, e, flops, info))
 
@@ -242,7 +255,11 @@ def run_ours(args):
 
     rank, world, local, pg = distributed.init_from_env("nccl", timeout_s=300)
     torch.cuda.set_device(local)
-    cfg = pm.config_c3()
+    cfg = pm.config_c5() if args.config == "c5" else pm.config_c3()
+    if args.batch is None:
+        args.batch = SHAPES[args.config][0]
+    if args.seq is None:
+        args.seq = SHAPES[args.config][1]
     if args.config == "c4":
         from sejong_b200.param_vjp import VjpConfig
         tc = TrainConfig(sequence=args.seq, batch=args.batch, optimizer="sgd", learning_rate=1e-2, warmup_steps=0,
@@ -339,10 +356,11 @@ def run_ours(args):
     tensor_frac = step_flops / (ms / 1e3) / (pk["bf16_sustained"] * 1e12)
     roofline = None
     if fam:
-        g = fam.get("sj_gemm")
-        if g and g["ms"] > 0:
+        gs = [fam[k] for k in ("sj_gemm", "sj_gemm_grouped") if k in fam]
+        g = {"ms": sum(x["ms"] for x in gs), "flops": sum(x["flops"] for x in gs), "calls": sum(x["calls"] for x in gs)}
+        if g["ms"] > 0:
             achieved = g["flops"] / (g["ms"] / 1e3) / 1e12
-            roofline = {"bound": "tensor", "kernel": "gemm_tcgen05 (all GEMMs of one step)",
+            roofline = {"bound": "tensor", "kernel": "gemm_tcgen05 (all GEMMs of one step, grouped expert GEMMs included)",
                         "achieved": achieved, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": achieved / pk["bf16_sustained"], "peak_source": pk["source"] + " sustained bf16",
                         "traffic": NCU_GEMM_DRAM_BYTES_PER_STEP.get(args.config),
@@ -353,7 +371,7 @@ def run_ours(args):
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: Zipf(1.1) bytes from the reference Rng (seed 1000+rank); random-init N(0,0.02) weights",
         "config": {"workload": WORKLOADS[args.config],
-                   "model": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
+                   "model": MODELS[args.config],
                    "global_batch": tc.batch * world, "per_gpu_batch": tc.batch, "seq_len": tc.sequence,
                    "parallelism": f"dp{world}", "l2": "per-step working set of several GB > 126 MB L2; no flush"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * rows * 4, "d2h_bytes_per_step": 8},

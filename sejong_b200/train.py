@@ -695,6 +695,13 @@ class ByteTrainer:
         self._call("sj_device_error", ctypes.byref(code), 1, self.stream)
         return code.value
 
+    def routed_rows(self):
+        """Rows an MoE layer sends to its experts (rows x top-k of the MoE stage; 0 without experts)."""
+        for run in self.runs.values():
+            if run.moe:
+                return run.rows * run.stage.experts.top_k
+        return 0
+
     def step_flops(self):
         """Algorithmic FLOPs of one step (FMA = 2; attention 4*B*H*64*pairs fwd, 8*... bwd; no recompute)."""
         c, tc = self.c, self.tc
