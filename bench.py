@@ -38,8 +38,9 @@ METRIC = "train_bytes_per_s"
 WORKLOADS = {"c3": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
              "c4": "C4 hierarchical byte model, fwd + input VJP + parameter VJP (rank 16, fraction 0.25) + "
                    "compact SGD lr 1e-2 (BASELINE configs[3])",
-             "c5": "C5 byte MoE model, fwd+bwd+AdamW, all 8 experts of a layer on each GPU (BASELINE configs[4]; "
-                   "the expert-parallel all-to-all is not built yet)"}
+             "c5": "C5 byte MoE model, fwd+bwd+AdamW (BASELINE configs[4]): on one GPU all 8 experts of a layer "
+                   "are local; on N GPUs each owns 8/N experts and routed rows move over NVLink peer memory "
+                   "(expert parallelism), the rest is data parallel"}
 MODELS = {"c3": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
           "c4": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
           "c5": "byte MoE model: local d256 2+2 layers W128, global d1024 x12 HQ16/HK4, 8 SwiGLU experts of 2816 "
@@ -266,7 +267,10 @@ def run_ours(args):
                          steps=10000, parameter_vjp=VjpConfig())
     else:
         tc = TrainConfig(sequence=args.seq, batch=args.batch, warmup_steps=0, steps=10000)
-    trainer = ByteTrainer(cfg, tc, device=local, process_group=pg)
+    # C5 on several GPUs: the experts are sharded over the ranks (expert parallelism), the rest is
+    # data parallel
+    ep = args.config == "c5" and world > 1
+    trainer = ByteTrainer(cfg, tc, device=local, process_group=pg, expert_parallel=ep)
     rows = tc.batch * tc.sequence
     total = args.warmup + args.steps
     toks = synthetic_corpus_tokens(distributed.rank_seed(1000, rank), 1 << 22)
@@ -341,6 +345,7 @@ def run_ours(args):
     fam = {} if args.no_kernel_timing else kernel_timing(trainer, args.kernel_report if rank == 0 else None)
     if world > 1:
         trainer.release_graphs()
+    trainer.close()
 
     if rank != 0:
         if world > 1:
@@ -373,7 +378,8 @@ def run_ours(args):
         "config": {"workload": WORKLOADS[args.config],
                    "model": MODELS[args.config],
                    "global_batch": tc.batch * world, "per_gpu_batch": tc.batch, "seq_len": tc.sequence,
-                   "parallelism": f"dp{world}", "l2": "per-step working set of several GB > 126 MB L2; no flush"},
+                   "parallelism": f"dp{world}" + (f"+ep{world}" if ep else ""),
+                   "l2": "per-step working set of several GB > 126 MB L2; no flush"},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * rows * 4, "d2h_bytes_per_step": 8},
         "gpu_launches": per_step_launches * K,
         "roofline": roofline,

@@ -53,7 +53,9 @@ enum {
   SJ_DEV_GEMM_EPILOGUE_WAIT = 103,
   SJ_DEV_GEMM_DRAIN_WAIT = 104,
   SJ_DEV_ATTN_WAIT = 105,
-  SJ_DEV_BAD_INDEX = 110
+  SJ_DEV_BAD_INDEX = 110,
+  SJ_DEV_EP_WAIT = 111,     /* an expert-parallel barrier gave up waiting for a peer */
+  SJ_DEV_EP_CAPACITY = 112  /* an expert-parallel receive buffer would overflow */
 };
 
 int sj_version(void);
@@ -163,6 +165,10 @@ int sj_rope(const void* x, void* y, int rows, int heads, int head_dim, int t, in
 /* Engine::swiglu_backward (lib.rs:711-733; kernels.py:95-101): gu [rows,2f] bf16 interleaved by 16
  * columns (as written by SJ_EPI_SWIGLU), dh [rows,f] bf16 -> dgu [rows,2f] bf16 (same interleave). */
 int sj_swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, void* stream);
+/* The same over the first *live_rows (device int32, at most rows) rows of a packed MoE buffer whose
+ * used extent is known only on the device (group_rows[groups] of sj_ep_route_pack). */
+int sj_swiglu_bwd_live(const void* gu, const void* dh, void* dgu, int rows, int f, const int32_t* live_rows,
+                       void* stream);
 /* Engine::patch_pool (crates/sejong-gpu/src/hierarchy_ops.rs:149-205; hierarchy.py:107-131). */
 int sj_patch_pool_fwd(const void* x, void* y, int batch, int t, int d, int patch, void* stream);
 /* dx[b,t,:] += dy[b, t/P, :] / count  (f32 accumulate) */
@@ -249,6 +255,64 @@ int sj_moe_combine_bwd(const void* out, const int32_t* row_slot, const float* ga
 int sj_route_topk_bwd(const float* logits, int ld, const int32_t* ids, const float* gates, const float* d_gates,
                       void* dlogits, int ldd, int rows, int experts, int k, void* stream);
 int sj_moe_dispatch_bwd(const float* da, const int32_t* pos, float* dz, int ldz, int rows, int k, int d, void* stream);
+
+/* ------------------------------------------------------------------ expert parallelism */
+/* The MoE FFN with the experts sharded over the ranks of the data-parallel group (experts / world
+ * experts per rank, rank r owning experts [r*local, (r+1)*local)).  No counterpart in the reference,
+ * which runs every expert on one device (hierarchy_ops.rs:280-454); a step over `world` ranks
+ * computes what sj_route_pack / sj_moe_* compute on one device for the ranks' rows concatenated in
+ * rank order (same packed order inside each expert).
+ *
+ * Transport: a symmetric heap -- one device allocation of the same size on every rank, opened in
+ * every peer with CUDA IPC (plain NVLink loads and stores, no multicast).  `peers` is a host array
+ * of `world` heap base addresses as mapped in this process (peers[rank] = this rank's own heap);
+ * buffers shared between ranks are given as byte offsets into the heap (16-byte aligned), the same
+ * on every rank.  Cross-rank ordering uses a flag array (uint32 [world], heap offset flags_off) and
+ * a per-rank device epoch counter (uint32, zero at start) that every barrier advances; every rank
+ * must issue the same sequence of sj_ep_route_pack / sj_ep_barrier calls.  A wait that exceeds
+ * timeout_ms records SJ_DEV_EP_WAIT in the device error word and returns.
+ *
+ *   sj_ipc_alloc / sj_ipc_free      a zero-filled device allocation for the heap.
+ *   sj_ipc_handle / sj_ipc_open / sj_ipc_close   export a heap (SJ_IPC_HANDLE_BYTES bytes) and map a
+ *                                   peer's heap into this process.
+ *   sj_ep_receive_capacity          packed rows a rank must be able to receive (every routed slot of
+ *                                   every rank on its experts, each segment padded to 128).
+ *   sj_ep_route_pack   counts (int32 [world][experts] at counts_off, one matrix per MoE layer)
+ *                      published to every rank, barrier, then group_rows [2*local + 1] (this rank's
+ *                      segment starts and end, then the end of the valid rows of each segment) and
+ *                      pos [rows*k] (the packed row, at the owner of ids[slot], of each of this rank's
+ *                      slots).  One CTA.
+ *   sj_ep_dispatch     A_owner[pos[s]] = z[s / k] pushed to the owners (A bf16 [cap, d] at a_off),
+ *                      and this rank's padding rows of A zeroed.
+ *   sj_ep_barrier      every earlier write of every rank visible to every rank.
+ *   sj_ep_combine      y = x + sum_j gates[:, j] out_owner[pos[:, j]] (out bf16 [cap, d] at out_off),
+ *                      pulled from the owners.
+ *   sj_ep_combine_bwd  d_out_owner[pos[s]] = gate[s] dy[s / k] pushed (bf16, at d_out_off),
+ *                      d_gates[s] = <out_owner[pos[s]], dy[s / k]> pulled, padding rows of this
+ *                      rank's d_out zeroed.
+ *   sj_ep_dispatch_bwd dz[t] = sum_j dA_owner[pos[t, j]] (dA f32 [cap, d] at da_off), pulled. */
+#define SJ_IPC_HANDLE_BYTES 64
+int sj_ipc_alloc(size_t bytes, void** ptr);
+int sj_ipc_free(void* ptr);
+int sj_ipc_handle(const void* ptr, void* handle);
+int sj_ipc_open(const void* handle, void** ptr);
+int sj_ipc_close(void* ptr);
+int sj_ep_receive_capacity(int rows, int k, int experts, int world);
+int sj_ep_route_pack(const int32_t* ids, int rows, int experts, int k, int rank, int world, const void* const* peers,
+                     size_t counts_off, size_t flags_off, uint32_t* epoch, int32_t* group_rows, int32_t* pos, int cap,
+                     int timeout_ms, void* stream);
+int sj_ep_dispatch(const void* z, int ldz, const int32_t* ids, const int32_t* pos, int rows, int k, int d, int experts,
+                   int rank, int world, const void* const* peers, size_t a_off, const int32_t* group_rows,
+                   void* stream);
+int sj_ep_barrier(int rank, int world, const void* const* peers, size_t flags_off, uint32_t* epoch, int timeout_ms,
+                  void* stream);
+int sj_ep_combine(const void* const* peers, int world, size_t out_off, const int32_t* ids, const int32_t* pos,
+                  const float* gates, const float* x, float* y, int rows, int k, int d, int experts, void* stream);
+int sj_ep_combine_bwd(const void* const* peers, int rank, int world, size_t out_off, size_t d_out_off,
+                      const int32_t* ids, const int32_t* pos, const float* gates, const float* dy, float* d_gates,
+                      const int32_t* group_rows, int rows, int k, int d, int experts, void* stream);
+int sj_ep_dispatch_bwd(const void* const* peers, int world, size_t da_off, const int32_t* ids, const int32_t* pos,
+                       float* dz, int ldz, int rows, int k, int d, int experts, void* stream);
 
 /* ------------------------------------------------------------------ BERT encoder (MiniLM) forward */
 /* BertEncoder::hidden (crates/sejong-model/src/native/bert.rs:360-411) on a batch of sequences packed

@@ -39,6 +39,23 @@ SIGNATURES = {
     "sj_route_topk_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                   c_void_p]),
     "sj_moe_dispatch_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "sj_ipc_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p)]),
+    "sj_ipc_free": (c_int, [c_void_p]),
+    "sj_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "sj_ipc_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "sj_ipc_close": (c_int, [c_void_p]),
+    "sj_ep_receive_capacity": (c_int, [c_int, c_int, c_int, c_int]),
+    "sj_ep_route_pack": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_size_t, c_void_p,
+                                 c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "sj_ep_dispatch": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                               c_size_t, c_void_p, c_void_p]),
+    "sj_ep_barrier": (c_int, [c_int, c_int, c_void_p, c_size_t, c_void_p, c_int, c_void_p]),
+    "sj_ep_combine": (c_int, [c_void_p, c_int, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                              c_int, c_int, c_void_p]),
+    "sj_ep_combine_bwd": (c_int, [c_void_p, c_int, c_int, c_size_t, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "sj_ep_dispatch_bwd": (c_int, [c_void_p, c_int, c_size_t, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                   c_int, c_void_p]),
     "sj_gemm_bias": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int,
                              c_int, c_int, c_float, c_void_p, c_void_p, c_int, c_void_p]),
     "sj_bert_embed": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
@@ -56,6 +73,7 @@ SIGNATURES = {
     "sj_embedding_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "sj_rope": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p]),
     "sj_swiglu_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "sj_swiglu_bwd_live": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "sj_patch_pool_fwd": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "sj_patch_pool_bwd": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
     "sj_patch_broadcast_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,

@@ -118,12 +118,16 @@ __global__ void rope_table_kernel(float2* table, int t, int half, int offset, fl
 
 // ---------------------------------------------------------------- SwiGLU backward (kernels.py:95-101)
 // gu: per row, blocks of 32 columns = 16 gate features then the same 16 up features.
+// `live` (optional, device): the number of leading rows that hold data (a packed MoE buffer
+// whose used extent is known only on the device); the grid strides over them.
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* gu, const __nv_bfloat16* dh,
-                                  __nv_bfloat16* dgu, int rows, int f) {
+                                  __nv_bfloat16* dgu, int rows, int f, const int32_t* live) {
   pdl_wait();
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // one per 8 features
   const int groups = f / 8;
-  if (i >= static_cast<size_t>(rows) * groups) return;
+  if (live != nullptr) rows = min(rows, *live);
+  const size_t n = static_cast<size_t>(rows) * groups;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;  // one per 8 features
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
   const int row = static_cast<int>(i / groups);
   const int f0 = static_cast<int>(i % groups) * 8;
   const int gcol = (f0 / 16) * 32 + (f0 % 16);
@@ -142,6 +146,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* gu, const __nv_bfloat16* 
   }
   *reinterpret_cast<uint4*>(dgu + rb + gcol) = make_uint4(dg[0], dg[1], dg[2], dg[3]);
   *reinterpret_cast<uint4*>(dgu + rb + gcol + 16) = make_uint4(du[0], du[1], du[2], du[3]);
+  }
 }
 
 // ---------------------------------------------------------------- hierarchy (hierarchy.py:107-172)
@@ -371,16 +376,29 @@ extern "C" int sj_rope_table(float* table, int t, int head_dim, int offset, floa
   return SJ_OK;
 }
 
-extern "C" int sj_swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, void* stream) {
+static int swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, const int32_t* live,
+                      void* stream) {
   if (rows <= 0 || f <= 0 || f % 16) return fail(SJ_ERR_SHAPE, "sj_swiglu_bwd: f=%d must be a multiple of 16", f);
   if (!aligned16(gu) || !aligned16(dh) || !aligned16(dgu))
     return fail(SJ_ERR_ARGUMENT, "sj_swiglu_bwd: 16-byte alignment required");
   const size_t threads = static_cast<size_t>(rows) * (f / 8);
-  launch(swiglu_bwd_kernel, static_cast<unsigned>((threads + 255) / 256), 256, 0, as_stream(stream), 
+  size_t blocks = (threads + 255) / 256;
+  if (live != nullptr) blocks = std::min<size_t>(blocks, static_cast<size_t>(sm_count()) * 8);
+  launch(swiglu_bwd_kernel, static_cast<unsigned>(blocks), 256, 0, as_stream(stream),
       static_cast<const __nv_bfloat16*>(gu), static_cast<const __nv_bfloat16*>(dh), static_cast<__nv_bfloat16*>(dgu),
-      rows, f);
+      rows, f, live);
   SJ_LAUNCH_CHECK("swiglu_bwd");
   return SJ_OK;
+}
+
+extern "C" int sj_swiglu_bwd(const void* gu, const void* dh, void* dgu, int rows, int f, void* stream) {
+  return swiglu_bwd(gu, dh, dgu, rows, f, nullptr, stream);
+}
+
+extern "C" int sj_swiglu_bwd_live(const void* gu, const void* dh, void* dgu, int rows, int f, const int32_t* live_rows,
+                                  void* stream) {
+  if (!live_rows) return fail(SJ_ERR_ARGUMENT, "sj_swiglu_bwd_live: null row count");
+  return swiglu_bwd(gu, dh, dgu, rows, f, live_rows, stream);
 }
 
 extern "C" int sj_patch_pool_fwd(const void* x, void* y, int batch, int t, int d, int patch, void* stream) {

@@ -25,14 +25,20 @@ def ce_seed(rows_per_rank, world, loss_scale=1.0):
     return float(loss_scale) / (int(rows_per_rank) * int(world))
 
 
-def exchange(grad_flat, loss_sum, group=None):
-    """In-place SUM all-reduce of the flat gradient buffer and of the loss sum."""
+def exchange(grad_flat, loss_sum, group=None, norm_partials=None):
+    """In-place SUM all-reduce of the flat gradient buffer and of the loss sum.
+
+    With expert parallelism `grad_flat` is the replicated range only and `norm_partials` (FP64)
+    carries the sums of squares of each rank's own experts' gradients, so that after the
+    exchange every rank sees the global gradient norm."""
     if group is None and not dist.is_initialized():
         return
     if dist.get_world_size(group) == 1:
         return
     dist.all_reduce(grad_flat, group=group)
     dist.all_reduce(loss_sum, group=group)
+    if norm_partials is not None:
+        dist.all_reduce(norm_partials, group=group)
 
 
 def init_from_env(backend="nccl", timeout_s=300):

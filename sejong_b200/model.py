@@ -186,10 +186,16 @@ def router_pad(experts):
 
 
 class FlatLayout:
-    """Placement of every (fused) parameter in the flat master / gradient / moment buffers."""
+    """Placement of every (fused) parameter in the flat master / gradient / moment buffers.
 
-    def __init__(self, c):
+    With `expert_shard=(rank, world)` (expert parallelism) the layout holds only this rank's experts
+    of every MoE layer, experts [rank * E/world, (rank + 1) * E/world), and places them first:
+    [0, shared_begin) is rank-local, [shared_begin, total) is replicated on every rank (the range
+    the data-parallel all-reduce covers).  Without it shared_begin is 0."""
+
+    def __init__(self, c, expert_shard=None):
         self.config = c
+        self.expert_shard = expert_shard
         ref = reference_layout(c)
         shapes = {n: s for n, s, _ in ref}
         entries = []
@@ -232,16 +238,29 @@ class FlatLayout:
             grouped += [e for e in run if e[0].endswith(".gate_up")] + [e for e in run if e[0].endswith(".down")]
             i = j
         entries = grouped
-        ordered = [e for e in entries if e[2]] + [e for e in entries if not e[2]]
+        experts_first = []
+        if expert_shard is not None:
+            rank, world = expert_shard
+            count = c.experts.count if c.experts is not None else 0
+            if count == 0 or count % world or not 0 <= rank < world:
+                raise ValueError(f"expert shard {expert_shard} of {count} experts")
+            local = range(rank * count // world, (rank + 1) * count // world)
+            mine = {f".experts.{x}." for x in local}
+            experts_first = [e for e in entries if ".experts." in e[0] and any(m in e[0] for m in mine)]
+            entries = [e for e in entries if ".experts." not in e[0]]
+        ordered = experts_first + [e for e in entries if e[2]] + [e for e in entries if not e[2]]
         self.entries = {}
         off = 0
         self.n_decay = 0
-        for name, shape, decay, parts in ordered:
+        self.shared_begin = 0
+        for i, (name, shape, decay, parts) in enumerate(ordered):
             self.entries[name] = Entry(name, tuple(shape), off, decay, parts)
             off += int(np.prod(shape))
             off = (off + ALIGN - 1) // ALIGN * ALIGN
             if decay:
                 self.n_decay = off
+            if i + 1 == len(experts_first):
+                self.shared_begin = off
         self.total = off
 
     def __getitem__(self, name):

@@ -34,6 +34,7 @@ import numpy as np
 import torch
 
 from . import _lib, distributed, param_vjp
+from .expert_parallel import EpContext
 from ._lib import (EPI_ACCUM, EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call)
 from .model import (HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage,
                     reference_layout, router_pad)
@@ -69,7 +70,7 @@ def _ptr(t, offset_elems=0):
 class _StageRun:
     """Activation and gradient buffers of one stage (encoder, global or decoder)."""
 
-    def __init__(self, stage, batch, seq, dev):
+    def __init__(self, stage, batch, seq, dev, ep=None):
         self.stage, self.batch, self.seq = stage, batch, seq
         n, d, f, cq = batch * seq, stage.width, stage.ffn, stage.qkv_width
         self.rows = n
@@ -94,7 +95,30 @@ class _StageRun:
         self.delta = e(_lib.load().sj_attn_workspace(batch, seq, stage.heads, stage.kv_heads), dt=f32)
         self.partials = e(_lib.load().sj_rmsnorm_workspace(n, d), dt=f32)
         self.moe = stage.experts is not None
-        if self.moe:
+        self.ep = ep if self.moe else None
+        if self.ep is not None:
+            # expert-parallel MoE: this rank routes its own rows and runs its experts on every rank's
+            # rows routed to them; the packed A / expert output of each layer, d_out and dA live in the
+            # symmetric heap (peers write and read them), the rest is rank-local
+            ex, W = stage.experts, ep.world
+            local = ex.count // W
+            cap = _lib.load().sj_ep_receive_capacity(n, ex.top_k, ex.count, W)
+            fe, i32 = ex.ffn_width, torch.int32
+            self.cap = cap
+            for i, L in enumerate(self.layers):
+                p = f"{stage.prefix}.{i}"
+                L.update(logits=e(n, router_pad(ex.count), dt=f32), ids=e(n, ex.top_k, dt=i32),
+                         gates=e(n, ex.top_k, dt=f32), group_rows=e(2 * local + 1, dt=i32), pos=e(n * ex.top_k, dt=i32),
+                         gu=e(cap, 2 * fe), h=e(cap, fe))
+                ep.reserve(f"{p}.counts", 4 * W * ex.count)
+                ep.reserve(f"{p}.a", 2 * cap * d)
+                ep.reserve(f"{p}.out", 2 * cap * d)
+            ep.reserve(f"{stage.prefix}.d_out", 2 * cap * d)
+            ep.reserve(f"{stage.prefix}.da", 4 * cap * d)
+            self.d_gates = e(n * ex.top_k, dt=f32)
+            self.dh_packed, self.dgu_packed = e(cap, fe), e(cap, 2 * fe)
+            self.dlogits = e(n, router_pad(ex.count))
+        elif self.moe:
             # MoE FFN (architecture.rs:229-241): routing and the expert rows packed per expert, each
             # expert's segment padded to 128 rows (sj_route_pack); kept per layer for the backward
             ex = stage.experts
@@ -114,7 +138,8 @@ class _StageRun:
 class ByteTrainer:
     """One data-parallel replica of the byte-model training step on the current CUDA device."""
 
-    def __init__(self, config, train, device=None, params=None, process_group=None):
+    def __init__(self, config, train, device=None, params=None, process_group=None, expert_parallel=False,
+                 ep_timeout_ms=10000):
         self.c, self.tc = config, train
         self.launches = 0
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
@@ -123,7 +148,15 @@ class ByteTrainer:
         call("sj_device_init", self.dev.index)
         self.pg = process_group
         self.world = torch.distributed.get_world_size(process_group) if process_group is not None else 1
-        self.layout = FlatLayout(config)
+        rank = torch.distributed.get_rank(process_group) if process_group is not None else 0
+        self.ep = None
+        if expert_parallel:
+            if config.experts is None or config.experts.count % self.world:
+                raise ValueError("expert parallelism needs an MoE model whose expert count the world size divides")
+            if train.parameter_vjp is not None:
+                raise ValueError("expert parallelism with the parameter VJP is not supported")
+            self.ep = EpContext(rank, self.world, self.dev, process_group, ep_timeout_ms)
+        self.layout = FlatLayout(config, expert_shard=(rank, self.world) if self.ep else None)
         if params is None:
             params = initialize(config, self.lib)
         total = self.layout.total
@@ -133,7 +166,10 @@ class ByteTrainer:
         self.g = torch.zeros(total, dtype=f32, device=self.dev)
         self.m = torch.zeros(total, dtype=f32, device=self.dev)
         self.v = torch.zeros(total, dtype=f32, device=self.dev)
-        self.n_partials = self.lib.sj_sumsq_partials(total)
+        # gradient-norm partials: [replicated range | rank-local expert range (all-reduced)]
+        sb = self.layout.shared_begin
+        self.n_shared_partials = self.lib.sj_sumsq_partials(total - sb)
+        self.n_partials = self.n_shared_partials + (self.lib.sj_sumsq_partials(sb) if sb else 0)
         self.partials = torch.zeros(self.n_partials, dtype=torch.float64, device=self.dev)
         self.opt_state = torch.zeros(2, dtype=torch.float64, device=self.dev)
         self.hyper = torch.zeros(8, dtype=f32, device=self.dev)
@@ -149,13 +185,13 @@ class ByteTrainer:
         self.ids = torch.zeros(self.rows, dtype=torch.int32, device=self.dev)
         self.targets = torch.zeros(self.rows, dtype=torch.int32, device=self.dev)
         if h is None:
-            self.runs = {"global": _StageRun(global_stage(config), b, t, self.dev)}
+            self.runs = {"global": _StageRun(global_stage(config), b, t, self.dev, self.ep)}
             top_width = config.width
         else:
             assert t % h.patch_size == 0, "sequence must be a multiple of the patch size"
             self.patches = t // h.patch_size
             self.runs = {"encoder": _StageRun(local_stage(config, True), b, t, self.dev),
-                         "global": _StageRun(global_stage(config), b, self.patches, self.dev),
+                         "global": _StageRun(global_stage(config), b, self.patches, self.dev, self.ep),
                          "decoder": _StageRun(local_stage(config, False), b, t, self.dev)}
             de, dg, dd = h.encoder_width, config.width, h.decoder_width
             np_ = b * self.patches
@@ -188,6 +224,8 @@ class ByteTrainer:
                 tab = torch.empty(run.seq * HEAD_DIM, dtype=torch.float32, device=self.dev)
                 call("sj_rope_table", _ptr(tab), run.seq, HEAD_DIM, 0, float(config.rope_theta), self.stream)
                 self.rope_tables[run.seq] = tab
+        if self.ep is not None:
+            self.ep.finalize()
         self.graph = None
         self.vjp = None
         if train.parameter_vjp is not None:
@@ -401,6 +439,8 @@ class ByteTrainer:
         """The MoE FFN of a block (architecture.rs:229-241): router logits, top-k routing, the routed
         rows packed per expert, one grouped GEMM per projection over all experts, and the gated
         combine with the residual add into the block output `xn`."""
+        if run.ep is not None:
+            return self._moe_fwd_ep(run, a, p, xn)
         ex = run.stage.experts
         n, d, fe, E, k, cap = run.rows, run.stage.width, ex.ffn_width, ex.count, ex.top_k, run.cap
         gp = _ptr(a["group_rows"])
@@ -419,6 +459,8 @@ class ByteTrainer:
     def _moe_bwd(self, run, a, p):
         """Backward of _moe_fwd into run.dz (the gradient at the FFN norm's output), accumulating the
         expert and router weight gradients (graph.rs:600-624 for the routing terms)."""
+        if run.ep is not None:
+            return self._moe_bwd_ep(run, a, p)
         ex = run.stage.experts
         n, d, fe, E, k, cap = run.rows, run.stage.width, ex.ffn_width, ex.count, ex.top_k, run.cap
         gp = _ptr(a["group_rows"])
@@ -441,6 +483,72 @@ class ByteTrainer:
         self._gemm(_ptr(run.dlogits), ep, 0, self.wb_ptr(f"{p}.router"), ep, 1, _ptr(run.dz), d, SJ_F32, n, d, ep,
                    EPI_ACCUM)
         self._gemm(_ptr(a["z2"]), d, 1, _ptr(run.dlogits), ep, 0, self.g_ptr(f"{p}.router"), ep, SJ_F32, d, ep, n,
+                   EPI_ACCUM)
+
+    def _ep_barrier(self, ep):
+        self._call("sj_ep_barrier", ep.rank, ep.world, ep.peers, ep.offset("flags"), _ptr(ep.epoch), ep.timeout_ms,
+                   self.stream)
+
+    def _moe_fwd_ep(self, run, a, p, xn):
+        """_moe_fwd with the experts sharded over the ranks: the routing is local; the counts go to
+        every rank, which lays out its experts' rows (sj_ep_route_pack); the rows are pushed to their
+        owners, which run their experts on them; the outputs are pulled back by the combine."""
+        ep, ex = run.ep, run.stage.experts
+        n, d, fe, E, k, cap = run.rows, run.stage.width, ex.ffn_width, ex.count, ex.top_k, run.cap
+        local = E // ep.world
+        first = local * ep.rank
+        gp = _ptr(a["group_rows"])
+        ids, pos = _ptr(a["ids"]), _ptr(a["pos"])
+        erp = router_pad(E)
+        self._gemm(_ptr(a["z2"]), d, 0, self.wb_ptr(f"{p}.router"), erp, 0, _ptr(a["logits"]), erp, SJ_F32, n, erp, d)
+        self._call("sj_route_topk", _ptr(a["logits"]), erp, n, E, k, ids, _ptr(a["gates"]), self.stream)
+        self._call("sj_ep_route_pack", ids, n, E, k, ep.rank, ep.world, ep.peers, ep.offset(f"{p}.counts"),
+                   ep.offset("flags"), _ptr(ep.epoch), gp, pos, cap, ep.timeout_ms, self.stream)
+        self._call("sj_ep_dispatch", _ptr(a["z2"]), d, ids, pos, n, k, d, E, ep.rank, ep.world, ep.peers,
+                   ep.offset(f"{p}.a"), gp, self.stream)
+        self._ep_barrier(ep)
+        self._gemm_grouped(ep.ptr(f"{p}.a"), d, 0, self.wb_ptr(f"{p}.experts.{first}.gate_up"), 2 * fe, 0, _ptr(a["gu"]),
+                           2 * fe, SJ_BF16, cap, 2 * fe, d, EPI_SWIGLU, local, gp, 1, b_rows=d, aux=_ptr(a["h"]),
+                           ld_aux=fe)
+        self._gemm_grouped(_ptr(a["h"]), fe, 0, self.wb_ptr(f"{p}.experts.{first}.down"), d, 0, ep.ptr(f"{p}.out"), d,
+                           SJ_BF16, cap, d, fe, EPI_STORE, local, gp, 1, b_rows=fe)
+        self._ep_barrier(ep)
+        self._call("sj_ep_combine", ep.peers, ep.world, ep.offset(f"{p}.out"), ids, pos, _ptr(a["gates"]),
+                   _ptr(a["x1"]), _ptr(xn), n, k, d, E, self.stream)
+
+    def _moe_bwd_ep(self, run, a, p):
+        """Backward of _moe_fwd_ep: gate * dy pushed to the owners, which run the expert backward
+        GEMMs on their rows; dA pulled back and summed per row; the router backward is local."""
+        ep, ex = run.ep, run.stage.experts
+        n, d, fe, E, k, cap = run.rows, run.stage.width, ex.ffn_width, ex.count, ex.top_k, run.cap
+        local = E // ep.world
+        first = local * ep.rank
+        gp = _ptr(a["group_rows"])
+        ids, pos = _ptr(a["ids"]), _ptr(a["pos"])
+        gate_up, down = f"{p}.experts.{first}.gate_up", f"{p}.experts.{first}.down"
+        d_out, da = f"{run.stage.prefix}.d_out", f"{run.stage.prefix}.da"
+        self._call("sj_ep_combine_bwd", ep.peers, ep.rank, ep.world, ep.offset(f"{p}.out"), ep.offset(d_out), ids, pos,
+                   _ptr(a["gates"]), _ptr(run.dx), _ptr(run.d_gates), gp, n, k, d, E, self.stream)
+        self._ep_barrier(ep)
+        self._gemm_grouped(_ptr(a["h"]), fe, 1, ep.ptr(d_out), d, 0, self.g_ptr(down), d, SJ_F32, fe, d, cap,
+                           EPI_ACCUM, local, gp, 2, c_rows=fe)
+        self._gemm_grouped(ep.ptr(d_out), d, 0, self.wb_ptr(down), d, 1, _ptr(run.dh_packed), fe, SJ_BF16, cap, fe,
+                           d, EPI_STORE, local, gp, 1, b_rows=fe)
+        self._call("sj_swiglu_bwd_live", _ptr(a["gu"]), _ptr(run.dh_packed), _ptr(run.dgu_packed), cap, fe,
+                   gp + 4 * local, self.stream)
+        self._gemm_grouped(ep.ptr(f"{p}.a"), d, 1, _ptr(run.dgu_packed), 2 * fe, 0, self.g_ptr(gate_up), 2 * fe,
+                           SJ_F32, d, 2 * fe, cap, EPI_ACCUM, local, gp, 2, c_rows=d)
+        self._gemm_grouped(_ptr(run.dgu_packed), 2 * fe, 0, self.wb_ptr(gate_up), 2 * fe, 1, ep.ptr(da), d, SJ_F32,
+                           cap, d, 2 * fe, EPI_STORE, local, gp, 1, b_rows=d)
+        self._ep_barrier(ep)
+        self._call("sj_ep_dispatch_bwd", ep.peers, ep.world, ep.offset(da), ids, pos, _ptr(run.dz), d, n, k, d, E,
+                   self.stream)
+        erp = router_pad(E)
+        self._call("sj_route_topk_bwd", _ptr(a["logits"]), erp, ids, _ptr(a["gates"]), _ptr(run.d_gates),
+                   _ptr(run.dlogits), erp, n, E, k, self.stream)
+        self._gemm(_ptr(run.dlogits), erp, 0, self.wb_ptr(f"{p}.router"), erp, 1, _ptr(run.dz), d, SJ_F32, n, d, erp,
+                   EPI_ACCUM)
+        self._gemm(_ptr(a["z2"]), d, 1, _ptr(run.dlogits), erp, 0, self.g_ptr(f"{p}.router"), erp, SJ_F32, d, erp, n,
                    EPI_ACCUM)
 
     def _stage_fwd(self, run):
@@ -561,12 +669,19 @@ class ByteTrainer:
         self._zero(self.loss_sum)
         top, width = self._forward()
         self._backward(top, width)
+        sb = self.layout.shared_begin
+        if sb:  # sum of squares of this rank's experts' gradients, summed over the ranks by the exchange
+            self._call("sj_grad_sumsq", _ptr(self.g), sb, _ptr(self.partials, self.n_shared_partials), self.stream)
 
     def _exchange(self):
         """Data-parallel exchange: sum of the per-rank gradients (each seeded with 1/global rows, so
         the sum is the global-batch mean gradient) and of the loss, over NCCL."""
         if self.world > 1:
-            distributed.exchange(self.g, self.loss_sum, self.pg)
+            sb = self.layout.shared_begin
+            if sb:  # expert parallelism: the experts' gradients stay with their owners
+                distributed.exchange(self.g[sb:], self.loss_sum, self.pg, self.partials[self.n_shared_partials:])
+            else:
+                distributed.exchange(self.g, self.loss_sum, self.pg)
 
     def forward_backward(self):
         """Loss (into self.loss_sum) and gradients (into self.g) for the staged batch."""
@@ -578,7 +693,8 @@ class ByteTrainer:
         self.stream = torch.cuda.current_stream(self.dev).cuda_stream
         tc = self.tc
         total = self.layout.total
-        self._call("sj_grad_sumsq", _ptr(self.g), total, _ptr(self.partials), self.stream)
+        sb = self.layout.shared_begin
+        self._call("sj_grad_sumsq", _ptr(self.g, sb), total - sb, _ptr(self.partials), self.stream)
         self._call("sj_optim_prepare", _ptr(self.partials), self.n_partials, _ptr(self.opt_state), _ptr(self.hyper),
              tc.learning_rate, tc.min_learning_rate, tc.warmup_steps, tc.steps, tc.beta1, tc.beta2, tc.clip_norm,
              int(tc.clip_enabled), tc.loss_scale, self.stream)
@@ -604,6 +720,9 @@ class ByteTrainer:
         reference's parameter names, the AdamW moments as m.<name> / v.<name>, the optimizer step
         (the device optimizer state) and the training config, written atomically."""
         from . import checkpoint
+        if self.ep is not None:
+            raise checkpoint.ArtifactError("checkpoints of an expert-parallel trainer are not supported: each rank "
+                                           "holds only its own experts")
         torch.cuda.synchronize(self.dev)
         params = self.layout.unpack(self.w.cpu().numpy())
         optimizer = None
@@ -678,6 +797,15 @@ class ByteTrainer:
     def release_graphs(self):
         """Drop captured graphs (before destroying a process group)."""
         self.graph = None
+
+    def close(self):
+        """Release the expert-parallel heap (every rank, after its last step; then a barrier)."""
+        self.graph = None
+        if self.ep is not None:
+            torch.cuda.synchronize(self.dev)
+            if self.pg is not None:
+                torch.distributed.barrier(self.pg)
+            self.ep.close()
 
     # ------------------------------------------------------------------ inspection
     def loss(self):
