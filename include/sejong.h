@@ -256,6 +256,22 @@ int sj_route_topk_bwd(const float* logits, int ld, const int32_t* ids, const flo
                       void* dlogits, int ldd, int rows, int experts, int k, void* stream);
 int sj_moe_dispatch_bwd(const float* da, const int32_t* pos, float* dz, int ldz, int rows, int k, int d, void* stream);
 
+/* ------------------------------------------------------------------ NativeValue head */
+/* The categorical value head of NativeValue::forward_batch (crates/sejong-model/src/native/value.rs:
+ * 111-160) with its loss (Engine::cross_entropy, lib.rs:524-543) and backward.  hidden bf16 [rows,
+ * ldh] is the body's final-norm output; sel int32 [batch] the SEP row of each request; W f32 [d, nv]
+ * (native_value), bias f32 [nv] (native_bias); labels int32 [batch].
+ *   sj_value_head_fwd: logits f32 [batch, nv] = f32(hidden[sel]) W + bias; dlogits f32 [batch, nv] =
+ *     (softmax - onehot(label)) * seed (optional); loss_sum += sum_b loss_b * weight (optional).
+ *     A row or label out of range records SJ_DEV_BAD_INDEX and skips that request.  d <= 4096.
+ *   sj_value_head_bwd: dW += f32(hidden[sel])^T dlogits, dbias += sum_b dlogits, dh[sel[b], :] =
+ *     dlogits[b] W^T (f32 [rows, ldd]; only the selected rows are written). */
+int sj_value_head_fwd(const void* hidden, int ldh, int rows, const int32_t* sel, int batch, int d, const float* w,
+                      const float* bias, int nv, const int32_t* labels, float seed, float* logits, float* dlogits,
+                      double* loss_sum, double weight, void* stream);
+int sj_value_head_bwd(const void* hidden, int ldh, int rows, const int32_t* sel, int batch, int d, const float* w,
+                      const float* dlogits, int nv, float* dw, float* dbias, float* dh, int ldd, void* stream);
+
 /* ------------------------------------------------------------------ expert parallelism */
 /* The MoE FFN with the experts sharded over the ranks of the data-parallel group (experts / world
  * experts per rank, rank r owning experts [r*local, (r+1)*local)).  No counterpart in the reference,

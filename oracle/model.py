@@ -243,12 +243,20 @@ def _blocks(p, s, x, seq, c):
 
 def hidden(p, c, ids, seq):
     """crates/sejong-model/src/lib.rs:254-277 + architecture.rs:330-393."""
+    return hidden_from(p, c, ops.embedding(p["embedding"], ids), seq)
+
+
+def hidden_from(p, c, x, seq, project=False):
+    """The body from its input rows x (architecture.rs:353-393).  `project`: x is an injected input
+    of the model width (hidden_from, architecture.rs:360-365), mapped to the encoder width by
+    input_projection before the encoder; the byte LM embeds at the encoder width directly."""
     eps = c.norm_epsilon
-    x = ops.embedding(p["embedding"], ids)
     h = c.hierarchy
     if h is None:
         x = _blocks(p, global_stage(c), x, seq, c)
         return ops.rmsnorm(x, p["final_norm"], eps)
+    if project:
+        x = mm(x, p, "input_projection")
     x = _blocks(p, local_stage(c, True), x, seq, c)
     x = ops.rmsnorm(x, p["encoder_norm"], eps)
     pooled = ops.patch_pool(x, seq, h.patch_size)

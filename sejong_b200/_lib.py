@@ -39,6 +39,10 @@ SIGNATURES = {
     "sj_route_topk_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                   c_void_p]),
     "sj_moe_dispatch_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "sj_value_head_fwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                                  c_float, c_void_p, c_void_p, c_void_p, c_double, c_void_p]),
+    "sj_value_head_bwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
+                                  c_void_p, c_void_p, c_int, c_void_p]),
     "sj_ipc_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p)]),
     "sj_ipc_free": (c_int, [c_void_p]),
     "sj_ipc_handle": (c_int, [c_void_p, c_void_p]),

@@ -185,6 +185,17 @@ def router_pad(experts):
     return (experts + 7) // 8 * 8
 
 
+NATIVE_VOCAB = 259          # 256 bytes, PAD 256, BOS 257, SEP 258 (value.rs:15-17)
+NATIVE_PAD, NATIVE_BOS, NATIVE_SEP = 256, 257, 258
+
+
+def value_layout(c, values):
+    """(name, shape, is_norm) of NativeValue's own parameters (value.rs:84-106, 53-67)."""
+    return [("native_embedding", (NATIVE_VOCAB, c.width), False),
+            ("native_value", (c.width, values), False),
+            ("native_bias", (1, values), False)]
+
+
 class FlatLayout:
     """Placement of every (fused) parameter in the flat master / gradient / moment buffers.
 
@@ -193,10 +204,15 @@ class FlatLayout:
     [0, shared_begin) is rank-local, [shared_begin, total) is replicated on every rank (the range
     the data-parallel all-reduce covers).  Without it shared_begin is 0."""
 
-    def __init__(self, c, expert_shard=None):
+    def __init__(self, c, expert_shard=None, values=0):
         self.config = c
         self.expert_shard = expert_shard
+        self.values = values
         ref = reference_layout(c)
+        if values:
+            # NativeValue (crates/sejong-model/src/native/value.rs:84-106): the body without its byte
+            # embedding and output head, plus the 259-row native embedding and the f32 value head
+            ref = [r for r in ref if r[0] not in ("embedding", "output")] + value_layout(c, values)
         shapes = {n: s for n, s, _ in ref}
         entries = []
         fused_done = set()

@@ -36,7 +36,7 @@ import torch
 from . import _lib, distributed, param_vjp
 from .expert_parallel import EpContext
 from ._lib import (EPI_ACCUM, EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call)
-from .model import (HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage,
+from .model import (HEAD_DIM, NATIVE_VOCAB, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage,
                     reference_layout, router_pad)
 
 
@@ -61,6 +61,9 @@ class TrainConfig:
     # weight gradients through the parameter VJP (low-rank factors + selected rows), as the
     # reference's control-variate trainer does (crates/sejong-train/src/control_variate.rs)
     parameter_vjp: Optional[param_vjp.VjpConfig] = None
+    # NativeValue training (crates/sejong-train/src/memory.rs:799-1065) when > 0: the number of values
+    # of the categorical head; `batch` requests per step, each padded to `sequence` bytes
+    values: int = 0
 
 
 def _ptr(t, offset_elems=0):
@@ -156,9 +159,13 @@ class ByteTrainer:
             if train.parameter_vjp is not None:
                 raise ValueError("expert parallelism with the parameter VJP is not supported")
             self.ep = EpContext(rank, self.world, self.dev, process_group, ep_timeout_ms)
-        self.layout = FlatLayout(config, expert_shard=(rank, self.world) if self.ep else None)
+        self.values = int(train.values)
+        self.layout = FlatLayout(config, expert_shard=(rank, self.world) if self.ep else None, values=self.values)
         if params is None:
             params = initialize(config, self.lib)
+            if self.values:
+                from .value import initialize_value
+                params.update(initialize_value(config, self.values, self.lib))
         total = self.layout.total
         f32 = torch.float32
         self.w = torch.from_numpy(self.layout.pack(params)).to(self.dev)
@@ -211,8 +218,16 @@ class ByteTrainer:
             self.top_partials = e(self.lib.sj_rmsnorm_workspace(self.rows, max(dg, de, dd)), dt=torch.float32)
             top_width = dg
         self.hf, self.invF = e(self.rows, top_width), e(self.rows, dt=torch.float32)
-        self.logits = e(self.rows, VOCAB_PAD, dt=torch.float32)
-        self.dlogits = e(self.rows, VOCAB_PAD)
+        if self.values:  # NativeValue head: SEP row and label per request, f32 value logits
+            self.sel = torch.zeros(b, dtype=torch.int32, device=self.dev)
+            self.labels = torch.zeros(b, dtype=torch.int32, device=self.dev)
+            self.vlogits = e(b, self.values, dt=torch.float32)
+            self.vdlogits = e(b, self.values, dt=torch.float32)
+            if h is not None:
+                self.xin = e(self.rows, config.width)  # native embedding output, input_projection operand
+        else:
+            self.logits = e(self.rows, VOCAB_PAD, dt=torch.float32)
+            self.dlogits = e(self.rows, VOCAB_PAD)
         self.dhead = e(self.rows, top_width, dt=torch.float32)
         self.dheadb = e(self.rows, top_width)
         if h is None:
@@ -564,10 +579,11 @@ class ByteTrainer:
         c, h = self.c, self.c.hierarchy
         n = self.rows
         b = self.tc.batch
+        emb, vocab = ("native_embedding", NATIVE_VOCAB) if self.values else ("embedding", VOCAB)
         if h is None:
             run = self.runs["global"]
-            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(run.x[0]), SJ_F32, n,
-                       c.width, VOCAB, self.stream)
+            self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(run.x[0]), SJ_F32, n,
+                       c.width, vocab, self.stream)
             self._stage_fwd(run)
             top = run.x[-1]
             top_width = c.width
@@ -575,8 +591,14 @@ class ByteTrainer:
             enc, glob, dec = self.runs["encoder"], self.runs["global"], self.runs["decoder"]
             de, dg, dd, pt = h.encoder_width, c.width, h.decoder_width, h.patch_size
             np_ = b * self.patches
-            self._call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(enc.x[0]), SJ_F32, n, de,
-                       VOCAB, self.stream)
+            if self.values:  # hidden_from (architecture.rs:353-367): native embedding -> input_projection
+                self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(self.xin), SJ_BF16, n, dg,
+                           vocab, self.stream)
+                self._gemm(_ptr(self.xin), dg, 0, self.wb_ptr("input_projection"), de, 0, _ptr(enc.x[0]), de, SJ_F32,
+                           n, de, dg)
+            else:
+                self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(enc.x[0]), SJ_F32, n, de,
+                           VOCAB, self.stream)
             self._stage_fwd(enc)
             self._norm(enc.x[-1], "encoder_norm", self.zE, self.invE, n, de)
             self._call("sj_patch_pool_fwd", _ptr(self.zE), _ptr(self.pooled), b, self.tc.sequence, de, pt, self.stream)
@@ -599,6 +621,15 @@ class ByteTrainer:
             top = self.y
             top_width = dg
         self._norm(top, "final_norm", self.hf, self.invF, n, top_width)
+        if self.values:
+            # value.rs:147-152: the SEP rows, cast to f32, through the f32 affine head; the loss is the
+            # mean cross entropy over the requests of the global batch (seed 1 / requests)
+            bt = self.tc.batch
+            self._call("sj_value_head_fwd", _ptr(self.hf), top_width, n, _ptr(self.sel), bt, top_width,
+                       self.w_ptr("native_value"), self.w_ptr("native_bias"), self.values, _ptr(self.labels),
+                       distributed.ce_seed(bt, self.world, self.tc.loss_scale), _ptr(self.vlogits),
+                       _ptr(self.vdlogits), _ptr(self.loss_sum), distributed.ce_seed(bt, self.world), self.stream)
+            return top, top_width
         self._gemm(_ptr(self.hf), top_width, 0, self.wb_ptr("output"), VOCAB_PAD, 0, _ptr(self.logits), VOCAB_PAD,
                    SJ_F32, n, VOCAB, top_width)
         self._call("sj_cross_entropy", _ptr(self.logits), VOCAB_PAD, _ptr(self.targets), n, VOCAB,
@@ -609,17 +640,25 @@ class ByteTrainer:
     def _backward(self, top, top_width):
         c, h = self.c, self.c.hierarchy
         n, b = self.rows, self.tc.batch
-        # head: dW_out += h^T dlogits ; dh = dlogits W_out^T
-        self._gemm(_ptr(self.hf), top_width, 1, _ptr(self.dlogits), VOCAB_PAD, 0, self.g_ptr("output"), VOCAB_PAD,
-                   SJ_F32, top_width, VOCAB, n, EPI_ACCUM)
-        self._gemm(_ptr(self.dlogits), VOCAB_PAD, 0, self.wb_ptr("output"), VOCAB_PAD, 1, _ptr(self.dhead), top_width,
-                   SJ_F32, n, top_width, VOCAB)
+        if self.values:
+            # value head: dW, dbias and the SEP rows of dh (every other row of dh is zero)
+            self._zero(self.dhead)
+            self._call("sj_value_head_bwd", _ptr(self.hf), top_width, n, _ptr(self.sel), b, top_width,
+                       self.w_ptr("native_value"), _ptr(self.vdlogits), self.values, self.g_ptr("native_value"),
+                       self.g_ptr("native_bias"), _ptr(self.dhead), top_width, self.stream)
+        else:
+            # head: dW_out += h^T dlogits ; dh = dlogits W_out^T
+            self._gemm(_ptr(self.hf), top_width, 1, _ptr(self.dlogits), VOCAB_PAD, 0, self.g_ptr("output"), VOCAB_PAD,
+                       SJ_F32, top_width, VOCAB, n, EPI_ACCUM)
+            self._gemm(_ptr(self.dlogits), VOCAB_PAD, 0, self.wb_ptr("output"), VOCAB_PAD, 1, _ptr(self.dhead),
+                       top_width, SJ_F32, n, top_width, VOCAB)
+        emb, vocab = ("native_embedding", NATIVE_VOCAB) if self.values else ("embedding", VOCAB)
         if h is None:
             run = self.runs["global"]
             self._zero(run.dx)
             self._norm_bwd(top, "final_norm", self.invF, self.dhead, run.dx, run.dxb, self.top_partials, n, c.width)
             self._stage_bwd(run)
-            self._call("sj_embedding_bwd", _ptr(run.dx), _ptr(self.ids), self.g_ptr("embedding"), n, c.width, VOCAB,
+            self._call("sj_embedding_bwd", _ptr(run.dx), _ptr(self.ids), self.g_ptr(emb), n, c.width, vocab,
                  self.stream)
             return
         enc, glob, dec = self.runs["encoder"], self.runs["global"], self.runs["decoder"]
@@ -660,7 +699,14 @@ class ByteTrainer:
         self._zero(enc.dx)
         self._norm_bwd(enc.x[-1], "encoder_norm", self.invE, self.dE, enc.dx, enc.dxb, enc.partials, n, de)
         self._stage_bwd(enc)
-        self._call("sj_embedding_bwd", _ptr(enc.dx), _ptr(self.ids), self.g_ptr("embedding"), n, de, VOCAB, self.stream)
+        if self.values:  # input_projection, then the native embedding (dy32 is free again: [rows, width] f32)
+            self._gemm(_ptr(self.xin), dg, 1, _ptr(enc.dxb), de, 0, self.g_ptr("input_projection"), de, SJ_F32, dg, de,
+                       n, EPI_ACCUM)
+            self._gemm(_ptr(enc.dxb), de, 0, self.wb_ptr("input_projection"), de, 1, _ptr(self.dy32), dg, SJ_F32, n,
+                       dg, de)
+            self._call("sj_embedding_bwd", _ptr(self.dy32), _ptr(self.ids), self.g_ptr(emb), n, dg, vocab, self.stream)
+        else:
+            self._call("sj_embedding_bwd", _ptr(enc.dx), _ptr(self.ids), self.g_ptr(emb), n, de, VOCAB, self.stream)
 
     # ------------------------------------------------------------------ public step API
     def _local_forward_backward(self):
@@ -713,6 +759,14 @@ class ByteTrainer:
         """Copy a batch (host or device int32 tensors) into the step's input buffers."""
         self.ids.copy_(torch.as_tensor(ids, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
         self.targets.copy_(torch.as_tensor(targets, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
+
+    def stage_requests(self, ids, sel, labels, non_blocking=True):
+        """NativeValue mode: a batch of requests (sejong_b200.value.request_batch) and their labels."""
+        if not self.values:
+            raise ValueError("stage_requests needs a trainer built with TrainConfig.values > 0")
+        self.ids.copy_(torch.as_tensor(ids, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
+        self.sel.copy_(torch.as_tensor(sel, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
+        self.labels.copy_(torch.as_tensor(labels, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
 
     # ------------------------------------------------------------------ artifacts
     def save_checkpoint(self, directory, data_fingerprint=None, rng_state=None):
@@ -854,7 +908,7 @@ class ByteTrainer:
         h = c.hierarchy
         if h is None:
             stage_cost(global_stage(c), b * t, t)
-            lin += 2 * b * t * c.width * VOCAB
+            lin += 2 * b * c.width * self.values if self.values else 2 * b * t * c.width * VOCAB
         else:
             p = t // h.patch_size
             stage_cost(local_stage(c, True), b * t, t)
@@ -864,7 +918,9 @@ class ByteTrainer:
             lin += 2 * b * p * c.width * h.decoder_width            # global_to_decoder
             lin += 2 * b * t * h.encoder_width * h.decoder_width    # encoder_to_decoder
             lin += 2 * b * t * h.decoder_width * c.width            # output_projection
-            lin += 2 * b * t * c.width * VOCAB                      # head
+            lin += 2 * b * c.width * self.values if self.values else 2 * b * t * c.width * VOCAB  # head
+            if self.values:
+                lin += 2 * b * t * c.width * h.encoder_width        # input_projection
         total = 3 * lin + 3 * att  # fwd + (dX + dW) for linear; fwd (4) + bwd (8) for attention
         if self.vjp is not None:
             # executed work of the parameter VJP instead of the dense dW of each compressed group:
