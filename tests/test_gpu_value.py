@@ -84,3 +84,22 @@ def test_value_step_parity_dense_body():
     from sejong_b200 import model as pm
     c = pm.with_(pm.config_c1(), layers=2)
     _parity(c, values=5, batch=16, seed=8)
+
+
+def test_planner_sizes_the_batch_from_device_memory():
+    """value_execution::prepare with the device's free memory (cudaMemGetInfo) and a workspace
+    budget: the planned batch is positive, within the inventory, and this build's trainer (every
+    activation retained) allocates at that batch without running out of memory."""
+    from sejong_b200 import model as pm
+    from sejong_b200 import planner
+    from sejong_b200 import value as pv
+    c = pm.small_hierarchy()
+    prompts = _prompts(300, 5)
+    free = planner.available_bytes(0)
+    assert free > 0
+    p = planner.plan(c, prompts, 6, len(prompts), free, memory_bytes=512 << 20)
+    assert 1 <= p.batch <= len(prompts) and p.available <= free
+    ok, used = planner.fits_this_build(c, p.batch, pv.sequence_for(c, prompts), 6, 0)
+    print("planned batch", p.batch, "checkpointing", p.checkpointing, "reference bytes",
+          p.fixed_bytes + p.workspace_bytes, "this build allocates", used)
+    assert ok and used > 0
