@@ -35,19 +35,26 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "train_bytes_per_s"
-WORKLOADS = {"c3": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
+WORKLOADS = {"c1": "C1 dense byte model, one training step in fp32: fwd+bwd+AdamW (BASELINE configs[0]), f32 CUDA-core "
+                   "GEMMs and attention",
+             "c3": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
              "c4": "C4 hierarchical byte model, fwd + input VJP + parameter VJP (rank 16, fraction 0.25) + "
                    "compact SGD lr 1e-2 (BASELINE configs[3])",
              "c5": "C5 byte MoE model, fwd+bwd+AdamW (BASELINE configs[4]): on one GPU all 8 experts of a layer "
                    "are local; on N GPUs each owns 8/N experts and routed rows move over NVLink peer memory "
                    "(expert parallelism), the rest is data parallel"}
-MODELS = {"c3": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
+MODELS = {"c1": "dense byte model: d256 x4, HQ4/HK2, SwiGLU 1024, eps 1e-6, RoPE 1e4",
+          "c3": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
           "c4": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
           "c5": "byte MoE model: local d256 2+2 layers W128, global d1024 x12 HQ16/HK4, 8 SwiGLU experts of 2816 "
                 "top-2 (router N(0,0.006))"}
-SHAPES = {"c3": (8, 4096), "c4": (8, 4096), "c5": (4, 8192)}  # per-GPU batch x bytes
+SHAPES = {"c1": (8, 512), "c3": (8, 4096), "c4": (8, 4096), "c5": (4, 8192)}  # per-GPU batch x bytes
+L2_NOTE = {"c1": "per-step working set of about 0.3 GB (f32 activations) > 126 MB L2; no flush"}
+# the f32 step runs on the CUDA cores: 148 SMs x 128 FMA lanes x 2 FLOP x 1965 MHz (nominal)
+FP32_SIMT_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
 UNIT = "bytes/s"
 CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ = 1, 1024
+CPU_SAMPLES = {"c1": (8, 512)}  # C1 is small enough for the CPU to run the whole step
 # DRAM bytes (read + write) of all GEMM launches of one C3 step, from the ncu launch list of
 # `python bench.py --steps 1 --warmup 3 --no-cpu-baseline --no-kernel-timing` summarised in
 # profiles/c3_step_launch_list.txt (ncu flushes caches between launches: an upper bound)
@@ -62,8 +69,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=None, help="per-GPU batch (default: the config's)")
     ap.add_argument("--seq", type=int, default=None, help="bytes per row (default: the config's)")
-    ap.add_argument("--config", choices=["c2", "c3", "c4", "c5"], default="c3",
-                    help="c3: AdamW (BASELINE configs[2]); c4: parameter-VJP SGD (configs[3]); "
+    ap.add_argument("--config", choices=["c1", "c2", "c3", "c4", "c5"], default="c3",
+                    help="c1: dense fp32 step (BASELINE configs[0]); c3: AdamW (configs[2]); "
+                         "c4: parameter-VJP SGD (configs[3]); "
                          "c2: MiniLM encoder forward (configs[1]); c5: byte MoE (configs[4])")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-kernel-timing", action="store_true")
@@ -138,33 +146,35 @@ def cpu_step_rate(steps, warmup, threads=None, config="c3"):
     from oracle.rng import Rng
     if threads:
         torch.set_num_threads(threads)
-    c = omodel.config_c5() if config == "c5" else omodel.config_c3()
+    c = {"c1": omodel.config_c1, "c5": omodel.config_c5}.get(config, omodel.config_c3)()
     params = omodel.initialize(c)
     corp = synthetic_corpus(1000, 1 << 20)
     rng = Rng(123)
     state = omodel.AdamState()
-    tc = omodel.TrainConfig(sequence=CPU_SAMPLE_SEQ, batch=CPU_SAMPLE_BATCH,
-                            learning_rate=1e-2 if config == "c4" else 3e-4)
+    batch, seq = CPU_SAMPLES.get(config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))
+    tc = omodel.TrainConfig(sequence=seq, batch=batch, learning_rate=1e-2 if config == "c4" else 3e-4)
     vcfg = opv.VjpConfig()
     vrng = Rng(vcfg.seed)
     times = []
     for i in range(warmup + steps):
-        ids, tg = corp.batch(rng, CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ)
+        ids, tg = corp.batch(rng, batch, seq)
         t0 = time.perf_counter()
         if config == "c4":
-            _, grads, _ = opv.vjp_gradients(params, c, ids, tg, CPU_SAMPLE_SEQ, vcfg, vrng)
+            _, grads, _ = opv.vjp_gradients(params, c, ids, tg, seq, vcfg, vrng)
             params, _ = opv.sgd_update(params, grads, tc, i)
         else:
-            loss, grads = omodel.loss_and_grads(params, c, ids, tg, CPU_SAMPLE_SEQ, dtype=torch.float32)
+            loss, grads = omodel.loss_and_grads(params, c, ids, tg, seq, dtype=torch.float32)
             params, _ = omodel.adam_update(params, grads, state, tc)
         params = {k: np.asarray(v, dtype=np.float32) for k, v in params.items()}
         if i >= warmup:
             times.append(time.perf_counter() - t0)
     sec = sum(times) / len(times)
-    return CPU_SAMPLE_BATCH * CPU_SAMPLE_SEQ / sec, sec, torch.get_num_threads()
+    return batch * seq / sec, sec, torch.get_num_threads()
 
 
 def cpu_sample_text(steps, config="c3"):
+    if config == "c1":
+        return f"C1, the whole step (8 x 512 bytes), fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps"
     if config == "c4":
         return (f"C4 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
                 f"FP64 CPU fwd + input VJP + parameter VJP + compact SGD, mean of {steps} steps")
@@ -185,7 +195,9 @@ def run_reference(args):
             "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic Zipf(1.1) bytes, random-init N(0,0.02) weights",
             "config": {"workload": WORKLOADS[args.config] + " (bounded CPU sample)",
-                       "per_gpu_batch": CPU_SAMPLE_BATCH, "seq_len": CPU_SAMPLE_SEQ, "parallelism": "none"},
+                       "per_gpu_batch": CPU_SAMPLES.get(args.config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))[0],
+                       "seq_len": CPU_SAMPLES.get(args.config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))[1],
+                       "parallelism": "none"},
             "impl": "reference",
             "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
                              "sample": cpu_sample_text(steps, args.config)},
@@ -213,6 +225,8 @@ def kernel_timing(trainer, report=None):
         original(name, *a)
         e.record(stream)
         flops = 2.0 * a[9] * a[10] * a[11] if name == "sj_gemm" else 0.0
+        if name == "sj_sgemm":
+            flops = 2.0 * a[8] * a[9] * a[10]
         if name == "sj_gemm_grouped":  # algorithmic rows: the routed ones, not the padded capacity
             routed = trainer.routed_rows()
             flops = 2.0 * a[10] * (a[11] * routed if a[17] == 1 else a[9] * routed)
@@ -256,7 +270,7 @@ def run_ours(args):
 
     rank, world, local, pg = distributed.init_from_env("nccl", timeout_s=300)
     torch.cuda.set_device(local)
-    cfg = pm.config_c5() if args.config == "c5" else pm.config_c3()
+    cfg = {"c1": pm.config_c1, "c5": pm.config_c5}.get(args.config, pm.config_c3)()
     if args.batch is None:
         args.batch = SHAPES[args.config][0]
     if args.seq is None:
@@ -270,7 +284,11 @@ def run_ours(args):
     # C5 on several GPUs: the experts are sharded over the ranks (expert parallelism), the rest is
     # data parallel
     ep = args.config == "c5" and world > 1
-    trainer = ByteTrainer(cfg, tc, device=local, process_group=pg, expert_parallel=ep)
+    if args.config == "c1":
+        from sejong_b200.train_f32 import F32Trainer
+        trainer = F32Trainer(cfg, tc, device=local, process_group=pg)
+    else:
+        trainer = ByteTrainer(cfg, tc, device=local, process_group=pg, expert_parallel=ep)
     rows = tc.batch * tc.sequence
     total = args.warmup + args.steps
     toks = synthetic_corpus_tokens(distributed.rank_seed(1000, rank), 1 << 22)
@@ -360,7 +378,18 @@ def run_ours(args):
     step_flops = trainer.step_flops()
     tensor_frac = step_flops / (ms / 1e3) / (pk["bf16_sustained"] * 1e12)
     roofline = None
-    if fam:
+    if fam and args.config == "c1":
+        g = fam.get("sj_sgemm")
+        if g and g["ms"] > 0:
+            achieved = g["flops"] / (g["ms"] / 1e3) / 1e12
+            tensor_frac = step_flops / (ms / 1e3) / (FP32_SIMT_PEAK_TFLOPS * 1e12)
+            roofline = {"bound": "fp32 CUDA cores", "kernel": "sgemm_kernel (all f32 GEMMs of one step)",
+                        "achieved": achieved, "peak": FP32_SIMT_PEAK_TFLOPS, "unit": "TFLOP/s",
+                        "frac": achieved / FP32_SIMT_PEAK_TFLOPS,
+                        "peak_source": "nominal fp32 FMA peak (148 SMs x 128 lanes x 2 x 1965 MHz); no measured fp32 "
+                                       "peak in MEASURED_PEAKS.json",
+                        "traffic": None, "launches": g["calls"], "ms_per_step": g["ms"]}
+    elif fam:
         gs = [fam[k] for k in ("sj_gemm", "sj_gemm_grouped") if k in fam]
         g = {"ms": sum(x["ms"] for x in gs), "flops": sum(x["flops"] for x in gs), "calls": sum(x["calls"] for x in gs)}
         if g["ms"] > 0:
@@ -373,13 +402,14 @@ def run_ours(args):
                         "launches": g["calls"], "ms_per_step": g["ms"]}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32" if args.config == "c1" else "bf16",
         "data": "synthetic: Zipf(1.1) bytes from the reference Rng (seed 1000+rank); random-init N(0,0.02) weights",
         "config": {"workload": WORKLOADS[args.config],
                    "model": MODELS[args.config],
                    "global_batch": tc.batch * world, "per_gpu_batch": tc.batch, "seq_len": tc.sequence,
                    "parallelism": f"dp{world}" + (f"+ep{world}" if ep else ""),
-                   "l2": "per-step working set of several GB > 126 MB L2; no flush"},
+                   "l2": L2_NOTE.get(args.config, "per-step working set of several GB > 126 MB L2; no flush")},
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 2 * rows * 4, "d2h_bytes_per_step": 8},
         "gpu_launches": per_step_launches * K,
         "roofline": roofline,

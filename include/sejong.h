@@ -256,6 +256,38 @@ int sj_route_topk_bwd(const float* logits, int ld, const int32_t* ids, const flo
                       void* dlogits, int ldd, int rows, int experts, int k, void* stream);
 int sj_moe_dispatch_bwd(const float* da, const int32_t* pos, float* dz, int ldz, int rows, int k, int d, void* stream);
 
+/* ------------------------------------------------------------------ f32 step (BASELINE C1) */
+/* The step in f32 arithmetic (the reference's DType::F32 precision): every operand, activation and
+ * gradient f32, f32 FMA accumulation on the CUDA cores.
+ *   sj_sgemm           C [m, n] = op(A) op(B) (f32) with the epilogues of sj_gemm: SJ_EPI_STORE, ACCUM
+ *                      (C +=), RESIDUAL (C = AB + aux), ROPE (pairs of the first rope_cols columns rotated by
+ *                      rope_table [rope_t, 64] at position row % rope_t), SWIGLU (C = the interleaved
+ *                      gate|up blocks of 16, aux [m, n/2] = silu(g) u; no rounding of g, u).
+ *   sj_rmsnorm_fwd_f32 sj_rmsnorm_fwd with an f32 x and y.  The backward is sj_rmsnorm_bwd (f32 x,
+ *                      dres_bf16 = NULL).
+ *   sj_cross_entropy_f32  sj_cross_entropy with f32 dlogits.
+ *   sj_swiglu_bwd_f32  sj_swiglu_bwd on f32 gu, dh, dgu.
+ *   sj_attn_f32_fwd / _bwd  sj_attn_gqa_fwd / _bwd on f32 q, k, v, o, dO, dq, dk, dv; the backward takes
+ *                      sj_attn_f32_workspace(batch, t, hq) floats and the RoPE table (inverse rotation of
+ *                      dq and dk). */
+int sj_sgemm(const float* a, int lda, int a_trans, const float* b, int ldb, int b_trans, float* c, int ldc, int m,
+             int n, int k, int epilogue, float* aux, int ld_aux, const float* rope_table, int rope_cols, int rope_t,
+             void* stream);
+int sj_rmsnorm_fwd_f32(const float* x, const float* w, float* y, float* inv_rms, int rows, int d, float eps,
+                       void* stream);
+/* sj_embedding_fwd with an f32 table and output (y[i] = w[ids[i]], row copies). */
+int sj_embedding_fwd_f32(const float* w, const int32_t* ids, float* y, int n, int d, int vocab, void* stream);
+int sj_cross_entropy_f32(const float* logits, int ld, const int32_t* targets, int rows, int vocab, float seed,
+                         float* loss_rows, float* dlogits, int ld_d, double* loss_sum, double weight, void* stream);
+int sj_swiglu_bwd_f32(const float* gu, const float* dh, float* dgu, int rows, int f, void* stream);
+int sj_attn_f32_fwd(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, float* o, int ldo,
+                    float* lse, int batch, int t, int hq, int hk, int head_dim, int window, void* stream);
+size_t sj_attn_f32_workspace(int batch, int t, int hq);
+int sj_attn_f32_bwd(const float* q, int ldq, const float* k, int ldk, const float* v, int ldv, const float* o, int ldo,
+                    const float* lse, const float* dout, int lddo, float* dq, int lddq, float* dk, int lddk, float* dv,
+                    int lddv, float* workspace, int batch, int t, int hq, int hk, int head_dim, int window,
+                    const float* rope_table, void* stream);
+
 /* ------------------------------------------------------------------ NativeValue head */
 /* The categorical value head of NativeValue::forward_batch (crates/sejong-model/src/native/value.rs:
  * 111-160) with its loss (Engine::cross_entropy, lib.rs:524-543) and backward.  hidden bf16 [rows,

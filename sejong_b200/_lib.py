@@ -39,6 +39,19 @@ SIGNATURES = {
     "sj_route_topk_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
                                   c_void_p]),
     "sj_moe_dispatch_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "sj_sgemm": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                         c_void_p, c_int, c_void_p, c_int, c_int, c_void_p]),
+    "sj_embedding_fwd_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "sj_rmsnorm_fwd_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
+    "sj_cross_entropy_f32": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p, c_int,
+                                     c_void_p, c_double, c_void_p]),
+    "sj_swiglu_bwd_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "sj_attn_f32_fwd": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int,
+                                c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "sj_attn_f32_workspace": (c_size_t, [c_int, c_int, c_int]),
+    "sj_attn_f32_bwd": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
+                                c_int, c_int, c_int, c_void_p, c_void_p]),
     "sj_value_head_fwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
                                   c_float, c_void_p, c_void_p, c_void_p, c_double, c_void_p]),
     "sj_value_head_bwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,

@@ -340,6 +340,21 @@ extern "C" int sj_embedding_fwd(const void* w, const int32_t* ids, void* y, int 
   return SJ_OK;
 }
 
+// f32 table and output: the same 16-byte row gather, four floats per vector.
+extern "C" int sj_embedding_fwd_f32(const float* w, const int32_t* ids, float* y, int n, int d, int vocab,
+                                    void* stream) {
+  if (n <= 0 || d <= 0 || d % 4 || vocab <= 0)
+    return fail(SJ_ERR_SHAPE, "sj_embedding_fwd_f32: d=%d must be a multiple of 4", d);
+  if (!aligned16(w) || !aligned16(y) || !ids)
+    return fail(SJ_ERR_ARGUMENT, "sj_embedding_fwd_f32: 16-byte alignment required");
+  const int vpr = d / 4;
+  const size_t total = static_cast<size_t>(n) * vpr;
+  launch(embedding_fwd_kernel<false>, static_cast<unsigned>((total + 255) / 256), 256, 0, as_stream(stream),
+         reinterpret_cast<const uint4*>(w), ids, static_cast<void*>(y), n, vpr, vocab);
+  SJ_LAUNCH_CHECK("embedding_fwd_f32");
+  return SJ_OK;
+}
+
 extern "C" int sj_embedding_bwd(const float* dy, const int32_t* ids, float* dw, int n, int d, int vocab, void* stream) {
   if (n <= 0 || d <= 0 || vocab <= 0 || vocab > 1024) return fail(SJ_ERR_SHAPE, "sj_embedding_bwd: bad shape");
   dim3 grid((n + kEmbRows - 1) / kEmbRows, (d + 31) / 32);

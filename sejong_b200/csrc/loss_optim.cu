@@ -8,9 +8,13 @@ namespace sj {
 
 // ---------------------------------------------------------------- cross entropy
 // One warp per row.  kernels.py:176-191 (forward, backward), kernels.py:254-262 (loss_summary).
+SJ_DEVICE void store_grad(__nv_bfloat16* d, float g) { *d = f2bf(g); }
+SJ_DEVICE void store_grad(float* d, float g) { *d = g; }
+
+template <typename D>
 __global__ void cross_entropy_kernel(const float* logits, int ld, const int32_t* targets,
                                      int rows, int vocab, float seed, float* loss_rows,
-                                     __nv_bfloat16* dlogits, int ld_d, double* loss_sum,
+                                     D* dlogits, int ld_d, double* loss_sum,
                                      double weight) {
   pdl_wait();
   __shared__ double block_sum[8];
@@ -33,12 +37,12 @@ __global__ void cross_entropy_kernel(const float* logits, int ld, const int32_t*
       contribution = static_cast<double>(loss) * weight;
     }
     if (dlogits) {
-      __nv_bfloat16* d = dlogits + static_cast<size_t>(row) * ld_d;
+      D* d = dlogits + static_cast<size_t>(row) * ld_d;
       const float inv = 1.0f / s;
       for (int j = lane; j < ld_d; j += 32) {
         float g = 0.f;
         if (j < vocab) g = (expf(x[j] - m) * inv - (j == target ? 1.0f : 0.0f)) * seed;
-        d[j] = f2bf(g);
+        store_grad(d + j, g);
       }
     }
   }
@@ -188,9 +192,21 @@ extern "C" int sj_cross_entropy(const float* logits, int ld, const int32_t* targ
   if (rows <= 0 || vocab <= 0 || ld < vocab || (dlogits && ld_d < vocab))
     return fail(SJ_ERR_SHAPE, "sj_cross_entropy: bad shape");
   const int warps = 8;
-  launch(cross_entropy_kernel, (rows + warps - 1) / warps, warps * 32, 0, as_stream(stream), 
+  launch(cross_entropy_kernel<__nv_bfloat16>, (rows + warps - 1) / warps, warps * 32, 0, as_stream(stream),
       logits, ld, targets, rows, vocab, seed, loss_rows, static_cast<__nv_bfloat16*>(dlogits), ld_d, loss_sum, weight);
   SJ_LAUNCH_CHECK("cross_entropy");
+  return SJ_OK;
+}
+
+extern "C" int sj_cross_entropy_f32(const float* logits, int ld, const int32_t* targets, int rows, int vocab,
+                                    float seed, float* loss_rows, float* dlogits, int ld_d, double* loss_sum,
+                                    double weight, void* stream) {
+  if (rows <= 0 || vocab <= 0 || ld < vocab || (dlogits && ld_d < vocab))
+    return fail(SJ_ERR_SHAPE, "sj_cross_entropy_f32: bad shape");
+  const int warps = 8;
+  launch(cross_entropy_kernel<float>, (rows + warps - 1) / warps, warps * 32, 0, as_stream(stream), logits, ld,
+         targets, rows, vocab, seed, loss_rows, dlogits, ld_d, loss_sum, weight);
+  SJ_LAUNCH_CHECK("cross_entropy_f32");
   return SJ_OK;
 }
 

@@ -27,6 +27,13 @@ SJ_DEVICE void load8<float>(const float* p, float (&v)[8]) {
   float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
+template <typename Y>
+SJ_DEVICE void store8(Y* p, const float (&v)[8]);
+template <>
+SJ_DEVICE void store8<float>(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
 SJ_DEVICE void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
   uint4 w;
   w.x = pack_bf16x2(v[0], v[1]);
@@ -36,8 +43,11 @@ SJ_DEVICE void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
   *reinterpret_cast<uint4*>(p) = w;
 }
 
-template <typename T, int VEC>
-__global__ void rmsnorm_fwd_kernel(const T* x, const float* w, __nv_bfloat16* y,
+template <>
+SJ_DEVICE void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) { store8_bf16(p, v); }
+
+template <typename T, int VEC, typename Y = __nv_bfloat16>
+__global__ void rmsnorm_fwd_kernel(const T* x, const float* w, Y* y,
                                    float* inv_rms, int rows, int d, float eps) {
   pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -64,7 +74,7 @@ __global__ void rmsnorm_fwd_kernel(const T* x, const float* w, __nv_bfloat16* y,
       float o[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * w[col + j];
-      store8_bf16(y + base + col, o);
+      store8<Y>(y + base + col, o);
     }
   }
   if (inv_rms && lane == 0) inv_rms[warp] = inv;
@@ -171,12 +181,12 @@ __global__ void __launch_bounds__(256) column_reduce_add_kernel(const float* par
 
 namespace sj {
 
-template <typename T, int VEC>
+template <typename T, int VEC, typename Y = __nv_bfloat16>
 static void launch_norm_fwd(const void* x, const float* w, void* y, float* inv, int rows, int d, float eps,
                             cudaStream_t s) {
   const int threads = 256, warps = threads / 32;
-  launch(rmsnorm_fwd_kernel<T, VEC>, (rows + warps - 1) / warps, threads, 0, s, 
-      static_cast<const T*>(x), w, static_cast<__nv_bfloat16*>(y), inv, rows, d, eps);
+  launch(rmsnorm_fwd_kernel<T, VEC, Y>, (rows + warps - 1) / warps, threads, 0, s,
+      static_cast<const T*>(x), w, static_cast<Y*>(y), inv, rows, d, eps);
 }
 
 template <typename T, int VEC>
@@ -225,6 +235,23 @@ extern "C" int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* 
   else
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd: x must be bf16 or f32");
   SJ_LAUNCH_CHECK("rmsnorm_fwd");
+  return SJ_OK;
+}
+
+extern "C" int sj_rmsnorm_fwd_f32(const float* x, const float* w, float* y, float* inv_rms, int rows, int d, float eps,
+                                  void* stream) {
+  using namespace sj;
+  if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
+    return fail(SJ_ERR_SHAPE, "sj_rmsnorm_fwd_f32: d=%d must be a multiple of 8 up to 1024", d);
+  if (!aligned16(x) || !aligned16(y)) return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd_f32: x/y must be 16-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  switch ((d + 255) / 256) {
+    case 1: launch_norm_fwd<float, 1, float>(x, w, y, inv_rms, rows, d, eps, s); break;
+    case 2: launch_norm_fwd<float, 2, float>(x, w, y, inv_rms, rows, d, eps, s); break;
+    case 3: launch_norm_fwd<float, 3, float>(x, w, y, inv_rms, rows, d, eps, s); break;
+    default: launch_norm_fwd<float, 4, float>(x, w, y, inv_rms, rows, d, eps, s); break;
+  }
+  SJ_LAUNCH_CHECK("rmsnorm_fwd_f32");
   return SJ_OK;
 }
 
