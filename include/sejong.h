@@ -288,6 +288,19 @@ int sj_attn_f32_bwd(const float* q, int ldq, const float* k, int ldk, const floa
                     int lddv, float* workspace, int batch, int t, int hq, int hk, int head_dim, int window,
                     const float* rope_table, void* stream);
 
+/* ------------------------------------------------------------------ KV-cached inference */
+/* cached_blocks (crates/sejong-model/src/architecture.rs:474-533).
+ *   sj_attn_cached  Engine::attention_grouped with OFFSET: q bf16 [rows, ldq] holds the chunk's RoPE'd
+ *                   queries at positions offset .. offset + rows - 1; k_cache / v_cache bf16 [offset +
+ *                   rows, ld] hold every position up to the chunk's last (the chunk's own rows
+ *                   appended first); causal with an optional window; o bf16 [rows, ldo].  Up to 16384
+ *                   visible keys per row.
+ *   sj_copy_rows    rows x row_bytes copy between strided buffers (the K/V append), 16-byte multiples. */
+int sj_attn_cached(const void* q, int ldq, const void* k_cache, int ldk, const void* v_cache, int ldv, void* o,
+                   int ldo, int rows, int offset, int hq, int hk, int head_dim, int window, void* stream);
+int sj_copy_rows(const void* src, size_t ld_src_bytes, void* dst, size_t ld_dst_bytes, int rows, size_t row_bytes,
+                 void* stream);
+
 /* ------------------------------------------------------------------ NativeValue head */
 /* The categorical value head of NativeValue::forward_batch (crates/sejong-model/src/native/value.rs:
  * 111-160) with its loss (Engine::cross_entropy, lib.rs:524-543) and backward.  hidden bf16 [rows,

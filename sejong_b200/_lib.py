@@ -52,6 +52,9 @@ SIGNATURES = {
     "sj_attn_f32_bwd": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                 c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
                                 c_int, c_int, c_int, c_void_p, c_void_p]),
+    "sj_attn_cached": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
+                               c_int, c_int, c_int, c_void_p]),
+    "sj_copy_rows": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_int, c_size_t, c_void_p]),
     "sj_value_head_fwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
                                   c_float, c_void_p, c_void_p, c_void_p, c_double, c_void_p]),
     "sj_value_head_bwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
