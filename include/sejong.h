@@ -300,6 +300,10 @@ int sj_attn_cached(const void* q, int ldq, const void* k_cache, int ldk, const v
                    int ldo, int rows, int offset, int hq, int hk, int head_dim, int window, void* stream);
 int sj_copy_rows(const void* src, size_t ld_src_bytes, void* dst, size_t ld_dst_bytes, int rows, size_t row_bytes,
                  void* stream);
+/* The patch state of hierarchical decoding (architecture.rs:749-770): acc f32 [d] = (reset ? 0 : acc) +
+ * the sum of rows bf16 x [rows, ldx]; y bf16 [n] = x f32 * alpha. */
+int sj_rows_sum_f32(const void* x, int ldx, int rows, int d, float* acc, int reset, void* stream);
+int sj_scale_to_bf16(const float* x, int n, float alpha, void* y, void* stream);
 
 /* ------------------------------------------------------------------ NativeValue head */
 /* The categorical value head of NativeValue::forward_batch (crates/sejong-model/src/native/value.rs:

@@ -55,6 +55,8 @@ SIGNATURES = {
     "sj_attn_cached": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                                c_int, c_int, c_int, c_void_p]),
     "sj_copy_rows": (c_int, [c_void_p, c_size_t, c_void_p, c_size_t, c_int, c_size_t, c_void_p]),
+    "sj_rows_sum_f32": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
+    "sj_scale_to_bf16": (c_int, [c_void_p, c_int, c_float, c_void_p, c_void_p]),
     "sj_value_head_fwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,
                                   c_float, c_void_p, c_void_p, c_void_p, c_double, c_void_p]),
     "sj_value_head_bwd": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p,

@@ -92,9 +92,43 @@ __global__ void copy_rows_kernel(const uint8_t* src, size_t ld_src, uint8_t* dst
   *reinterpret_cast<uint4*>(dst + r * ld_dst + c * 16) = *reinterpret_cast<const uint4*>(src + r * ld_src + c * 16);
 }
 
+// acc[c] = (reset ? 0 : acc[c]) + sum_r x[r, c]  (f32; thread per column) -- the running sum of the
+// encoded bytes of the current patch (architecture.rs:749-756, row_mean x count)
+__global__ void rows_sum_kernel(const __nv_bfloat16* x, int ldx, int rows, int d, float* acc, int reset) {
+  pdl_wait();
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= d) return;
+  float s = reset ? 0.f : acc[c];
+  for (int r = 0; r < rows; ++r) s += bf2f(x[static_cast<size_t>(r) * ldx + c]);
+  acc[c] = s;
+}
+
+// y = bf16(x * alpha): the pooled patch (architecture.rs:760-762)
+__global__ void scale_to_bf16_kernel(const float* x, int n, float alpha, __nv_bfloat16* y) {
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = f2bf(x[i] * alpha);
+}
+
 }  // namespace sj
 
 using namespace sj;
+
+extern "C" int sj_rows_sum_f32(const void* x, int ldx, int rows, int d, float* acc, int reset, void* stream) {
+  if (rows < 0 || d <= 0 || ldx < d) return fail(SJ_ERR_SHAPE, "sj_rows_sum_f32: bad shape");
+  if (!acc || (rows > 0 && !x)) return fail(SJ_ERR_ARGUMENT, "sj_rows_sum_f32: null");
+  launch(rows_sum_kernel, (d + 127) / 128, 128, 0, as_stream(stream), static_cast<const __nv_bfloat16*>(x), ldx, rows,
+         d, acc, reset);
+  SJ_LAUNCH_CHECK("rows_sum");
+  return SJ_OK;
+}
+
+extern "C" int sj_scale_to_bf16(const float* x, int n, float alpha, void* y, void* stream) {
+  if (n <= 0 || !x || !y) return fail(SJ_ERR_ARGUMENT, "sj_scale_to_bf16: bad argument");
+  launch(scale_to_bf16_kernel, (n + 255) / 256, 256, 0, as_stream(stream), x, n, alpha, static_cast<__nv_bfloat16*>(y));
+  SJ_LAUNCH_CHECK("scale_to_bf16");
+  return SJ_OK;
+}
 
 extern "C" int sj_attn_cached(const void* q, int ldq, const void* k_cache, int ldk, const void* v_cache, int ldv,
                               void* o, int ldo, int rows, int offset, int hq, int hk, int head_dim, int window,

@@ -1,7 +1,7 @@
 """KV-cached inference and generation for the byte model.
 
 Restates `Model::forward_cached` / `hidden_cached` (crates/sejong-model/src/lib.rs:362-390,
-architecture.rs:395-533, 651-799 dense branch) and the runtime's `generate` / `sample`
+architecture.rs:395-799, dense and hierarchical) and the runtime's `generate` / `sample`
 (crates/sejong-runtime/src/lib.rs:27-126) on the library's kernels:
 
   * a cache of K and V rows (bf16) per layer, `context` positions long;
@@ -10,6 +10,12 @@ architecture.rs:395-533, 651-799 dense branch) and the runtime's `generate` / `s
     the cache (sj_copy_rows), attention -- the tcgen05 kernel for a prefill (length 0), the cached
     kernel (sj_attn_cached) over every position up to the row otherwise -- and the rest of the block
     as in training; the final norm; the head on the chunk's last row (f32 logits);
+  * the hierarchical model: a prefill runs encoder, global stage over the (partial) patches and
+    decoder as in training and keeps the patch state -- the global context of the last completed
+    patch (or the BOS projection), the running f32 sum of the encoded bytes of the open patch;
+    afterwards bytes go through encoder and decoder (with the current global context added to
+    every row) and, when a patch completes, its mean goes through the global stage at the patch's
+    position and yields the next global context (architecture.rs:534-779);
   * `generate`: the prompt after EOS, prefilled, then one byte at a time: sample (temperature,
     top-k, top-p with Rng(seed)), stop at EOS or max_bytes; when the cache is full it restarts from
     the last `context` tokens, as the reference does.
@@ -25,7 +31,7 @@ import torch
 
 from . import _lib
 from ._lib import EPI_RESIDUAL, EPI_ROPE, EPI_STORE, EPI_SWIGLU, SJ_BF16, SJ_F32, call
-from .model import EOS, HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize
+from .model import EOS, HEAD_DIM, VOCAB, VOCAB_PAD, FlatLayout, global_stage, initialize, local_stage
 
 
 def _ptr(t, offset_elems=0):
@@ -87,21 +93,43 @@ def sample(logits, options, state):
     return int(order[keep - 1])
 
 
+class _Stage:
+    """K/V caches, RoPE table and working buffers of one stage (encoder, global or decoder) for chunks
+    of up to `rows` rows."""
+
+    def __init__(self, stage, capacity, rows, dev, theta, stream):
+        self.s = stage
+        d, f, cq = stage.width, stage.ffn, stage.qkv_width
+        self.kvw = stage.kv_heads * HEAD_DIM
+        bf, f32 = torch.bfloat16, torch.float32
+        e = lambda *shape, dt=bf: torch.empty(*shape, dtype=dt, device=dev)  # noqa: E731
+        self.capacity = capacity
+        self.k = [e(capacity, self.kvw) for _ in range(stage.layers)]
+        self.v = [e(capacity, self.kvw) for _ in range(stage.layers)]
+        self.rope = e(capacity * HEAD_DIM, dt=f32)
+        call("sj_rope_table", _ptr(self.rope), capacity, HEAD_DIM, 0, float(theta), stream)
+        self.x, self.x1 = e(rows, d, dt=f32), e(rows, d, dt=f32)
+        self.z, self.qkv, self.o = e(rows, d), e(rows, cq), e(rows, d)
+        self.gu, self.h = e(rows, 2 * f), e(rows, f)
+        self.inv, self.lse = e(rows, dt=f32), e(rows * stage.heads, dt=f32)
+
+
 class Generator:
-    """KV-cached forward of the dense byte model on one GPU.  `forward_cached(tokens)` appends the
-    tokens to the cache and returns the f32 logits [257] of the last one; `reset()` empties the
-    cache; `generate(prompt, Sampling)` returns (bytes, ended)."""
+    """KV-cached forward of the byte model (dense or hierarchical) on one GPU.  `forward_cached(tokens)`
+    appends the tokens and returns the f32 logits [257] of the last one; `hidden_cached(tokens)`
+    returns the final-norm rows of the chunk; `reset()` empties the cache; `generate(prompt,
+    Sampling)` returns (bytes, ended)."""
 
     def __init__(self, config, params=None, device=None, context=None):
-        if config.hierarchy is not None or config.experts is not None:
-            raise ValueError("cached inference covers the dense byte model")
+        if config.experts is not None:
+            raise ValueError("cached inference covers the dense and hierarchical byte models without experts")
         self.c = c = config
         self.dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
         torch.cuda.set_device(self.dev)
         self.lib = _lib.load()
         call("sj_device_init", self.dev.index)
         self.stream = torch.cuda.current_stream(self.dev).cuda_stream
-        self.context = int(context or c.context)
+        self.context = L = int(context or c.context)
         self.layout = FlatLayout(c)
         if params is None:
             params = initialize(c, self.lib)
@@ -109,20 +137,29 @@ class Generator:
         self.w = torch.from_numpy(self.layout.pack(params)).to(self.dev)
         self.wb = torch.empty(self.layout.total, dtype=torch.bfloat16, device=self.dev)
         call("sj_cast", _ptr(self.w), SJ_F32, _ptr(self.wb), SJ_BF16, self.layout.total, self.stream)
-        self.s = s = global_stage(c)
-        L, d, f, cq = self.context, s.width, s.ffn, s.qkv_width
-        self.kvw = s.kv_heads * HEAD_DIM
         bf, f32 = torch.bfloat16, torch.float32
         e = lambda *shape, dt=bf: torch.empty(*shape, dtype=dt, device=self.dev)  # noqa: E731
-        self.k_cache = [e(L, self.kvw) for _ in range(s.layers)]
-        self.v_cache = [e(L, self.kvw) for _ in range(s.layers)]
-        self.rope = e(L * HEAD_DIM, dt=f32)
-        call("sj_rope_table", _ptr(self.rope), L, HEAD_DIM, 0, float(c.rope_theta), self.stream)
         self.ids = torch.zeros(L, dtype=torch.int32, device=self.dev)
-        self.x, self.x1 = e(L, d, dt=f32), e(L, d, dt=f32)
-        self.z, self.qkv, self.o = e(L, d), e(L, cq), e(L, d)
-        self.gu, self.h = e(L, 2 * f), e(L, f)
-        self.inv, self.lse = e(L, dt=f32), e(L * s.heads, dt=f32)
+        self.h = h = c.hierarchy
+        if h is None:
+            self.glob = _Stage(global_stage(c), L, L, self.dev, c.rope_theta, self.stream)
+        else:
+            P = h.patch_size
+            self.patches_cap = -(-L // P)
+            self.enc = _Stage(local_stage(c, True), L, L, self.dev, c.rope_theta, self.stream)
+            self.glob = _Stage(global_stage(c), self.patches_cap, self.patches_cap, self.dev, c.rope_theta, self.stream)
+            self.dec = _Stage(local_stage(c, False), L, L, self.dev, c.rope_theta, self.stream)
+            de, dg, dd = h.encoder_width, c.width, h.decoder_width
+            self.zE = e(L, de)                       # encoded bytes (encoder norm output)
+            self.pooled = e(self.patches_cap, de)
+            self.zd = e(self.patches_cap, dd)        # global contexts (global_to_decoder of each patch)
+            self.bos = e(1, dd)
+            self.gctx = e(1, dd)                     # the global context of the current patch
+            self.patch_sum = e(de, dt=f32)
+            self.y = e(L, dg, dt=f32)
+            self.final = e(L, dg)
+            self.patch_count = 0
+            self.have_ctx = False
         self.logits = e(1, VOCAB_PAD, dt=f32)
         self.length = 0
 
@@ -133,58 +170,167 @@ class Generator:
         call("sj_gemm", a, lda, 0, b, ldb, 0, c, ldc, c_dtype, m, n, k, epi, 1.0, aux, ld_aux, rope_cols, rope_t,
              float(self.c.rope_theta) if epi == EPI_ROPE else 0.0, 0, self.stream)
 
-    def _norm(self, x, name, rows):
-        call("sj_rmsnorm_fwd", _ptr(x), SJ_F32, _ptr(self.w, self.layout[name].offset), _ptr(self.z), _ptr(self.inv),
-             rows, self.s.width, float(self.c.norm_epsilon), self.stream)
+    def _norm(self, x, name, y, inv, rows, d):
+        """y (a tensor or a device address) = RMSNorm(x) with the f32 norm weight `name`."""
+        y = y if isinstance(y, int) else _ptr(y)
+        call("sj_rmsnorm_fwd", _ptr(x), SJ_F32, _ptr(self.w, self.layout[name].offset), y, _ptr(inv), rows, d,
+             float(self.c.norm_epsilon), self.stream)
 
     def reset(self):
+        """HierarchyCache::reset and an empty cache (architecture.rs:406-412)."""
         self.length = 0
+        if self.h is not None:
+            self.patch_count = 0
+            self.have_ctx = False
 
-    def hidden_cached(self, tokens):
-        """Append `tokens` at position `length`; returns the final-norm rows of the chunk (bf16 view)."""
-        tokens = np.asarray(tokens, dtype=np.int32).reshape(-1)
-        n, off = len(tokens), self.length
-        if n == 0 or np.any(tokens < 0) or np.any(tokens > EOS):
-            raise ValueError("input tokens must be bytes or EOS")
-        if off + n > self.context:
-            raise ValueError("KV cache context limit reached")
-        self.stream = torch.cuda.current_stream(self.dev).cuda_stream
-        s, c = self.s, self.c
-        d, f, cq, kvw = s.width, s.ffn, s.qkv_width, self.kvw
+    def _blocks(self, st, n, offset):
+        """cached_blocks (architecture.rs:474-533) on st.x [n, d] (f32, in place) at position `offset`."""
+        s = st.s
+        d, f, cq, kvw = s.width, s.ffn, s.qkv_width, st.kvw
         kq, vq = s.heads * HEAD_DIM, (s.heads + s.kv_heads) * HEAD_DIM
-        self.ids[:n].copy_(torch.from_numpy(tokens), non_blocking=False)
-        call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids), _ptr(self.x), SJ_F32, n, d, VOCAB,
-             self.stream)
+        if offset + n > st.capacity:
+            raise ValueError("KV cache context limit reached")
         for i in range(s.layers):
             p = f"{s.prefix}.{i}"
-            self._norm(self.x, f"{p}.attention_norm", n)
-            self._gemm(_ptr(self.z), d, self.wb_ptr(f"{p}.qkv"), cq, _ptr(self.qkv), cq, SJ_BF16, n, cq, d, EPI_ROPE,
-                       aux=_ptr(self.rope, off * HEAD_DIM), rope_cols=vq, rope_t=self.context - off)
-            for cache, col in ((self.k_cache[i], kq), (self.v_cache[i], vq)):
-                call("sj_copy_rows", _ptr(self.qkv, col), cq * 2, _ptr(cache, off * kvw), kvw * 2, n, kvw * 2,
+            self._norm(st.x, f"{p}.attention_norm", st.z, st.inv, n, d)
+            self._gemm(_ptr(st.z), d, self.wb_ptr(f"{p}.qkv"), cq, _ptr(st.qkv), cq, SJ_BF16, n, cq, d, EPI_ROPE,
+                       aux=_ptr(st.rope, offset * HEAD_DIM), rope_cols=vq, rope_t=st.capacity - offset)
+            for cache, col in ((st.k[i], kq), (st.v[i], vq)):
+                call("sj_copy_rows", _ptr(st.qkv, col), cq * 2, _ptr(cache, offset * kvw), kvw * 2, n, kvw * 2,
                      self.stream)
-            if off == 0:
-                call("sj_attn_gqa_fwd", _ptr(self.qkv), cq, _ptr(self.qkv, kq), cq, _ptr(self.qkv, vq), cq,
-                     _ptr(self.o), d, _ptr(self.lse), 1, n, s.heads, s.kv_heads, HEAD_DIM, s.window, self.stream)
+            if offset == 0:
+                call("sj_attn_gqa_fwd", _ptr(st.qkv), cq, _ptr(st.qkv, kq), cq, _ptr(st.qkv, vq), cq, _ptr(st.o), d,
+                     _ptr(st.lse), 1, n, s.heads, s.kv_heads, HEAD_DIM, s.window, self.stream)
             else:
-                call("sj_attn_cached", _ptr(self.qkv), cq, _ptr(self.k_cache[i]), kvw, _ptr(self.v_cache[i]), kvw,
-                     _ptr(self.o), d, n, off, s.heads, s.kv_heads, HEAD_DIM, s.window, self.stream)
-            self._gemm(_ptr(self.o), d, self.wb_ptr(f"{p}.attention_output"), d, _ptr(self.x1), d, SJ_F32, n, d, d,
-                       EPI_RESIDUAL, aux=_ptr(self.x), ld_aux=d)
-            self._norm(self.x1, f"{p}.ffn_norm", n)
-            self._gemm(_ptr(self.z), d, self.wb_ptr(f"{p}.gate_up"), 2 * f, _ptr(self.gu), 2 * f, SJ_BF16, n, 2 * f,
-                       d, EPI_SWIGLU, aux=_ptr(self.h), ld_aux=f)
-            self._gemm(_ptr(self.h), f, self.wb_ptr(f"{p}.down"), d, _ptr(self.x), d, SJ_F32, n, d, f, EPI_RESIDUAL,
-                       aux=_ptr(self.x1), ld_aux=d)
-        self._norm(self.x, "final_norm", n)
-        self.length = off + n
-        return self.z[:n]
+                call("sj_attn_cached", _ptr(st.qkv), cq, _ptr(st.k[i]), kvw, _ptr(st.v[i]), kvw, _ptr(st.o), d, n,
+                     offset, s.heads, s.kv_heads, HEAD_DIM, s.window, self.stream)
+            self._gemm(_ptr(st.o), d, self.wb_ptr(f"{p}.attention_output"), d, _ptr(st.x1), d, SJ_F32, n, d, d,
+                       EPI_RESIDUAL, aux=_ptr(st.x), ld_aux=d)
+            self._norm(st.x1, f"{p}.ffn_norm", st.z, st.inv, n, d)
+            self._gemm(_ptr(st.z), d, self.wb_ptr(f"{p}.gate_up"), 2 * f, _ptr(st.gu), 2 * f, SJ_BF16, n, 2 * f, d,
+                       EPI_SWIGLU, aux=_ptr(st.h), ld_aux=f)
+            self._gemm(_ptr(st.h), f, self.wb_ptr(f"{p}.down"), d, _ptr(st.x), d, SJ_F32, n, d, f, EPI_RESIDUAL,
+                       aux=_ptr(st.x1), ld_aux=d)
+
+    def _embed(self, tokens, x, d, start=0):
+        n = len(tokens)
+        self.ids[start:start + n].copy_(torch.from_numpy(np.asarray(tokens, dtype=np.int32)), non_blocking=False)
+        call("sj_embedding_fwd", self.wb_ptr("embedding"), _ptr(self.ids, start), _ptr(x), SJ_F32, n, d, VOCAB,
+             self.stream)
+
+    def _decoder_tail(self, n, row0):
+        """decoder blocks -> decoder norm -> output projection -> final norm into self.final[row0:row0+n]."""
+        h, c = self.h, self.c
+        dd, dg = h.decoder_width, c.width
+        dec = self.dec
+        self._norm(dec.x, "decoder_norm", dec.z, dec.inv, n, dd)
+        self._gemm(_ptr(dec.z), dd, self.wb_ptr("output_projection"), dg, _ptr(self.y), dg, SJ_F32, n, dg, dd)
+        self._norm(self.y, "final_norm", _ptr(self.final, row0 * dg), dec.inv, n, dg)
+
+    def hidden_cached(self, tokens):
+        """Model::hidden_cached (architecture.rs:651-799): append `tokens` at position `length`; returns
+        the final-norm rows of the chunk (bf16)."""
+        tokens = [int(t) for t in np.asarray(tokens).reshape(-1)]
+        if not tokens or min(tokens) < 0 or max(tokens) > EOS:
+            raise ValueError("input tokens must be bytes or EOS")
+        if self.length + len(tokens) > self.context:
+            raise ValueError("KV cache context limit reached")
+        self.stream = torch.cuda.current_stream(self.dev).cuda_stream
+        c, h = self.c, self.h
+        if h is None:
+            n = len(tokens)
+            g = self.glob
+            self._embed(tokens, g.x, c.width)
+            self._blocks(g, n, self.length)
+            self._norm(g.x, "final_norm", g.z, g.inv, n, c.width)
+            self.length += n
+            return g.z[:n]
+        if self.length == 0 and len(tokens) >= h.patch_size:
+            return self._prefill(tokens)
+        return self._decode(tokens)
+
+    def _bos(self):
+        c, h = self.c, self.h
+        self._gemm(self.wb_ptr("global_bos"), c.width, self.wb_ptr("global_to_decoder"), h.decoder_width,
+                   _ptr(self.bos), h.decoder_width, SJ_BF16, 1, h.decoder_width, c.width)
+
+    def _prefill(self, tokens):
+        """hierarchical_prefill (architecture.rs:534-650)."""
+        c, h = self.c, self.h
+        n, P = len(tokens), h.patch_size
+        de, dg, dd = h.encoder_width, c.width, h.decoder_width
+        enc, glob, dec = self.enc, self.glob, self.dec
+        np_ = -(-n // P)
+        self._embed(tokens, enc.x, de)
+        self._blocks(enc, n, 0)
+        self._norm(enc.x, "encoder_norm", self.zE, enc.inv, n, de)
+        call("sj_patch_pool_fwd", _ptr(self.zE), _ptr(self.pooled), 1, n, de, P, self.stream)
+        self._gemm(_ptr(self.pooled), de, self.wb_ptr("encoder_to_global"), dg, _ptr(glob.x), dg, SJ_F32, np_, dg, de)
+        self._blocks(glob, np_, 0)
+        self._norm(glob.x, "global_norm", glob.z, glob.inv, np_, dg)
+        self._gemm(_ptr(glob.z), dg, self.wb_ptr("global_to_decoder"), dd, _ptr(self.zd), dd, SJ_BF16, np_, dd, dg)
+        self._bos()
+        self._gemm(_ptr(self.zE), de, self.wb_ptr("encoder_to_decoder"), dd, _ptr(dec.x), dd, SJ_F32, n, dd, de)
+        call("sj_patch_broadcast_fwd", _ptr(self.zd), _ptr(self.bos), _ptr(dec.x), SJ_F32, 1, 1, n, dd, P, self.stream)
+        self._blocks(dec, n, 0)
+        self._decoder_tail(n, 0)
+        completed = n // P
+        src = self.bos if completed == 0 else self.zd[completed - 1:completed]
+        call("sj_copy_rows", _ptr(src), dd * 2, _ptr(self.gctx), dd * 2, 1, dd * 2, self.stream)
+        self.have_ctx = True
+        self.patch_count = n % P
+        if self.patch_count:
+            call("sj_rows_sum_f32", _ptr(self.zE, (n - self.patch_count) * de), de, self.patch_count, de,
+                 _ptr(self.patch_sum), 1, self.stream)
+        self.length = n
+        return self.final[:n]
+
+    def _decode(self, tokens):
+        """The patch-by-patch branch of hidden_cached (architecture.rs:672-779)."""
+        c, h = self.c, self.h
+        P = h.patch_size
+        de, dg, dd = h.encoder_width, c.width, h.decoder_width
+        enc, glob, dec = self.enc, self.glob, self.dec
+        total, i = len(tokens), 0
+        while i < total:
+            count = min(P - self.patch_count, total - i)
+            position = self.length + i
+            self._embed(tokens[i:i + count], enc.x, de, start=i)
+            self._blocks(enc, count, position)
+            self._norm(enc.x, "encoder_norm", self.zE, enc.inv, count, de)
+            if not self.have_ctx:
+                self._bos()
+                call("sj_copy_rows", _ptr(self.bos), dd * 2, _ptr(self.gctx), dd * 2, 1, dd * 2, self.stream)
+                self.have_ctx = True
+            self._gemm(_ptr(self.zE), de, self.wb_ptr("encoder_to_decoder"), dd, _ptr(dec.x), dd, SJ_F32, count, dd,
+                       de)
+            # bias_add of the global context: every row of the piece lies in the current patch, so the
+            # broadcast's BOS row (patch index -1) is the context for all of them
+            call("sj_patch_broadcast_fwd", _ptr(self.zd), _ptr(self.gctx), _ptr(dec.x), SJ_F32, 1, 1, count, dd, P,
+                 self.stream)
+            self._blocks(dec, count, position)
+            self._decoder_tail(count, i)
+            call("sj_rows_sum_f32", _ptr(self.zE), de, count, de, _ptr(self.patch_sum), int(self.patch_count == 0),
+                 self.stream)
+            self.patch_count += count
+            if self.patch_count == P:
+                call("sj_scale_to_bf16", _ptr(self.patch_sum), de, 1.0 / P, _ptr(self.pooled), self.stream)
+                self._gemm(_ptr(self.pooled), de, self.wb_ptr("encoder_to_global"), dg, _ptr(glob.x), dg, SJ_F32, 1,
+                           dg, de)
+                self._blocks(glob, 1, position // P)
+                self._norm(glob.x, "global_norm", glob.z, glob.inv, 1, dg)
+                self._gemm(_ptr(glob.z), dg, self.wb_ptr("global_to_decoder"), dd, _ptr(self.gctx), dd, SJ_BF16, 1, dd,
+                           dg)
+                self.patch_count = 0
+            i += count
+        self.length += total
+        return self.final[:total]
 
     def forward_cached(self, tokens):
         """lib.rs:362-372: the chunk, then the head on its last row: f32 logits [257] (device)."""
-        h = self.hidden_cached(tokens)
-        n, d = h.shape[0], self.s.width
-        self._gemm(_ptr(self.z, (n - 1) * d), d, self.wb_ptr("output"), VOCAB_PAD, _ptr(self.logits), VOCAB_PAD, SJ_F32,
+        hs = self.hidden_cached(tokens)
+        n, d = hs.shape[0], self.c.width
+        self._gemm(_ptr(hs, (n - 1) * d), d, self.wb_ptr("output"), VOCAB_PAD, _ptr(self.logits), VOCAB_PAD, SJ_F32,
                    1, VOCAB, d)
         return self.logits[0, :VOCAB]
 
@@ -212,3 +358,4 @@ class Generator:
                 else:
                     logits = self.forward_cached([token])
         return bytes(out), False
+

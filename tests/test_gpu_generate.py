@@ -6,6 +6,10 @@ the dense branch of 651-799; runtime generate, crates/sejong-runtime/src/lib.rs:
 * A prefill (tcgen05 attention at offset 0, ragged length), single-token decode steps and a
   multi-row chunk at an offset reproduce, row for row, the FP64 forward of the whole sequence at the
   bf16-cast weights (2e-2 relative L2, the bf16 bar).
+* The hierarchical model (architecture.rs:534-779): a prefill that ends inside a patch, single bytes
+  across patch boundaries, chunks that span boundaries and a start shorter than a patch reproduce
+  the FP64 forward of the whole sequence row for row (the global stage sees each patch once it is
+  complete, through the running patch sum).
 * Greedy generation picks, at every step, a byte whose FP64 logit is within bf16 noise of the FP64
   maximum given the bytes before it; sampling with the cache wrapping around runs to max_bytes.
 """
@@ -54,9 +58,10 @@ def _model():
 
 
 def _oracle_config(c):
+    h = c.hierarchy
     return omodel.ModelConfig(width=c.width, layers=c.layers, heads=c.heads, ffn_width=c.ffn_width,
                               kv_heads=c.kv_heads, rope_theta=c.rope_theta, norm_epsilon=c.norm_epsilon, seed=c.seed,
-                              init_std=c.init_std)
+                              init_std=c.init_std, hierarchy=None if h is None else omodel.HierarchyConfig(**h.__dict__))
 
 
 def _oracle_logits(params, c, tokens):
@@ -113,3 +118,49 @@ def test_greedy_generation_follows_the_fp64_model_and_wraps_the_cache():
     out2, _ = gen.generate(b"x" * 60, Sampling(max_bytes=150, temperature=1.0, top_p=1.0, seed=5))
     assert gen.length <= 128
     torch.cuda.synchronize()
+
+
+def _full_hidden(params, c, tokens):
+    p = {k: torch.tensor(v, dtype=torch.float64) for k, v in omodel.compute_cast(params, "bf16").items()}
+    with torch.no_grad():
+        return omodel.hidden(p, _oracle_config(c), torch.as_tensor(np.asarray(tokens)), len(tokens)).numpy()
+
+
+@pytest.mark.parametrize("plan", [[37] + [1] * 30 + [20, 13, 1, 1], [5, 1, 1, 9, 2, 30, 1]])
+def test_hierarchical_prefill_and_decode_match_the_full_forward(plan):
+    from sejong_b200 import model as pm
+    from sejong_b200.generate import Generator
+    c = pm.small_hierarchy()
+    params = pm.initialize(c)
+    gen = Generator(c, params, device=0, context=256)
+    rng = np.random.default_rng(len(plan))
+    tokens = [256] + list(rng.integers(0, 256, size=sum(plan) - 1))
+    got, at = [], 0
+    for n in plan:
+        got.append(gen.hidden_cached(tokens[at:at + n]).float().cpu().numpy())
+        at += n
+    torch.cuda.synchronize()
+    got = np.concatenate(got)
+    ref = _full_hidden(params, c, tokens)
+    at = 0
+    for n in plan:
+        assert _rel(got[at:at + n], ref[at:at + n]) < 2e-2, (at, n, _rel(got[at:at + n], ref[at:at + n]))
+        at += n
+    assert gen.length == len(tokens)
+
+
+def test_hierarchical_generation_runs_and_follows_the_model():
+    from sejong_b200 import model as pm
+    from sejong_b200.generate import Generator, Sampling
+    c = pm.small_hierarchy()
+    params = pm.initialize(c)
+    gen = Generator(c, params, device=0, context=64)
+    prompt = b"hierarchy "
+    out, ended = gen.generate(prompt, Sampling(max_bytes=12, temperature=0.0))
+    seq = [256] + list(prompt)
+    for byte in out:
+        ref = _oracle_logits(params, c, seq)[-1][:257]
+        assert ref[byte] >= ref.max() - 0.05 * (np.abs(ref).max() + 1e-6), (len(seq), byte, int(ref.argmax()))
+        seq.append(byte)
+    out2, _ = gen.generate(b"y" * 40, Sampling(max_bytes=60, temperature=1.0, top_p=0.9, seed=9))
+    assert gen.length <= 64
