@@ -131,14 +131,15 @@ int sj_gemm_bias(const void* a, int lda, int a_trans, const void* b, int ldb, in
 
 /* ------------------------------------------------------------------ normalisation, embedding, elementwise */
 /* Engine::norm / rmsnorm (crates/sejong-gpu/src/lib.rs:688-699; kernels.py:54-61).
- * x [rows,d] (x_dtype bf16 or f32), w f32 [d]; y bf16 [rows,d]; inv_rms f32 [rows] (optional). */
+ * x [rows,d] (x_dtype bf16 or f32), w f32 [d]; y bf16 [rows,d]; inv_rms f32 [rows] (optional).
+ * x, y and w 16-byte aligned; d a multiple of 8 up to 1024. */
 int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* inv_rms, int rows, int d, float eps,
                    void* stream);
 /* Engine::norm_backward (crates/sejong-gpu/src/norm_ops.rs:14-134; kernels.py:63-87) fused with the
  * residual gradient accumulation of the tape (graph.rs:503-513):
  *   dres[r,:] += rms_dx(x, w, dz) ;  dres_bf16 = bf16(dres) (optional) ;  dw += sum_r dz*x*inv.
  * x bf16 or f32 (x_dtype), dz f32, dres f32 (in/out), dw f32 accumulated.  `partials` is workspace
- * of at least sj_rmsnorm_workspace(rows, d) floats. */
+ * of at least sj_rmsnorm_workspace(rows, d) floats.  x, dz, dres, dres_bf16 and w 16-byte aligned. */
 size_t sj_rmsnorm_workspace(int rows, int d);
 int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz, float* dres,
                    void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream);

@@ -46,38 +46,65 @@ SJ_DEVICE void store8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
 template <>
 SJ_DEVICE void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&v)[8]) { store8_bf16(p, v); }
 
+// Warp per R consecutive rows (R = 4 / VEC, at least 1): the loads of all R rows are issued before
+// any reduction, so a warp keeps R rows of x in flight (the narrow local-stage rows of 256 would
+// otherwise leave each warp one 1 KB load at a time).
 template <typename T, int VEC, typename Y = __nv_bfloat16>
 __global__ void rmsnorm_fwd_kernel(const T* x, const float* w, Y* y,
                                    float* inv_rms, int rows, int d, float eps) {
   pdl_wait();
+  constexpr int R = VEC >= 4 ? 1 : 4 / VEC;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  const size_t base = static_cast<size_t>(warp) * d;
-  float v[VEC][8];
-  float ss = 0.f;
+  const int row0 = warp * R;
+  if (row0 >= rows) return;
+  float v[R][VEC][8];
+#pragma unroll
+  for (int q = 0; q < R; ++q) {
+    const size_t base = static_cast<size_t>(row0 + q) * d;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int col = (lane + 32 * i) * 8;
+      if (row0 + q < rows && col < d) load8<T>(x + base + col, v[q][i]);
+    }
+  }
+  float inv[R];
+#pragma unroll
+  for (int q = 0; q < R; ++q) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) {
+      const int col = (lane + 32 * i) * 8;
+      if (row0 + q < rows && col < d) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss += v[q][i][j] * v[q][i][j];
+      }
+    }
+    ss = warp_sum(ss);
+    inv[q] = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
+  }
 #pragma unroll
   for (int i = 0; i < VEC; ++i) {
     const int col = (lane + 32 * i) * 8;
     if (col < d) {
-      load8<T>(x + base + col, v[i]);
+      float wv[8];
+      load8<float>(w + col, wv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+      for (int q = 0; q < R; ++q) {
+        if (row0 + q < rows) {
+          float o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = v[q][i][j] * inv[q] * wv[j];
+          store8<Y>(y + static_cast<size_t>(row0 + q) * d + col, o);
+        }
+      }
     }
   }
-  ss = warp_sum(ss);
-  const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
+  if (inv_rms && lane < R && row0 + lane < rows) {
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) {
-    const int col = (lane + 32 * i) * 8;
-    if (col < d) {
-      float o[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * w[col + j];
-      store8<Y>(y + base + col, o);
-    }
+    for (int q = 0; q < R; ++q)
+      if (lane == q) inv_rms[row0 + q] = inv[q];
   }
-  if (inv_rms && lane == 0) inv_rms[warp] = inv;
 }
 
 // One CTA = kNormWarps warps over kNormRowsPerCta rows; per-CTA dw partial row in `partials`.
@@ -95,48 +122,67 @@ __global__ void __launch_bounds__(kNormWarps * 32)
 #pragma unroll
     for (int j = 0; j < 8; ++j) dw_acc[i][j] = 0.f;
   const float inv_d = 1.0f / static_cast<float>(d);
-  for (int r = blockIdx.x * kNormRowsPerCta + warp; r < min(rows, (blockIdx.x + 1) * kNormRowsPerCta);
-       r += kNormWarps) {
-    const size_t base = static_cast<size_t>(r) * d;
-    float xv[VEC][8], gv[VEC][8], o[VEC][8];
-    float dot = 0.f;
-    const float inv = inv_rms[r];
-    // all loads of the row are issued before the reduction: one memory round trip per row
+  // R of the warp's rows (r, r + 8, ...) at a time, all their loads issued before any reduction
+  constexpr int R = VEC == 1 ? 2 : 1;
+  const int end = min(rows, (blockIdx.x + 1) * kNormRowsPerCta);
+  float wv[VEC][8];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      const int col = (lane + 32 * i) * 8;
-      if (col < d) {
-        load8<T>(x + base + col, xv[i]);
-        load8<float>(dz + base + col, gv[i]);
-        load8<float>(dres + base + col, o[i]);
-      }
-    }
+  for (int i = 0; i < VEC; ++i) {
+    const int col = (lane + 32 * i) * 8;
+    if (col < d) load8<float>(w + col, wv[i]);
+  }
+  for (int r0 = blockIdx.x * kNormRowsPerCta + warp; r0 < end; r0 += kNormWarps * R) {
+    float xv[R][VEC][8], gv[R][VEC][8], o[R][VEC][8], inv[R];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      const int col = (lane + 32 * i) * 8;
-      if (col < d) {
+    for (int q = 0; q < R; ++q) {
+      const int r = r0 + q * kNormWarps;
+      if (r < end) {
+        const size_t base = static_cast<size_t>(r) * d;
+        inv[q] = inv_rms[r];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float dzv = gv[i][j];
-          gv[i][j] = dzv * w[col + j];
-          dot += gv[i][j] * xv[i][j];
-          dw_acc[i][j] += dzv * xv[i][j] * inv;
+        for (int i = 0; i < VEC; ++i) {
+          const int col = (lane + 32 * i) * 8;
+          if (col < d) {
+            load8<T>(x + base + col, xv[q][i]);
+            load8<float>(dz + base + col, gv[q][i]);
+            load8<float>(dres + base + col, o[q][i]);
+          }
         }
       }
     }
-    dot = warp_sum(dot);
-    const float coef = dot * inv_d * inv * inv;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) {
-      const int col = (lane + 32 * i) * 8;
-      if (col < d) {
-        float (&oi)[8] = o[i];
+    for (int q = 0; q < R; ++q) {
+      const int r = r0 + q * kNormWarps;
+      if (r >= end) continue;  // warp-uniform
+      const size_t base = static_cast<size_t>(r) * d;
+      float dot = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) oi[j] += inv * (gv[i][j] - xv[i][j] * coef);
-        float4* dst = reinterpret_cast<float4*>(dres + base + col);
-        dst[0] = make_float4(oi[0], oi[1], oi[2], oi[3]);
-        dst[1] = make_float4(oi[4], oi[5], oi[6], oi[7]);
-        if (dres_bf16) store8_bf16(dres_bf16 + base + col, oi);
+      for (int i = 0; i < VEC; ++i) {
+        const int col = (lane + 32 * i) * 8;
+        if (col < d) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float dzv = gv[q][i][j];
+            gv[q][i][j] = dzv * wv[i][j];
+            dot += gv[q][i][j] * xv[q][i][j];
+            dw_acc[i][j] += dzv * xv[q][i][j] * inv[q];
+          }
+        }
+      }
+      dot = warp_sum(dot);
+      const float coef = dot * inv_d * inv[q] * inv[q];
+#pragma unroll
+      for (int i = 0; i < VEC; ++i) {
+        const int col = (lane + 32 * i) * 8;
+        if (col < d) {
+          float (&oi)[8] = o[q][i];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) oi[j] += inv[q] * (gv[q][i][j] - xv[q][i][j] * coef);
+          float4* dst = reinterpret_cast<float4*>(dres + base + col);
+          dst[0] = make_float4(oi[0], oi[1], oi[2], oi[3]);
+          dst[1] = make_float4(oi[4], oi[5], oi[6], oi[7]);
+          if (dres_bf16) store8_bf16(dres_bf16 + base + col, oi);
+        }
       }
     }
   }
@@ -184,8 +230,9 @@ namespace sj {
 template <typename T, int VEC, typename Y = __nv_bfloat16>
 static void launch_norm_fwd(const void* x, const float* w, void* y, float* inv, int rows, int d, float eps,
                             cudaStream_t s) {
-  const int threads = 256, warps = threads / 32;
-  launch(rmsnorm_fwd_kernel<T, VEC, Y>, (rows + warps - 1) / warps, threads, 0, s,
+  constexpr int R = VEC >= 4 ? 1 : 4 / VEC;  // rows per warp, as in the kernel
+  const int threads = 256, rows_per_cta = threads / 32 * R;
+  launch(rmsnorm_fwd_kernel<T, VEC, Y>, (rows + rows_per_cta - 1) / rows_per_cta, threads, 0, s,
       static_cast<const T*>(x), w, static_cast<Y*>(y), inv, rows, d, eps);
 }
 
@@ -226,7 +273,8 @@ extern "C" int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* 
   using namespace sj;
   if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
     return fail(SJ_ERR_SHAPE, "sj_rmsnorm_fwd: d=%d must be a multiple of 8 up to 1024", d);
-  if (!aligned16(x) || !aligned16(y)) return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd: x/y must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(y) || !aligned16(w))
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd: x/y/w must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   if (x_dtype == SJ_BF16)
     dispatch_norm_fwd<__nv_bfloat16>(x, w, y, inv_rms, rows, d, eps, s);
@@ -243,7 +291,8 @@ extern "C" int sj_rmsnorm_fwd_f32(const float* x, const float* w, float* y, floa
   using namespace sj;
   if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
     return fail(SJ_ERR_SHAPE, "sj_rmsnorm_fwd_f32: d=%d must be a multiple of 8 up to 1024", d);
-  if (!aligned16(x) || !aligned16(y)) return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd_f32: x/y must be 16-byte aligned");
+  if (!aligned16(x) || !aligned16(y) || !aligned16(w))
+    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_fwd_f32: x/y/w must be 16-byte aligned");
   cudaStream_t s = as_stream(stream);
   switch ((d + 255) / 256) {
     case 1: launch_norm_fwd<float, 1, float>(x, w, y, inv_rms, rows, d, eps, s); break;
@@ -268,7 +317,7 @@ extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const 
     return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd: bad d=%d", d);
   if (!x || !w || !inv_rms || !dz || !dres || !dw || !partials)
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: null pointer");
-  if (!aligned16(x) || !aligned16(dz) || !aligned16(dres) || (dres_bf16 && !aligned16(dres_bf16)))
+  if (!aligned16(x) || !aligned16(dz) || !aligned16(dres) || !aligned16(w) || (dres_bf16 && !aligned16(dres_bf16)))
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: rows must be 16-byte aligned");
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
   cudaStream_t s = as_stream(stream);
@@ -344,7 +393,7 @@ extern "C" int sj_rmsnorm_bwd_noalloc(const void* x, int x_dtype, const float* w
                 rows, d, need, kNoAllocPartials);
   if (!x || !w || !inv_rms || !dz || !dres || !dw)
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: null pointer");
-  if (!aligned16(x) || !aligned16(dz) || !aligned16(dres) || (dres_bf16 && !aligned16(dres_bf16)))
+  if (!aligned16(x) || !aligned16(dz) || !aligned16(dres) || !aligned16(w) || (dres_bf16 && !aligned16(dres_bf16)))
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: rows must be 16-byte aligned");
   if (x_dtype != SJ_BF16 && x_dtype != SJ_F32)
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: x must be bf16 or f32");

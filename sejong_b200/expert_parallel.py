@@ -61,7 +61,7 @@ class EpContext:
 
     def finalize(self):
         """Allocate this rank's heap (zero-filled), exchange IPC handles and map every peer's."""
-        lib = _lib.load()
+        _lib.load()
         torch.cuda.set_device(self.dev)
         p = ctypes.c_void_p()
         call("sj_ipc_alloc", self.size, ctypes.byref(p))
@@ -83,7 +83,6 @@ class EpContext:
                 self.opened.append(q.value)
         self.bases = bases
         self._table = (ctypes.c_void_p * self.world)(*bases)
-        del lib
 
     @property
     def peers(self):
