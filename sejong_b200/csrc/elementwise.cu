@@ -61,7 +61,8 @@ __global__ void embedding_fwd_kernel(const uint4* w, const int32_t* ids, void* y
 
 // Row-chunk x 32-column slices accumulated in shared memory, flushed with one atomic per
 // (vocab row, column) per CTA; avoids per-element global atomics on frequent bytes.
-constexpr int kEmbRows = 2048;
+constexpr int kEmbRows = 1024;
+constexpr int kEmbBatch = 8;  // rows whose loads a warp issues before its shared-memory adds
 __global__ void __launch_bounds__(256)
     embedding_bwd_kernel(const float* dy, const int32_t* ids, float* dw, int n,
                          int d, int vocab) {
@@ -71,10 +72,20 @@ __global__ void __launch_bounds__(256)
   for (int i = threadIdx.x; i < vocab * 32; i += blockDim.x) acc[i] = 0.f;
   __syncthreads();
   const int r0 = blockIdx.x * kEmbRows, r1 = min(n, r0 + kEmbRows);
+  const int warps = blockDim.x >> 5;
   if (col < d) {
-    for (int r = r0 + (threadIdx.x >> 5); r < r1; r += blockDim.x >> 5) {
-      const int id = ids[r];
-      if (id >= 0 && id < vocab) atomicAdd(&acc[id * 32 + (threadIdx.x & 31)], dy[static_cast<size_t>(r) * d + col]);
+    for (int rb = r0 + (threadIdx.x >> 5); rb < r1; rb += warps * kEmbBatch) {
+      int id[kEmbBatch];
+      float g[kEmbBatch];
+#pragma unroll
+      for (int q = 0; q < kEmbBatch; ++q) {
+        const int r = rb + q * warps;
+        id[q] = r < r1 ? ids[r] : -1;
+        g[q] = r < r1 ? dy[static_cast<size_t>(r) * d + col] : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < kEmbBatch; ++q)
+        if (id[q] >= 0 && id[q] < vocab) atomicAdd(&acc[id[q] * 32 + (threadIdx.x & 31)], g[q]);
     }
   }
   __syncthreads();
