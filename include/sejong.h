@@ -143,6 +143,10 @@ int sj_rmsnorm_fwd(const void* x, int x_dtype, const float* w, void* y, float* i
 size_t sj_rmsnorm_workspace(int rows, int d);
 int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz, float* dres,
                    void* dres_bf16, float* dw, float* partials, int rows, int d, void* stream);
+/* The same with accumulate = 0: dres = rms_dx(x, w, dz) (overwritten, not read), for the first
+ * gradient into a residual stream, which saves zero-filling it. */
+int sj_rmsnorm_bwd_ex(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz, float* dres,
+                      void* dres_bf16, float* dw, float* partials, int rows, int d, int accumulate, void* stream);
 /* No counterpart in the reference: an addition for callers that cannot allocate device memory
  * (a plugin interface that passes only the op's tensors, or a process whose device memory is held
  * by another allocator).  Same arguments and results as sj_rmsnorm_bwd without `partials`: the

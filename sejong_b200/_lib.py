@@ -87,6 +87,8 @@ SIGNATURES = {
     "sj_rmsnorm_fwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p]),
     "sj_rmsnorm_bwd": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                c_int, c_int, c_void_p]),
+    "sj_rmsnorm_bwd_ex": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_int, c_int, c_int, c_void_p]),
     "sj_rmsnorm_workspace": (c_size_t, [c_int, c_int]),
     "sj_rmsnorm_noalloc_limit": (c_size_t, []),
     "sj_rmsnorm_bwd_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -112,7 +112,7 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(kNormWarps * 32)
     rmsnorm_bwd_kernel(const T* x, const float* w,
                        const float* inv_rms, const float* dz, float* dres,
-                       __nv_bfloat16* dres_bf16, float* partials, int rows, int d) {
+                       __nv_bfloat16* dres_bf16, float* partials, int rows, int d, int accumulate) {
   pdl_wait();
   __shared__ float red[kNormWarps][VEC * 256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -145,7 +145,12 @@ __global__ void __launch_bounds__(kNormWarps * 32)
           if (col < d) {
             load8<T>(x + base + col, xv[q][i]);
             load8<float>(dz + base + col, gv[q][i]);
-            load8<float>(dres + base + col, o[q][i]);
+            if (accumulate) {
+              load8<float>(dres + base + col, o[q][i]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) o[q][i][j] = 0.f;
+            }
           }
         }
       }
@@ -238,10 +243,10 @@ static void launch_norm_fwd(const void* x, const float* w, void* y, float* inv, 
 
 template <typename T, int VEC>
 static void launch_norm_bwd(const void* x, const float* w, const float* inv, const float* dz, float* dres,
-                            void* dres_b, float* partials, int rows, int d, cudaStream_t s) {
+                            void* dres_b, float* partials, int rows, int d, int accumulate, cudaStream_t s) {
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
   launch(rmsnorm_bwd_kernel<T, VEC>, groups, kNormWarps * 32, 0, s, static_cast<const T*>(x), w, inv, dz, dres,
-                                                                 static_cast<__nv_bfloat16*>(dres_b), partials, rows, d);
+         static_cast<__nv_bfloat16*>(dres_b), partials, rows, d, accumulate);
 }
 
 template <typename T>
@@ -257,12 +262,12 @@ static void dispatch_norm_fwd(const void* x, const float* w, void* y, float* inv
 
 template <typename T>
 static void dispatch_norm_bwd(const void* x, const float* w, const float* inv, const float* dz, float* dres,
-                              void* dres_b, float* partials, int rows, int d, cudaStream_t s) {
+                              void* dres_b, float* partials, int rows, int d, int accumulate, cudaStream_t s) {
   switch ((d + 255) / 256) {
-    case 1: launch_norm_bwd<T, 1>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
-    case 2: launch_norm_bwd<T, 2>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
-    case 3: launch_norm_bwd<T, 3>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
-    default: launch_norm_bwd<T, 4>(x, w, inv, dz, dres, dres_b, partials, rows, d, s); break;
+    case 1: launch_norm_bwd<T, 1>(x, w, inv, dz, dres, dres_b, partials, rows, d, accumulate, s); break;
+    case 2: launch_norm_bwd<T, 2>(x, w, inv, dz, dres, dres_b, partials, rows, d, accumulate, s); break;
+    case 3: launch_norm_bwd<T, 3>(x, w, inv, dz, dres, dres_b, partials, rows, d, accumulate, s); break;
+    default: launch_norm_bwd<T, 4>(x, w, inv, dz, dres, dres_b, partials, rows, d, accumulate, s); break;
   }
 }
 
@@ -309,9 +314,9 @@ extern "C" size_t sj_rmsnorm_workspace(int rows, int d) {
   return static_cast<size_t>((rows + sj::kNormRowsPerCta - 1) / sj::kNormRowsPerCta) * static_cast<size_t>(d);
 }
 
-extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz,
-                              float* dres, void* dres_bf16, float* dw, float* partials, int rows, int d,
-                              void* stream) {
+extern "C" int sj_rmsnorm_bwd_ex(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz,
+                                 float* dres, void* dres_bf16, float* dw, float* partials, int rows, int d,
+                                 int accumulate, void* stream) {
   using namespace sj;
   if (rows <= 0 || d <= 0 || d % 8 || d > 32 * 8 * kNormMaxVec)
     return fail(SJ_ERR_SHAPE, "sj_rmsnorm_bwd: bad d=%d", d);
@@ -322,15 +327,21 @@ extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const 
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
   cudaStream_t s = as_stream(stream);
   if (x_dtype == SJ_BF16)
-    dispatch_norm_bwd<__nv_bfloat16>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
+    dispatch_norm_bwd<__nv_bfloat16>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, accumulate, s);
   else if (x_dtype == SJ_F32)
-    dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
+    dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, accumulate, s);
   else
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: x must be bf16 or f32");
   SJ_LAUNCH_CHECK("rmsnorm_bwd");
   launch(column_reduce_add_kernel, (d + 31) / 32, 256, 0, s, partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd reduce");
   return SJ_OK;
+}
+
+extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz,
+                              float* dres, void* dres_bf16, float* dw, float* partials, int rows, int d,
+                              void* stream) {
+  return sj_rmsnorm_bwd_ex(x, x_dtype, w, inv_rms, dz, dres, dres_bf16, dw, partials, rows, d, 1, stream);
 }
 
 // ------------------------------------------------------------------ RMSNorm backward without a workspace
@@ -403,9 +414,9 @@ extern "C" int sj_rmsnorm_bwd_noalloc(const void* x, int x_dtype, const float* w
   const int groups = (rows + kNormRowsPerCta - 1) / kNormRowsPerCta;
   cudaStream_t s = as_stream(stream);
   if (x_dtype == SJ_BF16)
-    dispatch_norm_bwd<__nv_bfloat16>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
+    dispatch_norm_bwd<__nv_bfloat16>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, 1, s);
   else
-    dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, s);
+    dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, 1, s);
   SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc");
   launch(column_reduce_add_kernel, (d + 31) / 32, 256, 0, s, partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc reduce");

@@ -247,7 +247,8 @@ class ByteTrainer:
             self._init_vjp(train.parameter_vjp)
 
     # kernels each entry point launches (zero fills are kernels too)
-    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_attn_gqa_fwd": 1, "sj_attn_gqa_bwd": 3,
+    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_rmsnorm_bwd_ex": 2, "sj_attn_gqa_fwd": 1,
+               "sj_attn_gqa_bwd": 3,
                "sj_zero": 1, "sj_param_basis": 5, "sj_param_prepare": 3}
 
     @classmethod
@@ -283,9 +284,12 @@ class ByteTrainer:
         self._call("sj_rmsnorm_fwd", _ptr(x), self._dt(x), self.w_ptr(wname), _ptr(y), _ptr(inv), rows, d,
              float(self.c.norm_epsilon), self.stream)
 
-    def _norm_bwd(self, x, wname, inv, dz, dres, dres_b, partials, rows, d):
-        self._call("sj_rmsnorm_bwd", _ptr(x), self._dt(x), self.w_ptr(wname), _ptr(inv), _ptr(dz), _ptr(dres),
-             _ptr(dres_b) if dres_b is not None else 0, self.g_ptr(wname), _ptr(partials), rows, d, self.stream)
+    def _norm_bwd(self, x, wname, inv, dz, dres, dres_b, partials, rows, d, accumulate=True):
+        """dres (+)= the norm's input gradient; accumulate=False writes it (the first gradient of a
+        residual stream, which then needs no zero fill)."""
+        self._call("sj_rmsnorm_bwd_ex", _ptr(x), self._dt(x), self.w_ptr(wname), _ptr(inv), _ptr(dz), _ptr(dres),
+             _ptr(dres_b) if dres_b is not None else 0, self.g_ptr(wname), _ptr(partials), rows, d, int(accumulate),
+             self.stream)
 
     def _zero(self, t):
         self._call("sj_zero", _ptr(t), t.numel() * t.element_size(), self.stream)
@@ -655,8 +659,8 @@ class ByteTrainer:
         emb, vocab = ("native_embedding", NATIVE_VOCAB) if self.values else ("embedding", VOCAB)
         if h is None:
             run = self.runs["global"]
-            self._zero(run.dx)
-            self._norm_bwd(top, "final_norm", self.invF, self.dhead, run.dx, run.dxb, self.top_partials, n, c.width)
+            self._norm_bwd(top, "final_norm", self.invF, self.dhead, run.dx, run.dxb, self.top_partials, n, c.width,
+                           accumulate=False)
             self._stage_bwd(run)
             self._call("sj_embedding_bwd", _ptr(run.dx), _ptr(self.ids), self.g_ptr(emb), n, c.width, vocab,
                  self.stream)
@@ -665,13 +669,13 @@ class ByteTrainer:
         de, dg, dd, pt = h.encoder_width, c.width, h.decoder_width, h.patch_size
         np_, t = b * self.patches, self.tc.sequence
         # final norm -> output_projection
-        self._zero(self.dy32)
-        self._norm_bwd(self.y, "final_norm", self.invF, self.dhead, self.dy32, self.dyb, self.top_partials, n, dg)
+        self._norm_bwd(self.y, "final_norm", self.invF, self.dhead, self.dy32, self.dyb, self.top_partials, n, dg,
+                       accumulate=False)
         self._gemm(_ptr(self.zD), dd, 1, _ptr(self.dyb), dg, 0, self.g_ptr("output_projection"), dg, SJ_F32, dd, dg,
                    n, EPI_ACCUM)
         self._gemm(_ptr(self.dyb), dg, 0, self.wb_ptr("output_projection"), dg, 1, _ptr(dec.dz), dd, SJ_F32, n, dd, dg)
-        self._zero(dec.dx)
-        self._norm_bwd(dec.x[-1], "decoder_norm", self.invD, dec.dz, dec.dx, dec.dxb, dec.partials, n, dd)
+        self._norm_bwd(dec.x[-1], "decoder_norm", self.invD, dec.dz, dec.dx, dec.dxb, dec.partials, n, dd,
+                       accumulate=False)
         self._stage_bwd(dec)
         # decoder input = encoder_to_decoder(zE) + broadcast(global_to_decoder(zG), bos)
         self._gemm(_ptr(self.zE), de, 1, _ptr(dec.dxb), dd, 0, self.g_ptr("encoder_to_decoder"), dd, SJ_F32, de, dd,
@@ -687,8 +691,8 @@ class ByteTrainer:
                    SJ_F32, 1, dg, dd, EPI_ACCUM)
         self._gemm(_ptr(self.dzd), dd, 0, self.wb_ptr("global_to_decoder"), dd, 1, _ptr(glob.dz), dg, SJ_F32, np_, dg,
                    dd)
-        self._zero(glob.dx)
-        self._norm_bwd(glob.x[-1], "global_norm", self.invG, glob.dz, glob.dx, glob.dxb, glob.partials, np_, dg)
+        self._norm_bwd(glob.x[-1], "global_norm", self.invG, glob.dz, glob.dx, glob.dxb, glob.partials, np_, dg,
+                       accumulate=False)
         self._stage_bwd(glob)
         # encoder_to_global, patch pool
         self._gemm(_ptr(self.pooled), de, 1, _ptr(glob.dxb), dg, 0, self.g_ptr("encoder_to_global"), dg, SJ_F32, de,
@@ -696,8 +700,8 @@ class ByteTrainer:
         self._gemm(_ptr(glob.dxb), dg, 0, self.wb_ptr("encoder_to_global"), dg, 1, _ptr(self.dpool), de, SJ_F32, np_,
                    de, dg)
         self._call("sj_patch_pool_bwd", _ptr(self.dpool), _ptr(self.dE), b, t, de, pt, self.stream)
-        self._zero(enc.dx)
-        self._norm_bwd(enc.x[-1], "encoder_norm", self.invE, self.dE, enc.dx, enc.dxb, enc.partials, n, de)
+        self._norm_bwd(enc.x[-1], "encoder_norm", self.invE, self.dE, enc.dx, enc.dxb, enc.partials, n, de,
+                       accumulate=False)
         self._stage_bwd(enc)
         if self.values:  # input_projection, then the native embedding (dy32 is free again: [rows, width] f32)
             self._gemm(_ptr(self.xin), dg, 1, _ptr(enc.dxb), de, 0, self.g_ptr("input_projection"), de, SJ_F32, dg, de,

@@ -27,7 +27,7 @@ def _ptr(t, offset_elems=0):
 class F32Trainer:
     """One data-parallel replica of the dense byte-model step in f32 on the current CUDA device."""
 
-    KERNELS = {"sj_rmsnorm_bwd": 2, "sj_attn_f32_bwd": 3}
+    KERNELS = {"sj_rmsnorm_bwd": 2, "sj_rmsnorm_bwd_ex": 2, "sj_attn_f32_bwd": 3}
 
     def __init__(self, config, train, device=None, params=None, process_group=None):
         if config.hierarchy is not None or config.experts is not None:
@@ -101,9 +101,9 @@ class F32Trainer:
         self._call("sj_rmsnorm_fwd_f32", _ptr(x), self.w_ptr(wname), _ptr(y), _ptr(inv), rows, d,
                    float(self.c.norm_epsilon), self.stream)
 
-    def _norm_bwd(self, x, wname, inv, dz, dres, rows, d):
-        self._call("sj_rmsnorm_bwd", _ptr(x), SJ_F32, self.w_ptr(wname), _ptr(inv), _ptr(dz), _ptr(dres), 0,
-                   self.g_ptr(wname), _ptr(self.norm_partials), rows, d, self.stream)
+    def _norm_bwd(self, x, wname, inv, dz, dres, rows, d, accumulate=True):
+        self._call("sj_rmsnorm_bwd_ex", _ptr(x), SJ_F32, self.w_ptr(wname), _ptr(inv), _ptr(dz), _ptr(dres), 0,
+                   self.g_ptr(wname), _ptr(self.norm_partials), rows, d, int(accumulate), self.stream)
 
     def _zero(self, t):
         self._call("sj_zero", _ptr(t), t.numel() * t.element_size(), self.stream)
@@ -174,8 +174,7 @@ class F32Trainer:
                    n, EPI_ACCUM)
         self._gemm(_ptr(self.dlogits), VOCAB_PAD, 0, self.w_ptr("output"), VOCAB_PAD, 1, _ptr(self.dhead), d, n, d,
                    VOCAB)
-        self._zero(self.dx)
-        self._norm_bwd(top, "final_norm", self.invF, self.dhead, self.dx, n, d)
+        self._norm_bwd(top, "final_norm", self.invF, self.dhead, self.dx, n, d, accumulate=False)
         for i in reversed(range(self.s.layers)):
             self._block_bwd(i)
         self._call("sj_embedding_bwd", _ptr(self.dx), _ptr(self.ids), self.g_ptr("embedding"), n, d, VOCAB,
