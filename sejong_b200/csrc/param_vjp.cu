@@ -286,24 +286,47 @@ __global__ void __launch_bounds__(256) param_left_kernel(const __nv_bfloat16* x,
   const int f0 = blockIdx.y * 64 + 2 * lane;
   const int t_begin = blockIdx.x * kTokens;
   const int tokens = min(kTokens, n - t_begin);
-  for (int idx = threadIdx.x; idx < tokens * R; idx += blockDim.x) {
-    const int t = idx / R, j = idx % R;
-    qs[idx] = j < r ? q[static_cast<size_t>(t_begin + t) * r + j] : 0.f;
+  if (r == R) {
+    // q rows are R floats: the block's tokens x R floats are one contiguous run, staged as 16-byte
+    // vectors whose loads are all issued before the shared-memory stores
+    constexpr int kVec = kTokens * R / 4 / 256;  // vectors per thread (4 for both ranks)
+    const float4* src = reinterpret_cast<const float4*>(q + static_cast<size_t>(t_begin) * R);
+    float4* dst = reinterpret_cast<float4*>(qs);
+    const int n4 = tokens * R / 4;
+    float4 v[kVec];
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      const int i = threadIdx.x + u * 256;
+      v[u] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kVec; ++u) {
+      const int i = threadIdx.x + u * 256;
+      if (i < n4) dst[i] = v[u];
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < tokens * R; idx += blockDim.x) {
+      const int t = idx / R, j = idx % R;
+      qs[idx] = j < r ? q[static_cast<size_t>(t_begin + t) * r + j] : 0.f;
+    }
   }
   __syncthreads();
   float acc0[R], acc1[R];
 #pragma unroll
   for (int j = 0; j < R; ++j) acc0[j] = acc1[j] = 0.f;
   if (f0 < a) {
-    for (int t0 = warp * 8; t0 < tokens; t0 += 64) {
-      uint32_t xw[8];
+    // each warp owns kTokens / 8 consecutive tokens of the block and issues all their loads first
+    constexpr int kU = kTokens / 8;
+    const int t0 = warp * kU;
+    {
+      uint32_t xw[kU];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < kU; ++u)
         xw[u] = t0 + u < tokens
                     ? *reinterpret_cast<const uint32_t*>(x + static_cast<size_t>(t_begin + t0 + u) * ldx + f0)
                     : 0u;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kU; ++u) {
         const float2 xv = unpack_bf16x2(xw[u]);   // zero past the last token
         const float4* q4 = reinterpret_cast<const float4*>(qs + (t0 + u < tokens ? t0 + u : 0) * R);
 #pragma unroll
