@@ -209,7 +209,9 @@ int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, const void* 
  * (graph.rs:879-882) is applied to dq and dk before the store.  All operands 16-byte aligned, row
  * strides multiples of 8 elements.  `workspace` is 16-byte aligned f32 scratch of
  * sj_attn_workspace(batch, t, hq, hk) elements: the f32 dQ accumulator [batch*t, hq*64], then Delta
- * and LSE*log2(e) laid out [hq][batch][t rounded up to 128]. */
+ * and LSE*log2(e) laid out [hq][batch][t rounded up to 128], then, when hq > hk and the
+ * batch * hk * ceil(t/128) work items are fewer than 148 (each then split by query head), the f32
+ * dK / dV accumulator [batch*t, hk, 128].  Returns 0 for a shape with hq not a multiple of hk. */
 size_t sj_attn_workspace(int batch, int t, int hq, int hk);
 int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o, int ldo,
                     const float* lse, const void* dout, int lddo, void* dq, int lddq, void* dk, int lddk, void* dv,

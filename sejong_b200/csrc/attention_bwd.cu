@@ -75,6 +75,8 @@ struct BwdParams {
   int lddk, lddv;
   const float2* rope_tab;  // [t][32] (cos, sin) or null
   float rope_log_theta;    // > 0 when no table: angles evaluated inline
+  int hsplit;              // head slices per (batch, kv head, key tile): 1, or the group size
+  float* dkv_acc;          // hsplit > 1: [rows, hk, dK 64 | dV 64] f32, zeroed; null otherwise
 };
 
 SJ_DEVICE float ex2b(float x) {
@@ -83,18 +85,21 @@ SJ_DEVICE float ex2b(float x) {
   return y;
 }
 
-// Item -> (batch, kv head, key tile) and its query range per head: heaviest first (the first key
-// tiles see the most causal query tiles).
+// Item -> (batch, kv head, key tile, head slice) and its query range per head: heaviest first (the
+// first key tiles see the most causal query tiles).  An item visits the query heads
+// [h0, h0 + gh) of its GQA group: all of them (hsplit 1) or one (hsplit = group).
 struct BItem {
-  int b, kvh, kt, k0, qt_lo, nq;
+  int b, kvh, kt, k0, qt_lo, nq, h0, gh;
 };
 SJ_DEVICE BItem decode_bitem(const BwdParams& p, int item) {
   BItem it;
-  const int bk = p.batch * p.hk;
+  const int bk = p.batch * p.hk * p.hsplit;
   const int rest = item % bk;
   it.kt = item / bk;
-  it.b = rest / p.hk;
-  it.kvh = rest % p.hk;
+  it.b = rest / (p.hk * p.hsplit);
+  it.kvh = (rest / p.hsplit) % p.hk;
+  it.gh = p.hq / p.hk / p.hsplit;
+  it.h0 = (rest % p.hsplit) * it.gh;
   it.k0 = it.kt * kBT;
   const int nqt = (p.t + kBT - 1) / kBT;
   it.qt_lo = it.kt;
@@ -201,8 +206,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
-      for (int hh = 0; hh < group && ok; ++hh) {
-        const int h = it.kvh * group + hh;
+      for (int hh = 0; hh < it.gh && ok; ++hh) {
+        const int h = it.kvh * group + it.h0 + hh;
         for (int j = 0; j < it.nq && ok; ++j, ++g) {
           const int st = g % kQdStages;
           const int q0 = (it.qt_lo + j) * kBT;
@@ -277,7 +282,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int ks = n % kKvStages;
         if (!mbar_wait_sleep(&kv_full[ks], (n / kKvStages) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
         const uint32_t ka = smem_u32(smem + kOffKb + ks * kTile), va = smem_u32(smem + kOffVb + ks * kTile);
-        const int steps = group * it.nq;
+        const int steps = it.gh * it.nq;
         for (int s = 0; s < steps && ok; ++s, ++g) {
           const int st = g % kQdStages;
           if (!mbar_wait_sleep(&qd_full[st], (g / kQdStages) & 1, abort_flag, SJ_DEV_ATTN_WAIT) ||
@@ -353,7 +358,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
-      if (kpos < p.t) {
+      if (kpos < p.t && p.dkv_acc != nullptr) {
+        // one slice of the group's heads: f32 partial sums (the finish kernel rotates dK and
+        // writes bf16 once every slice has added its part)
+        float* dst = p.dkv_acc + (row * p.hk + pend_it.kvh) * (2 * kBD) + c0;
+#pragma unroll
+        for (int c = 0; c < 16; c += 4) {
+          red_add_v4(dst + c, __uint_as_float(vk[c]), __uint_as_float(vk[c + 1]), __uint_as_float(vk[c + 2]),
+                     __uint_as_float(vk[c + 3]));
+          red_add_v4(dst + kBD + c, __uint_as_float(vv[c]), __uint_as_float(vv[c + 1]), __uint_as_float(vv[c + 2]),
+                     __uint_as_float(vv[c + 3]));
+        }
+      } else if (kpos < p.t) {
         const bool rope = p.rope_tab != nullptr || p.rope_log_theta > 0.f;
         uint32_t w[8];
 #pragma unroll
@@ -382,7 +398,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int item = blockIdx.x; item < p.items && alive; item += gridDim.x, ++n) {
       const BItem it = decode_bitem(p, item);
       const int kpos = it.k0 + r;
-      const int steps = group * it.nq;
+      const int steps = it.gh * it.nq;
       for (int s = 0; s < steps && alive; ++s, ++g) {
         const int st = g % kQdStages;
         const int q0 = (it.qt_lo + s % it.nq) * kBT;
@@ -462,7 +478,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (pend_g >= 0) read_out();
         pend_g = g;
         pend_it = it;
-        pend_h = it.kvh * group + s / it.nq;
+        pend_h = it.kvh * group + it.h0 + s / it.nq;
         pend_qpos = q0 + r;
         pend_last = s == steps - 1;
       }
@@ -484,21 +500,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
 // Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57) and the LSE times log2(e), both written
 // transposed to [head][batch][tpad] so that a step's 128 values are one contiguous run; the same
-// thread zeroes the (row, head) slice of the f32 dQ accumulator.  Thread <-> (head, row), rows
-// fastest, so the transposed stores are coalesced.
+// threads zero the (row, head) slice of the f32 dQ accumulator and, for head < hk when the items
+// are split by head, the (row, kv head) slice of the f32 dK / dV accumulator.  Eight lanes per
+// (row, head), each with 8 of its 64 columns: a warp reads four rows' 128-byte head slices of O and
+// dO and writes their accumulator slices as whole lines; heads outermost, rows next.
 __global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dout, int lddo,
-                                  const float* lse, float* delta_t, float* lse_t, float* dq_acc, int rows, int t,
-                                  int tpad, int hq) {
+                                  const float* lse, float* delta_t, float* lse_t, float* dq_acc, float* dkv_acc,
+                                  int rows, int t, int tpad, int hq, int hk) {
   pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<size_t>(rows) * hq) return;
-  const int h = static_cast<int>(i / rows), row = static_cast<int>(i % rows);
-  const uint4* a = reinterpret_cast<const uint4*>(dout + static_cast<size_t>(row) * lddo + h * kBD);
-  const uint4* c = reinterpret_cast<const uint4*>(o + static_cast<size_t>(row) * ldo + h * kBD);
+  const size_t slices = static_cast<size_t>(rows) * hq;
+  const bool live = i < slices * 8;
+  const size_t rh = live ? i >> 3 : 0;
+  const int j = static_cast<int>(i & 7);
+  const int h = static_cast<int>(rh / rows), row = static_cast<int>(rh % rows);
   float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < kBD / 8; ++j) {
-    const uint4 x = a[j], y = c[j];
+  if (live) {
+    const uint4 x = *reinterpret_cast<const uint4*>(dout + static_cast<size_t>(row) * lddo + h * kBD + 8 * j);
+    const uint4 y = *reinterpret_cast<const uint4*>(o + static_cast<size_t>(row) * ldo + h * kBD + 8 * j);
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -506,30 +525,32 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bf
       acc = fmaf(u.x, v.x, fmaf(u.y, v.y, acc));
     }
   }
-  const int b = row / t, pos = row % t;
-  const size_t dst = (static_cast<size_t>(h) * (rows / t) + b) * tpad + pos;
-  delta_t[dst] = acc;
-  lse_t[dst] = lse[static_cast<size_t>(row) * hq + h] * kLog2eB;
-  float4* z = reinterpret_cast<float4*>(dq_acc + (static_cast<size_t>(row) * hq + h) * kBD);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  if (!live) return;
+  if (j == 0) {
+    const int b = row / t, pos = row % t;
+    const size_t dst = (static_cast<size_t>(h) * (rows / t) + b) * tpad + pos;
+    delta_t[dst] = acc;
+    lse_t[dst] = lse[static_cast<size_t>(row) * hq + h] * kLog2eB;
+  }
+  float4* z = reinterpret_cast<float4*>(dq_acc + (static_cast<size_t>(row) * hq + h) * kBD + 8 * j);
+  z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (dkv_acc != nullptr && h < hk) {
+    z = reinterpret_cast<float4*>(dkv_acc + (static_cast<size_t>(row) * hk + h) * (2 * kBD) + 16 * j);
 #pragma unroll
-  for (int j = 0; j < kBD / 4; ++j) z[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int e = 0; e < 4; ++e) z[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 }
 
-// dq = bf16(inverse RoPE(dq_acc)), one thread per (row, head, 4 column pairs).
-__global__ void attn_dq_finish_kernel(const float* acc, __nv_bfloat16* dq, int lddq, int rows, int t, int hq,
-                                      const float2* tab, float log_theta) {
-  pdl_wait();
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  constexpr int kQuads = kBD / 8;
-  if (i >= static_cast<size_t>(rows) * hq * kQuads) return;
-  const int row = static_cast<int>(i / (hq * kQuads));
-  const int rem = static_cast<int>(i % (hq * kQuads));
-  const int h = rem / kQuads, q4 = rem % kQuads;
-  const float4* src = reinterpret_cast<const float4*>(acc + i * 8);
-  const float4 v0 = src[0], v1 = src[1];
+// 8 f32 values (4 column pairs from pair q4 on) -> bf16 at dst, inverse-rotated when `rotate`.
+SJ_DEVICE void finish_quad(const float* src, __nv_bfloat16* dst, bool rotate, const float2* tab, float log_theta,
+                           int pos, int q4) {
+  const float4 v0 = reinterpret_cast<const float4*>(src)[0], v1 = reinterpret_cast<const float4*>(src)[1];
   float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-  if (tab != nullptr || log_theta > 0.f) {
-    const int pos = row % t;
+  if (rotate) {
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 cs = rope_cs(tab, log_theta, pos, 4 * q4 + e);
@@ -538,20 +559,63 @@ __global__ void attn_dq_finish_kernel(const float* acc, __nv_bfloat16* dq, int l
       x[2 * e + 1] = -a * cs.y + b * cs.x;
     }
   }
-  *reinterpret_cast<uint4*>(dq + static_cast<size_t>(row) * lddq + h * kBD + 8 * q4) =
+  *reinterpret_cast<uint4*>(dst) =
       make_uint4(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]), pack_bf16x2(x[4], x[5]), pack_bf16x2(x[6], x[7]));
+}
+
+// dq = bf16(inverse RoPE(dq_acc)), one thread per (row, head, 4 column pairs); when the items were
+// split by head, further threads per (row, kv head, 4 column pairs) write dk = bf16(inverse
+// RoPE(dK partial sum)) and dv = bf16(dV partial sum).
+__global__ void attn_dq_finish_kernel(const float* acc, __nv_bfloat16* dq, int lddq, const float* dkv_acc,
+                                      __nv_bfloat16* dk, int lddk, __nv_bfloat16* dv, int lddv, int rows, int t,
+                                      int hq, int hk, const float2* tab, float log_theta) {
+  pdl_wait();
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  constexpr int kQuads = kBD / 8;
+  const bool rotate = tab != nullptr || log_theta > 0.f;
+  const size_t nq = static_cast<size_t>(rows) * hq * kQuads;
+  if (i < nq) {
+    const int row = static_cast<int>(i / (hq * kQuads));
+    const int rem = static_cast<int>(i % (hq * kQuads));
+    const int h = rem / kQuads, q4 = rem % kQuads;
+    finish_quad(acc + i * 8, dq + static_cast<size_t>(row) * lddq + h * kBD + 8 * q4, rotate, tab, log_theta,
+                row % t, q4);
+    return;
+  }
+  if (dkv_acc == nullptr) return;
+  const size_t j = i - nq;
+  if (j >= static_cast<size_t>(rows) * hk * kQuads) return;
+  const int row = static_cast<int>(j / (hk * kQuads));
+  const int rem = static_cast<int>(j % (hk * kQuads));
+  const int h = rem / kQuads, q4 = rem % kQuads;
+  const float* src = dkv_acc + (static_cast<size_t>(row) * hk + h) * (2 * kBD) + 8 * q4;
+  finish_quad(src, dk + static_cast<size_t>(row) * lddk + h * kBD + 8 * q4, rotate, tab, log_theta, row % t, q4);
+  finish_quad(src + kBD, dv + static_cast<size_t>(row) * lddv + h * kBD + 8 * q4, false, tab, log_theta, row % t,
+              q4);
 }
 
 }  // namespace sj
 
 using namespace sj;
 
+// Head slices per (batch, kv head, key tile) item: when those items are fewer than B200's 148 SMs,
+// each item takes one query head of its GQA group (the heaviest items, the first key tiles of a
+// causal sequence, would otherwise set the launch's length with SMs idle); a function of the
+// shape alone, so that the workspace size is too.
+static int bwd_head_slices(int batch, int t, int hq, int hk) {
+  constexpr int kB200Sms = 148;
+  const long items = static_cast<long>(batch) * hk * ((t + kBT - 1) / kBT);
+  return (hq > hk && items < kB200Sms) ? hq / hk : 1;
+}
+
 extern "C" size_t sj_attn_workspace(int batch, int t, int hq, int hk) {
-  if (batch <= 0 || t <= 0 || hq <= 0 || hk <= 0) return 0;
+  if (batch <= 0 || t <= 0 || hq <= 0 || hk <= 0 || hq % hk) return 0;
   const size_t rows = static_cast<size_t>(batch) * t;
   const size_t tpad = static_cast<size_t>((t + kBT - 1) / kBT) * kBT;
-  // the f32 dQ accumulator [rows, hq*64], then Delta and LSE*log2(e) transposed, [hq][batch][tpad] each
-  return rows * hq * kBD + 2 * static_cast<size_t>(hq) * batch * tpad;
+  // the f32 dQ accumulator [rows, hq*64], then Delta and LSE*log2(e) transposed, [hq][batch][tpad]
+  // each, then (items split by head) the f32 dK / dV accumulator [rows, hk, 128]
+  const size_t dkv = bwd_head_slices(batch, t, hq, hk) > 1 ? rows * hk * 2 * kBD : 0;
+  return rows * hq * kBD + 2 * static_cast<size_t>(hq) * batch * tpad + dkv;
 }
 
 extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, const void* v, int ldv, const void* o,
@@ -583,10 +647,12 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   float* dq_acc = workspace;
   float* delta_t = dq_acc + rows * hq * kBD;
   float* lse_t = delta_t + static_cast<size_t>(hq) * batch * tpad;
+  const int hsplit = bwd_head_slices(batch, t, hq, hk);
+  float* dkv_acc = hsplit > 1 ? lse_t + static_cast<size_t>(hq) * batch * tpad : nullptr;
   const size_t row_heads = rows * hq;
-  launch(attn_delta_kernel, static_cast<unsigned>((row_heads + 255) / 256), 256, 0, s,
+  launch(attn_delta_kernel, static_cast<unsigned>((row_heads * 8 + 255) / 256), 256, 0, s,
          static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo, lse, delta_t, lse_t,
-         dq_acc, static_cast<int>(rows), t, tpad, hq);
+         dq_acc, dkv_acc, static_cast<int>(rows), t, tpad, hq, hk);
   SJ_LAUNCH_CHECK("attn_delta");
   CUtensorMap maps[4];
   int rc = bf16_map(&maps[0], q, static_cast<uint64_t>(hq) * kBD, rows, ldq, kBD, kBT);
@@ -601,7 +667,9 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   p.window = window;
   p.batch = batch;
   p.nkt = (t + kBT - 1) / kBT;
-  p.items = batch * hk * p.nkt;
+  p.hsplit = hsplit;
+  p.dkv_acc = dkv_acc;
+  p.items = batch * hk * hsplit * p.nkt;
   p.scale = 0.125f;
   p.scale_log2 = 0.125f * kLog2eB;
   p.lse_t = lse_t;
@@ -617,9 +685,10 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   const int grid = std::min(p.items, sm_count());
   launch(attn_bwd_tc_kernel, grid, kBwdThreads, kSmemBwd, s, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("attn_bwd_tc");
-  const size_t quads = rows * hq * (kBD / 8);
-  launch(attn_dq_finish_kernel, static_cast<unsigned>((quads + 255) / 256), 256, 0, s,
-      dq_acc, static_cast<__nv_bfloat16*>(dq), lddq, static_cast<int>(rows), t, hq, p.rope_tab, p.rope_log_theta);
+  const size_t quads = rows * (hq + (dkv_acc ? hk : 0)) * (kBD / 8);
+  launch(attn_dq_finish_kernel, static_cast<unsigned>((quads + 255) / 256), 256, 0, s, dq_acc,
+         static_cast<__nv_bfloat16*>(dq), lddq, static_cast<const float*>(dkv_acc), p.dk, lddk, p.dv, lddv,
+         static_cast<int>(rows), t, hq, hk, p.rope_tab, p.rope_log_theta);
   SJ_LAUNCH_CHECK("attn_dq_finish");
   return SJ_OK;
 }
