@@ -207,23 +207,34 @@ __global__ void __launch_bounds__(kNormWarps * 32)
   }
 }
 
-// out[col] += sum over groups of partials[g][col]: 32 columns per CTA, the 8 warps split the
-// groups, coalesced 128-byte row reads, one shared-memory reduction.
-__global__ void __launch_bounds__(256) column_reduce_add_kernel(const float* partials, int groups, int d,
-                                                               float* out) {
+// out[col] += sum over groups of partials[g][col]: 32 columns per CTA, the 32 warps split the
+// groups (warp w takes w, w + 32, ...), each with four independent running sums so that four
+// coalesced 128-byte row reads are in flight per warp, then one shared-memory reduction.  The
+// order of the additions is fixed: the result does not depend on timing.
+__global__ void __launch_bounds__(1024) column_reduce_add_kernel(const float* partials, int groups, int d,
+                                                                float* out) {
   pdl_wait();
-  __shared__ float red[8][32];
+  __shared__ float red[32][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
-  float s = 0.f;
-  if (col < d)
-    for (int g = warp; g < groups; g += 8) s += partials[static_cast<size_t>(g) * d + col];
-  red[warp][lane] = s;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (col < d) {
+    const float* src = partials + col;
+    int g = warp;
+    for (; g + 96 < groups; g += 128) {
+      s0 += src[static_cast<size_t>(g) * d];
+      s1 += src[static_cast<size_t>(g + 32) * d];
+      s2 += src[static_cast<size_t>(g + 64) * d];
+      s3 += src[static_cast<size_t>(g + 96) * d];
+    }
+    for (; g < groups; g += 32) s0 += src[static_cast<size_t>(g) * d];
+  }
+  red[warp][lane] = (s0 + s1) + (s2 + s3);
   __syncthreads();
   if (warp == 0 && col < d) {
     float t = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) t += red[k][lane];
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) t += red[k][lane];
     out[col] += t;
   }
 }
@@ -333,7 +344,7 @@ extern "C" int sj_rmsnorm_bwd_ex(const void* x, int x_dtype, const float* w, con
   else
     return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd: x must be bf16 or f32");
   SJ_LAUNCH_CHECK("rmsnorm_bwd");
-  launch(column_reduce_add_kernel, (d + 31) / 32, 256, 0, s, partials, groups, d, dw);
+  launch(column_reduce_add_kernel, (d + 31) / 32, 1024, 0, s, partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd reduce");
   return SJ_OK;
 }
@@ -418,7 +429,7 @@ extern "C" int sj_rmsnorm_bwd_noalloc(const void* x, int x_dtype, const float* w
   else
     dispatch_norm_bwd<float>(x, w, inv_rms, dz, dres, dres_bf16, partials, rows, d, 1, s);
   SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc");
-  launch(column_reduce_add_kernel, (d + 31) / 32, 256, 0, s, partials, groups, d, dw);
+  launch(column_reduce_add_kernel, (d + 31) / 32, 1024, 0, s, partials, groups, d, dw);
   SJ_LAUNCH_CHECK("rmsnorm_bwd_noalloc reduce");
   return SJ_OK;
 }
