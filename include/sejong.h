@@ -152,8 +152,9 @@ int sj_rmsnorm_bwd_ex(const void* x, int x_dtype, const float* w, const float* i
  * by another allocator).  Same arguments and results as sj_rmsnorm_bwd without `partials`: the
  * partials live in a fixed 4 MiB array inside the library's device image, so the call allocates
  * nothing.  Limit: sj_rmsnorm_workspace(rows, d) <= sj_rmsnorm_noalloc_limit() floats, else
- * SJ_ERR_CAPACITY.  The first call on each device looks the array up (and loads the library's
- * device code there if needed): make it before any stream capture.  Calls that overlap in time on
+ * SJ_ERR_CAPACITY.  Every call looks the array's device address up in the current context; the
+ * first call in a context may load the library's device code there: make it before any stream
+ * capture.  Calls that overlap in time on
  * one device share the array and race: serialise them. */
 size_t sj_rmsnorm_noalloc_limit(void);
 int sj_rmsnorm_bwd_noalloc(const void* x, int x_dtype, const float* w, const float* inv_rms, const float* dz,

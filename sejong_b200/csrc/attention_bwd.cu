@@ -633,14 +633,10 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   if (!workspace || !aligned16(workspace)) return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: workspace must be aligned");
   if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7))
     return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: rope table must be 8-byte aligned");
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBwd);
-    if (e != cudaSuccess) return cuda_check(e, "attention backward shared-memory attribute");
-    configured_device = dev;
-  }
+  static KernelAttrOnce attr_once;
+  const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(attn_bwd_tc_kernel), kSmemBwd,
+                                      "attention backward shared-memory attribute");
+  if (attr_rc != SJ_OK) return attr_rc;
   cudaStream_t s = as_stream(stream);
   const size_t rows = static_cast<size_t>(batch) * t;
   const int tpad = ((t + kBT - 1) / kBT) * kBT;

@@ -439,14 +439,10 @@ extern "C" int sj_attn_gqa_fwd(const void* q, int ldq, const void* k, int ldk, c
     return fail(SJ_ERR_SHAPE, "attention: bad shape batch=%d t=%d hq=%d hk=%d window=%d", batch, t, hq, hk, window);
   if ((ldq | ldk | ldv | ldo) % 8 || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !lse)
     return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_fwd: 16-byte aligned rows required");
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd);
-    if (e != cudaSuccess) return cuda_check(e, "attention forward shared-memory attribute");
-    configured_device = dev;
-  }
+  static KernelAttrOnce attr_once;
+  const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(attn_fwd_tc_kernel), kSmemFwd,
+                                      "attention forward shared-memory attribute");
+  if (attr_rc != SJ_OK) return attr_rc;
   const uint64_t rows = static_cast<uint64_t>(batch) * t;
   CUtensorMap maps[3];
   int rc = bf16_map(&maps[0], q, static_cast<uint64_t>(hq) * kD, rows, ldq, kD, kT);

@@ -341,14 +341,10 @@ extern "C" int sj_bert_attention(const void* qkv, int ldqkv, const int32_t* cu_s
   if (!aligned16(qkv) || !aligned16(out) || (ldqkv % 8) || (ldo % 8) || ldqkv < 3 * heads * head_dim ||
       ldo < heads * head_dim)
     return fail(SJ_ERR_ARGUMENT, "sj_bert_attention: 16-byte aligned rows of [q | k | v] and of the output required");
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(bert_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemAttn);
-    if (e != cudaSuccess) return cuda_check(e, "bert attention shared-memory attribute");
-    configured_device = dev;
-  }
+  static KernelAttrOnce attr_once;
+  const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(bert_attention_kernel), kSmemAttn,
+                                      "bert attention shared-memory attribute");
+  if (attr_rc != SJ_OK) return attr_rc;
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
   launch(bert_attention_kernel, static_cast<unsigned>(batch * heads), 128, kSmemAttn, as_stream(stream),
          static_cast<const __nv_bfloat16*>(qkv), ldqkv, cu_seqlens, heads, scale_log2,

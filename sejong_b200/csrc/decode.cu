@@ -143,16 +143,10 @@ extern "C" int sj_attn_cached(const void* q, int ldq, const void* k_cache, int l
   if (!q || !k_cache || !v_cache || !o || (ldq | ldk | ldv | ldo) % 2)
     return fail(SJ_ERR_ARGUMENT, "sj_attn_cached: null operand or odd row stride");
   const size_t smem = static_cast<size_t>(visible) * sizeof(float);
-  static int configured = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured != dev) {
-    const int rc = cuda_check(cudaFuncSetAttribute(attn_cached_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                   static_cast<int>(kMaxCachedKeys * sizeof(float))),
-                              "sj_attn_cached: shared memory");
-    if (rc != SJ_OK) return rc;
-    configured = dev;
-  }
+  static KernelAttrOnce attr_once;
+  const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(attn_cached_kernel),
+                                      static_cast<int>(kMaxCachedKeys * sizeof(float)), "sj_attn_cached: shared memory");
+  if (attr_rc != SJ_OK) return attr_rc;
   launch(attn_cached_kernel, dim3(rows, hq), kCachedThreads, smem, as_stream(stream),
          static_cast<const __nv_bfloat16*>(q), ldq, static_cast<const __nv_bfloat16*>(k_cache), ldk,
          static_cast<const __nv_bfloat16*>(v_cache), ldv, static_cast<__nv_bfloat16*>(o), ldo, offset, hq, hk, window);

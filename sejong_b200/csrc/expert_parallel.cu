@@ -66,12 +66,14 @@ SJ_DEVICE bool flag_wait(const uint32_t* flag, uint32_t epoch, uint64_t limit_ns
   return true;
 }
 
-// Signal every rank, then wait for every rank (threads 0 .. world-1 of the calling CTA).
-SJ_DEVICE void exchange_epoch(const Peers& peers, int rank, int world, size_t flags_off, uint32_t epoch,
+// Signal every rank, then wait for every rank (threads 0 .. world-1 of the calling CTA).  Returns
+// false in the thread whose wait expired (SJ_DEV_EP_WAIT is then in the device error word).
+SJ_DEVICE bool exchange_epoch(const Peers& peers, int rank, int world, size_t flags_off, uint32_t epoch,
                               uint64_t limit_ns) {
   const int t = threadIdx.x;
   if (t < world) flag_release(at<uint32_t>(peers, t, flags_off) + rank, epoch);
-  if (t < world) flag_wait(at<uint32_t>(peers, rank, flags_off) + t, epoch, limit_ns);
+  if (t < world) return flag_wait(at<uint32_t>(peers, rank, flags_off) + t, epoch, limit_ns);
+  return true;
 }
 
 SJ_DEVICE void load8_bf16(const __nv_bfloat16* p, float (&v)[8]) {
@@ -123,9 +125,12 @@ __global__ void __launch_bounds__(kPackThreads) ep_route_pack_kernel(const int32
   }
   __threadfence_system();
   __syncthreads();
-  exchange_epoch(peers, rank, world, flags_off, epoch, limit_ns);
+  // A peer that never arrived leaves the count matrix stale: route nothing on it (the same exit as
+  // an overflow) and leave the epoch counter where it was.  After SJ_DEV_EP_WAIT the ranks' epoch
+  // counters disagree, so the expert-parallel context must be rebuilt before another step.
+  if (!exchange_epoch(peers, rank, world, flags_off, epoch, limit_ns)) overflow = 2;
   __syncthreads();
-  if (t == 0) {
+  if (t == 0 && !overflow) {
     *epoch_ctr = epoch;
     __threadfence_system();
     const volatile int* m = at<int>(peers, rank, counts_off);
@@ -152,8 +157,9 @@ __global__ void __launch_bounds__(kPackThreads) ep_route_pack_kernel(const int32
     }
   }
   __syncthreads();
-  if (overflow) {  // a receive buffer would overflow: route nothing (the host sizes cap so this cannot happen)
-    if (t == 0) record_error(SJ_DEV_EP_CAPACITY);
+  if (overflow) {  // a receive buffer would overflow (the host sizes cap so this cannot happen), or the
+                   // count exchange timed out: route nothing
+    if (t == 0 && overflow == 1) record_error(SJ_DEV_EP_CAPACITY);
     for (int i = t; i < slots; i += kPackThreads) pos[i] = -1;
     for (int i = t; i <= 2 * local; i += kPackThreads) group_rows[i] = 0;
     return;

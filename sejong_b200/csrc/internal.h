@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -24,6 +25,27 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // stride `ld` elements, box box_inner x box_outer (gemm.cu).
 int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
              uint32_t box_outer);
+
+// Per-device record of a kernel whose dynamic shared-memory limit has been raised.  Each call site
+// owns one (a function-local static); the flags are atomics, so host threads that drive different
+// devices do not race, and two threads that set the same device both just set the attribute
+// (cudaFuncSetAttribute is idempotent).
+struct KernelAttrOnce {
+  static constexpr int kMaxDevices = 64;
+  std::atomic<unsigned char> done[kMaxDevices] = {};
+};
+// Raise `kernel`'s dynamic shared-memory limit to `bytes` on the current device, once per device.
+inline int ensure_max_smem(KernelAttrOnce& once, const void* kernel, int bytes, const char* what) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_check(e, what);
+  const bool tracked = dev >= 0 && dev < KernelAttrOnce::kMaxDevices;
+  if (tracked && once.done[dev].load(std::memory_order_acquire)) return SJ_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_check(e, what);
+  if (tracked) once.done[dev].store(1, std::memory_order_release);
+  return SJ_OK;
+}
 
 // Zero `bytes` bytes at `ptr` on `stream` with a kernel (elementwise.cu).
 int zero_async(void* ptr, size_t bytes, cudaStream_t stream);

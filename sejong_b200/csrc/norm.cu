@@ -371,30 +371,20 @@ extern "C" int sj_rmsnorm_bwd(const void* x, int x_dtype, const float* w, const 
 namespace sj {
 
 constexpr size_t kNoAllocPartials = size_t(1) << 20;
-constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) float g_noalloc_partials[kNoAllocPartials];
 
-static std::mutex g_noalloc_mutex;
-static float* g_noalloc_address[kNoAllocMaxDevices];
-
-// Device address of g_noalloc_partials on the current device, looked up once per device.  The
-// first lookup loads the library's device image on that device if it is not loaded yet.
+// Device address of g_noalloc_partials in the current context.  In host code the array's name is
+// only a host-side stand-in, so the address is asked of the runtime; it is asked on every call
+// rather than cached, because it belongs to one CUDA context (a cudaDeviceReset or another context
+// made current on the device would leave a cached value pointing at nothing).  The first call in
+// a context loads the library's device image there if it is not loaded yet, so that first call
+// should come before any stream capture on the device.
 static int noalloc_partials(float** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_check(e, "sj_rmsnorm_bwd_noalloc: cudaGetDevice");
-  if (dev < 0 || dev >= kNoAllocMaxDevices)
-    return fail(SJ_ERR_ARGUMENT, "sj_rmsnorm_bwd_noalloc: device %d beyond the %d supported", dev,
-                kNoAllocMaxDevices);
-  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_address[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_partials);
-    if (e != cudaSuccess) return cuda_check(e, "sj_rmsnorm_bwd_noalloc: cudaGetSymbolAddress");
-    if (!p) return fail(SJ_ERR_CUDA, "sj_rmsnorm_bwd_noalloc: null scratch address");
-    g_noalloc_address[dev] = static_cast<float*>(p);
-  }
-  *out = g_noalloc_address[dev];
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+  if (e != cudaSuccess) return cuda_check(e, "sj_rmsnorm_bwd_noalloc: cudaGetSymbolAddress");
+  if (!p) return fail(SJ_ERR_CUDA, "sj_rmsnorm_bwd_noalloc: null scratch address");
+  *out = static_cast<float*>(p);
   return SJ_OK;
 }
 

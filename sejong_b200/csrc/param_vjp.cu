@@ -564,15 +564,10 @@ BasisWorkspace basis_workspace(void* base, int n, int a, int r) {
 template <int R>
 int launch_basis(const __nv_bfloat16* x, int ldx, int n, int a, const __nv_bfloat16* w, int ldw, int interleave,
                  const int32_t* columns, int r, float eps, float* q, const BasisWorkspace& ws, cudaStream_t s) {
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(param_ys_gram_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         200 * 1024);
-    if (e != cudaSuccess) return cuda_check(e, "param_ys_gram shared-memory attribute");
-    configured_device = dev;
-  }
+  static KernelAttrOnce attr_once;  // one per template instance
+  const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(param_ys_gram_kernel<R>), 200 * 1024,
+                                      "param_ys_gram shared-memory attribute");
+  if (attr_rc != SJ_OK) return attr_rc;
   const size_t smem = (static_cast<size_t>(a) * R + 8 * kYsRows * R) * sizeof(float);
   if (smem > 200 * 1024) return fail(SJ_ERR_SHAPE, "sj_param_basis: a = %d too wide for rank %d", a, r);
   const int zs = zero_async(ws.gram, sizeof(double) * r * r, s);

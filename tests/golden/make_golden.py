@@ -1,9 +1,9 @@
 """Generate golden vectors by running the reference's own Triton kernels on the CPU.
 
-Run in a container that holds the reference source (read-only) at
-$SEJONG_REFERENCE (default /root/reference):
+Run in a container that holds the reference source (read-only); point
+SEJONG_REFERENCE at its checkout (the directory that contains python/sejong_kernels):
 
-    python tests/golden/make_golden.py
+    SEJONG_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 The reference kernels (python/sejong_kernels/ops/{kernels,hierarchy,projection,
 common,parameter}.py) are imported unmodified and executed by Triton's CPU
@@ -19,7 +19,9 @@ import sys
 import types
 
 os.environ["TRITON_INTERPRET"] = "1"
-REFERENCE = os.environ.get("SEJONG_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("SEJONG_REFERENCE")
+if not REFERENCE or not os.path.isdir(os.path.join(REFERENCE, "python", "sejong_kernels")):
+    sys.exit("set SEJONG_REFERENCE to the reference checkout (the directory holding python/sejong_kernels)")
 sys.path.insert(0, os.path.join(REFERENCE, "python"))
 
 import numpy as np  # noqa: E402

@@ -74,12 +74,16 @@ def test_noalloc_matches_workspace_twice(rows, d, x_f32):
         dres, dres_b = dres0.clone(), torch.empty(rows, d, dtype=torch.bfloat16, device=DEV)
         dw = torch.full((d,), 0.5, device=DEV)
         torch.cuda.synchronize()
-        before = free_bytes()
+        before, reserved = free_bytes(), torch.cuda.memory_reserved()
         call("sj_rmsnorm_bwd_noalloc", ptr(x), xdt, ptr(w), ptr(inv), ptr(dz), ptr(dres), ptr(dres_b), ptr(dw),
              rows, d, stream())
         torch.cuda.synchronize()
         if attempt == 1:
-            assert free_bytes() == before, "the no-allocation entry point changed free device memory"
+            # torch's caching allocator was not asked for memory, and the device's free memory did not
+            # drop by a cudaMalloc's smallest granule (2 MiB); other processes on a shared GPU may move
+            # the device-wide figure a little, so it is not compared exactly
+            assert torch.cuda.memory_reserved() == reserved, "torch allocated during the no-allocation call"
+            assert before - free_bytes() < (2 << 20), "the no-allocation entry point took device memory"
         assert rel(dres, ref_dres) < 1e-4
         assert rel(dres_b, ref_dres_b) < 1e-2
         assert rel(dw, ref_dw) < 1e-4
