@@ -59,6 +59,9 @@ CPU_SAMPLES = {"c1": (8, 512)}  # C1 is small enough for the CPU to run the whol
 # `python bench.py --steps 1 --warmup 3 --no-cpu-baseline --no-kernel-timing` summarised in
 # profiles/c3_step_launch_list.txt (ncu flushes caches between launches: an upper bound)
 NCU_GEMM_DRAM_BYTES_PER_STEP = {"c3": 5.4978e9}
+NCU_TRAFFIC_SOURCE = ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum launch list of "
+                      "one C3 step (profiles/c3_step_launch_list.txt), summed over the GEMM launches; not measured in "
+                      "this run")
 
 
 def parse():
@@ -134,7 +137,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU restatement (oracle) timing
-def cpu_step_rate(steps, warmup, threads=None, config="c3"):
+def cpu_step_rate(steps, warmup, threads=None, config="c3", sample=None):
     """bytes/s of the oracle's fp32 CPU training step on the bounded sample of C3 (AdamW) or C4
     (parameter-VJP SGD)."""
     import numpy as np
@@ -151,7 +154,7 @@ def cpu_step_rate(steps, warmup, threads=None, config="c3"):
     corp = synthetic_corpus(1000, 1 << 20)
     rng = Rng(123)
     state = omodel.AdamState()
-    batch, seq = CPU_SAMPLES.get(config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))
+    batch, seq = sample or CPU_SAMPLES.get(config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))
     tc = omodel.TrainConfig(sequence=seq, batch=batch, learning_rate=1e-2 if config == "c4" else 3e-4)
     vcfg = opv.VjpConfig()
     vrng = Rng(vcfg.seed)
@@ -172,35 +175,53 @@ def cpu_step_rate(steps, warmup, threads=None, config="c3"):
     return batch * seq / sec, sec, torch.get_num_threads()
 
 
-def cpu_sample_text(steps, config="c3"):
+def cpu_sample_text(steps, config="c3", sample=None):
+    b, t = sample or CPU_SAMPLES.get(config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))
     if config == "c1":
-        return f"C1, the whole step (8 x 512 bytes), fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps"
+        whole = "the whole step" if (b, t) == (8, 512) else "a reduced batch"
+        return f"C1, {whole} ({b} x {t} bytes), fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps"
     if config == "c4":
-        return (f"C4 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
+        return (f"C4 architecture, batch {b} x {t} bytes (vs 8 x 4096 on the GPU), "
                 f"FP64 CPU fwd + input VJP + parameter VJP + compact SGD, mean of {steps} steps")
     if config == "c5":
-        return (f"C5 architecture (8 experts, top-2), batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 4 x 8192 "
+        return (f"C5 architecture (8 experts, top-2), batch {b} x {t} bytes (vs 4 x 8192 "
                 f"on the GPU), fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps")
-    return (f"C3 architecture, batch {CPU_SAMPLE_BATCH} x {CPU_SAMPLE_SEQ} bytes (vs 8 x 4096 on the GPU), "
+    return (f"C3 architecture, batch {b} x {t} bytes (vs 8 x 4096 on the GPU), "
             f"fp32 torch CPU fwd+bwd+AdamW, mean of {steps} steps")
+
+
+REFERENCE_ARM_BUDGET_S = 150.0
+
+
+def reference_sample(steps, warmup, config):
+    """The per-step CPU sample of the reference arm: the config's bounded sample, shrunk (bytes per
+    row, or rows for C1) so that warmup + steps steps take about REFERENCE_ARM_BUDGET_S seconds on
+    this host; one untimed calibration step decides."""
+    b, t = CPU_SAMPLES.get(config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))
+    _, sec, _ = cpu_step_rate(1, 0, config=config, sample=(b, t))
+    scale = REFERENCE_ARM_BUDGET_S / max(sec * (steps + warmup), 1e-9)
+    if scale >= 1.0:
+        return b, t
+    if config == "c1":
+        return max(1, int(b * scale)), t
+    return b, max(256, int(t * scale) // 256 * 256)
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps, warmup = max(1, min(args.steps, 10)), max(0, min(args.warmup, 2))
-    rate, sec, cores = cpu_step_rate(steps, warmup, config=args.config)
+    steps, warmup = max(1, args.steps), max(0, args.warmup)
+    sample = reference_sample(steps, warmup, args.config)
+    rate, sec, cores = cpu_step_rate(steps, warmup, config=args.config, sample=sample)
     line = {"metric": METRIC, "value": rate, "unit": UNIT, "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
             "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic Zipf(1.1) bytes, random-init N(0,0.02) weights",
             "config": {"workload": WORKLOADS[args.config] + " (bounded CPU sample)",
-                       "per_gpu_batch": CPU_SAMPLES.get(args.config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))[0],
-                       "seq_len": CPU_SAMPLES.get(args.config, (CPU_SAMPLE_BATCH, CPU_SAMPLE_SEQ))[1],
-                       "parallelism": "none"},
+                       "per_gpu_batch": sample[0], "seq_len": sample[1], "parallelism": "none"},
             "impl": "reference",
             "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": cpu_sample_text(steps, args.config)},
+                             "sample": cpu_sample_text(steps, args.config, sample)},
             "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference has no CPU execution path (Engine::new needs HIP) and its Rust host cannot "
                     "be built in this image; this arm times the CPU restatement of its step in oracle/"}
@@ -208,19 +229,20 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- GPU arm
-def kernel_timing(trainer, report=None):
-    """One eager step with CUDA events around every C-ABI call: per-family time and FLOPs.
-
-    The stream first runs a ~0.15 s sleep kernel so that the host has enqueued the whole step
-    (and its events) before the GPU reaches it: the events then bracket back-to-back kernels and
-    no host launch gap is counted as kernel time."""
+def kernel_timing(trainer, report=None, replays=3):
+    """Per-family kernel time and FLOPs of one step, measured in the regime of the headline: the step
+    (forward, backward and update; no collective) is captured as a CUDA graph with an event node
+    before and after every C-ABI call, and the graph is replayed `replays` times.  The event nodes
+    cut the programmatic-launch overlap between neighbouring kernels, so each family's time is an
+    upper bound of its share of the event-free graph; the sum over families is reported beside the
+    headline step time."""
     import torch
-    stream = torch.cuda.current_stream()
     records = []
     original = trainer._call
 
     def timed(name, *a):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s, e = torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True)
+        stream = torch.cuda.current_stream()
         s.record(stream)
         original(name, *a)
         e.record(stream)
@@ -234,17 +256,31 @@ def kernel_timing(trainer, report=None):
         records.append((name, s, e, flops, info))
 
     torch.cuda.synchronize()
-    torch.cuda._sleep(300_000_000)
+    side = torch.cuda.Stream(trainer.dev)
+    side.wait_stream(torch.cuda.current_stream(trainer.dev))
+    graph = torch.cuda.CUDAGraph()
     trainer._call = timed
     try:
-        trainer.step()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                trainer._local_forward_backward()
+                trainer.optimizer_step()
     finally:
         trainer._call = original
+    torch.cuda.current_stream(trainer.dev).wait_stream(side)
     torch.cuda.synchronize()
+    graph.replay()  # warm
+    torch.cuda.synchronize()
+    per_call = [0.0] * len(records)
+    for _ in range(replays):
+        graph.replay()
+        torch.cuda.synchronize()
+        for i, (_, s, e, _, _) in enumerate(records):
+            per_call[i] += s.elapsed_time(e) / replays
+    graph.reset()
     fam = {}
     rows = []
-    for name, s, e, flops, info in records:
-        ms = s.elapsed_time(e)
+    for (name, s, e, flops, info), ms in zip(records, per_call):
         f = fam.setdefault(name, {"ms": 0.0, "calls": 0, "flops": 0.0})
         f["ms"] += ms
         f["calls"] += 1
@@ -398,7 +434,9 @@ def run_ours(args):
                         "achieved": achieved, "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
                         "frac": achieved / pk["bf16_sustained"], "peak_source": pk["source"] + " sustained bf16",
                         "traffic": NCU_GEMM_DRAM_BYTES_PER_STEP.get(args.config),
-                        "traffic_unit": "bytes per step, all GEMM launches (ncu, cold cache)",
+                        "traffic_unit": "bytes per step, all GEMM launches",
+                        "traffic_source": NCU_TRAFFIC_SOURCE if args.config in NCU_GEMM_DRAM_BYTES_PER_STEP else None,
+                        "timing": "graph replay of one step with an event node around every call (mean of 3)",
                         "launches": g["calls"], "ms_per_step": g["ms"]}
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
@@ -421,6 +459,7 @@ def run_ours(args):
         line["clocks"] = clk
     if fam:
         line["kernel_ms_per_step"] = {k.replace("sj_", ""): round(v["ms"], 4) for k, v in sorted(fam.items())}
+        line["kernel_ms_sum"] = round(sum(v["ms"] for v in fam.values()), 4)
     if world == 1 and not args.no_cpu_baseline:
         rate, _, cores = cpu_step_rate(2, 1, config=args.config)
         line["cpu_baseline"] = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
