@@ -85,6 +85,11 @@ int sj_zipf_bytes(uint64_t seed, double s, uint8_t* out, size_t n);
  * `tokens` (EOS + bytes + ... + EOS, lib.rs:24-71). */
 int sj_corpus_batch(const int32_t* tokens, size_t n_tokens, uint64_t* rng_state, int batch, int sequence,
                     int32_t* inputs, int32_t* targets);
+/* BLAKE3 (32-byte plain hash) of the concatenation of `count` parts, streamed (host code).  Used for
+ * Corpus::open's fingerprint (crates/sejong-train/src/lib.rs:24-51: the blake3 crate over a domain
+ * string and, per document, its u64 little-endian length and bytes), which checkpoints carry and a
+ * resume compares. */
+int sj_blake3(const void* const* parts, const uint64_t* lengths, int count, uint8_t* out);
 
 /* ------------------------------------------------------------------ GEMM (tcgen05 / TMEM / TMA) */
 /* Epilogues of sj_gemm. */

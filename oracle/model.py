@@ -198,6 +198,11 @@ def initialize(c):
 # Every parameter matmul goes through `mm`, in the reference's node-creation order, so that a
 # recorder (param_vjp.py) can replay the tape's backward visit order (graph.rs:567-913).
 MATMUL_HOOK = None
+# Test hook: {block prefix: LongTensor [rows, top_k]} of expert ids to use instead of the top-k of the
+# oracle's own router logits (the gates stay the full-softmax probabilities of those experts).  A
+# parity test sets it to the routing the GPU chose, so that the FP64 arithmetic is compared on the
+# same routing decisions; near-tied router logits may otherwise pick different experts in FP64.
+ROUTE_OVERRIDE = None
 
 
 def mm(x, p, name):
@@ -220,6 +225,9 @@ def _block(p, prefix, s, x, seq, theta, eps):
     if s.experts is not None:
         logits = mm(z, p, f"{prefix}.router")
         gates, ids = ops.route_topk(logits, s.experts.top_k)
+        if ROUTE_OVERRIDE is not None and prefix in ROUTE_OVERRIDE:
+            ids = ROUTE_OVERRIDE[prefix].to(ids.device)
+            gates = torch.softmax(logits, dim=1).gather(1, ids)
         update = torch.zeros_like(z)
         for e in range(s.experts.count):
             rows, slot = torch.nonzero(ids == e, as_tuple=True)

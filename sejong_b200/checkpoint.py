@@ -140,19 +140,76 @@ def model_config_from_json(m, init_std=0.0):
 
 def train_config_json(tc):
     """TrainConfig as the reference serialises it (crates/sejong-core/src/lib.rs:308-362); fields this
-    build does not use keep the reference defaults, `accumulation` is 1 (one batch per step)."""
+    build does not use keep the reference defaults."""
     out = {"optimizer": tc.optimizer, "control_variate": None}
     if tc.parameter_vjp is not None:
         v = tc.parameter_vjp
         out["parameter_vjp"] = {"rank": v.rank, "residual_fraction": float(v.residual_fraction),
                                 "block_rows": v.block_rows, "seed": int(v.seed)}
     out.update({"gradient_diagnostics_every": 0, "activation_checkpointing": False, "steps": tc.steps,
-                "sequence": tc.sequence, "batch": tc.batch, "accumulation": 1,
+                "sequence": tc.sequence, "batch": tc.batch, "accumulation": int(getattr(tc, "accumulation", 1)),
                 "learning_rate": float(tc.learning_rate), "min_learning_rate": float(tc.min_learning_rate),
                 "warmup_steps": tc.warmup_steps, "beta1": float(tc.beta1), "beta2": float(tc.beta2),
                 "epsilon": float(tc.epsilon), "weight_decay": float(tc.weight_decay),
                 "clip_norm": float(tc.clip_norm), "clip_enabled": bool(tc.clip_enabled),
-                "loss_scale": float(tc.loss_scale), "checkpoint_every": 500, "log_every": 10, "seed": int(tc.seed)})
+                "loss_scale": float(tc.loss_scale), "checkpoint_every": int(getattr(tc, "checkpoint_every", 500)),
+                "log_every": int(getattr(tc, "log_every", 10)), "seed": int(tc.seed)})
+    out["gradient_diagnostics_every"] = int(getattr(tc, "gradient_diagnostics_every", 0))
+    out["activation_checkpointing"] = bool(getattr(tc, "activation_checkpointing", False))
+    return out
+
+
+# ---------------------------------------------------------------------------------- SGD state
+SGD_SAMPLING_MIX = 0x38B87C4D9F0A1265   # SgdState::new (control_variate.rs:66-74)
+SGD_BASIS_MIX = 0xA41239C507EF68BD
+
+
+def rng_words(state):
+    """rng_tensor (control_variate.rs:42-47): a generator state as four 16-bit words, in f32."""
+    state = int(state) & (2**64 - 1)
+    return np.array([(state >> (16 * i)) & 0xFFFF for i in range(4)], dtype=np.float32)
+
+
+def rng_from_words(words, key):
+    """read_rng (control_variate.rs:49-64)."""
+    w = np.asarray(words)
+    if w.shape != (4,):
+        raise ArtifactError("RNG state requires four 16-bit words")
+    value = 0
+    for i, x in enumerate(w.tolist()):
+        if not (np.isfinite(x) and 0.0 <= x <= 65535.0 and float(x).is_integer()):
+            raise ArtifactError(f"invalid optimizer RNG word in {key}")
+        value |= int(x) << (16 * i)
+    return value
+
+
+def sgd_state_tensors(seed, parameter_rng=None):
+    """SgdState::tensors for the plain SGD route: sgd.version = [1], the sampling and basis generators
+    (never advanced by plain SGD, so still at their seeds) and, with the parameter VJP, its generator."""
+    out = {"sgd.version": np.array([1.0], dtype=np.float32),
+           "sgd.sampling_rng": rng_words(int(seed) ^ SGD_SAMPLING_MIX),
+           "sgd.basis_rng": rng_words(int(seed) ^ SGD_BASIS_MIX)}
+    if parameter_rng is not None:
+        out["sgd.parameter_rng"] = rng_words(parameter_rng)
+    return out
+
+
+def read_sgd_state(tensors, parameter_vjp):
+    """Checks of SgdState::load (control_variate.rs:122-195) for the plain SGD route; returns the
+    generator states by key."""
+    version = tensors.get("sgd.version")
+    if version is None:
+        raise ArtifactError("SGD state version missing")
+    if np.shape(version) != (1,) or float(np.asarray(version)[0]) != 1.0:
+        raise ArtifactError("unsupported SGD state version")
+    keys = ["sgd.sampling_rng", "sgd.basis_rng"] + (["sgd.parameter_rng"] if parameter_vjp else [])
+    out = {}
+    for k in keys:
+        if k not in tensors:
+            raise ArtifactError(f"missing optimizer state {k}")
+        out[k] = rng_from_words(tensors[k], k)
+    if len(tensors) != 1 + len(keys):
+        raise ArtifactError("SGD checkpoint tensor count differs from its configuration")
     return out
 
 

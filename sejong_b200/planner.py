@@ -258,9 +258,10 @@ def available_bytes(device=None):
     return int(free.value)
 
 
-def fits_this_build(c: ModelConfig, batch, sequence, values, device=None):
-    """Whether this build's trainer (every activation retained) fits `batch` requests of `sequence`
-    bytes in free memory: allocates the trainer, reports (fits, bytes allocated), frees it."""
+def fits_this_build(c: ModelConfig, batch, sequence, values, device=None, activation_checkpointing=False):
+    """Whether this build's trainer fits `batch` requests of `sequence` bytes in free memory, with every
+    activation retained or with the global stage checkpointed: allocates the trainer, reports (fits,
+    bytes allocated), frees it."""
     import torch
 
     from .train import ByteTrainer, TrainConfig
@@ -268,7 +269,8 @@ def fits_this_build(c: ModelConfig, batch, sequence, values, device=None):
     torch.cuda.synchronize(dev)
     before = torch.cuda.memory_allocated(dev)
     try:
-        tr = ByteTrainer(c, TrainConfig(sequence=sequence, batch=batch, values=values), device=dev.index)
+        tr = ByteTrainer(c, TrainConfig(sequence=sequence, batch=batch, values=values,
+                                        activation_checkpointing=activation_checkpointing), device=dev.index)
     except torch.cuda.OutOfMemoryError:
         return False, None
     used = torch.cuda.memory_allocated(dev) - before

@@ -64,6 +64,17 @@ class TrainConfig:
     # NativeValue training (crates/sejong-train/src/memory.rs:799-1065) when > 0: the number of values
     # of the categorical head; `batch` requests per step, each padded to `sequence` bytes
     values: int = 0
+    # loop settings of the train CLI (TrainConfig::checkpoint_every / log_every /
+    # gradient_diagnostics_every, crates/sejong-core/src/lib.rs:308-362); the step itself ignores them
+    # observations per optimizer step (TrainConfig::accumulation): each observation's loss and
+    # gradient enter with weight 1 / accumulation (crates/sejong-train/src/lib.rs:387-415)
+    accumulation: int = 1
+    checkpoint_every: int = 500
+    log_every: int = 10
+    gradient_diagnostics_every: int = 0
+    # recompute the forward of each global-stage block inside the backward from its saved input
+    # instead of keeping its activations (Graph::checkpoint, crates/sejong-gpu/src/graph.rs:151-174)
+    activation_checkpointing: bool = False
 
 
 def _ptr(t, offset_elems=0):
@@ -73,7 +84,7 @@ def _ptr(t, offset_elems=0):
 class _StageRun:
     """Activation and gradient buffers of one stage (encoder, global or decoder)."""
 
-    def __init__(self, stage, batch, seq, dev, ep=None):
+    def __init__(self, stage, batch, seq, dev, ep=None, checkpoint=False):
         self.stage, self.batch, self.seq = stage, batch, seq
         n, d, f, cq = batch * seq, stage.width, stage.ffn, stage.qkv_width
         self.rows = n
@@ -82,8 +93,15 @@ class _StageRun:
         # the residual stream (block inputs x[i], x[L] = stage output, and the mid-block x1) is f32;
         # GEMM operands (normalised activations, attention output, SwiGLU output) are bf16
         self.x = [e(n, d, dt=f32) for _ in range(stage.layers + 1)]
+        # activation checkpointing (Graph::checkpoint, crates/sejong-gpu/src/graph.rs:151-174): only the
+        # block inputs x[i] are kept; every block shares one set of activation buffers, which the
+        # backward refills by running the block's forward again just before the block's backward
+        self.checkpoint = bool(checkpoint)
         self.layers = []
-        for _ in range(stage.layers):
+        for i in range(stage.layers):
+            if self.checkpoint and i > 0:
+                self.layers.append(self.layers[0])
+                continue
             self.layers.append(dict(z1=e(n, d), inv1=e(n, dt=f32), qkv=e(n, cq), o=e(n, d),
                                     lse=e(n * stage.heads, dt=f32), x1=e(n, d, dt=f32), z2=e(n, d),
                                     inv2=e(n, dt=f32), gu=e(n, 2 * f), h=e(n, f)))
@@ -128,7 +146,9 @@ class _StageRun:
             cap = _lib.load().sj_moe_capacity(n, ex.top_k, ex.count)
             fe, i32 = ex.ffn_width, torch.int32
             self.cap = cap
-            for L in self.layers:
+            for i, L in enumerate(self.layers):
+                if self.checkpoint and i > 0:
+                    continue  # the shared set of the first block
                 L.update(logits=e(n, router_pad(ex.count), dt=f32), ids=e(n, ex.top_k, dt=i32), gates=e(n, ex.top_k, dt=f32),
                          group_rows=e(ex.count + 1, dt=i32), pos=e(n * ex.top_k, dt=i32), row_slot=e(cap, dt=i32),
                          a=e(cap, d), gu=e(cap, 2 * fe), h=e(cap, fe), out=e(cap, d))
@@ -191,14 +211,17 @@ class ByteTrainer:
         e = lambda *s, dt=bf: torch.empty(*s, dtype=dt, device=self.dev)  # noqa: E731
         self.ids = torch.zeros(self.rows, dtype=torch.int32, device=self.dev)
         self.targets = torch.zeros(self.rows, dtype=torch.int32, device=self.dev)
+        ckpt = bool(train.activation_checkpointing)
+        if ckpt and self.ep is not None:
+            raise ValueError("activation checkpointing with expert parallelism is not supported")
         if h is None:
-            self.runs = {"global": _StageRun(global_stage(config), b, t, self.dev, self.ep)}
+            self.runs = {"global": _StageRun(global_stage(config), b, t, self.dev, self.ep, checkpoint=ckpt)}
             top_width = config.width
         else:
             assert t % h.patch_size == 0, "sequence must be a multiple of the patch size"
             self.patches = t // h.patch_size
             self.runs = {"encoder": _StageRun(local_stage(config, True), b, t, self.dev),
-                         "global": _StageRun(global_stage(config), b, self.patches, self.dev, self.ep),
+                         "global": _StageRun(global_stage(config), b, self.patches, self.dev, self.ep, checkpoint=ckpt),
                          "decoder": _StageRun(local_stage(config, False), b, t, self.dev)}
             de, dg, dd = h.encoder_width, config.width, h.decoder_width
             np_ = b * self.patches
@@ -324,6 +347,23 @@ class ByteTrainer:
         self.vjp_left = torch.empty(left, dtype=f32, device=dev)
         self.vjp_e = torch.empty(e, dtype=torch.bfloat16, device=dev)
         self.vjp_coeff = torch.empty(coeff, dtype=f32, device=dev)
+
+    def vjp_statistics(self):
+        """The counts of the reference's VjpStatistics for one backward pass (graph.rs:915-1005):
+        matrices whose gradient is factored, matrices with an exact gradient, bases computed and
+        groups prepared."""
+        nodes = param_vjp.matmul_nodes(self.c, self.tc.batch, self.tc.sequence)
+        compressed = len(self.vjp.compressed)
+        return {"compressed_matrices": compressed, "dense_matrices": len(nodes) - compressed,
+                "basis_groups": sum(1 for g in self.vjp.groups.values() if g.new_basis),
+                "projection_groups": len(self.vjp.groups)}
+
+    def evaluate(self):
+        """Mean cross entropy of the staged batch, forward only (benchmark.rs:71-97 `evaluate`)."""
+        self.stream = torch.cuda.current_stream(self.dev).cuda_stream
+        self._zero(self.loss_sum)
+        self._forward()
+        return float(self.loss_sum.item()) * max(1, self.tc.accumulation) * self.world
 
     def vjp_rng_state(self):
         """The device generator state as the reference Rng's u64."""
@@ -576,6 +616,12 @@ class ByteTrainer:
 
     def _stage_bwd(self, run):
         for i in reversed(range(run.stage.layers)):
+            if run.checkpoint and i < run.stage.layers - 1:
+                # Op::Checkpoint's backward (graph.rs:756-799): the block's forward again, from its saved
+                # input x[i], into the shared activation buffers (it rewrites x[i+1] with the values it
+                # already holds: the forward kernels are deterministic).  The last block's activations
+                # are still in the buffers from the forward pass, so it is not run again.
+                self._block_fwd(run, i)
             self._block_bwd(run, i)
 
     # ------------------------------------------------------------------ model
@@ -583,6 +629,7 @@ class ByteTrainer:
         c, h = self.c, self.c.hierarchy
         n = self.rows
         b = self.tc.batch
+        acc = float(max(1, self.tc.accumulation))
         emb, vocab = ("native_embedding", NATIVE_VOCAB) if self.values else ("embedding", VOCAB)
         if h is None:
             run = self.runs["global"]
@@ -631,14 +678,14 @@ class ByteTrainer:
             bt = self.tc.batch
             self._call("sj_value_head_fwd", _ptr(self.hf), top_width, n, _ptr(self.sel), bt, top_width,
                        self.w_ptr("native_value"), self.w_ptr("native_bias"), self.values, _ptr(self.labels),
-                       distributed.ce_seed(bt, self.world, self.tc.loss_scale), _ptr(self.vlogits),
-                       _ptr(self.vdlogits), _ptr(self.loss_sum), distributed.ce_seed(bt, self.world), self.stream)
+                       distributed.ce_seed(bt, self.world, self.tc.loss_scale) / acc, _ptr(self.vlogits),
+                       _ptr(self.vdlogits), _ptr(self.loss_sum), distributed.ce_seed(bt, self.world) / acc, self.stream)
             return top, top_width
         self._gemm(_ptr(self.hf), top_width, 0, self.wb_ptr("output"), VOCAB_PAD, 0, _ptr(self.logits), VOCAB_PAD,
                    SJ_F32, n, VOCAB, top_width)
         self._call("sj_cross_entropy", _ptr(self.logits), VOCAB_PAD, _ptr(self.targets), n, VOCAB,
-                   distributed.ce_seed(n, self.world, self.tc.loss_scale), 0, _ptr(self.dlogits), VOCAB_PAD,
-                   _ptr(self.loss_sum), distributed.ce_seed(n, self.world), self.stream)
+                   distributed.ce_seed(n, self.world, self.tc.loss_scale) / acc, 0, _ptr(self.dlogits), VOCAB_PAD,
+                   _ptr(self.loss_sum), distributed.ce_seed(n, self.world) / acc, self.stream)
         return top, top_width
 
     def _backward(self, top, top_width):
@@ -713,10 +760,13 @@ class ByteTrainer:
             self._call("sj_embedding_bwd", _ptr(enc.dx), _ptr(self.ids), self.g_ptr(emb), n, de, VOCAB, self.stream)
 
     # ------------------------------------------------------------------ public step API
-    def _local_forward_backward(self):
+    def _local_forward_backward(self, first=True):
+        """Loss and gradients of the staged batch; `first` = False adds them to those of the previous
+        observations of the same step (gradient accumulation) instead of starting from zero."""
         self.stream = torch.cuda.current_stream(self.dev).cuda_stream
-        self._zero(self.g)
-        self._zero(self.loss_sum)
+        if first:
+            self._zero(self.g)
+            self._zero(self.loss_sum)
         top, width = self._forward()
         self._backward(top, width)
         sb = self.layout.shared_begin
@@ -733,10 +783,12 @@ class ByteTrainer:
             else:
                 distributed.exchange(self.g, self.loss_sum, self.pg)
 
-    def forward_backward(self):
-        """Loss (into self.loss_sum) and gradients (into self.g) for the staged batch."""
-        self._local_forward_backward()
-        self._exchange()
+    def forward_backward(self, first=True, last=True):
+        """Loss (into self.loss_sum) and gradients (into self.g) for the staged batch; with gradient
+        accumulation, call once per observation (first / last mark the step's first and last)."""
+        self._local_forward_backward(first)
+        if last:
+            self._exchange()
 
     def optimizer_step(self):
         """Adam::update (crates/sejong-train/src/lib.rs:199-238) or the dense SGD step, in two launches."""
@@ -773,10 +825,14 @@ class ByteTrainer:
         self.labels.copy_(torch.as_tensor(labels, dtype=torch.int32).reshape(-1), non_blocking=non_blocking)
 
     # ------------------------------------------------------------------ artifacts
-    def save_checkpoint(self, directory, data_fingerprint=None, rng_state=None):
-        """save_training (crates/sejong-train/src/lib.rs:472-491): the FP32 master weights under the
-        reference's parameter names, the AdamW moments as m.<name> / v.<name>, the optimizer step
-        (the device optimizer state) and the training config, written atomically."""
+    def save_checkpoint(self, directory, data_fingerprint=None, rng_state=None, model_id="sejong", precision="f16"):
+        """save_training (crates/sejong-train/src/lib.rs:472-491) and the SGD route's `save`
+        (crates/sejong-train/src/control_variate.rs:389-406): the FP32 master weights under the
+        reference's parameter names, the optimizer step (the device optimizer state), the training
+        config, the data fingerprint and the data generator's state, written atomically, with the
+        optimizer state: AdamW moments as m.<name> / v.<name>, or the SGD state of
+        SgdState::tensors (control_variate.rs:208-233: sgd.version, and the sampling, basis and
+        parameter-VJP generators as four 16-bit words each)."""
         from . import checkpoint
         if self.ep is not None:
             raise checkpoint.ArtifactError("checkpoints of an expert-parallel trainer are not supported: each rank "
@@ -789,9 +845,12 @@ class ByteTrainer:
             for prefix, buf in (("m", self.m), ("v", self.v)):
                 for name, value in self.layout.unpack(buf.cpu().numpy()).items():
                     optimizer[f"{prefix}.{name}"] = value
+        else:
+            optimizer = checkpoint.sgd_state_tensors(self.tc.seed, self.vjp_rng_state() if self.vjp is not None
+                                                     else None)
         step = int(self.opt_state[0].item())
         return checkpoint.save(directory, self.c, params, step, optimizer, checkpoint.train_config_json(self.tc),
-                               data_fingerprint, rng_state)
+                               data_fingerprint, rng_state, model_id=model_id, precision=precision)
 
     def load_checkpoint(self, directory):
         """Resume from an artifact directory (Model::load, crates/sejong-model/src/lib.rs:134-170):
@@ -803,7 +862,17 @@ class ByteTrainer:
             raise checkpoint.ArtifactError("artifact model layout differs from this trainer's")
         torch.cuda.synchronize(self.dev)
         self.w.copy_(torch.from_numpy(self.layout.pack(params)).to(self.dev))
-        if optimizer is not None:
+        if self.tc.optimizer != "adamw":
+            # SgdState::load (control_variate.rs:122-195): the version, the generators, and nothing else
+            if optimizer is None:
+                raise checkpoint.ArtifactError("resume requires SGD optimizer state")
+            rngs = checkpoint.read_sgd_state(optimizer, self.vjp is not None)
+            if self.vjp is not None:
+                self.vjp_rng.copy_(torch.from_numpy(np.array([rngs["sgd.parameter_rng"]], dtype=np.uint64)
+                                                    .view(np.int64)).to(self.dev))
+            self.m.zero_()
+            self.v.zero_()
+        elif optimizer is not None:
             for prefix, buf in (("m", self.m), ("v", self.v)):
                 named = {k[len(prefix) + 1:]: v for k, v in optimizer.items() if k.startswith(prefix + ".")}
                 if set(named) != set(params):

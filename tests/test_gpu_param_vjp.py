@@ -169,9 +169,13 @@ def oracle_config(c):
                           hierarchy=oh, seed=c.seed, init_std=c.init_std, router_std=c.router_std)
 
 
-@pytest.mark.parametrize("config_name,batch,seq", [("small_hierarchy", 1, 2048), ("config_c1", 2, 512)])
+@pytest.mark.parametrize("config_name,batch,seq", [("small_hierarchy", 1, 2048), ("config_c1", 2, 512),
+                                                    ("config_c3", 2, 4096)])
 def test_step_parity(config_name, batch, seq):
-    """One training step with the parameter VJP and compact SGD against the FP64 oracle."""
+    """One training step with the parameter VJP and compact SGD against the FP64 oracle.  The C4 case is
+    C3's architecture at 2 x 4096 bytes with fraction 0.25: 1,024 global rows >= 768 features, so the
+    global QKV and gate/up gradients are factored too, with 24 of 768 feature rows' blocks (192 rows)
+    selected, beside the local stages' 2 of 8 blocks (64 rows)."""
     from sejong_b200 import model as pm
     from sejong_b200.param_vjp import VjpConfig
     from sejong_b200.train import ByteTrainer, TrainConfig
@@ -184,6 +188,8 @@ def test_step_parity(config_name, batch, seq):
                      parameter_vjp=vcfg)
     tr = ByteTrainer(c, tc, device=0, params=params)
     assert tr.vjp.compressed, "the case must compress some weight gradients"
+    if config_name == "config_c3":
+        assert tr.vjp.groups["layers.0.z1"].k == 192 and tr.vjp.groups["encoder.0.z1"].k == 64
     tr.stage_batch(ids, targets)
     tr.forward_backward()
     torch.cuda.synchronize()
@@ -239,3 +245,41 @@ def test_draws_advance_per_step():
         host.next_u64()
     assert tr.vjp_rng_state() == host.state & MASK64
     tr.release_graphs()
+
+
+def test_adamw_with_parameter_vjp():
+    """AdamW fed the parameter VJP's materialised gradient (GradientMaterializer,
+    crates/sejong-gpu/src/parameter_vjp.rs:347-380; used by the NativeValue trainer, crates/sejong-train/
+    src/memory.rs:1001-1010): the gradient equals the SGD route's for the same draws, and the update is
+    the FP64 AdamW transition of that gradient."""
+    from sejong_b200 import model as pm
+    from sejong_b200.param_vjp import VjpConfig
+    from sejong_b200.train import ByteTrainer, TrainConfig
+    c = pm.small_hierarchy()
+    params = pm.initialize(c)
+    ids, targets = synthetic_corpus(5, 200000).batch(Rng(77), 1, 2048)
+    out = {}
+    for opt in ("sgd", "adamw"):
+        tc = TrainConfig(sequence=2048, batch=1, optimizer=opt, learning_rate=1e-3, warmup_steps=0, steps=100,
+                         parameter_vjp=VjpConfig())
+        tr = ByteTrainer(c, tc, device=0, params=params)
+        tr.stage_batch(ids, targets)
+        tr.forward_backward()
+        torch.cuda.synchronize()
+        assert tr.device_error() == 0
+        grads = tr.gradients()
+        rng_state = tr.vjp_rng_state()
+        tr.optimizer_step()
+        torch.cuda.synchronize()
+        out[opt] = (grads, rng_state, tr.parameters(), float(tr.hyper[4]))
+        tr.close()
+    g_sgd, rng_sgd, _, _ = out["sgd"]
+    g_adam, rng_adam, new, norm_gpu = out["adamw"]
+    assert rng_sgd == rng_adam
+    for k in g_sgd:
+        assert rel(g_adam[k], g_sgd[k]) < 1e-5, k
+    otc = om.TrainConfig(sequence=2048, batch=1, learning_rate=1e-3, warmup_steps=0, steps=100)
+    ref_new, norm = om.adam_update(params, {k: v.astype(np.float64) for k, v in g_adam.items()}, om.AdamState(), otc)
+    assert abs(norm_gpu - norm) < 1e-5 * max(norm, 1.0)
+    for k in params:
+        assert float(np.max(np.abs(new[k] - ref_new[k]))) < 2e-6, k

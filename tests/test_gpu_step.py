@@ -144,3 +144,52 @@ def test_graph_replay_matches_eager_and_loss_decreases():
     np.testing.assert_allclose(losses_g, losses_e, rtol=0, atol=2e-3)
     assert rel(graphed.w.cpu().numpy(), eager.w.cpu().numpy()) < 1e-3
     assert float(eager.opt_state[0]) == 6.0 and float(graphed.opt_state[0]) == 6.0
+
+
+def test_step_parity_c5_architecture_reduced_batch():
+    """C5's architecture as BASELINE states it -- global d1024 x 12 layers HQ16/HK4, 8 SwiGLU experts of
+    2816 with top-2 routing, router N(0, 0.006) -- on one 1024-byte row.  Besides the loss and gradient
+    bars: in every MoE layer the routing of the GPU's own f32 router logits equals the reference rule
+    (softmax, top-k, lowest index on ties; hierarchy.py:175-191) bit for bit, and each expert's packed
+    segment lists its slots in the reference's order.  The FP64 oracle then routes with those decisions
+    (oracle.model.ROUTE_OVERRIDE): at router std 0.006 the router logits of a row are close together,
+    and a bf16 rounding can tip a near tie to the other expert, which would compare two different
+    computations rather than the arithmetic of one."""
+    from oracle.ops import route_topk
+    from sejong_b200.model import initialize
+    from sejong_b200.train import ByteTrainer, TrainConfig
+    c, ids, tg = make_case("config_c5", 1, 1024)
+    assert c.experts.count == 8 and c.experts.top_k == 2 and c.experts.ffn_width == 2816 and c.layers == 12
+    assert c.router_std == 0.006
+    params = initialize(c)
+    tr = ByteTrainer(c, TrainConfig(sequence=1024, batch=1, warmup_steps=0, steps=100), device=0, params=params)
+    tr.stage_batch(ids, tg)
+    tr.forward_backward()
+    torch.cuda.synchronize()
+    assert tr.device_error() == 0
+    run = tr.runs["global"]
+    E, k = c.experts.count, c.experts.top_k
+    override = {}
+    for i, L in enumerate(run.layers):
+        override[f"layers.{i}"] = L["ids"].cpu().long()
+        logits = L["logits"][:, :E].double().cpu()
+        gates_ref, ids_ref = route_topk(logits, k)
+        assert np.array_equal(L["ids"].cpu().numpy(), ids_ref.numpy()), f"layer {i} routing"
+        slots = L["ids"].cpu().numpy().reshape(-1)
+        gr, row_slot = L["group_rows"].cpu().numpy(), L["row_slot"].cpu().numpy()
+        for x in range(E):
+            want = np.nonzero(slots == x)[0]
+            assert np.array_equal(row_slot[gr[x]:gr[x] + len(want)], want), f"layer {i} expert {x} pack order"
+    loss, grads = tr.loss(), tr.gradients()
+    tr.close()
+    del tr
+    omodel.ROUTE_OVERRIDE = override
+    try:
+        ref_loss, ref_grads = omodel.loss_and_grads(params, oracle_config(c), ids, tg, 1024, cast="bf16")
+    finally:
+        omodel.ROUTE_OVERRIDE = None
+    assert abs(loss - ref_loss) < LOSS_TOL, (loss, ref_loss)
+    worst = {n: rel(grads[n], g) for n, g in ref_grads.items() if np.any(g != 0)}
+    print("C5 worst gradients", sorted(worst.items(), key=lambda kv: -kv[1])[:5])
+    bad = {n: v for n, v in worst.items() if v > GRAD_TOL}
+    assert not bad, f"gradients beyond {GRAD_TOL}: {bad}"
