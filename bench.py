@@ -40,9 +40,10 @@ WORKLOADS = {"c1": "C1 dense byte model, one training step in fp32: fwd+bwd+Adam
              "c3": "C3 hierarchical byte model, fwd+bwd+AdamW (BASELINE configs[2])",
              "c4": "C4 hierarchical byte model, fwd + input VJP + parameter VJP (rank 16, fraction 0.25) + "
                    "compact SGD lr 1e-2 (BASELINE configs[3])",
-             "c5": "C5 byte MoE model, fwd+bwd+AdamW (BASELINE configs[4]): on one GPU all 8 experts of a layer "
-                   "are local; on N GPUs each owns 8/N experts and routed rows move over NVLink peer memory "
-                   "(expert parallelism), the rest is data parallel"}
+             "c5": "C5 byte MoE model, fwd+bwd+AdamW (BASELINE configs[4]) with expert capacity factor 1.25 and "
+                   "load-balance loss weight 0.01: on one GPU all 8 experts of a layer are local; on N GPUs each "
+                   "owns 8/N experts and routed rows move over NVLink peer memory (expert parallelism), the rest is "
+                   "data parallel"}
 MODELS = {"c1": "dense byte model: d256 x4, HQ4/HK2, SwiGLU 1024, eps 1e-6, RoPE 1e4",
           "c3": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
           "c4": "hierarchical byte model: local d256 2+2 layers W128, global d768 x8 HQ12/HK4 SwiGLU2048",
@@ -315,6 +316,11 @@ def run_ours(args):
         from sejong_b200.param_vjp import VjpConfig
         tc = TrainConfig(sequence=args.seq, batch=args.batch, optimizer="sgd", learning_rate=1e-2, warmup_steps=0,
                          steps=10000, parameter_vjp=VjpConfig())
+    elif args.config == "c5":
+        # capacity factor 1.25 and load-balance loss weight 0.01 (this build's additions;
+        # the reference keeps every routed row and has no auxiliary loss); the capacity counts each rank's rows
+        tc = TrainConfig(sequence=args.seq, batch=args.batch, warmup_steps=0, steps=10000, moe_capacity_factor=1.25,
+                         moe_aux_loss_weight=0.01)
     else:
         tc = TrainConfig(sequence=args.seq, batch=args.batch, warmup_steps=0, steps=10000)
     # C5 on several GPUs: the experts are sharded over the ranks (expert parallelism), the rest is

@@ -260,6 +260,21 @@ int sj_moe_capacity(int rows, int k, int experts);
 int sj_route_topk(const float* logits, int ld, int rows, int experts, int k, int32_t* ids, float* gates, void* stream);
 int sj_route_pack(const int32_t* ids, int rows, int experts, int k, int32_t* group_rows, int32_t* pos,
                   int32_t* row_slot, int cap, void* stream);
+/* No counterpart in the reference (its experts take every routed row and it has no auxiliary loss);
+ * opt-in additions for the MoE benchmark configuration (capacity factor 1.25, loss weight 0.01).
+ * Expert capacity: each expert keeps at most `capacity` of the slots in
+ * ids [rows, k] (every row's first choice before any second choice, rows in order within a choice);
+ * dropped slots get id -1 in place, which the pack, combine and backwards skip.  Call between
+ * sj_route_topk and sj_route_pack / sj_ep_route_pack. */
+int sj_route_capacity(int32_t* ids, int rows, int k, int experts, int capacity, void* stream);
+/* Load-balancing loss aux = weight * E * sum_e f_e P_e (f_e: share of the top-k choices, before any
+ * capacity drop, that picked e; P_e: mean router probability of e), recomputed from the f32 router
+ * logits (two kernels; no atomics): loss_sum[0] += loss_seed * aux, and dlogits (bf16 [rows, ldd], the router gradient that
+ * sj_route_topk_bwd wrote) += grad_scale * d aux / d logits. */
+int sj_moe_aux(const float* logits, int ld, int rows, int experts, int k, float weight, double loss_seed,
+               double* loss_sum, void* dlogits, int ldd, float grad_scale, float* workspace, void* stream);
+/* Floats of sj_moe_aux's workspace (per 256 rows, the choice counts and probability sums). */
+size_t sj_moe_aux_workspace(int rows, int experts);
 int sj_moe_dispatch(const void* z, int ldz, const int32_t* row_slot, int cap, int k, int d, void* a, void* stream);
 int sj_moe_combine(const void* out, const int32_t* pos, const float* gates, const float* x, float* y, int rows, int k,
                    int d, void* stream);

@@ -20,6 +20,7 @@ and are still updated.
 Gradients are exact FP64 derivatives of the forward (torch autograd); the
 reference's explicit backward kernels are pinned separately in `ops.py`.
 """
+import math
 from dataclasses import dataclass, field, replace
 from typing import Optional
 
@@ -68,6 +69,10 @@ class ModelConfig:
     seed: int = 42
     init_std: float = 0.02       # 0 selects the reference's fan-in init (lib.rs:82-116)
     router_std: float = 0.02
+    # MoE additions that the reference lacks (0 keeps its semantics): expert capacity factor and the
+    # weight of the load-balancing loss, restated from their definitions in sejong_b200/csrc/moe.cu
+    moe_capacity_factor: float = 0.0
+    moe_aux_weight: float = 0.0
 
 
 @dataclass
@@ -203,6 +208,11 @@ MATMUL_HOOK = None
 # parity test sets it to the routing the GPU chose, so that the FP64 arithmetic is compared on the
 # same routing decisions; near-tied router logits may otherwise pick different experts in FP64.
 ROUTE_OVERRIDE = None
+# Test hook for the load-balancing loss: {block prefix: LongTensor [rows, top_k]} of the top-k choices
+# (before any capacity drop) whose shares f_e the loss uses.  f is piecewise constant in the logits, so a
+# near tie that rounds the other way changes it by a whole choice; a parity test passes the GPU's own
+# choices so that both sides weigh the same shares.
+AUX_CHOICES = None
 
 
 def mm(x, p, name):
@@ -212,7 +222,33 @@ def mm(x, p, name):
     return y
 
 
-def _block(p, prefix, s, x, seq, theta, eps):
+AUX_TERMS = []   # load-balancing losses of the current forward (summed into the loss)
+
+
+def apply_capacity(ids, experts, capacity):
+    """Expert capacity: each expert keeps at most `capacity` slots; every row's first choice before any
+    second choice, rows in order within one choice; dropped slots become -1."""
+    out = ids.clone()
+    fill = torch.zeros(experts, dtype=torch.int64)
+    for j in range(ids.shape[1]):
+        col = ids[:, j]
+        onehot = torch.nn.functional.one_hot(col, experts)           # [rows, E]
+        rank = torch.cumsum(onehot, dim=0) - onehot + fill[None, :]  # slots of e before this row
+        keep = (rank * onehot).sum(1) < capacity
+        out[~keep, j] = -1
+        fill += onehot.sum(0)
+    return out
+
+
+def aux_loss(logits, ids_topk, experts, weight):
+    """Load-balancing loss weight * E * sum_e f_e P_e: f_e the share of the top-k choices (before any
+    capacity drop) that picked e, P_e the mean router probability (differentiable) of e."""
+    p = torch.softmax(logits, dim=1)
+    f = torch.nn.functional.one_hot(ids_topk.reshape(-1), experts).to(p.dtype).mean(0)
+    return weight * experts * (f * p.mean(0)).sum()
+
+
+def _block(p, prefix, s, x, seq, theta, eps, c=None):
     z = ops.rmsnorm(x, p[f"{prefix}.attention_norm"], eps)
     q = mm(z, p, f"{prefix}.query")
     k = mm(z, p, f"{prefix}.key")
@@ -227,7 +263,15 @@ def _block(p, prefix, s, x, seq, theta, eps):
         gates, ids = ops.route_topk(logits, s.experts.top_k)
         if ROUTE_OVERRIDE is not None and prefix in ROUTE_OVERRIDE:
             ids = ROUTE_OVERRIDE[prefix].to(ids.device)
-            gates = torch.softmax(logits, dim=1).gather(1, ids)
+            gates = torch.softmax(logits, dim=1).gather(1, ids.clamp(min=0))
+        if c is not None and c.moe_aux_weight > 0:
+            choices = (AUX_CHOICES[prefix] if AUX_CHOICES is not None and prefix in AUX_CHOICES
+                       else ops.route_topk(logits.detach(), s.experts.top_k)[1])
+            AUX_TERMS.append(aux_loss(logits, choices, s.experts.count, c.moe_aux_weight))
+        if c is not None and c.moe_capacity_factor > 0 and (ROUTE_OVERRIDE is None or prefix not in ROUTE_OVERRIDE):
+            rows, k = ids.shape
+            ids = apply_capacity(ids, s.experts.count, max(1, math.ceil(c.moe_capacity_factor * rows * k /
+                                                                         s.experts.count)))
         update = torch.zeros_like(z)
         for e in range(s.experts.count):
             rows, slot = torch.nonzero(ids == e, as_tuple=True)
@@ -245,7 +289,7 @@ def _block(p, prefix, s, x, seq, theta, eps):
 
 def _blocks(p, s, x, seq, c):
     for i in range(s.layers):
-        x = _block(p, f"{s.prefix}.{i}", s, x, seq, c.rope_theta, c.norm_epsilon)
+        x = _block(p, f"{s.prefix}.{i}", s, x, seq, c.rope_theta, c.norm_epsilon, c)
     return x
 
 
@@ -310,10 +354,14 @@ def loss_and_grads(params, c, ids, targets, seq, dtype=torch.float64, scale=1.0,
     p = {k: torch.tensor(v, dtype=dtype, requires_grad=True) for k, v in params.items()}
     ids = torch.as_tensor(np.asarray(ids, dtype=np.int64))
     targets = torch.as_tensor(np.asarray(targets, dtype=np.int64))
+    AUX_TERMS.clear()
     h = hidden(p, c, ids, seq)
     logits = mm(h, p, "output")
     per_row = ops.cross_entropy(logits, targets)
     loss = per_row.mean()
+    for term in AUX_TERMS:
+        loss = loss + term
+    AUX_TERMS.clear()
     (loss * scale).backward()
     grads = {k: (t.grad.detach().numpy().copy() if t.grad is not None
                  else np.zeros(t.shape, dtype=np.float64 if dtype == torch.float64 else np.float32))

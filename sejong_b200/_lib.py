@@ -33,6 +33,10 @@ SIGNATURES = {
     "sj_moe_capacity": (c_int, [c_int, c_int, c_int]),
     "sj_route_topk": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "sj_route_pack": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_void_p]),
+    "sj_route_capacity": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_void_p]),
+    "sj_moe_aux": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_float, c_double, c_void_p, c_void_p, c_int, c_float,
+                           c_void_p, c_void_p]),
+    "sj_moe_aux_workspace": (c_size_t, [c_int, c_int]),
     "sj_moe_dispatch": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "sj_moe_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "sj_moe_combine_bwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,

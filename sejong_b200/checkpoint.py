@@ -154,6 +154,10 @@ def train_config_json(tc):
                 "clip_norm": float(tc.clip_norm), "clip_enabled": bool(tc.clip_enabled),
                 "loss_scale": float(tc.loss_scale), "checkpoint_every": int(getattr(tc, "checkpoint_every", 500)),
                 "log_every": int(getattr(tc, "log_every", 10)), "seed": int(tc.seed)})
+    if getattr(tc, "moe_capacity_factor", 0.0) or getattr(tc, "moe_aux_loss_weight", 0.0):
+        # this build's MoE additions; absent (and so reference-compatible) when they are off
+        out["moe_capacity_factor"] = float(tc.moe_capacity_factor)
+        out["moe_aux_loss_weight"] = float(tc.moe_aux_loss_weight)
     out["gradient_diagnostics_every"] = int(getattr(tc, "gradient_diagnostics_every", 0))
     out["activation_checkpointing"] = bool(getattr(tc, "activation_checkpointing", False))
     return out

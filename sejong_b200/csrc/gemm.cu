@@ -577,14 +577,10 @@ int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, 
 template <int BN, bool A_MN, bool B_MN>
 static int launch_gemm(const CUtensorMap* maps, const GemmParams& p, int grid, int smem, cudaStream_t stream) {
   auto kernel = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-    if (e != cudaSuccess) return cuda_check(e, "gemm shared-memory attribute");
-    configured_device = dev;
-  }
+  static KernelAttrOnce attr_once;  // one per template instance
+  const int attr_rc =
+      ensure_max_smem(attr_once, reinterpret_cast<const void*>(kernel), kSmemLimit, "gemm shared-memory attribute");
+  if (attr_rc != SJ_OK) return attr_rc;
   launch(kernel, grid, kThreads, smem, stream, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("gemm launch");
   return SJ_OK;

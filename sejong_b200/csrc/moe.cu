@@ -4,7 +4,9 @@
 // 174-250; Engine::route_topk, expert_routes, expert_combine and their backwards, crates/sejong-gpu/
 // src/hierarchy_ops.rs:280-454; the block, crates/sejong-model/src/architecture.rs:229-241): softmax
 // over the experts, top-k by logit with the lowest index on ties, gate = the full-softmax
-// probability of the chosen expert, every routed row kept (no capacity drop, no auxiliary loss).
+// probability of the chosen expert, every routed row kept.  Two opt-in additions that the reference
+// lacks (the MoE benchmark configuration asks for them): an expert capacity (sj_route_capacity) and the load-balancing
+// loss (sj_moe_aux); with capacity unlimited and weight 0 the path is the reference's.
 //
 // Where the reference reads the expert counts back to the host and runs one small GEMM per expert,
 // everything here stays on the device: the pack writes, per expert, a segment of packed rows padded
@@ -217,8 +219,9 @@ __global__ void route_topk_bwd_kernel(const float* logits, int ld, const int32_t
   float total = 0.f;
   for (int j = 0; j < k; ++j) {
     const int e = ids[static_cast<size_t>(r) * k + j];
+    if (e < 0 || e >= experts) continue;  // a slot dropped by the capacity: no output, no gradient
     const float dyj = d_gates[static_cast<size_t>(r) * k + j];
-    if (e >= 0 && e < experts) sel[e] += dyj;
+    sel[e] += dyj;
     total += gates[static_cast<size_t>(r) * k + j] * dyj;
   }
   for (int e = 0; e < ldd; ++e)
@@ -247,9 +250,197 @@ __global__ void moe_dispatch_bwd_kernel(const float* da, const int32_t* pos, flo
   o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
+// Expert capacity (an addition to the reference, whose experts take every routed row): each expert
+// keeps at most `capacity` slots; every row's first choice comes before any second choice, and within
+// one choice rows go in order; a dropped slot's expert id becomes -1, so the pack, the combine and the
+// backwards leave it out (its row keeps the residual and its other experts).  One CTA: per choice j,
+// chunks of 1024 rows ranked per expert with warp ballots on top of the running fill.
+__global__ void __launch_bounds__(kPackThreads) route_capacity_kernel(int32_t* ids, int rows, int k, int experts,
+                                                                      int capacity) {
+  pdl_wait();
+  __shared__ int fill[kMaxExperts];
+  __shared__ int warp_count[kPackThreads / 32][kMaxExperts];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  if (t < kMaxExperts) fill[t] = 0;
+  __syncthreads();
+  for (int j = 0; j < k; ++j) {
+    for (int r0 = 0; r0 < rows; r0 += kPackThreads) {
+      const int r = r0 + t;
+      int32_t* slot = ids + static_cast<size_t>(r) * k + j;
+      const int e = r < rows ? *slot : -1;
+      const unsigned lt = (1u << lane) - 1u;
+      int rank = 0;
+      for (int x = 0; x < experts; ++x) {
+        const unsigned m = __ballot_sync(0xffffffffu, e == x);
+        if (lane == 0) warp_count[warp][x] = __popc(m);
+        if (e == x) rank = __popc(m & lt);
+      }
+      __syncthreads();
+      if (e >= 0 && e < experts) {
+        int before = fill[e];
+        for (int w = 0; w < warp; ++w) before += warp_count[w][e];
+        if (before + rank >= capacity) *slot = -1;
+      }
+      __syncthreads();
+      if (t < experts) {
+        int total = 0;
+        for (int w = 0; w < kPackThreads / 32; ++w) total += warp_count[w][t];
+        fill[t] += total;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Load-balancing loss (an addition; the Switch Transformer form): aux = weight * E * sum_e f_e P_e with
+// f_e the fraction of the rows' top-k choices (before any capacity drop) that picked expert e and
+// P_e the mean router probability of e.  f is piecewise constant, so d aux / d logit[r, e'] =
+// weight * E / rows * p[r, e'] * (f_e' - sum_e f_e p[r, e]).  One CTA: the routing and probabilities
+// are recomputed from the logits (the rule of route_topk_kernel), reduced, then the loss is added to
+// the FP64 loss sum (times loss_seed) and the gradient (times grad_scale) to the bf16 router gradient.
+constexpr int kAuxThreads = 256;  // rows per CTA (thread per row) of the two load-balancing kernels
+
+// Pass 1: per CTA (256 rows), the rows' top-k choice counts and summed router probabilities, written
+// to partials[cta][0 .. E) (counts) and [E .. 2E) (probability sums); no atomics on global memory, so
+// pass 2 reduces them in a fixed order.
+__global__ void __launch_bounds__(kAuxThreads) moe_aux_stats_kernel(const float* logits, int ld, int rows, int experts,
+                                                                    int k, float* partials) {
+  pdl_wait();
+  __shared__ float part[kAuxThreads / 32][2 * kMaxExperts];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int r = blockIdx.x * kAuxThreads + t;
+  // per-expert arrays indexed by compile-time constants only (guarded by `experts`): registers
+  float s[kMaxExperts], x[kMaxExperts], cnt[kMaxExperts];
+  float mx = -INFINITY, den = 0.f;
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    s[e] = (r < rows && e < experts) ? logits[static_cast<size_t>(r) * ld + e] : -INFINITY;
+    mx = fmaxf(mx, s[e]);
+    cnt[e] = 0.f;
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    x[e] = (r < rows && e < experts) ? expf(s[e] - mx) : 0.f;
+    den += x[e];
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) x[e] = r < rows ? x[e] / den : 0.f;
+  if (r < rows) {
+    for (int j = 0; j < k; ++j) {
+      float best = -INFINITY;
+      int idx = experts;
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e)
+        if (e < experts && s[e] > best) {  // strict: the lowest index wins a tie
+          best = s[e];
+          idx = e;
+        }
+#pragma unroll
+      for (int e = 0; e < kMaxExperts; ++e)
+        if (e == idx) {
+          cnt[e] += 1.f;
+          s[e] = -INFINITY;
+        }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    if (e >= experts) break;
+    const float c = warp_sum(cnt[e]), q = warp_sum(x[e]);
+    if (lane == 0) {
+      part[warp][e] = c;
+      part[warp][experts + e] = q;
+    }
+  }
+  __syncthreads();
+  if (t < 2 * experts) {
+    float tot = 0.f;
+    for (int w = 0; w < kAuxThreads / 32; ++w) tot += part[w][t];
+    partials[static_cast<size_t>(blockIdx.x) * 2 * experts + t] = tot;
+  }
+}
+
+// Pass 2: every CTA reduces the partials (same order in every CTA), then adds the loss (CTA 0) and the
+// gradient of its 256 rows to the bf16 router gradient.
+__global__ void __launch_bounds__(kAuxThreads) moe_aux_grad_kernel(const float* logits, int ld, int rows, int experts,
+                                                                   int k, int ctas, const float* partials,
+                                                                   float weight, double loss_seed, double* loss_sum,
+                                                                   __nv_bfloat16* dlogits, int ldd, float grad_scale) {
+  pdl_wait();
+  __shared__ float fP[2 * kMaxExperts];
+  const int t = threadIdx.x;
+  if (t < 2 * experts) {
+    float tot = 0.f;
+    for (int c = 0; c < ctas; ++c) tot += partials[static_cast<size_t>(c) * 2 * experts + t];
+    fP[t] = t < experts ? tot / static_cast<float>(rows * k) : tot / static_cast<float>(rows);
+  }
+  __syncthreads();
+  if (blockIdx.x == 0 && t == 0) {
+    double aux = 0.0;
+    for (int e = 0; e < experts; ++e) aux += static_cast<double>(fP[e]) * fP[experts + e];
+    loss_sum[0] += loss_seed * static_cast<double>(weight) * experts * aux;
+  }
+  const int r = blockIdx.x * kAuxThreads + t;
+  if (r >= rows) return;
+  float p[kMaxExperts], fr[kMaxExperts];
+  float mx = -INFINITY, den = 0.f, fp = 0.f;
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    p[e] = e < experts ? logits[static_cast<size_t>(r) * ld + e] : -INFINITY;
+    fr[e] = e < experts ? fP[e] : 0.f;
+    mx = fmaxf(mx, p[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    p[e] = e < experts ? expf(p[e] - mx) : 0.f;
+    den += p[e];
+  }
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e) {
+    p[e] /= den;
+    fp += fr[e] * p[e];
+  }
+  const float scale = grad_scale * weight * static_cast<float>(experts) / static_cast<float>(rows);
+  __nv_bfloat16* row = dlogits + static_cast<size_t>(r) * ldd;
+#pragma unroll
+  for (int e = 0; e < kMaxExperts; ++e)
+    if (e < experts) row[e] = f2bf(bf2f(row[e]) + scale * p[e] * (fr[e] - fp));
+}
+
 }  // namespace sj
 
 using namespace sj;
+
+extern "C" int sj_route_capacity(int32_t* ids, int rows, int k, int experts, int capacity, void* stream) {
+  if (rows <= 0 || k <= 0 || experts <= 0 || experts > kMaxExperts || capacity <= 0)
+    return fail(SJ_ERR_SHAPE, "sj_route_capacity: rows=%d k=%d experts=%d (<= %d) capacity=%d", rows, k, experts,
+                kMaxExperts, capacity);
+  if (!ids) return fail(SJ_ERR_ARGUMENT, "sj_route_capacity: null ids");
+  launch(route_capacity_kernel, 1, kPackThreads, 0, as_stream(stream), ids, rows, k, experts, capacity);
+  SJ_LAUNCH_CHECK("route_capacity");
+  return SJ_OK;
+}
+
+extern "C" size_t sj_moe_aux_workspace(int rows, int experts) {
+  if (rows <= 0 || experts <= 0) return 0;
+  return static_cast<size_t>((rows + kAuxThreads - 1) / kAuxThreads) * 2 * experts;
+}
+
+extern "C" int sj_moe_aux(const float* logits, int ld, int rows, int experts, int k, float weight, double loss_seed,
+                          double* loss_sum, void* dlogits, int ldd, float grad_scale, float* workspace,
+                          void* stream) {
+  if (rows <= 0 || experts <= 0 || experts > kMaxExperts || k <= 0 || k > experts || ld < experts || ldd < experts)
+    return fail(SJ_ERR_SHAPE, "sj_moe_aux: rows=%d experts=%d k=%d", rows, experts, k);
+  if (!logits || !loss_sum || !dlogits || !workspace) return fail(SJ_ERR_ARGUMENT, "sj_moe_aux: null pointer");
+  const int ctas = (rows + kAuxThreads - 1) / kAuxThreads;
+  launch(moe_aux_stats_kernel, ctas, kAuxThreads, 0, as_stream(stream), logits, ld, rows, experts, k, workspace);
+  SJ_LAUNCH_CHECK("moe_aux_stats");
+  launch(moe_aux_grad_kernel, ctas, kAuxThreads, 0, as_stream(stream), logits, ld, rows, experts, k, ctas,
+         static_cast<const float*>(workspace), weight, loss_seed, loss_sum, static_cast<__nv_bfloat16*>(dlogits), ldd,
+         grad_scale);
+  SJ_LAUNCH_CHECK("moe_aux_grad");
+  return SJ_OK;
+}
 
 extern "C" int sj_moe_capacity(int rows, int k, int experts) {
   if (rows <= 0 || k <= 0 || experts <= 0) return 0;

@@ -66,6 +66,11 @@ class TrainConfig:
     values: int = 0
     # loop settings of the train CLI (TrainConfig::checkpoint_every / log_every /
     # gradient_diagnostics_every, crates/sejong-core/src/lib.rs:308-362); the step itself ignores them
+    # MoE additions the reference lacks (opt-in; 0 keeps its semantics): the capacity factor of each
+    # expert (capacity = ceil(factor * rows * top_k / experts), sj_route_capacity) and the weight of
+    # the load-balancing loss (sj_moe_aux)
+    moe_capacity_factor: float = 0.0
+    moe_aux_loss_weight: float = 0.0
     # observations per optimizer step (TrainConfig::accumulation): each observation's loss and
     # gradient enter with weight 1 / accumulation (crates/sejong-train/src/lib.rs:387-415)
     accumulation: int = 1
@@ -117,6 +122,8 @@ class _StageRun:
         self.partials = e(_lib.load().sj_rmsnorm_workspace(n, d), dt=f32)
         self.moe = stage.experts is not None
         self.ep = ep if self.moe else None
+        if self.moe:  # the load-balancing loss's per-256-row partials (sj_moe_aux)
+            self.aux_ws = e(max(1, _lib.load().sj_moe_aux_workspace(n, stage.experts.count)), dt=f32)
         if self.ep is not None:
             # expert-parallel MoE: this rank routes its own rows and runs its experts on every rank's
             # rows routed to them; the packed A / expert output of each layer, d_out and dA live in the
@@ -270,7 +277,7 @@ class ByteTrainer:
             self._init_vjp(train.parameter_vjp)
 
     # kernels each entry point launches (zero fills are kernels too)
-    KERNELS = {"sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_rmsnorm_bwd_ex": 2, "sj_attn_gqa_fwd": 1,
+    KERNELS = {"sj_moe_aux": 2, "sj_gemm": 1, "sj_rmsnorm_fwd": 1, "sj_rmsnorm_bwd": 2, "sj_rmsnorm_bwd_ex": 2, "sj_attn_gqa_fwd": 1,
                "sj_attn_gqa_bwd": 3,
                "sj_zero": 1, "sj_param_basis": 5, "sj_param_prepare": 3}
 
@@ -506,6 +513,7 @@ class ByteTrainer:
         ep = router_pad(E)  # router columns (and logits) padded to 8; the padding is zero and ignored
         self._gemm(_ptr(a["z2"]), d, 0, self.wb_ptr(f"{p}.router"), ep, 0, _ptr(a["logits"]), ep, SJ_F32, n, ep, d)
         self._call("sj_route_topk", _ptr(a["logits"]), ep, n, E, k, _ptr(a["ids"]), _ptr(a["gates"]), self.stream)
+        self._route_capacity(a, n, k, E)
         self._call("sj_route_pack", _ptr(a["ids"]), n, E, k, gp, _ptr(a["pos"]), _ptr(a["row_slot"]), cap, self.stream)
         self._call("sj_moe_dispatch", _ptr(a["z2"]), d, _ptr(a["row_slot"]), cap, k, d, _ptr(a["a"]), self.stream)
         self._gemm_grouped(_ptr(a["a"]), d, 0, self.wb_ptr(f"{p}.experts.0.gate_up"), 2 * fe, 0, _ptr(a["gu"]), 2 * fe,
@@ -539,10 +547,28 @@ class ByteTrainer:
         ep = router_pad(E)
         self._call("sj_route_topk_bwd", _ptr(a["logits"]), ep, _ptr(a["ids"]), _ptr(a["gates"]), _ptr(run.d_gates),
                    _ptr(run.dlogits), ep, n, E, k, self.stream)
+        self._moe_aux(a, run, n, k, E)
         self._gemm(_ptr(run.dlogits), ep, 0, self.wb_ptr(f"{p}.router"), ep, 1, _ptr(run.dz), d, SJ_F32, n, d, ep,
                    EPI_ACCUM)
         self._gemm(_ptr(a["z2"]), d, 1, _ptr(run.dlogits), ep, 0, self.g_ptr(f"{p}.router"), ep, SJ_F32, d, ep, n,
                    EPI_ACCUM)
+
+    def _route_capacity(self, a, n, k, E):
+        """The expert capacity (an addition to the reference): slots beyond it leave their expert."""
+        cf = float(self.tc.moe_capacity_factor)
+        if cf > 0:
+            self._call("sj_route_capacity", _ptr(a["ids"]), n, k, E, max(1, math.ceil(cf * n * k / E)), self.stream)
+
+    def _moe_aux(self, a, run, n, k, E):
+        """The load-balancing loss (an addition to the reference) of this rank's rows: its value joins
+        the loss sum (as the mean over the ranks and observations), its gradient the router's."""
+        w = float(self.tc.moe_aux_loss_weight)
+        if w > 0:
+            acc = float(max(1, self.tc.accumulation))
+            erp = router_pad(E)
+            self._call("sj_moe_aux", _ptr(a["logits"]), erp, n, E, k, w, 1.0 / (self.world * acc),
+                       _ptr(self.loss_sum), _ptr(run.dlogits), erp, float(self.tc.loss_scale) / (self.world * acc),
+                       _ptr(run.aux_ws), self.stream)
 
     def _ep_barrier(self, ep):
         self._call("sj_ep_barrier", ep.rank, ep.world, ep.peers, ep.offset("flags"), _ptr(ep.epoch), ep.timeout_ms,
@@ -561,6 +587,7 @@ class ByteTrainer:
         erp = router_pad(E)
         self._gemm(_ptr(a["z2"]), d, 0, self.wb_ptr(f"{p}.router"), erp, 0, _ptr(a["logits"]), erp, SJ_F32, n, erp, d)
         self._call("sj_route_topk", _ptr(a["logits"]), erp, n, E, k, ids, _ptr(a["gates"]), self.stream)
+        self._route_capacity(a, n, k, E)
         self._call("sj_ep_route_pack", ids, n, E, k, ep.rank, ep.world, ep.peers, ep.offset(f"{p}.counts"),
                    ep.offset("flags"), _ptr(ep.epoch), gp, pos, cap, ep.timeout_ms, self.stream)
         self._call("sj_ep_dispatch", _ptr(a["z2"]), d, ids, pos, n, k, d, E, ep.rank, ep.world, ep.peers,
@@ -605,6 +632,7 @@ class ByteTrainer:
         erp = router_pad(E)
         self._call("sj_route_topk_bwd", _ptr(a["logits"]), erp, ids, _ptr(a["gates"]), _ptr(run.d_gates),
                    _ptr(run.dlogits), erp, n, E, k, self.stream)
+        self._moe_aux(a, run, n, k, E)
         self._gemm(_ptr(run.dlogits), erp, 0, self.wb_ptr(f"{p}.router"), erp, 1, _ptr(run.dz), d, SJ_F32, n, d, erp,
                    EPI_ACCUM)
         self._gemm(_ptr(a["z2"]), d, 1, _ptr(run.dlogits), erp, 0, self.g_ptr(f"{p}.router"), erp, SJ_F32, d, erp, n,

@@ -206,3 +206,43 @@ def test_grouped_gemm_at_c5_shapes():
         assert float((gu[sample].float() - ref).norm() / ref.norm()) < 2e-2, x
         refo = h[sample].float() @ wd[x * f:(x + 1) * f].float()
         assert float((out[sample].float() - refo).norm() / refo.norm()) < 2e-2, x
+
+
+def test_capacity_and_aux_kernels_match_the_restatement():
+    """sj_route_capacity drops exactly the slots of oracle.model.apply_capacity; sj_moe_aux adds the
+    restated loss to the loss sum and its gradient (closed form) to the router gradient."""
+    import math
+
+    from oracle import model as om
+    from oracle import ops as oops
+    rows, k, E, w = 4096, 2, 8, 0.01
+    gen = torch.Generator().manual_seed(5)
+    logits = (0.2 * torch.randn(rows, E, generator=gen)).float()
+    ld = 8
+    dl = logits.cuda().contiguous()
+    ids = torch.empty(rows, k, dtype=torch.int32, device="cuda")
+    gates = torch.empty(rows, k, dtype=torch.float32, device="cuda")
+    call("sj_route_topk", dl.data_ptr(), ld, rows, E, k, ids.data_ptr(), gates.data_ptr(), st())
+    cap = (rows * k) // E - 200   # below the balanced load: some experts must drop slots
+    call("sj_route_capacity", ids.data_ptr(), rows, k, E, cap, st())
+    torch.cuda.synchronize()
+    _, ids_ref = oops.route_topk(logits.double(), k)
+    want = om.apply_capacity(ids_ref, E, cap)
+    got = ids.cpu().long()
+    assert torch.equal(got, want)
+    assert (got == -1).sum() > 0
+    # aux: loss and gradient increments
+    dlog = (0.01 * torch.randn(rows, ld, generator=gen)).to(torch.bfloat16).cuda()
+    before = dlog.float().cpu()
+    loss = torch.zeros(1, dtype=torch.float64, device="cuda")
+    ws = torch.empty(lib().sj_moe_aux_workspace(rows, E), device="cuda")
+    call("sj_moe_aux", dl.data_ptr(), ld, rows, E, k, w, 0.5, loss.data_ptr(), dlog.data_ptr(), ld, 2.0, ws.data_ptr(),
+         st())
+    torch.cuda.synchronize()
+    lg = logits.double().clone().requires_grad_(True)
+    ref = om.aux_loss(lg, ids_ref, E, w)
+    ref.backward()
+    assert abs(float(loss[0]) - 0.5 * float(ref.detach())) < 1e-6 * float(ref.detach())
+    inc = dlog.float().cpu() - before
+    want_inc = 2.0 * lg.grad.float()
+    assert float((inc[:, :E] - want_inc).abs().max()) < 1e-2 * float(want_inc.abs().max()) + 2e-5

@@ -193,3 +193,49 @@ def test_step_parity_c5_architecture_reduced_batch():
     print("C5 worst gradients", sorted(worst.items(), key=lambda kv: -kv[1])[:5])
     bad = {n: v for n, v in worst.items() if v > GRAD_TOL}
     assert not bad, f"gradients beyond {GRAD_TOL}: {bad}"
+
+
+@pytest.mark.parametrize("cf,aux", [(1.0, 0.0), (0.0, 0.01), (1.0, 0.01)])
+def test_step_parity_moe_capacity_and_aux_loss(cf, aux):
+    """The MoE additions (capacity factor 1.0, load-balancing weight 0.01; each alone and both) on a small
+    MoE hierarchy:
+    the step against the FP64 restatement, which routes with the GPU's decisions after the capacity
+    drop (oracle.model.ROUTE_OVERRIDE) and adds the load-balancing loss of every MoE layer with the shares
+    of the GPU's own choices (oracle.model.AUX_CHOICES; a near tie can flip a choice between bf16 and
+    FP64 arithmetic, and the loss's gradient p (f - <f, p>) is sensitive to one choice when the shares
+    are close to uniform)."""
+    from sejong_b200 import model as pm
+    from sejong_b200.model import initialize
+    from sejong_b200.train import ByteTrainer, TrainConfig
+    c, ids, tg = make_case("small_hierarchy", 2, 512, experts=pm.ExpertConfig(4, 2, 128))
+    params = initialize(c)
+    tr = ByteTrainer(c, TrainConfig(sequence=512, batch=2, warmup_steps=0, steps=100, moe_capacity_factor=cf,
+                                    moe_aux_loss_weight=aux), device=0, params=params)
+    tr.stage_batch(ids, tg)
+    tr.forward_backward()
+    torch.cuda.synchronize()
+    assert tr.device_error() == 0
+    from oracle.ops import route_topk
+    run = tr.runs["global"]
+    E = c.experts.count
+    override = {f"layers.{i}": L["ids"].cpu().long() for i, L in enumerate(run.layers)}
+    # the shares of the load-balancing loss from the GPU's own (pre-drop) choices on its f32 logits
+    choices = {f"layers.{i}": route_topk(L["logits"][:, :E].double().cpu(), c.experts.top_k)[1]
+               for i, L in enumerate(run.layers)}
+    dropped = sum(int((v == -1).sum()) for v in override.values())
+    loss, grads = tr.loss(), tr.gradients()
+    tr.close()
+    oc = oracle_config(c)
+    oc.moe_capacity_factor, oc.moe_aux_weight = cf, aux
+    omodel.ROUTE_OVERRIDE, omodel.AUX_CHOICES = override, choices
+    try:
+        ref_loss, ref_grads = omodel.loss_and_grads(params, oc, ids, tg, 512, cast="bf16")
+    finally:
+        omodel.ROUTE_OVERRIDE = omodel.AUX_CHOICES = None
+    worst = {n: rel(grads[n], g) for n, g in ref_grads.items() if np.any(g != 0)}
+    routers = {n: (round(worst[n], 4), float(np.linalg.norm(ref_grads[n]))) for n in ref_grads if n.endswith("router")}
+    print("cf", cf, "aux", aux, "dropped slots", dropped, "loss", loss, ref_loss, "routers", routers)
+    assert (dropped > 0) == (cf > 0)
+    assert abs(loss - ref_loss) < LOSS_TOL
+    bad = {n: v for n, v in worst.items() if v > GRAD_TOL}
+    assert not bad, f"gradients beyond {GRAD_TOL}: {bad}"
