@@ -643,7 +643,16 @@ class ByteTrainer:
             self._block_fwd(run, i)
 
     def _stage_bwd(self, run):
+        for _ in self._stage_bwd_gen(run):
+            pass
+
+    def _stage_bwd_gen(self, run):
+        """The stage's blocks backward; yields "half" once the upper half of the blocks is done (their
+        weight gradients are final: a gradient bucket of the overlapped exchange)."""
+        half = run.stage.layers // 2
         for i in reversed(range(run.stage.layers)):
+            if i == half - 1 and half > 0:
+                yield "half"
             if run.checkpoint and i < run.stage.layers - 1:
                 # Op::Checkpoint's backward (graph.rs:756-799): the block's forward again, from its saved
                 # input x[i], into the shared activation buffers (it rewrites x[i+1] with the values it
@@ -717,6 +726,12 @@ class ByteTrainer:
         return top, top_width
 
     def _backward(self, top, top_width):
+        for _ in self._backward_gen(top, top_width):
+            pass
+
+    def _backward_gen(self, top, top_width):
+        """The backward pass; yields a tag where a range of the flat gradient has become final (the
+        gradient buckets of the overlapped data-parallel exchange, `grad_buckets`)."""
         c, h = self.c, self.c.hierarchy
         n, b = self.rows, self.tc.batch
         if self.values:
@@ -736,7 +751,8 @@ class ByteTrainer:
             run = self.runs["global"]
             self._norm_bwd(top, "final_norm", self.invF, self.dhead, run.dx, run.dxb, self.top_partials, n, c.width,
                            accumulate=False)
-            self._stage_bwd(run)
+            for tag in self._stage_bwd_gen(run):
+                yield f"global_{tag}"
             self._call("sj_embedding_bwd", _ptr(run.dx), _ptr(self.ids), self.g_ptr(emb), n, c.width, vocab,
                  self.stream)
             return
@@ -752,6 +768,7 @@ class ByteTrainer:
         self._norm_bwd(dec.x[-1], "decoder_norm", self.invD, dec.dz, dec.dx, dec.dxb, dec.partials, n, dd,
                        accumulate=False)
         self._stage_bwd(dec)
+        yield "decoder"
         # decoder input = encoder_to_decoder(zE) + broadcast(global_to_decoder(zG), bos)
         self._gemm(_ptr(self.zE), de, 1, _ptr(dec.dxb), dd, 0, self.g_ptr("encoder_to_decoder"), dd, SJ_F32, de, dd,
                    n, EPI_ACCUM)
@@ -768,7 +785,9 @@ class ByteTrainer:
                    dd)
         self._norm_bwd(glob.x[-1], "global_norm", self.invG, glob.dz, glob.dx, glob.dxb, glob.partials, np_, dg,
                        accumulate=False)
-        self._stage_bwd(glob)
+        for tag in self._stage_bwd_gen(glob):
+            yield f"global_{tag}"
+        yield "global"
         # encoder_to_global, patch pool
         self._gemm(_ptr(self.pooled), de, 1, _ptr(glob.dxb), dg, 0, self.g_ptr("encoder_to_global"), dg, SJ_F32, de,
                    dg, np_, EPI_ACCUM)
@@ -791,12 +810,20 @@ class ByteTrainer:
     def _local_forward_backward(self, first=True):
         """Loss and gradients of the staged batch; `first` = False adds them to those of the previous
         observations of the same step (gradient accumulation) instead of starting from zero."""
+        for _ in self._local_forward_backward_gen(first):
+            pass
+
+    def _local_forward_backward_gen(self, first=True):
+        """_local_forward_backward, yielding the tags of _backward_gen (the stream may change between
+        phases: each phase reads the current stream)."""
         self.stream = torch.cuda.current_stream(self.dev).cuda_stream
         if first:
             self._zero(self.g)
             self._zero(self.loss_sum)
         top, width = self._forward()
-        self._backward(top, width)
+        for tag in self._backward_gen(top, width):
+            yield tag
+            self.stream = torch.cuda.current_stream(self.dev).cuda_stream
         sb = self.layout.shared_begin
         if sb:  # sum of squares of this rank's experts' gradients, summed over the ranks by the exchange
             self._call("sj_grad_sumsq", _ptr(self.g), sb, _ptr(self.partials, self.n_shared_partials), self.stream)
@@ -811,12 +838,44 @@ class ByteTrainer:
             else:
                 distributed.exchange(self.g, self.loss_sum, self.pg)
 
+    # ------------------------------------------------------------------ overlapped data-parallel exchange
+    def overlapped_exchange(self):
+        """Whether the gradient exchange runs in buckets that overlap the backward pass: data parallel,
+        without expert parallelism (whose exchange covers only the replicated range) and without the
+        NativeValue head (whose native embedding sits among the first-final matrices)."""
+        return self.world > 1 and self.layout.shared_begin == 0 and not self.values
+
+    def grad_buckets(self):
+        """The flat gradient's buckets (`gradient_buckets`)."""
+        return gradient_buckets(self.layout, self.c)
+
+    def _bucket_reduce(self, tag, works):
+        """Start the SUM all-reduce of every bucket that `tag` completes (NCCL's stream, after the work
+        enqueued so far on this one); `works` collects the handles."""
+        for t, b, e in self._buckets:
+            if t == tag:
+                works.append(torch.distributed.all_reduce(self.g[b:e], group=self.pg, async_op=True))
+
+    def _finish_exchange(self, works):
+        self._bucket_reduce(None, works)
+        works.append(torch.distributed.all_reduce(self.loss_sum, group=self.pg, async_op=True))
+        for w in works:
+            w.wait()  # this stream waits for NCCL's (the host does not block)
+
     def forward_backward(self, first=True, last=True):
         """Loss (into self.loss_sum) and gradients (into self.g) for the staged batch; with gradient
-        accumulation, call once per observation (first / last mark the step's first and last)."""
-        self._local_forward_backward(first)
-        if last:
-            self._exchange()
+        accumulation, call once per observation (first / last mark the step's first and last).
+        With data parallelism the exchange overlaps the backward pass (`grad_buckets`)."""
+        if not (last and self.overlapped_exchange()):
+            self._local_forward_backward(first)
+            if last:
+                self._exchange()
+            return
+        self._buckets = self.grad_buckets()
+        works = []
+        for tag in self._local_forward_backward_gen(first):
+            self._bucket_reduce(tag, works)
+        self._finish_exchange(works)
 
     def optimizer_step(self):
         """Adam::update (crates/sejong-train/src/lib.rs:199-238) or the dense SGD step, in two launches."""
@@ -919,8 +978,10 @@ class ByteTrainer:
         """Capture the step as CUDA graphs (replayed by `replay`).
 
         One graph (forward + backward + update) on a single GPU.  With data parallelism the
-        forward/backward and the update are two graphs and the NCCL exchange runs between them
-        on the same stream, so no collective is captured."""
+        forward / backward is one graph per phase between gradient buckets and the update one more;
+        the NCCL all-reduces of the buckets run between the replays, on NCCL's stream, overlapping the
+        later phases (expert parallelism and the NativeValue head: one forward / backward graph, the
+        exchange, the update), so no collective is captured."""
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         graphs = []
@@ -930,6 +991,25 @@ class ByteTrainer:
                 with torch.cuda.graph(g, stream=s):
                     self.step()
                 graphs.append(g)
+            elif self.overlapped_exchange():
+                # one graph per phase of the forward / backward, split where gradient buckets become
+                # final; replay starts each bucket's all-reduce between the phases (no collective is
+                # captured), then the update graph
+                self._buckets = self.grad_buckets()
+                gen = self._local_forward_backward_gen()
+                done = False
+                while not done:
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=s):
+                        try:
+                            tag = next(gen)
+                        except StopIteration:
+                            tag, done = None, True
+                    graphs.append((g, tag))
+                g2 = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g2, stream=s):
+                    self.optimizer_step()
+                graphs.append((g2, "update"))
             else:
                 g1, g2 = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g1, stream=s):
@@ -944,6 +1024,14 @@ class ByteTrainer:
     def replay(self):
         if len(self.graph) == 1:
             self.graph[0].replay()
+        elif isinstance(self.graph[0], tuple):
+            works = []
+            for g, tag in self.graph[:-1]:
+                g.replay()
+                if tag is not None:
+                    self._bucket_reduce(tag, works)
+            self._finish_exchange(works)
+            self.graph[-1][0].replay()
         else:
             self.graph[0].replay()
             self._exchange()
@@ -1035,6 +1123,30 @@ class ByteTrainer:
                 total += 2 * n * a * r * (2 if g.new_basis else 1) + 2 * n * k * r
                 total += 2 * (r + k) * n * width + 2 * a * active * r
         return total
+
+
+def gradient_buckets(layout, c):
+    """The flat gradient's buckets for the overlapped data-parallel exchange, as (tag, begin, end): the
+    range becomes final when the backward yields `tag` (tag None: at its end).  The rank > 1 tensors lie
+    in the forward order of the model, so the backward finishes them from the end: the decoder blocks
+    and heads first, then the upper and the lower half of the global blocks, then the rest together
+    with the norm vectors."""
+    nd = layout.n_decay
+    ents = list(layout.entries.values())
+
+    def first(prefix):
+        return min(e.offset for e in ents if e.name.startswith(prefix) and e.decay)
+
+    half = global_stage(c).layers // 2
+    g0 = first("layers.0.")
+    gh = first(f"layers.{half}.") if half > 0 else g0
+    if c.hierarchy is not None:
+        dec = first("decoder.")
+        out = [("decoder", dec, nd), ("global_half", gh, dec), ("global", g0, gh)]
+        out += [(None, 0, g0), (None, nd, layout.total)]
+    else:
+        out = [("global_half", gh, nd), (None, 0, gh), (None, nd, layout.total)]
+    return [b for b in out if b[2] > b[1]]
 
 
 def synthetic_corpus_tokens(seed, length, s=1.1):

@@ -101,3 +101,34 @@ def test_dead_rank_surfaces_as_error_not_hang():
             pass
         r0 = np.load(os.path.join(d, "rank0.npz"))
     assert str(r0["status"]).startswith("error"), str(r0["status"])
+
+
+@pytest.mark.parametrize("name", ["config_c3", "config_c1", "small_hierarchy"])
+def test_gradient_buckets_partition_the_flat_gradient(name):
+    """The overlapped exchange's buckets cover every element of the flat gradient exactly once, never
+    split a parameter, and list a stage's matrices only where the backward has finished them."""
+    from sejong_b200 import model as pm
+    from sejong_b200.train import gradient_buckets
+    c = getattr(pm, name)()
+    lay = pm.FlatLayout(c)
+    buckets = gradient_buckets(lay, c)
+    spans = sorted((b, e) for _, b, e in buckets)
+    assert spans[0][0] == 0 and spans[-1][1] == lay.total
+    assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    tags = {}
+    for e in lay.entries.values():
+        owner = [t for t, b, en in buckets if b <= e.offset < en]
+        assert len(owner) == 1
+        t = owner[0]
+        b, en = next((b, en) for tt, b, en in buckets if tt == t and b <= e.offset < en)
+        assert e.offset + e.size <= en, e.name
+        tags[e.name] = t
+    half = pm.global_stage(c).layers // 2
+    for name_, t in tags.items():
+        if name_.startswith("decoder.") and lay[name_].decay:
+            assert t == "decoder"
+        if name_.startswith("layers.") and lay[name_].decay:
+            layer = int(name_.split(".")[1])
+            assert t == ("global_half" if layer >= half else ("global" if c.hierarchy else None))
+        if not lay[name_].decay:
+            assert t is None  # norm vectors: at the end
