@@ -53,6 +53,7 @@ enum {
   SJ_DEV_GEMM_EPILOGUE_WAIT = 103,
   SJ_DEV_GEMM_DRAIN_WAIT = 104,
   SJ_DEV_ATTN_WAIT = 105,
+  SJ_DEV_SMEM_ALIGN = 106,  /* a kernel's dynamic shared memory lacked the alignment its layout needs */
   SJ_DEV_BAD_INDEX = 110,
   SJ_DEV_EP_WAIT = 111,     /* an expert-parallel barrier gave up waiting for a peer */
   SJ_DEV_EP_CAPACITY = 112  /* an expert-parallel receive buffer would overflow */

@@ -116,6 +116,39 @@ SJ_DEVICE float2 rope_cs(const float2* tab, float log_theta, int pos, int i) {
   return make_float2(c, s);
 }
 
+// The (cos, sin) pairs c0/2 .. c0/2 + 7 of position pos.  With a table all eight loads are issued
+// together (before the TMEM reads they overlap): taken one by one, each behind the previous, they
+// were most of the time of a step.
+SJ_DEVICE void rope_row8(float2 (&cs)[8], const float2* tab, float log_theta, int pos, int c0) {
+  if (tab != nullptr) {
+    const float2* src = tab + static_cast<size_t>(pos) * 32 + (c0 >> 1);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cs[i] = src[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cs[i] = rope_cs(nullptr, log_theta, pos, (c0 >> 1) + i);
+  }
+}
+
+// 16 f32 values of one row (columns c0 .. c0+15 of a head) -> bf16, inverse-rotated by `cs` when `rope`.
+SJ_DEVICE void store_row16(__nv_bfloat16* dst, const uint32_t (&v)[16], bool rope, const float2 (&cs)[8]) {
+  uint32_t w[8];
+#pragma unroll
+  for (int c = 0; c < 16; c += 2) {
+    float a = __uint_as_float(v[c]), b = __uint_as_float(v[c + 1]);
+    if (rope) {
+      const float2 e = cs[c >> 1];
+      const float na = a * e.x + b * e.y, nb = -a * e.y + b * e.x;  // inverse rotation
+      a = na;
+      b = nb;
+    }
+    w[c >> 1] = pack_bf16x2(a, b);
+  }
+  uint4* out = reinterpret_cast<uint4*>(dst);
+  out[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  out[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 // 1-D bulk copy global -> shared completing on an mbarrier (16-byte aligned, size a multiple of 16).
 SJ_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -371,26 +404,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       } else if (kpos < p.t) {
         const bool rope = p.rope_tab != nullptr || p.rope_log_theta > 0.f;
-        uint32_t w[8];
-#pragma unroll
-        for (int c = 0; c < 16; c += 2) {
-          float a = __uint_as_float(vk[c]), b = __uint_as_float(vk[c + 1]);
-          if (rope) {
-            const float2 cs = rope_cs(p.rope_tab, p.rope_log_theta, kpos, (c0 + c) >> 1);
-            const float na = a * cs.x + b * cs.y, nb = -a * cs.y + b * cs.x;  // inverse rotation
-            a = na;
-            b = nb;
-          }
-          w[c >> 1] = pack_bf16x2(a, b);
-        }
-        uint4* out = reinterpret_cast<uint4*>(p.dk + row * p.lddk + pend_it.kvh * kBD + c0);
-        out[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        out[1] = make_uint4(w[4], w[5], w[6], w[7]);
-#pragma unroll
-        for (int c = 0; c < 16; c += 2) w[c >> 1] = pack_bf16x2(__uint_as_float(vv[c]), __uint_as_float(vv[c + 1]));
-        out = reinterpret_cast<uint4*>(p.dv + row * p.lddv + pend_it.kvh * kBD + c0);
-        out[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        out[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        float2 cs[8];
+        if (rope) rope_row8(cs, p.rope_tab, p.rope_log_theta, kpos, c0);
+        store_row16(p.dk + row * p.lddk + pend_it.kvh * kBD + c0, vk, rope, cs);
+        store_row16(p.dv + row * p.lddv + pend_it.kvh * kBD + c0, vv, false, cs);
       }
     };
     int n = 0, g = 0;
@@ -498,10 +515,538 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------- banded backward
+// A sliding window of at most 128 keys with one query head per kv head (the local stages of the
+// hierarchical model): query tile q sees only key tiles q-1 and q, key tile k only query tiles k and
+// k+1.  Each CTA takes a contiguous range of the key tiles of all (batch, head) pairs, flattened as
+// u = (b * hk + h) * nkt + kt, and walks it with the steps
+//   halo (kt-1, kt)  only at a range start inside a sequence: the part of dQ of query tile kt that
+//                    the previous range's key tile contributes (recomputed here, nothing exchanged);
+//   diag (kt, kt)    completes dQ of query tile kt;
+//   off  (kt, kt+1)  completes dK / dV of key tile kt, and starts dQ of query tile kt+1 when that tile
+//                    is in the range (else the next range's halo makes it).
+// dQ accumulates in TMEM over two consecutive steps (two buffers by query-tile parity), dK / dV over
+// two, and the CTA that completes a tile writes it once in bf16 (inverse RoPE on dQ and dK): no f32
+// accumulator, no zero fill, no finish pass.  Each K / V and Q / dO tile is loaded once per range.
+// Roles, shared-memory layout and TMEM columns are those of attn_bwd_tc_kernel.
+enum : int {
+  kStKv = 1, kStKvFirst = 2, kStKvLast = 4, kStDq = 8, kStDqFirst = 16, kStDqLast = 32,
+  kStNewK = 64, kStLastK = 128, kStNewQ = 256, kStLastQ = 512
+};
+struct BandStep {
+  int bh, kt, qt, flags;
+};
+struct BandCursor {
+  int u, u0, u1, phase;  // phase 0: halo (when due), 1: diag, 2: off
+};
+// Advance to the next step of the range; false past its end.  Every role walks the same sequence.
+SJ_DEVICE bool band_next(int nkt, BandCursor& c, BandStep& s) {
+  while (c.u < c.u1) {
+    const int kt = c.u % nkt, bh = c.u / nkt;
+    if (c.phase == 0) {
+      c.phase = 1;
+      if (kt > 0 && c.u == c.u0) {
+        s = {bh, kt - 1, kt, kStDq | kStDqFirst | kStNewK | kStLastK | kStNewQ};
+        return true;
+      }
+    } else if (c.phase == 1) {
+      const bool off = kt + 1 < nkt;
+      c.phase = 2;
+      s = {bh, kt, kt,
+           kStKv | kStKvFirst | (off ? 0 : kStKvLast) | kStDq | (kt == 0 ? kStDqFirst : 0) | kStDqLast | kStNewK |
+               (off ? 0 : kStLastK) | (kt == 0 ? kStNewQ : 0) | kStLastQ};
+      return true;
+    } else {
+      c.phase = 0;
+      ++c.u;
+      if (kt + 1 < nkt) {
+        const bool own = c.u < c.u1;  // the range goes on with key tile kt+1, so query tile kt+1 is its own
+        s = {bh, kt, kt + 1, kStKv | kStKvLast | (own ? (kStDq | kStDqFirst) : kStLastQ) | kStLastK | kStNewQ};
+        return true;
+      }
+    }
+  }
+  return false;
+}
+
+struct BandParams {
+  int t, nkt, tiles, batch, hk, window;
+  float scale, scale_log2;
+  const float* lse_t;    // [hq][batch][tpad]: LSE * log2(e)
+  const float* delta_t;  // [hq][batch][tpad]: Delta
+  int tpad;
+  int rope;              // dq, dk leave rotated back by the table (map_rope)
+};
+
+// Banded kernel layout.  Eight elementwise warps (two per TMEM lane quarter) with about 200
+// registers each: a thread owns one key row of 64 query columns of S^T / dP^T, and 32 head columns
+// of a dQ / dK / dV row.  Each of those warps has a 4 KB shared-memory slab that takes, in turn, the
+// RoPE rows of a tile (32 positions x 32 floats, by TMA) and the warp's bf16 output slabs (32 rows x
+// 64 B each) that a TMA store writes out: a thread's row-wise loads and stores, 32 distinct lines per
+// instruction, were most of the kernel's time.
+constexpr int kBandEw = 8;
+constexpr int kBandThreads = 32 * (2 + kBandEw);
+constexpr int kBandSlab = 4096;
+constexpr int kBOffStage = kOffLd + kQdStages * 2 * kBT * 4;  // 1024-aligned (194 KB)
+constexpr int kBOffBar = kBOffStage + kBandEw * kBandSlab;
+constexpr int kBandLayout = kBOffBar + 256;
+constexpr int kSmemBand = 232448;  // the per-block maximum; what the layout leaves is alignment slack
+static_assert(kBOffStage % 1024 == 0, "slabs hold 128-byte-swizzled TMA boxes");
+static_assert(kBandLayout <= kSmemBand, "banded attention backward shared memory");
+
+SJ_DEVICE void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+SJ_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+SJ_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+SJ_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+SJ_DEVICE void bulk_wait_all_groups() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// 32 f32 values of a row -> 16 bf16 pairs, inverse-rotated by the row's (cos, sin) pairs when `rope`.
+SJ_DEVICE void rotate_pack32(uint32_t (&w)[16], const uint32_t (&v)[32], bool rope, const float (&cs)[32]) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float a = __uint_as_float(v[c]), b = __uint_as_float(v[c + 1]);
+    if (rope) {
+      const float co = cs[c], si = cs[c + 1];
+      const float na = a * co + b * si, nb = -a * si + b * co;  // inverse rotation
+      a = na;
+      b = nb;
+    }
+    w[c >> 1] = pack_bf16x2(a, b);
+  }
+}
+// Row `lane` (64 bytes) of a 32 x 64-byte SWIZZLE_64B slab: chunk j at lane*64 + ((j ^ ((lane >> 1) & 3)) * 16).
+SJ_DEVICE void stage_row64b(uint8_t* slab, int lane, const uint32_t (&w)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(slab + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+
+__global__ void __launch_bounds__(kBandThreads, 1)
+    attn_bwd_band_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                         const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
+                         const __grid_constant__ CUtensorMap map_dq, const __grid_constant__ CUtensorMap map_dk,
+                         const __grid_constant__ CUtensorMap map_dv, const __grid_constant__ CUtensorMap map_rope,
+                         const BandParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad + kBandLayout > kSmemBand) {  // uniform over the CTA, before any barrier or TMEM use
+    if (threadIdx.x == 0) record_error(SJ_DEV_SMEM_ALIGN);
+    pdl_wait();
+    return;
+  }
+  uint8_t* smem = smem_raw + pad;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBOffBar);
+  uint64_t* kv_full = bars;         // 2: K / V slots
+  uint64_t* kv_empty = bars + 2;    // 2
+  uint64_t* qd_full = bars + 4;     // 2: Q / dO (+ LSE, Delta) slots
+  uint64_t* qd_empty = bars + 6;    // 2
+  uint64_t* sp_full = bars + 8;     // S^T, dP^T in TMEM
+  uint64_t* sp_empty = bars + 9;    // the elementwise warps have them in registers
+  uint64_t* ps_full = bars + 10;    // P^T, dS^T in shared memory
+  uint64_t* ps_empty = bars + 11;   // their MMAs are done
+  uint64_t* dq_empty = bars + 12;   // 2: dQ buffer (query-tile parity) read out
+  uint64_t* acc_empty = bars + 14;  // dK / dV read out
+  uint64_t* drain = bars + 15;
+  uint64_t* rope_full = bars + 16;  // kBandEw: a warp's RoPE rows in its slab
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16 + kBandEw);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* ldbuf = reinterpret_cast<float*>(smem + kOffLd);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int u0 = static_cast<int>(static_cast<long long>(blockIdx.x) * p.tiles / gridDim.x);
+  const int u1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * p.tiles / gridDim.x);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+      mbar_init(&dq_empty[i], kBandEw);
+    }
+    mbar_init(sp_full, 1);
+    mbar_init(sp_empty, kBandEw);
+    mbar_init(ps_full, kBandEw);
+    mbar_init(ps_empty, 1);
+    mbar_init(acc_empty, kBandEw);
+    mbar_init(drain, 1);
+    for (int i = 0; i < kBandEw; ++i) mbar_init(&rope_full[i], 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_map(&map_q);
+    tma_prefetch_map(&map_k);
+    tma_prefetch_map(&map_v);
+    tma_prefetch_map(&map_do);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemColsB);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_wait();  // operands may come from the previous kernel
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (one thread)
+    if (lane == 0) {
+      BandCursor c{u0, u0, u1, 0};
+      BandStep s;
+      int nk = 0, nq = 0;
+      bool ok = true;
+      while (ok && band_next(p.nkt, c, s)) {
+        const int b = s.bh / p.hk, h = s.bh % p.hk;
+        const int row_base = b * p.t;
+        if (s.flags & kStNewK) {
+          const int slot = nk & 1;
+          ok = mbar_wait_sleep(&kv_empty[slot], ((nk >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&kv_full[slot], 2 * kTile);
+          tma_load_2d(smem + kOffKb + slot * kTile, &map_k, &kv_full[slot], h * kBD, row_base + s.kt * kBT);
+          tma_load_2d(smem + kOffVb + slot * kTile, &map_v, &kv_full[slot], h * kBD, row_base + s.kt * kBT);
+          ++nk;
+        }
+        if (s.flags & kStNewQ) {
+          const int slot = nq & 1;
+          ok = mbar_wait_sleep(&qd_empty[slot], ((nq >> 1) & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT);
+          if (!ok) break;
+          const int q0 = s.qt * kBT;
+          float* lsl = ldbuf + slot * 2 * kBT;
+          const size_t run = (static_cast<size_t>(h) * p.batch + b) * p.tpad + q0;
+          mbar_arrive_expect_tx(&qd_full[slot], 2 * kTile + 2 * kBT * 4);
+          tma_load_2d(smem + kOffQb + slot * kTile, &map_q, &qd_full[slot], h * kBD, row_base + q0);
+          tma_load_2d(smem + kOffDOb + slot * kTile, &map_do, &qd_full[slot], h * kBD, row_base + q0);
+          bulk_load(lsl, p.lse_t + run, kBT * 4, &qd_full[slot]);
+          bulk_load(lsl + kBT, p.delta_t + run, kBT * 4, &qd_full[slot]);
+          ++nq;
+        }
+      }
+      // copies still in flight must land before the CTA exits
+      for (int i = max(0, nk - 2); i < nk; ++i) mbar_wait_sleep(&kv_full[i & 1], (i >> 1) & 1, nullptr, SJ_DEV_ATTN_WAIT);
+      for (int i = max(0, nq - 2); i < nq; ++i) mbar_wait_sleep(&qd_full[i & 1], (i >> 1) & 1, nullptr, SJ_DEV_ATTN_WAIT);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (one thread)
+    if (lane == 0) {
+      constexpr uint32_t kIdS = umma_idesc_bf16(kBT, kBT, 0, 0);   // K-major A, K-major B
+      constexpr uint32_t kIdAcc = umma_idesc_bf16(kBT, kBD, 0, 1);  // K-major A, MN-major B
+      constexpr uint32_t kIdDq = umma_idesc_bf16(kBT, kBD, 1, 1);   // MN-major A, MN-major B
+      BandStep pend{};
+      int pend_g = -1, pend_ks = 0, pend_qs = 0;
+      int nkv = 0, dq_uses[2] = {0, 0};
+      bool ok = true;
+      // the second half of a step: dV, dK (accumulated over the key tile's steps) and dQ (over the
+      // query tile's) from its P^T / dS^T
+      auto issue_acc = [&]() -> bool {
+        const int f = pend.flags;
+        if (!mbar_wait(ps_full, pend_g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        if ((f & kStKvFirst) && !mbar_wait(acc_empty, (nkv & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+        if (f & kStKvFirst) ++nkv;
+        const int qb = pend.qt & 1;
+        if ((f & kStDqFirst) && !mbar_wait(&dq_empty[qb], (dq_uses[qb] & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT))
+          return false;
+        if (f & kStDqFirst) ++dq_uses[qb];
+        tc_fence_after();
+        const uint64_t d_pt = umma_desc(smem_u32(smem + kOffPt), 16, 1024);
+        const uint64_t d_dst = umma_desc(smem_u32(smem + kOffDSt), 16, 1024);
+        const uint64_t d_dst_mn = umma_desc(smem_u32(smem + kOffDSt), kTile, 1024);
+        const uint64_t d_q = umma_desc(smem_u32(smem + kOffQb + pend_qs * kTile), 8192, 1024);
+        const uint64_t d_do = umma_desc(smem_u32(smem + kOffDOb + pend_qs * kTile), 8192, 1024);
+        const uint64_t d_k = umma_desc(smem_u32(smem + kOffKb + pend_ks * kTile), 8192, 1024);
+#pragma unroll
+        for (int kk = 0; kk < kBT / 16; ++kk) {
+          const uint64_t kmaj = ((kk >> 2) * kTile + (kk & 3) * 32) >> 4;  // K-major step in a 128 x 128 tile
+          const uint64_t mn = (kk * 2048) >> 4;                              // MN-major step
+          if (f & kStKv) {
+            const uint32_t acc = ((f & kStKvFirst) && kk == 0) ? 0u : 1u;
+            umma_f16(tmem + kColDV, d_pt + kmaj, d_do + mn, kIdAcc, acc);
+            umma_f16(tmem + kColDK, d_dst + kmaj, d_q + mn, kIdAcc, acc);
+          }
+          if (f & kStDq)
+            umma_f16(tmem + kColDQ + qb * kBD, d_dst_mn + mn, d_k + mn, kIdDq, ((f & kStDqFirst) && kk == 0) ? 0u : 1u);
+        }
+        umma_commit(ps_empty);  // also: the step's dQ / dK / dV contributions are in TMEM
+        if (f & kStLastQ) umma_commit(&qd_empty[pend_qs]);
+        if (f & kStLastK) umma_commit(&kv_empty[pend_ks]);
+        pend_g = -1;
+        return true;
+      };
+      BandCursor c{u0, u0, u1, 0};
+      BandStep s;
+      int g = 0, nk = 0, nq = 0, ks = 0, qs = 0;
+      while (ok && band_next(p.nkt, c, s)) {
+        if (s.flags & kStNewK) {
+          ks = nk & 1;
+          if (!mbar_wait(&kv_full[ks], (nk >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
+          ++nk;
+        }
+        if (s.flags & kStNewQ) {
+          qs = nq & 1;
+          if (!mbar_wait(&qd_full[qs], (nq >> 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
+          ++nq;
+        }
+        if (!mbar_wait(sp_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) break;
+        tc_fence_after();
+        const uint64_t d_k = umma_desc(smem_u32(smem + kOffKb + ks * kTile), 16, 1024);
+        const uint64_t d_v = umma_desc(smem_u32(smem + kOffVb + ks * kTile), 16, 1024);
+        const uint64_t d_q = umma_desc(smem_u32(smem + kOffQb + qs * kTile), 16, 1024);
+        const uint64_t d_do = umma_desc(smem_u32(smem + kOffDOb + qs * kTile), 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < kBD / 16; ++kk) {
+          const uint64_t step = (kk * 32) >> 4;
+          umma_f16(tmem + kColSt, d_k + step, d_q + step, kIdS, kk > 0 ? 1u : 0u);
+          umma_f16(tmem + kColDPt, d_v + step, d_do + step, kIdS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(sp_full);
+        if (pend_g >= 0 && !issue_acc()) {
+          ok = false;
+          break;
+        }
+        pend = s;
+        pend_g = g;
+        pend_ks = ks;
+        pend_qs = qs;
+        ++g;
+      }
+      if (ok && pend_g >= 0) issue_acc();
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, SJ_DEV_ATTN_WAIT);
+    }
+  } else {
+    // ---------------------------------------------------------------- elementwise warps
+    // thread <-> TMEM lane r: a key row for P^T / dS^T (query columns [64 part, 64 part + 64)) and for
+    // dK / dV, a query row for dQ (head columns [32 part, 32 part + 32) of those three)
+    const int ew = warp - 2;
+    const int quarter = warp & 3;
+    const int part = ew >> 2;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const int hc = part * 32;  // head columns of dQ / dK / dV
+    uint8_t* slab = smem + kBOffStage + ew * kBandSlab;
+    BandStep pend{};
+    int pend_g = -1;
+    // RoPE rows of one tile (this warp's 32 positions, its 16 (cos, sin) pairs) in registers: the
+    // diagonal step's dQ and the off-diagonal step's dK, read out one after the other, share them
+    float cs[32];
+    int cs_tile = -1, cs_bh = -1;   // tile whose rows `cs` (or, while in flight, the slab) holds
+    int rope_loads = 0;             // loads issued into the slab (their barrier's phase count)
+    bool rope_pending = false;      // a load issued and not yet read into `cs`
+    // the rows a read-out of step `st` rotates with: its query tile (dQ) or key tile (dK)
+    auto rope_tile_of = [&](const BandStep& st) { return (st.flags & kStDqLast) ? st.qt : st.kt; };
+    // request the RoPE rows of the pending step's tile when `cs` holds another tile's: the slab must
+    // first be done with the stores that read it
+    auto request_rope = [&]() {
+      if (!p.rope || pend_g < 0 || !(pend.flags & (kStDqLast | kStKvLast))) return;
+      const int tile = rope_tile_of(pend);
+      if (tile == cs_tile && pend.bh == cs_bh) return;
+      if (lane == 0) {
+        bulk_wait_read_all();
+        mbar_arrive_expect_tx(&rope_full[ew], 32 * 32 * 4);
+        tma_load_2d(slab, &map_rope, &rope_full[ew], hc, tile * kBT + quarter * 32);
+      }
+      __syncwarp();
+      ++rope_loads;
+      rope_pending = true;
+      cs_tile = tile;
+      cs_bh = pend.bh;
+    };
+    // a completed step's finished tiles: dQ of its query tile and / or dK, dV of its key tile, staged
+    // in the slab and written by TMA (the 3-D maps clip rows past the sequence end)
+    auto read_out = [&]() -> bool {
+      const int b = pend.bh / p.hk, h = pend.bh % p.hk;
+      const bool dq_last = pend.flags & kStDqLast, kv_last = pend.flags & kStKvLast;
+      if (!dq_last && !kv_last) return true;
+      if (rope_pending) {
+        if (!mbar_wait(&rope_full[ew], (rope_loads - 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // 128-byte swizzled row `lane`
+          const float4 v = *reinterpret_cast<const float4*>(slab + lane * 128 + ((j ^ (lane & 7)) << 4));
+          cs[4 * j] = v.x;
+          cs[4 * j + 1] = v.y;
+          cs[4 * j + 2] = v.z;
+          cs[4 * j + 3] = v.w;
+        }
+        rope_pending = false;
+      } else if (lane == 0) {
+        bulk_wait_read_all();  // the slab's previous stores have read it
+      }
+      __syncwarp();
+      const int y = rope_tile_of(pend) * kBT + quarter * 32;
+      uint32_t w[16];
+      int used = 0;  // 2 KB halves of the slab holding staged rows
+      if (dq_last) {
+        const int qb = pend.qt & 1;
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + kColDQ + qb * kBD + hc, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&dq_empty[qb]);
+        rotate_pack32(w, v, p.rope != 0, cs);
+        stage_row64b(slab, lane, w);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) tma_store_3d(&map_dq, slab, h * kBD + hc, y, b);
+        used = 1;
+      }
+      if (kv_last) {
+        uint32_t vk[32], vv[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + kColDK + hc, vk);
+        tmem_ld_32x32b_x32(tmem + lane_off + kColDV + hc, vv);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty);
+        rotate_pack32(w, vk, p.rope != 0, cs);
+        stage_row64b(slab + used * 2048, lane, w);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) tma_store_3d(&map_dk, slab + used * 2048, h * kBD + hc, y, b);
+        if (used) {  // dQ and dK fill the slab: dV follows once both have been read
+          if (lane == 0) {
+            bulk_commit_group();
+            bulk_wait_read_all();
+          }
+          __syncwarp();
+          used = 0;
+        } else {
+          used = 1;
+        }
+        rotate_pack32(w, vv, false, cs);
+        stage_row64b(slab + used * 2048, lane, w);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) tma_store_3d(&map_dv, slab + used * 2048, h * kBD + hc, y, b);
+      }
+      if (lane == 0) bulk_commit_group();
+      __syncwarp();
+      return true;
+    };
+    BandCursor c{u0, u0, u1, 0};
+    BandStep s;
+    int g = 0, nq = 0, qs = 0;
+    uint32_t qpar = 0;
+    bool alive = true;
+    while (alive && band_next(p.nkt, c, s)) {
+      if (s.flags & kStNewQ) {
+        qs = nq & 1;
+        qpar = (nq >> 1) & 1;
+        ++nq;
+      }
+      request_rope();  // lands while this step computes; read out at its end
+      // LSE / Delta of the step's query tile (their bulk copies complete on qd_full), then S^T, dP^T
+      if (!mbar_wait(&qd_full[qs], qpar, abort_flag, SJ_DEV_ATTN_WAIT) ||
+          !mbar_wait(sp_full, g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+        alive = false;
+        break;
+      }
+      tc_fence_after();
+      const float* lsl = ldbuf + qs * 2 * kBT + part * 64;
+      const float* dls = lsl + kBT;
+      // visible queries of this key row among this thread's 64 columns: [lo, hi]
+      const int kpos = s.kt * kBT + r;
+      const int cbase = s.qt * kBT + part * 64;
+      const int lo = kpos - cbase;
+      const int hi = kpos < p.t ? min(kpos + p.window - 1, p.t - 1) - cbase : -1;
+      uint8_t* pt = smem + kOffPt + part * kTile;
+      uint8_t* dst = smem + kOffDSt + part * kTile;
+      // two halves of 32 columns: each read from TMEM, turned into P^T / dS^T, and (the first once
+      // the previous step's MMAs are done with the buffers) stored as four 16-byte chunks
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tmem + lane_off + kColSt + part * 64 + half * 32, sv);
+        tmem_ld_32x32b_x32(tmem + lane_off + kColDPt + part * 64 + half * 32, dv);
+        tmem_wait_ld();
+        if (half == 1) {  // S^T / dP^T are in registers: the next step's products may start
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(sp_empty);
+        }
+        uint32_t pw[16], dw[16];
+#pragma unroll
+        for (int c4 = 0; c4 < 32; c4 += 4) {
+          const int cc = half * 32 + c4;
+          const float4 l4 = *reinterpret_cast<const float4*>(lsl + cc);
+          const float4 d4 = *reinterpret_cast<const float4*>(dls + cc);
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dlv[4] = {d4.x, d4.y, d4.z, d4.w};
+          float pr[4], ds[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const bool valid = cc + e >= lo && cc + e <= hi;
+            pr[e] = ex2b(valid ? fmaf(__uint_as_float(sv[c4 + e]), p.scale_log2, -lv[e]) : -INFINITY);  // P^T
+            ds[e] = pr[e] * (__uint_as_float(dv[c4 + e]) - dlv[e]) * p.scale;                           // dS^T
+          }
+          pw[c4 >> 1] = pack_bf16x2(pr[0], pr[1]);
+          pw[(c4 >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
+          dw[c4 >> 1] = pack_bf16x2(ds[0], ds[1]);
+          dw[(c4 >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
+        }
+        if (half == 0) {  // P^T and dS^T overwrite the buffers once the previous step's MMAs have read them
+          if (!mbar_wait(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+            alive = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int off = r * 128 + (((half * 4 + j) ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pw[4 * j], pw[4 * j + 1], pw[4 * j + 2], pw[4 * j + 3]);
+          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dw[4 * j], dw[4 * j + 1], dw[4 * j + 2], dw[4 * j + 3]);
+        }
+      }
+      if (!alive) break;
+      fence_proxy_async_shared();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ps_full);
+      if (pend_g >= 0 && !read_out()) {
+        alive = false;
+        break;
+      }
+      pend = s;
+      pend_g = g;
+      ++g;
+    }
+    if (alive && pend_g >= 0 && mbar_wait(ps_empty, pend_g & 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+      tc_fence_after();
+      request_rope();
+      read_out();
+    }
+    // a RoPE load still in flight (an abandoned read-out) lands before the slab goes away; the
+    // stores finish reading their slabs
+    if (rope_pending) mbar_wait(&rope_full[ew], (rope_loads - 1) & 1, nullptr, SJ_DEV_ATTN_WAIT);
+    if (lane == 0) bulk_wait_all_groups();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemColsB);
+  }
+}
+
 // Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57) and the LSE times log2(e), both written
 // transposed to [head][batch][tpad] so that a step's 128 values are one contiguous run; the same
-// threads zero the (row, head) slice of the f32 dQ accumulator and, for head < hk when the items
-// are split by head, the (row, kv head) slice of the f32 dK / dV accumulator.  Eight lanes per
+// threads zero the (row, head) slice of the f32 dQ accumulator (when there is one: the banded kernel
+// has none) and, for head < hk when the items are split by head, the (row, kv head) slice of the f32
+// dK / dV accumulator.  Eight lanes per
 // (row, head), each with 8 of its 64 columns: a warp reads four rows' 128-byte head slices of O and
 // dO and writes their accumulator slices as whole lines; heads outermost, rows next.
 __global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dout, int lddo,
@@ -535,6 +1080,7 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bf
     delta_t[dst] = acc;
     lse_t[dst] = lse[static_cast<size_t>(row) * hq + h] * kLog2eB;
   }
+  if (dq_acc == nullptr) return;
   float4* z = reinterpret_cast<float4*>(dq_acc + (static_cast<size_t>(row) * hq + h) * kBD + 8 * j);
   z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
   z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -608,6 +1154,22 @@ static int bwd_head_slices(int batch, int t, int hq, int hk) {
   return (hq > hk && items < kB200Sms) ? hq / hk : 1;
 }
 
+// The banded kernel (attn_bwd_band_kernel) serves a window of at most one key tile with one query
+// head per kv head; everything else takes the general kernel.
+// (with a RoPE table, or no rotation: the banded kernel reads the table's rows by TMA).
+static bool bwd_banded(int window, int hq, int hk, float rope_theta, const float* rope_table) {
+  return window > 0 && window <= kBT && hq == hk && (rope_table != nullptr || rope_theta <= 0.f);
+}
+
+// 3-D bf16 map [batch][t][cols] (row stride ld elements) with 32 x 32 boxes and the 64-byte
+// swizzle: a store of a box never crosses into the next sequence's rows.
+static int bf16_map_bt(CUtensorMap* map, const void* ptr, int cols, int t, int batch, int ld) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(t), static_cast<uint64_t>(batch)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(ld) * 2 * t};
+  const uint32_t box[3] = {32, 32, 1};
+  return tensor_map(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
 extern "C" size_t sj_attn_workspace(int batch, int t, int hq, int hk) {
   if (batch <= 0 || t <= 0 || hq <= 0 || hk <= 0 || hq % hk) return 0;
   const size_t rows = static_cast<size_t>(batch) * t;
@@ -633,9 +1195,15 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   if (!workspace || !aligned16(workspace)) return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: workspace must be aligned");
   if (rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 7))
     return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: rope table must be 8-byte aligned");
-  static KernelAttrOnce attr_once;
-  const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(attn_bwd_tc_kernel), kSmemBwd,
-                                      "attention backward shared-memory attribute");
+  const bool band = bwd_banded(window, hq, hk, rope_theta, rope_table);
+  if (band && rope_table && (reinterpret_cast<uintptr_t>(rope_table) & 15))
+    return fail(SJ_ERR_ARGUMENT, "sj_attn_gqa_bwd: rope table must be 16-byte aligned for a window <= 128");
+  static KernelAttrOnce attr_once, band_attr_once;
+  const int attr_rc =
+      band ? ensure_max_smem(band_attr_once, reinterpret_cast<const void*>(attn_bwd_band_kernel), kSmemBand,
+                             "banded attention backward shared-memory attribute")
+           : ensure_max_smem(attr_once, reinterpret_cast<const void*>(attn_bwd_tc_kernel), kSmemBwd,
+                             "attention backward shared-memory attribute");
   if (attr_rc != SJ_OK) return attr_rc;
   cudaStream_t s = as_stream(stream);
   const size_t rows = static_cast<size_t>(batch) * t;
@@ -644,11 +1212,11 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   float* delta_t = dq_acc + rows * hq * kBD;
   float* lse_t = delta_t + static_cast<size_t>(hq) * batch * tpad;
   const int hsplit = bwd_head_slices(batch, t, hq, hk);
-  float* dkv_acc = hsplit > 1 ? lse_t + static_cast<size_t>(hq) * batch * tpad : nullptr;
+  float* dkv_acc = !band && hsplit > 1 ? lse_t + static_cast<size_t>(hq) * batch * tpad : nullptr;
   const size_t row_heads = rows * hq;
   launch(attn_delta_kernel, static_cast<unsigned>((row_heads * 8 + 255) / 256), 256, 0, s,
          static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo, lse, delta_t, lse_t,
-         dq_acc, dkv_acc, static_cast<int>(rows), t, tpad, hq, hk);
+         band ? nullptr : dq_acc, dkv_acc, static_cast<int>(rows), t, tpad, hq, hk);
   SJ_LAUNCH_CHECK("attn_delta");
   CUtensorMap maps[4];
   int rc = bf16_map(&maps[0], q, static_cast<uint64_t>(hq) * kBD, rows, ldq, kBD, kBT);
@@ -656,6 +1224,38 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   if (!rc) rc = bf16_map(&maps[2], v, static_cast<uint64_t>(hk) * kBD, rows, ldv, kBD, kBT);
   if (!rc) rc = bf16_map(&maps[3], dout, static_cast<uint64_t>(hq) * kBD, rows, lddo, kBD, kBT);
   if (rc) return rc;
+  const float2* rope_tab = reinterpret_cast<const float2*>(rope_table);
+  const float rope_log_theta = rope_table ? 0.f : (rope_theta > 0.f ? logf(rope_theta) : 0.f);
+  if (band) {
+    CUtensorMap out[4];
+    rc = bf16_map_bt(&out[0], dq, hq * kBD, t, batch, lddq);
+    if (!rc) rc = bf16_map_bt(&out[1], dk, hk * kBD, t, batch, lddk);
+    if (!rc) rc = bf16_map_bt(&out[2], dv, hk * kBD, t, batch, lddv);
+    if (!rc) {  // [t][64] f32 (cos, sin) pairs, 32 x 32 boxes (with no table, an unused map of the workspace)
+      const uint64_t dims[2] = {64, static_cast<uint64_t>(t)}, strides[1] = {256};
+      const uint32_t box[2] = {32, 32};
+      rc = tensor_map(&out[3], rope_table ? static_cast<const void*>(rope_table) : static_cast<const void*>(lse_t),
+                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (rc) return rc;
+    BandParams bp;
+    bp.t = t;
+    bp.nkt = (t + kBT - 1) / kBT;
+    bp.tiles = batch * hk * bp.nkt;
+    bp.batch = batch;
+    bp.hk = hk;
+    bp.window = window;
+    bp.scale = 0.125f;
+    bp.scale_log2 = 0.125f * kLog2eB;
+    bp.lse_t = lse_t;
+    bp.delta_t = delta_t;
+    bp.tpad = tpad;
+    bp.rope = rope_table != nullptr;
+    launch(attn_bwd_band_kernel, std::min(bp.tiles, sm_count()), kBandThreads, kSmemBand, s, maps[0], maps[1],
+           maps[2], maps[3], out[0], out[1], out[2], out[3], bp);
+    SJ_LAUNCH_CHECK("attn_bwd_band");
+    return SJ_OK;
+  }
   BwdParams p;
   p.t = t;
   p.hq = hq;
@@ -676,8 +1276,8 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   p.dv = static_cast<__nv_bfloat16*>(dv);
   p.lddk = lddk;
   p.lddv = lddv;
-  p.rope_tab = reinterpret_cast<const float2*>(rope_table);
-  p.rope_log_theta = rope_table ? 0.f : (rope_theta > 0.f ? logf(rope_theta) : 0.f);
+  p.rope_tab = rope_tab;
+  p.rope_log_theta = rope_log_theta;
   const int grid = std::min(p.items, sm_count());
   launch(attn_bwd_tc_kernel, grid, kBwdThreads, kSmemBwd, s, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("attn_bwd_tc");

@@ -568,6 +568,25 @@ static int make_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype
   return SJ_OK;
 }
 
+int tensor_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(SJ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (rank < 1 || rank > 5) return fail(SJ_ERR_ARGUMENT, "tensor map rank %d", rank);
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    estr[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, rank, const_cast<void*>(ptr), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SJ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return SJ_OK;
+}
+
 int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
              uint32_t box_outer) {
   return make_map(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, ld, box_inner, box_outer,

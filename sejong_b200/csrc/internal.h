@@ -25,6 +25,10 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // stride `ld` elements, box box_inner x box_outer (gemm.cu).
 int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
              uint32_t box_outer);
+// TMA map of any rank (gemm.cu): dims[0] contiguous elements, strides_bytes[i] the byte stride of
+// dimension i + 1, box[i] elements per copy along dimension i.
+int tensor_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
 // Per-device record of a kernel whose dynamic shared-memory limit has been raised.  Each call site
 // owns one (a function-local static); the flags are atomics, so host threads that drive different

@@ -284,6 +284,11 @@ class ByteTrainer:
     @classmethod
     def kernels_of(cls, name, args):
         """Kernel launches one C-ABI call makes."""
+        if name == "sj_attn_gqa_bwd":
+            # the banded kernel (window <= 128, one query head per kv head, a RoPE table or no
+            # rotation) needs no dQ finish pass
+            hq, hk, window, theta, table = args[20], args[21], args[23], args[24], args[25]
+            return 2 if 0 < window <= 128 and hq == hk and (table or theta <= 0) else 3
         return cls.KERNELS.get(name, 1)
 
     def _call(self, name, *args):

@@ -6,7 +6,12 @@ blocks, then the rest; ByteTrainer.grad_buckets), on NCCL's stream while later p
 run.  The step -- eagerly, and replayed from the per-phase CUDA graphs -- must equal one device's
 step on the two batches concatenated in rank order: loss, gradients, the FP64 gradient norm and the
 AdamW update.  Bars: loss and norm 1e-6 / 1e-5 relative; gradients 1e-4 relative L2 (the two ranks'
-weight-gradient sums meet in the all-reduce, one device's in one reduction); weights 1e-6 absolute.
+weight-gradient sums meet in the all-reduce, one device's in one reduction), except `global_bos`: its
+gradient is a GEMM of the batch-summed BOS gradient, which each rank rounds to bf16 (the GEMM operand)
+over its own rows, so it carries one bf16 rounding of a partial sum, 5e-3 (measured 1.9e-3).  The two
+ranks' weights after the update are bit-identical (they apply the same all-reduced gradient); against
+one device they agree to 0.05 of the learning rate: AdamW's first step moves a weight by about
+lr * g / (|g| + eps), so where |g| is near eps the step follows the gradient's last bits.
 """
 import os
 import socket
@@ -111,6 +116,8 @@ def test_two_ranks_with_overlapped_exchange_match_one_device():
     ref.optimizer_step()
     torch.cuda.synchronize()
     ref_norm, ref_w = float(ref.hyper[4]), ref.parameters()
+    from sejong_b200.train import TrainConfig
+    lr = TrainConfig().learning_rate
     worst_g, worst_w = 0.0, 0.0
     for r, res in enumerate(ranks):
         for mode in ("eager", "graph"):
@@ -119,8 +126,10 @@ def test_two_ranks_with_overlapped_exchange_match_one_device():
             assert abs(float(res[f"{mode}_norm"]) - ref_norm) < 1e-5 * ref_norm, (r, mode)
             for k, v in ref_w.items():
                 worst_w = max(worst_w, float(np.abs(res[f"w{mode[0]}/{k}"] - v).max()))
+                assert np.array_equal(res[f"w{mode[0]}/{k}"], ranks[0][f"w{mode[0]}/{k}"]), (r, mode, k)
         for k, g in ref_grads.items():
-            worst_g = max(worst_g, _rel(res[f"g/{k}"], g))
+            e = _rel(res[f"g/{k}"], g)
+            assert e < (5e-3 if k == "global_bos" else 1e-4), (r, k, e)
+            worst_g = max(worst_g, e)
     print("worst gradient", worst_g, "worst weight", worst_w)
-    assert worst_g < 1e-4
-    assert worst_w < 1e-6
+    assert worst_w < 0.05 * lr

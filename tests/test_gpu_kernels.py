@@ -263,8 +263,13 @@ def test_attention_more_items_than_sms(b, t, hq, hk, window):
 
 
 @pytest.mark.parametrize("b,t,hq,hk,window", [(2, 128, 4, 2, 0), (1, 200, 4, 4, 0), (2, 256, 4, 4, 64),
-                                              (1, 300, 6, 2, 100), (2, 512, 12, 4, 0), (1, 4096, 4, 4, 128)])
+                                              (1, 300, 6, 2, 100), (2, 512, 12, 4, 0), (1, 4096, 4, 4, 128),
+                                              (3, 1000, 2, 2, 128), (2, 300, 2, 2, 100), (5, 700, 4, 4, 2)])
 def test_attention_forward_backward(b, t, hq, hk, window):
+    """Forward and backward against the FP64 restatement.  The windowed cases with one query head per
+    kv head take the banded backward: (3, 1000, 2, 2, 128) has 48 key tiles, one per CTA, so every
+    range starts with a halo step and ends with a query tile left to the next range; (2, 300, ...)
+    ends on a partial tile; with window 2 most of each off-diagonal step is masked."""
     d = 64
     n = b * t
     cq = (hq + 2 * hk) * d
@@ -296,15 +301,18 @@ def test_attention_forward_backward(b, t, hq, hk, window):
     assert rel(dqkv[:, vo:], v.grad) < 2e-2
 
 
-def test_attention_backward_inverse_rope():
-    b, t, hq, hk, d = 1, 128, 2, 1, 64
+@pytest.mark.parametrize("b,t,hq,hk,window", [(1, 128, 2, 1, 0), (2, 384, 2, 2, 128)])
+def test_attention_backward_inverse_rope(b, t, hq, hk, window):
+    """dq and dk leave the kernel rotated back (table or inline angles); the second case runs the banded
+    backward."""
+    d = 64
     n, cq = b * t, (hq + 2 * hk) * 64
     qkv = bf(randn(n, cq))
     o = torch.empty(n, hq * d, dtype=torch.bfloat16, device=DEV)
     lse = torch.empty(n * hq, device=DEV)
     ko, vo = hq * d, (hq + hk) * d
     call("sj_attn_gqa_fwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), b, t, hq, hk,
-         d, 0, stream())
+         d, window, stream())
     do = bf(randn(n, hq * d))
     table = torch.empty(t * 64, device=DEV)
     call("sj_rope_table", ptr(table), t, 64, 0, 10000.0, stream())
@@ -314,7 +322,7 @@ def test_attention_backward_inverse_rope():
         from sejong_b200 import _lib
         delta = torch.empty(_lib.load().sj_attn_workspace(b, t, hq, hk), device=DEV)
         call("sj_attn_gqa_bwd", ptr(qkv), cq, ptr(qkv, ko), cq, ptr(qkv, vo), cq, ptr(o), hq * d, ptr(lse), ptr(do),
-             hq * d, ptr(dqkv), cq, ptr(dqkv, ko), cq, ptr(dqkv, vo), cq, ptr(delta), b, t, hq, hk, d, 0, theta,
+             hq * d, ptr(dqkv), cq, ptr(dqkv, ko), cq, ptr(dqkv, vo), cq, ptr(delta), b, t, hq, hk, d, window, theta,
              tab, stream())
         outs.append(dqkv.double().cpu())
     plain = outs[0]
