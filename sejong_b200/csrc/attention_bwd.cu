@@ -116,39 +116,6 @@ SJ_DEVICE float2 rope_cs(const float2* tab, float log_theta, int pos, int i) {
   return make_float2(c, s);
 }
 
-// The (cos, sin) pairs c0/2 .. c0/2 + 7 of position pos.  With a table all eight loads are issued
-// together (before the TMEM reads they overlap): taken one by one, each behind the previous, they
-// were most of the time of a step.
-SJ_DEVICE void rope_row8(float2 (&cs)[8], const float2* tab, float log_theta, int pos, int c0) {
-  if (tab != nullptr) {
-    const float2* src = tab + static_cast<size_t>(pos) * 32 + (c0 >> 1);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) cs[i] = src[i];
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) cs[i] = rope_cs(nullptr, log_theta, pos, (c0 >> 1) + i);
-  }
-}
-
-// 16 f32 values of one row (columns c0 .. c0+15 of a head) -> bf16, inverse-rotated by `cs` when `rope`.
-SJ_DEVICE void store_row16(__nv_bfloat16* dst, const uint32_t (&v)[16], bool rope, const float2 (&cs)[8]) {
-  uint32_t w[8];
-#pragma unroll
-  for (int c = 0; c < 16; c += 2) {
-    float a = __uint_as_float(v[c]), b = __uint_as_float(v[c + 1]);
-    if (rope) {
-      const float2 e = cs[c >> 1];
-      const float na = a * e.x + b * e.y, nb = -a * e.y + b * e.x;  // inverse rotation
-      a = na;
-      b = nb;
-    }
-    w[c >> 1] = pack_bf16x2(a, b);
-  }
-  uint4* out = reinterpret_cast<uint4*>(dst);
-  out[0] = make_uint4(w[0], w[1], w[2], w[3]);
-  out[1] = make_uint4(w[4], w[5], w[6], w[7]);
-}
-
 // 1-D bulk copy global -> shared completing on an mbarrier (16-byte aligned, size a multiple of 16).
 SJ_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -404,10 +371,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       } else if (kpos < p.t) {
         const bool rope = p.rope_tab != nullptr || p.rope_log_theta > 0.f;
-        float2 cs[8];
-        if (rope) rope_row8(cs, p.rope_tab, p.rope_log_theta, kpos, c0);
-        store_row16(p.dk + row * p.lddk + pend_it.kvh * kBD + c0, vk, rope, cs);
-        store_row16(p.dv + row * p.lddv + pend_it.kvh * kBD + c0, vv, false, cs);
+        uint32_t w[8];
+#pragma unroll
+        for (int c = 0; c < 16; c += 2) {
+          float a = __uint_as_float(vk[c]), b = __uint_as_float(vk[c + 1]);
+          if (rope) {
+            const float2 cs = rope_cs(p.rope_tab, p.rope_log_theta, kpos, (c0 + c) >> 1);
+            const float na = a * cs.x + b * cs.y, nb = -a * cs.y + b * cs.x;  // inverse rotation
+            a = na;
+            b = nb;
+          }
+          w[c >> 1] = pack_bf16x2(a, b);
+        }
+        uint4* out = reinterpret_cast<uint4*>(p.dk + row * p.lddk + pend_it.kvh * kBD + c0);
+        out[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        out[1] = make_uint4(w[4], w[5], w[6], w[7]);
+#pragma unroll
+        for (int c = 0; c < 16; c += 2) w[c >> 1] = pack_bf16x2(__uint_as_float(vv[c]), __uint_as_float(vv[c + 1]));
+        out = reinterpret_cast<uint4*>(p.dv + row * p.lddv + pend_it.kvh * kBD + c0);
+        out[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        out[1] = make_uint4(w[4], w[5], w[6], w[7]);
       }
     };
     int n = 0, g = 0;
@@ -578,18 +561,22 @@ struct BandParams {
   int rope;              // dq, dk leave rotated back by the table (map_rope)
 };
 
-// Banded kernel layout.  Eight elementwise warps (two per TMEM lane quarter) with about 200
-// registers each: a thread owns one key row of 64 query columns of S^T / dP^T, and 32 head columns
-// of a dQ / dK / dV row.  Each of those warps has a 4 KB shared-memory slab that takes, in turn, the
-// RoPE rows of a tile (32 positions x 32 floats, by TMA) and the warp's bf16 output slabs (32 rows x
-// 64 B each) that a TMA store writes out: a thread's row-wise loads and stores, 32 distinct lines per
-// instruction, were most of the kernel's time.
-constexpr int kBandEw = 8;
+// Banded kernel layout.  Sixteen elementwise warps (four per TMEM lane quarter): a thread owns one key
+// row of 32 query columns of S^T / dP^T, and 16 head columns of a dQ / dK / dV row.  Each of those
+// warps has a 2 KB shared-memory slab that takes, in turn, the RoPE rows of a tile (32 positions x 16
+// floats, by TMA) and the warp's bf16 output slabs (32 rows x 32 B each) that a TMA store writes out:
+// a thread's row-wise loads and stores, 32 distinct lines per instruction, were most of the kernel's
+// time.
+constexpr int kBandEw = 16;
+constexpr int kBandCols = kBT / (kBandEw / 4);   // query columns of S^T / dP^T per thread
+constexpr int kBandHc = kBD / (kBandEw / 4);     // head columns of dQ / dK / dV per thread
 constexpr int kBandThreads = 32 * (2 + kBandEw);
-constexpr int kBandSlab = 4096;
+constexpr int kBandSlab = 32 * kBandHc * 4;      // the RoPE rows; also two output slabs of 32 x kBandHc bf16
+constexpr int kBandOut = 32 * kBandHc * 2;
+static_assert(kBandCols == 32 && kBandHc == 16, "banded elementwise mapping");
 constexpr int kBOffStage = kOffLd + kQdStages * 2 * kBT * 4;  // 1024-aligned (194 KB)
 constexpr int kBOffBar = kBOffStage + kBandEw * kBandSlab;
-constexpr int kBandLayout = kBOffBar + 256;
+constexpr int kBandLayout = kBOffBar + 512;
 constexpr int kSmemBand = 232448;  // the per-block maximum; what the layout leaves is alignment slack
 static_assert(kBOffStage % 1024 == 0, "slabs hold 128-byte-swizzled TMA boxes");
 static_assert(kBandLayout <= kSmemBand, "banded attention backward shared memory");
@@ -611,10 +598,10 @@ SJ_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" 
 SJ_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 SJ_DEVICE void bulk_wait_all_groups() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// 32 f32 values of a row -> 16 bf16 pairs, inverse-rotated by the row's (cos, sin) pairs when `rope`.
-SJ_DEVICE void rotate_pack32(uint32_t (&w)[16], const uint32_t (&v)[32], bool rope, const float (&cs)[32]) {
+// 16 f32 values of a row -> 8 bf16 pairs, inverse-rotated by the row's (cos, sin) pairs when `rope`.
+SJ_DEVICE void rotate_pack16(uint32_t (&w)[8], const uint32_t (&v)[16], bool rope, const float (&cs)[16]) {
 #pragma unroll
-  for (int c = 0; c < 32; c += 2) {
+  for (int c = 0; c < 16; c += 2) {
     float a = __uint_as_float(v[c]), b = __uint_as_float(v[c + 1]);
     if (rope) {
       const float co = cs[c], si = cs[c + 1];
@@ -625,11 +612,11 @@ SJ_DEVICE void rotate_pack32(uint32_t (&w)[16], const uint32_t (&v)[32], bool ro
     w[c >> 1] = pack_bf16x2(a, b);
   }
 }
-// Row `lane` (64 bytes) of a 32 x 64-byte SWIZZLE_64B slab: chunk j at lane*64 + ((j ^ ((lane >> 1) & 3)) * 16).
-SJ_DEVICE void stage_row64b(uint8_t* slab, int lane, const uint32_t (&w)[16]) {
+// Row `lane` (32 bytes) of a 32 x 32-byte SWIZZLE_32B slab: chunk j at lane*32 + ((j ^ ((lane >> 2) & 1)) * 16).
+SJ_DEVICE void stage_row32b(uint8_t* slab, int lane, const uint32_t (&w)[8]) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j)
-    *reinterpret_cast<uint4*>(slab + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+  for (int j = 0; j < 2; ++j)
+    *reinterpret_cast<uint4*>(slab + lane * 32 + ((j ^ ((lane >> 2) & 1)) << 4)) =
         make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
 }
 
@@ -827,41 +814,33 @@ __global__ void __launch_bounds__(kBandThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- elementwise warps
-    // thread <-> TMEM lane r: a key row for P^T / dS^T (query columns [64 part, 64 part + 64)) and for
-    // dK / dV, a query row for dQ (head columns [32 part, 32 part + 32) of those three)
+    // thread <-> TMEM lane r: a key row for P^T / dS^T (query columns [32 part, 32 part + 32)) and for
+    // dK / dV, a query row for dQ (head columns [16 part, 16 part + 16) of those three)
     const int ew = warp - 2;
     const int quarter = warp & 3;
     const int part = ew >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const int hc = part * 32;  // head columns of dQ / dK / dV
+    const int hc = part * kBandHc;  // head columns of dQ / dK / dV
     uint8_t* slab = smem + kBOffStage + ew * kBandSlab;
     BandStep pend{};
     int pend_g = -1;
-    // RoPE rows of one tile (this warp's 32 positions, its 16 (cos, sin) pairs) in registers: the
-    // diagonal step's dQ and the off-diagonal step's dK, read out one after the other, share them
-    float cs[32];
-    int cs_tile = -1, cs_bh = -1;   // tile whose rows `cs` (or, while in flight, the slab) holds
-    int rope_loads = 0;             // loads issued into the slab (their barrier's phase count)
-    bool rope_pending = false;      // a load issued and not yet read into `cs`
+    int rope_loads = 0;          // loads issued into the slab (their barrier's phase count)
+    bool rope_pending = false;   // a load issued and not yet read
     // the rows a read-out of step `st` rotates with: its query tile (dQ) or key tile (dK)
     auto rope_tile_of = [&](const BandStep& st) { return (st.flags & kStDqLast) ? st.qt : st.kt; };
-    // request the RoPE rows of the pending step's tile when `cs` holds another tile's: the slab must
-    // first be done with the stores that read it
+    // request the RoPE rows of the pending step's read-out (this warp's 32 positions, its 8 (cos, sin)
+    // pairs), once the slab's previous stores have read it; they land while the step computes
     auto request_rope = [&]() {
       if (!p.rope || pend_g < 0 || !(pend.flags & (kStDqLast | kStKvLast))) return;
-      const int tile = rope_tile_of(pend);
-      if (tile == cs_tile && pend.bh == cs_bh) return;
       if (lane == 0) {
         bulk_wait_read_all();
-        mbar_arrive_expect_tx(&rope_full[ew], 32 * 32 * 4);
-        tma_load_2d(slab, &map_rope, &rope_full[ew], hc, tile * kBT + quarter * 32);
+        mbar_arrive_expect_tx(&rope_full[ew], kBandSlab);
+        tma_load_2d(slab, &map_rope, &rope_full[ew], hc, rope_tile_of(pend) * kBT + quarter * 32);
       }
       __syncwarp();
       ++rope_loads;
       rope_pending = true;
-      cs_tile = tile;
-      cs_bh = pend.bh;
     };
     // a completed step's finished tiles: dQ of its query tile and / or dK, dV of its key tile, staged
     // in the slab and written by TMA (the 3-D maps clip rows past the sequence end)
@@ -869,11 +848,12 @@ __global__ void __launch_bounds__(kBandThreads, 1)
       const int b = pend.bh / p.hk, h = pend.bh % p.hk;
       const bool dq_last = pend.flags & kStDqLast, kv_last = pend.flags & kStKvLast;
       if (!dq_last && !kv_last) return true;
+      float cs[16];
       if (rope_pending) {
         if (!mbar_wait(&rope_full[ew], (rope_loads - 1) & 1, abort_flag, SJ_DEV_ATTN_WAIT)) return false;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {  // 128-byte swizzled row `lane`
-          const float4 v = *reinterpret_cast<const float4*>(slab + lane * 128 + ((j ^ (lane & 7)) << 4));
+        for (int j = 0; j < 4; ++j) {  // 64-byte swizzled row `lane`
+          const float4 v = *reinterpret_cast<const float4*>(slab + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4));
           cs[4 * j] = v.x;
           cs[4 * j + 1] = v.y;
           cs[4 * j + 2] = v.z;
@@ -885,36 +865,36 @@ __global__ void __launch_bounds__(kBandThreads, 1)
       }
       __syncwarp();
       const int y = rope_tile_of(pend) * kBT + quarter * 32;
-      uint32_t w[16];
-      int used = 0;  // 2 KB halves of the slab holding staged rows
+      uint32_t w[8];
+      int used = 0;  // output slabs holding staged rows
       if (dq_last) {
         const int qb = pend.qt & 1;
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kColDQ + qb * kBD + hc, v);
+        uint32_t v[16];
+        tmem_ld_32x32b_x16(tmem + lane_off + kColDQ + qb * kBD + hc, v);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&dq_empty[qb]);
-        rotate_pack32(w, v, p.rope != 0, cs);
-        stage_row64b(slab, lane, w);
+        rotate_pack16(w, v, p.rope != 0, cs);
+        stage_row32b(slab, lane, w);
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) tma_store_3d(&map_dq, slab, h * kBD + hc, y, b);
         used = 1;
       }
       if (kv_last) {
-        uint32_t vk[32], vv[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kColDK + hc, vk);
-        tmem_ld_32x32b_x32(tmem + lane_off + kColDV + hc, vv);
+        uint32_t vk[16], vv[16];
+        tmem_ld_32x32b_x16(tmem + lane_off + kColDK + hc, vk);
+        tmem_ld_32x32b_x16(tmem + lane_off + kColDV + hc, vv);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(acc_empty);
-        rotate_pack32(w, vk, p.rope != 0, cs);
-        stage_row64b(slab + used * 2048, lane, w);
+        rotate_pack16(w, vk, p.rope != 0, cs);
+        stage_row32b(slab + used * kBandOut, lane, w);
         fence_proxy_async_shared();
         __syncwarp();
-        if (lane == 0) tma_store_3d(&map_dk, slab + used * 2048, h * kBD + hc, y, b);
+        if (lane == 0) tma_store_3d(&map_dk, slab + used * kBandOut, h * kBD + hc, y, b);
         if (used) {  // dQ and dK fill the slab: dV follows once both have been read
           if (lane == 0) {
             bulk_commit_group();
@@ -925,11 +905,11 @@ __global__ void __launch_bounds__(kBandThreads, 1)
         } else {
           used = 1;
         }
-        rotate_pack32(w, vv, false, cs);
-        stage_row64b(slab + used * 2048, lane, w);
+        rotate_pack16(w, vv, false, cs);
+        stage_row32b(slab + used * kBandOut, lane, w);
         fence_proxy_async_shared();
         __syncwarp();
-        if (lane == 0) tma_store_3d(&map_dv, slab + used * 2048, h * kBD + hc, y, b);
+        if (lane == 0) tma_store_3d(&map_dv, slab + used * kBandOut, h * kBD + hc, y, b);
       }
       if (lane == 0) bulk_commit_group();
       __syncwarp();
@@ -954,32 +934,33 @@ __global__ void __launch_bounds__(kBandThreads, 1)
         break;
       }
       tc_fence_after();
-      const float* lsl = ldbuf + qs * 2 * kBT + part * 64;
+      const float* lsl = ldbuf + qs * 2 * kBT + part * kBandCols;
       const float* dls = lsl + kBT;
-      // visible queries of this key row among this thread's 64 columns: [lo, hi]
+      // visible queries of this key row among this thread's 32 columns: [lo, hi]
       const int kpos = s.kt * kBT + r;
-      const int cbase = s.qt * kBT + part * 64;
+      const int cbase = s.qt * kBT + part * kBandCols;
       const int lo = kpos - cbase;
       const int hi = kpos < p.t ? min(kpos + p.window - 1, p.t - 1) - cbase : -1;
-      uint8_t* pt = smem + kOffPt + part * kTile;
-      uint8_t* dst = smem + kOffDSt + part * kTile;
-      // two halves of 32 columns: each read from TMEM, turned into P^T / dS^T, and (the first once
-      // the previous step's MMAs are done with the buffers) stored as four 16-byte chunks
+      // columns [32 part, 32 part + 32): 64-query half part / 2 of P^T / dS^T, 16-byte chunks 4 (part & 1) ..
+      uint8_t* pt = smem + kOffPt + (part >> 1) * kTile;
+      uint8_t* dst = smem + kOffDSt + (part >> 1) * kTile;
+      // two chunks of 16 columns, each read from TMEM, turned into P^T / dS^T and stored (the first once
+      // the previous step's MMAs are done with the buffers)
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + kColSt + part * 64 + half * 32, sv);
-        tmem_ld_32x32b_x32(tmem + lane_off + kColDPt + part * 64 + half * 32, dv);
+      for (int chunk = 0; chunk < 2; ++chunk) {
+        uint32_t sv[16], dv[16];
+        tmem_ld_32x32b_x16(tmem + lane_off + kColSt + part * kBandCols + chunk * 16, sv);
+        tmem_ld_32x32b_x16(tmem + lane_off + kColDPt + part * kBandCols + chunk * 16, dv);
         tmem_wait_ld();
-        if (half == 1) {  // S^T / dP^T are in registers: the next step's products may start
+        if (chunk == 1) {  // S^T / dP^T are in registers: the next step's products may start
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(sp_empty);
         }
-        uint32_t pw[16], dw[16];
+        uint32_t pw[8], dw[8];
 #pragma unroll
-        for (int c4 = 0; c4 < 32; c4 += 4) {
-          const int cc = half * 32 + c4;
+        for (int c4 = 0; c4 < 16; c4 += 4) {
+          const int cc = chunk * 16 + c4;
           const float4 l4 = *reinterpret_cast<const float4*>(lsl + cc);
           const float4 d4 = *reinterpret_cast<const float4*>(dls + cc);
           const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dlv[4] = {d4.x, d4.y, d4.z, d4.w};
@@ -988,14 +969,14 @@ __global__ void __launch_bounds__(kBandThreads, 1)
           for (int e = 0; e < 4; ++e) {
             const bool valid = cc + e >= lo && cc + e <= hi;
             pr[e] = ex2b(valid ? fmaf(__uint_as_float(sv[c4 + e]), p.scale_log2, -lv[e]) : -INFINITY);  // P^T
-            ds[e] = pr[e] * (__uint_as_float(dv[c4 + e]) - dlv[e]) * p.scale;                           // dS^T
+            ds[e] = pr[e] * fmaf(__uint_as_float(dv[c4 + e]), p.scale, -dlv[e]);  // dS^T (Delta pre-scaled)
           }
           pw[c4 >> 1] = pack_bf16x2(pr[0], pr[1]);
           pw[(c4 >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
           dw[c4 >> 1] = pack_bf16x2(ds[0], ds[1]);
           dw[(c4 >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
         }
-        if (half == 0) {  // P^T and dS^T overwrite the buffers once the previous step's MMAs have read them
+        if (chunk == 0) {  // P^T and dS^T overwrite the buffers once the previous step's MMAs have read them
           if (!mbar_wait(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
             alive = false;
             break;
@@ -1003,8 +984,8 @@ __global__ void __launch_bounds__(kBandThreads, 1)
           tc_fence_after();
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int off = r * 128 + (((half * 4 + j) ^ (r & 7)) << 4);
+        for (int j = 0; j < 2; ++j) {
+          const int off = r * 128 + ((((part & 1) * 4 + chunk * 2 + j) ^ (r & 7)) << 4);
           *reinterpret_cast<uint4*>(pt + off) = make_uint4(pw[4 * j], pw[4 * j + 1], pw[4 * j + 2], pw[4 * j + 3]);
           *reinterpret_cast<uint4*>(dst + off) = make_uint4(dw[4 * j], dw[4 * j + 1], dw[4 * j + 2], dw[4 * j + 3]);
         }
@@ -1042,16 +1023,17 @@ __global__ void __launch_bounds__(kBandThreads, 1)
   }
 }
 
-// Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57) and the LSE times log2(e), both written
-// transposed to [head][batch][tpad] so that a step's 128 values are one contiguous run; the same
-// threads zero the (row, head) slice of the f32 dQ accumulator (when there is one: the banded kernel
-// has none) and, for head < hk when the items are split by head, the (row, kv head) slice of the f32
-// dK / dV accumulator.  Eight lanes per
-// (row, head), each with 8 of its 64 columns: a warp reads four rows' 128-byte head slices of O and
-// dO and writes their accumulator slices as whole lines; heads outermost, rows next.
+// Delta = sum_d dO * O per (row, head) (hierarchy.py:53-57), times `delta_scale` (the banded kernel
+// takes Delta pre-multiplied by the softmax scale), and the LSE times log2(e), both written transposed
+// to [head][batch][tpad] so that a step's 128 values are one contiguous run; the same threads zero the
+// (row, head) slice of the f32 dQ accumulator (when there is one: the banded kernel has none) and, for
+// head < hk when the items are split by head, the (row, kv head) slice of the f32 dK / dV accumulator.
+// Eight lanes per (row, head), each with 8 of its 64 columns: a warp reads four rows' 128-byte head
+// slices of O and dO and writes their accumulator slices as whole lines; heads outermost, rows next
+// (measured faster than rows outermost, and than four slices per thread).
 __global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bfloat16* dout, int lddo,
                                   const float* lse, float* delta_t, float* lse_t, float* dq_acc, float* dkv_acc,
-                                  int rows, int t, int tpad, int hq, int hk) {
+                                  int rows, int t, int tpad, int hq, int hk, float delta_scale) {
   pdl_wait();
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const size_t slices = static_cast<size_t>(rows) * hq;
@@ -1077,7 +1059,7 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* o, int ldo, const __nv_bf
   if (j == 0) {
     const int b = row / t, pos = row % t;
     const size_t dst = (static_cast<size_t>(h) * (rows / t) + b) * tpad + pos;
-    delta_t[dst] = acc;
+    delta_t[dst] = acc * delta_scale;
     lse_t[dst] = lse[static_cast<size_t>(row) * hq + h] * kLog2eB;
   }
   if (dq_acc == nullptr) return;
@@ -1161,13 +1143,15 @@ static bool bwd_banded(int window, int hq, int hk, float rope_theta, const float
   return window > 0 && window <= kBT && hq == hk && (rope_table != nullptr || rope_theta <= 0.f);
 }
 
-// 3-D bf16 map [batch][t][cols] (row stride ld elements) with 32 x 32 boxes and the 64-byte
-// swizzle: a store of a box never crosses into the next sequence's rows.
+// 3-D bf16 map [batch][t][cols] (row stride ld elements) with boxes of 32 rows x the banded kernel's
+// head columns per thread and the 32-byte swizzle: a store of a box never crosses into the next
+// sequence's rows.
 static int bf16_map_bt(CUtensorMap* map, const void* ptr, int cols, int t, int batch, int ld) {
   const uint64_t dims[3] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(t), static_cast<uint64_t>(batch)};
   const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(ld) * 2 * t};
-  const uint32_t box[3] = {32, 32, 1};
-  return tensor_map(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+  const uint32_t box[3] = {kBandHc, 32, 1};
+  static_assert(kBandHc * 2 == 32, "32-byte rows: the 32-byte swizzle");
+  return tensor_map(map, ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B);
 }
 
 extern "C" size_t sj_attn_workspace(int batch, int t, int hq, int hk) {
@@ -1214,9 +1198,10 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   const int hsplit = bwd_head_slices(batch, t, hq, hk);
   float* dkv_acc = !band && hsplit > 1 ? lse_t + static_cast<size_t>(hq) * batch * tpad : nullptr;
   const size_t row_heads = rows * hq;
-  launch(attn_delta_kernel, static_cast<unsigned>((row_heads * 8 + 255) / 256), 256, 0, s,
+  const size_t delta_threads = row_heads * 8;
+  launch(attn_delta_kernel, static_cast<unsigned>((delta_threads + 255) / 256), 256, 0, s,
          static_cast<const __nv_bfloat16*>(o), ldo, static_cast<const __nv_bfloat16*>(dout), lddo, lse, delta_t, lse_t,
-         band ? nullptr : dq_acc, dkv_acc, static_cast<int>(rows), t, tpad, hq, hk);
+         band ? nullptr : dq_acc, dkv_acc, static_cast<int>(rows), t, tpad, hq, hk, band ? 0.125f : 1.0f);
   SJ_LAUNCH_CHECK("attn_delta");
   CUtensorMap maps[4];
   int rc = bf16_map(&maps[0], q, static_cast<uint64_t>(hq) * kBD, rows, ldq, kBD, kBT);
@@ -1231,11 +1216,12 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
     rc = bf16_map_bt(&out[0], dq, hq * kBD, t, batch, lddq);
     if (!rc) rc = bf16_map_bt(&out[1], dk, hk * kBD, t, batch, lddk);
     if (!rc) rc = bf16_map_bt(&out[2], dv, hk * kBD, t, batch, lddv);
-    if (!rc) {  // [t][64] f32 (cos, sin) pairs, 32 x 32 boxes (with no table, an unused map of the workspace)
+    if (!rc) {  // [t][64] f32 (cos, sin) pairs, boxes of 32 positions x 16 floats (64-byte rows)
+                // (with no table, an unused map of the workspace)
       const uint64_t dims[2] = {64, static_cast<uint64_t>(t)}, strides[1] = {256};
-      const uint32_t box[2] = {32, 32};
+      const uint32_t box[2] = {kBandHc, 32};
       rc = tensor_map(&out[3], rope_table ? static_cast<const void*>(rope_table) : static_cast<const void*>(lse_t),
-                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+                      CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
     }
     if (rc) return rc;
     BandParams bp;
