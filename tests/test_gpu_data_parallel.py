@@ -117,7 +117,7 @@ def test_two_ranks_with_overlapped_exchange_match_one_device():
     torch.cuda.synchronize()
     ref_norm, ref_w = float(ref.hyper[4]), ref.parameters()
     from sejong_b200.train import TrainConfig
-    lr = TrainConfig().learning_rate
+    lr = TrainConfig(sequence=SEQ, batch=BATCH).learning_rate
     worst_g, worst_w = 0.0, 0.0
     for r, res in enumerate(ranks):
         for mode in ("eager", "graph"):
