@@ -486,6 +486,49 @@ int sj_param_prepare(const void* x, int ldx, int n, int a, const float* q, int r
 int sj_param_materialize(const float* left, const float* coeff, int ldc, const int32_t* row_map, int a, int b, int r,
                          float* g, int ldg, int accumulate, void* stream);
 
+/* ---- control-variate SGD (crates/sejong-train/src/control_variate.rs:236-877) ---------------- */
+/* SgdState::new / refresh_bases' Engine::orthonormalize_columns (hierarchy_ops.rs:592-615; kernel
+ * hierarchy_orthogonal_column, hierarchy.py:346-397): q [rows, cols] f32 = the columns of x
+ * orthonormalised in order by two passes of Gram-Schmidt each (a column left with a squared norm
+ * below 1e-20 restarts from the unit vector at the row the earlier columns occupy least); gram (or
+ * null) [cols, cols] = q^T q.  One CTA; x and q distinct; 0 < cols <= rows. */
+int sj_cv_orthonormalize(const float* x, float* q, float* gram, int rows, int cols, void* stream);
+/* Engine::transport_coefficients (hierarchy_ops.rs:512-553, hierarchy_coefficient_transport): for
+ * each of `features` rows of h (row stride ld floats), the rank x rank coefficient at column col0 ->
+ * y (same place) = left^T C right.  rank <= 55; h and y distinct. */
+int sj_cv_transport(const float* h, int ld, int col0, const float* left, const float* right, float* y, int features,
+                    int rank, void* stream);
+/* augmented_feature (control_variate.rs:375-387): out [3 width + 1] = [row means of the encoded rows
+ * (bf16 or f32, row stride ld), row means of the f32 embedding rows of `labels` (row stride emb_ld,
+ * vocab rows), row means of their product, 1].  A label outside [0, vocab) records
+ * SJ_DEV_BAD_INDEX and counts as a zero row. */
+int sj_cv_feature(const void* encoded, int dtype, int ld, const float* embedding, int emb_ld, const int32_t* labels,
+                  int rows, int width, int vocab, float* out, void* stream);
+/* The gradient norm's correction terms (control_variate.rs:365-373,699-706), FP64 per block j:
+ * out[j] = scale * (<X_j, GU_j X_j GV_j> + t_weight <T_j, X_j>), X, T, GU, GV [blocks][rank][rank]
+ * f32 (t may be null).  Written into the optimizer's FP64 partials they enter the clipped norm. */
+int sj_cv_block_terms(const float* gram_u, const float* gram_v, const float* x, const float* t, double* out,
+                      int blocks, int rank, float t_weight, double scale, void* stream);
+/* The deferred coefficient update (control_variate.rs:796-806): a = a (1 - lr wd) - lr clip delta
+ * with lr = hyper[0] and clip = hyper[3] * loss_scale (the sj_optim_prepare output). */
+int sj_cv_deferred_update(float* a, const float* delta, const float* hyper, float weight_decay, float loss_scale,
+                          size_t n, void* stream);
+/* The bound weight of a corrected matrix (Model::bind_with_corrections, crates/sejong-model/src/
+ * lib.rs:206-250, with graph.rs:244-271's x W + ((x U) A) V^T folded into the weight):
+ * wb (bf16) = master + correction, n elements. */
+int sj_cv_bind(const float* master, const float* correction, void* wb, size_t n, void* stream);
+/* out [out_rows, cols] = 0 except out[map[i], :] = v[i, :], i < rows (a member matrix's basis rows
+ * placed at its columns of a fused weight); sj_cv_gather_rows the inverse, out[i, :] = alpha *
+ * v[map[i], :].  An index outside the target records SJ_DEV_BAD_INDEX. */
+int sj_cv_scatter_rows(const float* v, int rows, int cols, const int32_t* map, float* out, int out_rows,
+                       void* stream);
+int sj_cv_gather_rows(const float* v, int v_rows, int cols, const int32_t* map, float* out, int rows, float alpha,
+                      void* stream);
+/* The predictor gradient's outer product (control_variate.rs:718-725): out [f, n] += alpha x[i]
+ * (p[j] - beta t[j]). */
+int sj_cv_outer(const float* x, int f, const float* p, const float* t, float beta, int n, float alpha, float* out,
+                void* stream);
+
 #ifdef __cplusplus
 }
 #endif

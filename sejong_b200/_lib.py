@@ -119,6 +119,17 @@ SIGNATURES = {
                                 c_int, c_int, c_int, c_float, c_void_p, c_void_p]),
     "sj_rope_table": (c_int, [c_void_p, c_int, c_int, c_int, c_float, c_void_p]),
     "sj_attn_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "sj_cv_orthonormalize": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "sj_cv_transport": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "sj_cv_feature": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_void_p,
+                              c_void_p]),
+    "sj_cv_block_terms": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_double,
+                                  c_void_p]),
+    "sj_cv_deferred_update": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_float, c_size_t, c_void_p]),
+    "sj_cv_bind": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "sj_cv_scatter_rows": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_void_p]),
+    "sj_cv_gather_rows": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_float, c_void_p]),
+    "sj_cv_outer": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_float, c_int, c_float, c_void_p, c_void_p]),
     "sj_sumsq_partials": (c_int, [c_size_t]),
     "sj_grad_sumsq": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p]),
     "sj_optim_prepare": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_float, c_float, c_int, c_int, c_float, c_float,

@@ -95,7 +95,9 @@ __global__ void optim_prepare_kernel(const double* partials, int n_partials, dou
   if (threadIdx.x != 0) return;
   double total = 0.0;
   for (int w = 0; w < (blockDim.x >> 5); ++w) total += red[w];
-  const double norm = sqrt(total) / static_cast<double>(loss_scale);
+  // max(0): the control-variate correction terms make the total a sum of signed parts, a squared
+  // norm only up to rounding
+  const double norm = sqrt(fmax(total, 0.0)) / static_cast<double>(loss_scale);
   const double clipping = (clip_enabled && norm > static_cast<double>(clip_norm)) ? clip_norm / norm : 1.0;
   const int step = static_cast<int>(state[0]);  // optimizer.step before the update
   // TrainConfig::lr (crates/sejong-core/src/lib.rs:422-433), f32 arithmetic as in the reference

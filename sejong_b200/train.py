@@ -273,6 +273,9 @@ class ByteTrainer:
             self.ep.finalize()
         self.graph = None
         self.vjp = None
+        # weight of the staged observation's loss and gradient; None = 1 / accumulation (the control-
+        # variate trainer sets each control's own weight)
+        self.obs_weight = None
         if train.parameter_vjp is not None:
             self._init_vjp(train.parameter_vjp)
 
@@ -569,10 +572,10 @@ class ByteTrainer:
         the loss sum (as the mean over the ranks and observations), its gradient the router's."""
         w = float(self.tc.moe_aux_loss_weight)
         if w > 0:
-            acc = float(max(1, self.tc.accumulation))
+            obs = self.obs_weight if self.obs_weight is not None else 1.0 / float(max(1, self.tc.accumulation))
             erp = router_pad(E)
-            self._call("sj_moe_aux", _ptr(a["logits"]), erp, n, E, k, w, 1.0 / (self.world * acc),
-                       _ptr(self.loss_sum), _ptr(run.dlogits), erp, float(self.tc.loss_scale) / (self.world * acc),
+            self._call("sj_moe_aux", _ptr(a["logits"]), erp, n, E, k, w, obs / self.world,
+                       _ptr(self.loss_sum), _ptr(run.dlogits), erp, float(self.tc.loss_scale) * obs / self.world,
                        _ptr(run.aux_ws), self.stream)
 
     def _ep_barrier(self, ep):
@@ -667,16 +670,40 @@ class ByteTrainer:
             self._block_bwd(run, i)
 
     # ------------------------------------------------------------------ model
-    def _forward(self):
+    def encode(self):
+        """Model::encode (architecture.rs:330-351) of the staged batch: the embedding and, for the
+        hierarchical model, the encoder stage and its norm.  Returns (rows buffer, dtype code, width):
+        the f32 embedding rows of the dense model, the bf16 encoder output zE of the hierarchical one."""
         c, h = self.c, self.c.hierarchy
         n = self.rows
-        b = self.tc.batch
-        acc = float(max(1, self.tc.accumulation))
         emb, vocab = ("native_embedding", NATIVE_VOCAB) if self.values else ("embedding", VOCAB)
         if h is None:
             run = self.runs["global"]
             self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(run.x[0]), SJ_F32, n,
                        c.width, vocab, self.stream)
+            return run.x[0], SJ_F32, c.width
+        enc = self.runs["encoder"]
+        de, dg = h.encoder_width, c.width
+        if self.values:  # hidden_from (architecture.rs:353-367): native embedding -> input_projection
+            self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(self.xin), SJ_BF16, n, dg,
+                       vocab, self.stream)
+            self._gemm(_ptr(self.xin), dg, 0, self.wb_ptr("input_projection"), de, 0, _ptr(enc.x[0]), de, SJ_F32,
+                       n, de, dg)
+        else:
+            self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(enc.x[0]), SJ_F32, n, de,
+                       VOCAB, self.stream)
+        self._stage_fwd(enc)
+        self._norm(enc.x[-1], "encoder_norm", self.zE, self.invE, n, de)
+        return self.zE, SJ_BF16, de
+
+    def _forward(self):
+        c, h = self.c, self.c.hierarchy
+        n = self.rows
+        b = self.tc.batch
+        weight = self.obs_weight if self.obs_weight is not None else 1.0 / float(max(1, self.tc.accumulation))
+        if h is None:
+            run = self.runs["global"]
+            self.encode()
             self._stage_fwd(run)
             top = run.x[-1]
             top_width = c.width
@@ -684,16 +711,7 @@ class ByteTrainer:
             enc, glob, dec = self.runs["encoder"], self.runs["global"], self.runs["decoder"]
             de, dg, dd, pt = h.encoder_width, c.width, h.decoder_width, h.patch_size
             np_ = b * self.patches
-            if self.values:  # hidden_from (architecture.rs:353-367): native embedding -> input_projection
-                self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(self.xin), SJ_BF16, n, dg,
-                           vocab, self.stream)
-                self._gemm(_ptr(self.xin), dg, 0, self.wb_ptr("input_projection"), de, 0, _ptr(enc.x[0]), de, SJ_F32,
-                           n, de, dg)
-            else:
-                self._call("sj_embedding_fwd", self.wb_ptr(emb), _ptr(self.ids), _ptr(enc.x[0]), SJ_F32, n, de,
-                           VOCAB, self.stream)
-            self._stage_fwd(enc)
-            self._norm(enc.x[-1], "encoder_norm", self.zE, self.invE, n, de)
+            self.encode()
             self._call("sj_patch_pool_fwd", _ptr(self.zE), _ptr(self.pooled), b, self.tc.sequence, de, pt, self.stream)
             self._gemm(_ptr(self.pooled), de, 0, self.wb_ptr("encoder_to_global"), dg, 0, _ptr(glob.x[0]), dg,
                        SJ_F32, np_, dg, de)
@@ -720,14 +738,15 @@ class ByteTrainer:
             bt = self.tc.batch
             self._call("sj_value_head_fwd", _ptr(self.hf), top_width, n, _ptr(self.sel), bt, top_width,
                        self.w_ptr("native_value"), self.w_ptr("native_bias"), self.values, _ptr(self.labels),
-                       distributed.ce_seed(bt, self.world, self.tc.loss_scale) / acc, _ptr(self.vlogits),
-                       _ptr(self.vdlogits), _ptr(self.loss_sum), distributed.ce_seed(bt, self.world) / acc, self.stream)
+                       distributed.ce_seed(bt, self.world, self.tc.loss_scale) * weight, _ptr(self.vlogits),
+                       _ptr(self.vdlogits), _ptr(self.loss_sum), distributed.ce_seed(bt, self.world) * weight,
+                       self.stream)
             return top, top_width
         self._gemm(_ptr(self.hf), top_width, 0, self.wb_ptr("output"), VOCAB_PAD, 0, _ptr(self.logits), VOCAB_PAD,
                    SJ_F32, n, VOCAB, top_width)
         self._call("sj_cross_entropy", _ptr(self.logits), VOCAB_PAD, _ptr(self.targets), n, VOCAB,
-                   distributed.ce_seed(n, self.world, self.tc.loss_scale) / acc, 0, _ptr(self.dlogits), VOCAB_PAD,
-                   _ptr(self.loss_sum), distributed.ce_seed(n, self.world) / acc, self.stream)
+                   distributed.ce_seed(n, self.world, self.tc.loss_scale) * weight, 0, _ptr(self.dlogits), VOCAB_PAD,
+                   _ptr(self.loss_sum), distributed.ce_seed(n, self.world) * weight, self.stream)
         return top, top_width
 
     def _backward(self, top, top_width):
