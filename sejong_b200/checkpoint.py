@@ -141,7 +141,10 @@ def model_config_from_json(m, init_std=0.0):
 def train_config_json(tc):
     """TrainConfig as the reference serialises it (crates/sejong-core/src/lib.rs:308-362); fields this
     build does not use keep the reference defaults."""
-    out = {"optimizer": tc.optimizer, "control_variate": None}
+    cv = getattr(tc, "control_variate", None)
+    out = {"optimizer": tc.optimizer, "control_variate": None if cv is None else {
+        "controls": int(cv.controls), "rank": int(cv.rank), "sampling": str(cv.sampling), "strata": int(cv.strata),
+        "basis_refresh": int(cv.basis_refresh), "predictor_learning_rate": float(cv.predictor_learning_rate)}}
     if tc.parameter_vjp is not None:
         v = tc.parameter_vjp
         out["parameter_vjp"] = {"rank": v.rank, "residual_fraction": float(v.residual_fraction),

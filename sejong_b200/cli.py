@@ -61,6 +61,8 @@ def train(cfg, corpus, output, resume=None, measure=False):
     from . import checkpoint
     from .config import device_of
     from .train import ByteTrainer
+    if cfg.training.optimizer == "control_variate_sgd":
+        return train_control_variate(cfg, corpus, output, resume, measure)
     complete_started = time.perf_counter()
     tc = cfg.training
     if os.path.exists(output):
@@ -154,6 +156,112 @@ def train(cfg, corpus, output, resume=None, measure=False):
                    "scope": "initialization_training_checkpoint_and_save", "launches": trainer.launches}, fh,
                   indent=2)
     trainer.close()
+    return TrainingSummary(step, last_loss, model_dir)
+
+
+def train_control_variate(cfg, corpus, output, resume=None, measure=False):
+    """control_variate::train_configured (control_variate.rs:417-895) for optimizer
+    "control_variate_sgd": per step `accumulation` corpus batches through ControlVariateTrainer, the
+    reference's metrics.jsonl record, and checkpoints holding the flushed weights with the SGD and
+    control-variate state (SgdState::tensors)."""
+    import torch
+
+    from . import checkpoint
+    from .config import device_of
+    from .control_variate import ControlVariateTrainer
+    complete_started = time.perf_counter()
+    tc = cfg.training
+    if os.path.exists(output):
+        raise checkpoint.ArtifactError(f"training destination already exists: {output}")
+    if corpus.count <= tc.sequence:
+        raise checkpoint.ArtifactError("corpus is shorter than the training sequence")
+    dev = device_of(cfg)
+    rng = ctypes.c_uint64(int(tc.seed))
+    params, state, step = None, None, 0
+    if resume is not None:
+        manifest = checkpoint.load_manifest(resume)
+        if manifest["model"] != checkpoint.model_config_json(cfg.model, cfg.model_id, cfg.precision):
+            raise checkpoint.ArtifactError("resume model configuration differs from checkpoint")
+        if manifest.get("data_fingerprint") != corpus.fingerprint:
+            raise checkpoint.ArtifactError("resume corpus differs from checkpoint")
+        if manifest.get("training") is None:
+            raise checkpoint.ArtifactError("checkpoint training configuration missing")
+        if not _same_training(manifest["training"], checkpoint.train_config_json(tc)):
+            raise checkpoint.ArtifactError("resume SGD, predictor, schedule or batch settings differ from checkpoint")
+        if manifest.get("rng_state") is None:
+            raise checkpoint.ArtifactError("checkpoint corpus RNG state missing")
+        _, params, manifest, state = checkpoint.load(resume, cfg.model.init_std)
+        if state is None:
+            raise checkpoint.ArtifactError("resume requires SGD optimizer state")
+        rng.value = int(manifest["rng_state"])
+        step = int(manifest["step"])
+    trainer = ControlVariateTrainer(cfg.model, tc, tc.control_variate, device=dev, params=params)
+    if state is not None:
+        trainer.load_state_tensors(state)
+        trainer.step_count = step
+        trainer.tr.opt_state[0] = float(step)
+    if step >= tc.steps:
+        raise checkpoint.ArtifactError("checkpoint already reached configured training steps")
+    os.makedirs(output)
+    with open(os.path.join(output, "config.json"), "w") as fh:
+        json.dump(cfg.to_json(), fh, indent=2)
+
+    def save(directory):
+        params_now, tensors = trainer.snapshot()
+        checkpoint.save(directory, cfg.model, params_now, trainer.step_count, tensors,
+                        checkpoint.train_config_json(tc), corpus.fingerprint, rng.value, model_id=cfg.model_id,
+                        precision=cfg.precision)
+
+    acc = tc.accumulation
+    started = time.perf_counter()
+    last_loss = 0.0
+    with open(os.path.join(output, "metrics.jsonl"), "w") as log:
+        while step < tc.steps:
+            t0 = time.perf_counter()
+            observations = [corpus.batch(rng, tc.batch, tc.sequence) for _ in range(acc)]
+            m = trainer.step(observations)
+            step_seconds = time.perf_counter() - t0
+            if trainer.tr.device_error():
+                raise RuntimeError(f"device error {trainer.tr.device_error()} in step {step + 1}")
+            step = trainer.step_count
+            last_loss = m["loss"]
+            if step == 1 or step % tc.log_every == 0 or step == tc.steps:
+                controls = m["controls"]
+                backward = controls * tc.batch * tc.sequence
+                diag = m["gradient_diagnostics"]
+                record = {"step": step, "optimizer": tc.optimizer, "loss": m["loss"],
+                          "loss_estimator": "weighted_control_mean", "gradient_norm": m["gradient_norm"],
+                          "parameter_vjp": None,
+                          "parameter_vjp_statistics": {"compressed_matrices": 0, "dense_matrices": 0,
+                                                       "basis_groups": 0, "projection_groups": 0},
+                          "learning_rate": m["learning_rate"], "step_seconds": step_seconds,
+                          "elapsed_seconds": time.perf_counter() - started,
+                          "observed_bytes": acc * tc.batch * tc.sequence, "exact_bytes": backward,
+                          "backward_bytes": backward, "controls": controls,
+                          "basis_refreshed": m["basis_refreshed"],
+                          "basis_source": "control_gradient_contrast" if controls > 1 else "control_gradient",
+                          "gradient_diagnostics": diag,
+                          "diagnostic_seconds": m.get("diagnostic_seconds") if diag else None,
+                          "predictor_mse": m.get("predictor_mse") if diag else None,
+                          "control_gradient_dispersion": m.get("control_gradient_dispersion") if diag else None,
+                          "control_residual_dispersion": m.get("control_residual_dispersion") if diag else None,
+                          "residual_variance_ratio_diagnostic":
+                              m.get("residual_variance_ratio_diagnostic") if diag else None,
+                          "peak_gpu_mib": _peak_mib(trainer.tr.dev),
+                          "counters": {"launches": trainer.tr.launches} if measure else None}
+                log.write(json.dumps(record) + "\n")
+                log.flush()
+                _eprint(json.dumps(record))
+            if tc.checkpoint_every > 0 and step % tc.checkpoint_every == 0 and step < tc.steps:
+                save(os.path.join(output, "checkpoints", f"step-{step:08d}"))
+    model_dir = os.path.join(output, "model")
+    save(model_dir)
+    with open(os.path.join(output, "execution.json"), "w") as fh:
+        json.dump({"elapsed_seconds": time.perf_counter() - complete_started, "metrics_collected": bool(measure),
+                   "scope": "initialization_training_checkpoint_and_save", "launches": trainer.tr.launches}, fh,
+                  indent=2)
+    trainer.close()
+    torch.cuda.synchronize()
     return TrainingSummary(step, last_loss, model_dir)
 
 

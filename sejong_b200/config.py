@@ -27,6 +27,7 @@ TRAIN_DEFAULTS = {"optimizer": "adamw", "gradient_diagnostics_every": 0, "activa
                   "weight_decay": 0.1, "clip_norm": 1.0, "clip_enabled": True, "loss_scale": 1.0,
                   "checkpoint_every": 500, "log_every": 10, "seed": 123}
 VJP_DEFAULTS = {"rank": 16, "residual_fraction": 0.25, "block_rows": 32, "seed": 124}
+CV_FIELDS = ("controls", "rank", "sampling", "strata", "basis_refresh", "predictor_learning_rate")
 GPU_DEFAULTS = {"device": 0, "architecture": "", "wavefront": 32, "memory_mb": 0}
 
 
@@ -87,11 +88,29 @@ def model_from_table(m):
 def training_from_table(t):
     _check_keys(t, list(TRAIN_DEFAULTS) + ["parameter_vjp", "control_variate"], "training")
     v = {**TRAIN_DEFAULTS, **{k: t[k] for k in t if k not in ("parameter_vjp", "control_variate")}}
-    if v["optimizer"] not in ("adamw", "sgd"):
-        raise ConfigError(f"optimizer {v['optimizer']!r}: this build trains with adamw or sgd (the control-variate "
-                          "optimizer is not built)")
+    if v["optimizer"] not in ("adamw", "sgd", "control_variate_sgd"):
+        raise ConfigError(f"optimizer {v['optimizer']!r}: adamw, sgd or control_variate_sgd")
+    cv = None
     if t.get("control_variate") is not None:
-        raise ConfigError("[training.control_variate]: the control-variate optimizer is not built")
+        from .control_variate import ControlVariateConfig
+        c = t["control_variate"]
+        _check_keys(c, CV_FIELDS, "training.control_variate")
+        missing = [k for k in CV_FIELDS if k not in c]
+        if missing:
+            raise ConfigError(f"[training.control_variate] lacks {', '.join(missing)}")
+        cv = ControlVariateConfig(controls=int(c["controls"]), rank=int(c["rank"]), sampling=str(c["sampling"]),
+                                  strata=int(c["strata"]), basis_refresh=int(c["basis_refresh"]),
+                                  predictor_learning_rate=float(c["predictor_learning_rate"]))
+    if v["optimizer"] == "control_variate_sgd":
+        # TrainConfig::validate (crates/sejong-core/src/lib.rs:380-396)
+        if cv is None:
+            raise ConfigError("control_variate_sgd requires an explicit training.control_variate budget")
+        try:
+            cv.validate(int(v["accumulation"]))
+        except ValueError as e:
+            raise ConfigError(str(e)) from None
+        if "parameter_vjp" in t:
+            raise ConfigError("this build's control-variate trainer takes dense gradients (no parameter_vjp)")
     if int(v["accumulation"]) < 1:
         raise ConfigError("accumulation must be positive")
     vjp = None
@@ -111,7 +130,7 @@ def training_from_table(t):
     for k in ("learning_rate", "min_learning_rate", "beta1", "beta2", "epsilon", "weight_decay", "clip_norm",
               "loss_scale"):
         kw[k] = float(kw[k])
-    tc = TrainConfig(parameter_vjp=vjp, **kw)
+    tc = TrainConfig(parameter_vjp=vjp, control_variate=cv, **kw)
     if tc.steps <= 0 or tc.sequence <= 0 or tc.batch <= 0 or tc.log_every <= 0:
         raise ConfigError("steps, sequence, batch and log_every must be positive")
     return tc

@@ -22,6 +22,7 @@ The parameter VJP is not combined with control variates here (`ControlVariateTra
 """
 import ctypes
 import math
+import time
 from dataclasses import dataclass, replace
 
 import numpy as np
@@ -150,6 +151,8 @@ class ControlVariateTrainer:
             raise ValueError("control-variate SGD with the parameter VJP is not supported by this build")
         if train.values:
             raise ValueError("control-variate SGD is the byte model's trainer (no value head)")
+        if config.hierarchy is not None and train.sequence <= config.hierarchy.patch_size:
+            raise ValueError("control-variate training sequence must exceed patch_size to observe global gradients")
         accumulation = int(train.accumulation)
         cv.validate(accumulation)
         self.cv = cv
@@ -327,6 +330,7 @@ class ControlVariateTrainer:
             call("sj_zero", _ptr(t), t.numel() * 4, self.s)
         losses = torch.zeros(controls, dtype=torch.float64, device=tr.dev)
         gsm = rsm = mse = 0.0
+        diag_seconds = 0.0
         k = 0
         for (ids, targets), w in zip(observations, weights):
             tr.stage_batch(ids, targets)
@@ -371,6 +375,7 @@ class ControlVariateTrainer:
                 self._add(_ptr(self.mean_target), _ptr(self.T), _ptr(self.mean_target), n_pred, w)
             self._add(_ptr(self.ctrl_pred), _ptr(self.pred), _ptr(self.ctrl_pred), n_pred, w)
             if diagnostics:
+                t_diag = time.perf_counter()
                 sample = self._sumsq(_ptr(tr.g), tr.layout.total) / (w * ls) ** 2
                 gsm += w * sample
                 rsm += w * sample
@@ -379,6 +384,7 @@ class ControlVariateTrainer:
                 call("sj_cv_block_terms", _ptr(self.GU), _ptr(self.GV), _ptr(self.pred), _ptr(self.T),
                      _ptr(self.terms), nb, r, -2.0, 1.0, self.s)
                 rsm += w * float(self.terms.sum().item())
+                diag_seconds += time.perf_counter() - t_diag
             call("sj_cv_outer", _ptr(self.feat), F, _ptr(self.pred), _ptr(self.T), 1.0, n_pred, 2.0 * w / rr,
                  _ptr(self.PG), self.s)
             k += 1
@@ -404,10 +410,12 @@ class ControlVariateTrainer:
         self._add(_ptr(self.P), _ptr(self.PG), _ptr(self.P), F * n_pred, -cv.predictor_learning_rate)
         base_norm = None
         if diagnostics:
+            t_diag = time.perf_counter()
             base_norm = self._sumsq(_ptr(self.G), tr.layout.total) / (ls * ls)
             call("sj_cv_block_terms", _ptr(self.GU), _ptr(self.GV), _ptr(self.ctrl_pred), _ptr(self.mean_target),
                  _ptr(self.terms), nb, r, -2.0, 1.0, self.s)
             residual_mean = base_norm + float(self.terms.sum().item())
+            diag_seconds += time.perf_counter() - t_diag
         self.step_count += 1
         if refreshed:
             self.refresh_bases()
@@ -421,6 +429,7 @@ class ControlVariateTrainer:
             gd = max(gsm - base_norm, 0.0)
             rd = max(rsm - residual_mean, 0.0)
             out.update(predictor_mse=mse, control_gradient_dispersion=gd, control_residual_dispersion=rd,
+                       diagnostic_seconds=diag_seconds,
                        residual_variance_ratio_diagnostic=(rd / gd if controls > 1 and gd > 0 else None))
         return out
 

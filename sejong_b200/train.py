@@ -80,6 +80,9 @@ class TrainConfig:
     # recompute the forward of each global-stage block inside the backward from its saved input
     # instead of keeping its activations (Graph::checkpoint, crates/sejong-gpu/src/graph.rs:151-174)
     activation_checkpointing: bool = False
+    # the control-variate budget (a control_variate.ControlVariateConfig) of optimizer
+    # "control_variate_sgd", which control_variate.ControlVariateTrainer runs
+    control_variate: Optional[object] = None
 
 
 def _ptr(t, offset_elems=0):

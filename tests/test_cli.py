@@ -1,6 +1,6 @@
 """Host logic of the command line (sejong_b200/cli.py, config.py, checkpoint SGD state), no GPU:
-the reference's TOML configurations parse (the control-variate ones are refused with a message),
-unknown fields are refused, the SGD optimizer state round-trips through its 16-bit-word encoding
+the control-variate budget parses and is validated as TrainConfig::validate does
+(crates/sejong-core/src/lib.rs:380-396), unknown fields are refused, the SGD optimizer state round-trips through its 16-bit-word encoding
 (crates/sejong-train/src/control_variate.rs:42-64, 208-233), the resume check ignores only
 checkpoint_every / log_every, and the NativeValue optimizer settings follow
 OptimizerPolicy::configuration (crates/sejong-core/src/native.rs:467-518)."""
@@ -73,6 +73,33 @@ def test_unknown_and_unsupported_fields_are_refused():
         cfgmod.parse(TINY.replace('optimizer = "sgd"', 'optimizer = "control_variate_sgd"'))
     with pytest.raises(cfgmod.ConfigError):
         cfgmod.parse(TINY.replace("sequence = 128", "sequence = 130"))  # not a multiple of the patch
+
+
+CV_TABLE = """
+[training.control_variate]
+controls = 2
+rank = 2
+sampling = "stratified"
+strata = 2
+basis_refresh = 2
+predictor_learning_rate = 0.1
+"""
+
+
+def test_control_variate_budget_parses_and_is_validated():
+    base = TINY.split("[training.parameter_vjp]")[0].replace('optimizer = "sgd"', 'optimizer = "control_variate_sgd"')
+    c = cfgmod.parse(base + CV_TABLE)
+    cv = c.training.control_variate
+    assert (cv.controls, cv.rank, cv.sampling, cv.strata, cv.basis_refresh) == (2, 2, "stratified", 2, 2)
+    j = ck.train_config_json(c.training)
+    assert j["optimizer"] == "control_variate_sgd" and j["control_variate"]["predictor_learning_rate"] == 0.1
+    for bad in ("controls = 3", "strata = 3", "rank = 0", 'sampling = "random"'):
+        key = bad.split(" =")[0]
+        line = next(x for x in CV_TABLE.splitlines() if x.startswith(key + " ="))
+        with pytest.raises(cfgmod.ConfigError):
+            cfgmod.parse(base + CV_TABLE.replace(line, bad))
+    with pytest.raises(cfgmod.ConfigError):  # a parameter VJP with control variates: not combined here
+        cfgmod.parse(TINY.replace('optimizer = "sgd"', 'optimizer = "control_variate_sgd"') + CV_TABLE)
 
 
 def test_sgd_state_round_trip():

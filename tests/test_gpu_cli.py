@@ -129,3 +129,32 @@ def test_benchmark_report(tmp_path):
     assert inf["decode_tokens"] == 4 and inf["cached_vs_full_last_logits_max_abs_error"] < 0.25
     top = json.load(open(tmp_path / "bench" / "benchmark.json"))
     assert top["format"] == "sejong-measured-benchmark-v1" and len(top["runs"]) == 1
+
+
+def test_train_control_variate_resume(tmp_path):
+    """control_variate_contract.rs:25-160 on this build: the diagnostic cadence of metrics.jsonl, a run
+    resumed from its step-3 checkpoint equal to the uninterrupted one (weights and the SGD /
+    control-variate state within 2e-5, generators exactly), a learned predictor and bases that the
+    refreshes moved."""
+    from tests.test_cli import CV_TABLE
+    text = (TINY.split("[training.parameter_vjp]")[0]
+            .replace('optimizer = "sgd"', 'optimizer = "control_variate_sgd"')
+            .replace("accumulation = 2", "accumulation = 4\ngradient_diagnostics_every = 2\nclip_enabled = false")
+            + CV_TABLE)
+    o_full, o_res = _resume_case(tmp_path, text)
+    assert _max_diff(o_full, o_res) < 2e-5
+    for k in ("sgd.version", "sgd.sampling_rng", "sgd.basis_rng"):
+        assert np.array_equal(o_full[k], o_res[k]), k
+    records = [json.loads(x) for x in open(tmp_path / "full" / "metrics.jsonl")]
+    for r in records:
+        enabled = r["step"] % 2 == 0
+        assert r["gradient_diagnostics"] == enabled
+        assert isinstance(r["predictor_mse"], float) == enabled and isinstance(r["diagnostic_seconds"], float) == enabled
+        assert r["controls"] == 2 and r["loss_estimator"] == "weighted_control_mean"
+        assert r["basis_refreshed"] == enabled and r["basis_source"] == "control_gradient_contrast"
+    learned = sum(float((np.asarray(v, np.float64) ** 2).sum()) for k, v in o_full.items() if k.endswith(".predictor"))
+    assert learned > 0 and np.isfinite(learned)
+    _, _, _, at3 = ck.load(str(tmp_path / "full" / "checkpoints" / "step-00000003"))
+    moved = sum(float(((np.asarray(o_full[k], np.float64) - at3[k]) ** 2).sum()) for k in o_full
+                if k.endswith(".left") or k.endswith(".right"))
+    assert moved > 0 and np.isfinite(moved)
