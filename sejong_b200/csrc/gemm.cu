@@ -25,6 +25,19 @@
 
 namespace sj {
 
+// tcgen05.wait::ld that also names the registers the pending load writes, so no use of them can be
+// scheduled above the wait.
+SJ_DEVICE void tmem_wait_ld_dep(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 struct GemmParams {
   int M, N, K;
   int m_tiles, n_tiles, splits, kb_per_split, kb_total;
@@ -156,7 +169,11 @@ SJ_DEVICE Unit unit_of(const GemmParams& p, const int* grp, int tile) {
   return u;
 }
 
-template <int BN, bool A_MN, bool B_MN>
+// OPS: the epilogue reads operands from global memory (a residual, the RoPE table, a bias), which it
+// prefetches into registers before the accumulator is ready; without them (plain store, split-K
+// accumulate, SwiGLU) those registers go to overlapping a unit's second TMEM read with the
+// arithmetic of its first half (local SwiGLU product 51.5 -> 45.4 us).
+template <int BN, bool A_MN, bool B_MN, bool OPS>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_h,
@@ -295,10 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;           // takes column units c with c % 2 == half
     uint8_t* my_c = staging_c + ew * 4096;  // one 32 x 128 B slab per warp
     uint8_t* my_h = staging_h + ew * 2048;
-    const bool residual = p.epilogue == SJ_EPI_RESIDUAL || p.epilogue == SJ_EPI_BIAS_RESIDUAL;
-    const bool rope = p.epilogue == SJ_EPI_ROPE;
+    const bool residual = OPS && (p.epilogue == SJ_EPI_RESIDUAL || p.epilogue == SJ_EPI_BIAS_RESIDUAL);
+    const bool rope = OPS && p.epilogue == SJ_EPI_ROPE;
     const bool gelu = p.epilogue == SJ_EPI_BIAS_GELU;
-    const float* bias = p.bias;
+    const float* bias = OPS ? p.bias : nullptr;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const Unit u = unit_of(p, grp, tile);
@@ -448,11 +465,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             // two halves of 32 columns: (RoPE pairs, SwiGLU gate|up blocks and residual all stay
             // within a half)
+            uint32_t rr[2][32];
+            if (!OPS) {  // both halves requested; the second completes during the first's arithmetic
+              tmem_ld_32x32b_x32(taddr + c * 64, rr[0]);
+              tmem_wait_ld();
+              tmem_ld_32x32b_x32(taddr + c * 64 + 32, rr[1]);
+            }
 #pragma unroll
             for (int hb = 0; hb < 2; ++hb) {
               uint32_t r[32];
-              tmem_ld_32x32b_x32(taddr + c * 64 + 32 * hb, r);
-              tmem_wait_ld();
+              if (OPS) {
+                tmem_ld_32x32b_x32(taddr + c * 64 + 32 * hb, r);
+                tmem_wait_ld();
+              } else {
+                if (hb == 1) tmem_wait_ld_dep(rr[1]);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) r[j] = rr[hb][j];
+              }
               float v[32];
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
@@ -595,10 +624,12 @@ int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, 
 
 template <int BN, bool A_MN, bool B_MN>
 static int launch_gemm(const CUtensorMap* maps, const GemmParams& p, int grid, int smem, cudaStream_t stream) {
-  auto kernel = gemm_tcgen05_kernel<BN, A_MN, B_MN>;
-  static KernelAttrOnce attr_once;  // one per template instance
-  const int attr_rc =
-      ensure_max_smem(attr_once, reinterpret_cast<const void*>(kernel), kSmemLimit, "gemm shared-memory attribute");
+  const bool ops = p.epilogue == SJ_EPI_RESIDUAL || p.epilogue == SJ_EPI_BIAS_RESIDUAL || p.epilogue == SJ_EPI_ROPE ||
+                   p.bias != nullptr;
+  auto kernel = ops ? gemm_tcgen05_kernel<BN, A_MN, B_MN, true> : gemm_tcgen05_kernel<BN, A_MN, B_MN, false>;
+  static KernelAttrOnce attr_once[2];  // one per template instance
+  const int attr_rc = ensure_max_smem(attr_once[ops ? 1 : 0], reinterpret_cast<const void*>(kernel), kSmemLimit,
+                                      "gemm shared-memory attribute");
   if (attr_rc != SJ_OK) return attr_rc;
   launch(kernel, grid, kThreads, smem, stream, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("gemm launch");
