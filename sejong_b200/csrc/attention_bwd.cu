@@ -20,12 +20,13 @@
 //                 buffers.
 //               S^T_{g+1} / dP^T_{g+1} are issued before waiting for P^T_g, so the two overlap.
 //   warps 2-17  elementwise: thread <-> key row (TMEM lane), four threads per row, 32 query columns
-//               each: P^T and dS^T computed from TMEM while the previous step's MMAs still read the
-//               shared-memory buffers, then stored in bf16 into K-major 128-byte-swizzled shared
-//               memory; after handing them over, the previous step's dQ goes into an f32
-//               accumulator [rows, hq*64] with vector reductions (attn_dq_finish_kernel applies the
-//               inverse RoPE and writes bf16) and, at the end of an item, dK (inverse RoPE) and dV
-//               go out of TMEM to global bf16.
+//               each, in two chunks of 16: P^T and dS^T computed from TMEM (the first chunk while the
+//               previous step's MMAs still read the shared-memory buffers), then stored in bf16 into
+//               K-major 128-byte-swizzled shared memory; after handing them over, the previous
+//               step's dQ goes through the warp's 2 KB slab into an f32 accumulator [rows, hq*64] by
+//               a TMA reduce-add (attn_dq_finish_kernel applies the inverse RoPE and writes bf16)
+//               and, at the end of an item, dK and dV likewise into f32 partial sums (items split by
+//               head) or, rotated back, to global bf16.
 // Every wait is bounded (SJ_DEV_ATTN_WAIT in the device error word).
 #include <algorithm>
 
@@ -44,7 +45,7 @@ constexpr int kEwHead = kBD / (kEwWarps / 4);    // 16 head columns of dQ / dK /
 static_assert(kEwCols == 32 && kEwHead == 16, "elementwise mapping");
 constexpr int kBwdThreads = 32 * (2 + kEwWarps);
 constexpr int kTile = kBT * kBD * 2;              // 16 KB: 128 rows x 128 B
-// shared memory: K | V | Q ring | dO ring | P^T | dS^T | LSE/Delta ring | barriers
+// shared memory: K | V | Q ring | dO ring | P^T | dS^T | LSE/Delta ring | staging slabs | barriers
 // K, V tiles per item: two, because the MMA thread issues an item's last dV / dK / dQ after the
 // next item's first S^T / dP^T, which need that item's K and V already loaded.
 constexpr int kKvStages = 2;
@@ -56,9 +57,6 @@ constexpr int kOffDOb = kOffQb + kQdStages * kTile;
 constexpr int kOffPt = kOffDOb + kQdStages * kTile;  // 32 KB: two 64-query halves
 constexpr int kOffDSt = kOffPt + 2 * kTile;          // 32 KB
 constexpr int kOffLd = kOffDSt + 2 * kTile;          // [kQdStages][LSE*log2e 128 | Delta 128] f32
-constexpr int kOffBarB = kOffLd + kQdStages * 2 * kBT * 4;
-constexpr int kSmemBwd = kOffBarB + 512 + 1024;
-static_assert(kSmemBwd <= 232448, "attention backward shared memory above the 227 KB per-CTA limit");
 static_assert(kKvStages == 2 && kQdStages <= 4, "K/V double buffer; barrier slots");
 constexpr uint32_t kTmemColsB = 512;
 constexpr uint32_t kColSt = 0, kColDPt = 128, kColDV = 256, kColDK = 320, kColDQ = 384;  // dQ: 2 x 64
@@ -124,20 +122,62 @@ SJ_DEVICE void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* b
                : "memory");
 }
 
-SJ_DEVICE void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+SJ_DEVICE void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+SJ_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+SJ_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+SJ_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+SJ_DEVICE void bulk_wait_all_groups() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+SJ_DEVICE void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+// Row `lane` (16 f32, 64 bytes) of a 32 x 64-byte SWIZZLE_64B slab.
+SJ_DEVICE void stage_f32x16(uint8_t* slab, int lane, const uint32_t (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    *reinterpret_cast<uint4*>(slab + lane * 64 + ((j ^ ((lane >> 1) & 3)) << 4)) =
+        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
+// General kernel's staging: a 2 KB slab per elementwise warp (32 rows x 16 f32) from which TMA
+// reduce-adds dQ (and, with the items split by head, the dK / dV partials) into their f32
+// accumulators -- thread-per-row vector reductions touched 32 cache lines per instruction.
+constexpr int kGSlab = 2048;
+constexpr int kGOffStage = kOffLd + kQdStages * 2 * kBT * 4;
+constexpr int kGOffBar = kGOffStage + kEwWarps * kGSlab;
+constexpr int kGLayout = kGOffBar + 256;
+constexpr int kSmemGen = 232448;  // the per-block maximum; what the layout leaves is alignment slack
+static_assert(kGOffStage % 1024 == 0 && kGLayout <= kSmemGen, "general attention backward shared memory");
 
 }  // namespace
 
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
+                       const __grid_constant__ CUtensorMap map_dq, const __grid_constant__ CUtensorMap map_dkv,
                        const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBarB);
+  const uint32_t pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+  if (pad + kGLayout > kSmemGen) {  // uniform over the CTA, before any barrier or TMEM use
+    if (threadIdx.x == 0) record_error(SJ_DEV_SMEM_ALIGN);
+    pdl_wait();
+    return;
+  }
+  uint8_t* smem = smem_raw + pad;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGOffBar);
   uint64_t* kv_full = bars;          // kKvStages (<= 2)
   uint64_t* kv_empty = bars + 2;     // kKvStages
   uint64_t* qd_full = bars + 4;      // kQdStages (<= 4)
@@ -325,10 +365,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     // step whose dQ (and, at an item's end, dK / dV) is still to be read out of TMEM
-    int pend_g = -1, pend_h = 0, pend_qpos = 0, pend_last = 0;
+    int pend_g = -1, pend_h = 0, pend_last = 0;
     BItem pend_it{};
-    // dQ_g: f32 vector reductions into the accumulator (attn_dq_finish_kernel writes bf16); at the
-    // item's last step also its dK (inverse RoPE) and dV rows, then the TMEM is released
+    uint8_t* slab = smem + kGOffStage + (warp - 2) * kGSlab;
+    int pend_q0 = 0;
+    // dQ_g: staged in the warp's slab and reduce-added into the f32 accumulator by TMA
+    // (attn_dq_finish_kernel writes bf16); at the item's last step also its dK and dV: reduce-added
+    // into the f32 partial sums when the items are split by head, else rotated back and written
+    // in bf16; then the TMEM is released
     auto read_out = [&]() {
       const int qb = pend_g & 1;
       const int c0 = part * kEwHead;
@@ -338,14 +382,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&dq_empty[qb]);
-        if (pend_qpos < p.t) {
-          float* dst = p.dq_acc + (static_cast<size_t>(pend_it.b) * p.t + pend_qpos) * (static_cast<size_t>(p.hq) * kBD) +
-                       pend_h * kBD + c0;
-#pragma unroll
-          for (int c = 0; c < 16; c += 4)
-            red_add_v4(dst + c, __uint_as_float(v[c]), __uint_as_float(v[c + 1]), __uint_as_float(v[c + 2]),
-                       __uint_as_float(v[c + 3]));
+        if (lane == 0) {
+          mbar_arrive(&dq_empty[qb]);
+          bulk_wait_read_all();  // the slab's previous reduce has read it
+        }
+        __syncwarp();
+        stage_f32x16(slab, lane, v);
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_3d(&map_dq, slab, pend_h * kBD + c0, pend_q0 + quarter * 32, pend_it.b);
+          bulk_commit_group();
         }
       }
       if (!pend_last) return;
@@ -358,16 +405,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
-      if (kpos < p.t && p.dkv_acc != nullptr) {
+      if (p.dkv_acc != nullptr) {
         // one slice of the group's heads: f32 partial sums (the finish kernel rotates dK and
-        // writes bf16 once every slice has added its part)
-        float* dst = p.dkv_acc + (row * p.hk + pend_it.kvh) * (2 * kBD) + c0;
+        // writes bf16 once every slice has added its part); the 3-D map clips rows past the end
+        const int y = pend_it.k0 + quarter * 32;
 #pragma unroll
-        for (int c = 0; c < 16; c += 4) {
-          red_add_v4(dst + c, __uint_as_float(vk[c]), __uint_as_float(vk[c + 1]), __uint_as_float(vk[c + 2]),
-                     __uint_as_float(vk[c + 3]));
-          red_add_v4(dst + kBD + c, __uint_as_float(vv[c]), __uint_as_float(vv[c + 1]), __uint_as_float(vv[c + 2]),
-                     __uint_as_float(vv[c + 3]));
+        for (int part_kv = 0; part_kv < 2; ++part_kv) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          stage_f32x16(slab, lane, part_kv == 0 ? vk : vv);
+          fence_proxy_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_3d(&map_dkv, slab, pend_it.kvh * 2 * kBD + part_kv * kBD + c0, y, pend_it.b);
+            bulk_commit_group();
+          }
         }
       } else if (kpos < p.t) {
         const bool rope = p.rope_tab != nullptr || p.rope_log_theta > 0.f;
@@ -421,9 +473,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           hi = min(p.window > 0 ? kpos + p.window - 1 : p.t - 1, p.t - 1) - cbase;
           if (kpos >= p.t) hi = -1;
         }
-        // this thread's 32 query columns of S^T and dP^T: P^T and dS^T are computed and packed to
-        // bf16 while the previous step's MMAs may still read the buffers
-        uint32_t pw[16], dw[16];
+        // this thread's 32 query columns of S^T and dP^T, in two chunks of 16: P^T and dS^T are computed
+        // and packed to bf16 (the first chunk while the previous step's MMAs may still read the
+        // buffers) and stored as two 16-byte pieces each: 64-query half part / 2, chunks 4 (part & 1) ..
+        uint8_t* pt = smem + kOffPt + (part >> 1) * kTile;
+        uint8_t* dst = smem + kOffDSt + (part >> 1) * kTile;
 #pragma unroll
         for (int chunk = 0; chunk < 2; ++chunk) {
           uint32_t sv[16], dv[16];
@@ -435,6 +489,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(sp_empty);
           }
+          uint32_t pw[8], dw[8];
 #pragma unroll
           for (int c = 0; c < 16; c += 4) {
             const int cc = chunk * 16 + c;
@@ -448,29 +503,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
               pr[e] = valid ? ex2b(fmaf(__uint_as_float(sv[c + e]), p.scale_log2, -lv[e])) : 0.f;  // P^T
               ds[e] = valid ? pr[e] * (__uint_as_float(dv[c + e]) - dlv[e]) * p.scale : 0.f;       // dS^T
             }
-            pw[cc >> 1] = pack_bf16x2(pr[0], pr[1]);
-            pw[(cc >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
-            dw[cc >> 1] = pack_bf16x2(ds[0], ds[1]);
-            dw[(cc >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
+            pw[c >> 1] = pack_bf16x2(pr[0], pr[1]);
+            pw[(c >> 1) + 1] = pack_bf16x2(pr[2], pr[3]);
+            dw[c >> 1] = pack_bf16x2(ds[0], ds[1]);
+            dw[(c >> 1) + 1] = pack_bf16x2(ds[2], ds[3]);
+          }
+          if (chunk == 0) {
+            // P^T and dS^T may overwrite the buffers once the previous step's MMAs have read them
+            // (which also completes that step's dQ and, at an item's end, its dK / dV)
+            if (!mbar_wait_sleep(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
+              alive = false;
+              break;
+            }
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int off = r * 128 + ((((part & 1) * 4 + chunk * 2 + j) ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(pt + off) = make_uint4(pw[4 * j], pw[4 * j + 1], pw[4 * j + 2], pw[4 * j + 3]);
+            *reinterpret_cast<uint4*>(dst + off) = make_uint4(dw[4 * j], dw[4 * j + 1], dw[4 * j + 2], dw[4 * j + 3]);
           }
         }
-        // P^T and dS^T may overwrite the buffers once the previous step's MMAs have read them
-        // (which also completes that step's dQ and, at an item's end, its dK / dV)
-        if (!mbar_wait_sleep(ps_empty, (g & 1) ^ 1, abort_flag, SJ_DEV_ATTN_WAIT)) {
-          alive = false;
-          break;
-        }
-        tc_fence_after();
-        // columns [32 part, 32 part + 32): 64-query half part / 2, 16-byte chunks 4 (part & 1) ..
-        uint8_t* pt = smem + kOffPt + (part >> 1) * kTile;
-        uint8_t* dst = smem + kOffDSt + (part >> 1) * kTile;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c8 = (part & 1) * 4 + j;
-          const int off = r * 128 + ((c8 ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(pt + off) = make_uint4(pw[4 * j], pw[4 * j + 1], pw[4 * j + 2], pw[4 * j + 3]);
-          *reinterpret_cast<uint4*>(dst + off) = make_uint4(dw[4 * j], dw[4 * j + 1], dw[4 * j + 2], dw[4 * j + 3]);
-        }
+        if (!alive) break;
         fence_proxy_async_shared();
         tc_fence_before();
         __syncwarp();
@@ -479,7 +533,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         pend_g = g;
         pend_it = it;
         pend_h = it.kvh * group + it.h0 + s / it.nq;
-        pend_qpos = q0 + r;
+        pend_q0 = q0;
         pend_last = s == steps - 1;
       }
     }
@@ -488,6 +542,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tc_fence_after();
       read_out();
     }
+    if (lane == 0) bulk_wait_all_groups();  // the reduces have read their slabs
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -581,22 +637,6 @@ constexpr int kSmemBand = 232448;  // the per-block maximum; what the layout lea
 static_assert(kBOffStage % 1024 == 0, "slabs hold 128-byte-swizzled TMA boxes");
 static_assert(kBandLayout <= kSmemBand, "banded attention backward shared memory");
 
-SJ_DEVICE void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-SJ_DEVICE void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-SJ_DEVICE void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-SJ_DEVICE void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-SJ_DEVICE void bulk_wait_all_groups() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // 16 f32 values of a row -> 8 bf16 pairs, inverse-rotated by the row's (cos, sin) pairs when `rope`.
 SJ_DEVICE void rotate_pack16(uint32_t (&w)[8], const uint32_t (&v)[16], bool rope, const float (&cs)[16]) {
@@ -1186,7 +1226,7 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   const int attr_rc =
       band ? ensure_max_smem(band_attr_once, reinterpret_cast<const void*>(attn_bwd_band_kernel), kSmemBand,
                              "banded attention backward shared-memory attribute")
-           : ensure_max_smem(attr_once, reinterpret_cast<const void*>(attn_bwd_tc_kernel), kSmemBwd,
+           : ensure_max_smem(attr_once, reinterpret_cast<const void*>(attn_bwd_tc_kernel), kSmemGen,
                              "attention backward shared-memory attribute");
   if (attr_rc != SJ_OK) return attr_rc;
   cudaStream_t s = as_stream(stream);
@@ -1265,7 +1305,27 @@ extern "C" int sj_attn_gqa_bwd(const void* q, int ldq, const void* k, int ldk, c
   p.rope_tab = rope_tab;
   p.rope_log_theta = rope_log_theta;
   const int grid = std::min(p.items, sm_count());
-  launch(attn_bwd_tc_kernel, grid, kBwdThreads, kSmemBwd, s, maps[0], maps[1], maps[2], maps[3], p);
+  // f32 accumulators as [batch][t][cols] with 32-row x 16-column boxes (64-byte rows, 64-byte swizzle)
+  CUtensorMap acc_maps[2];
+  {
+    const uint64_t dq_dims[3] = {static_cast<uint64_t>(hq) * kBD, static_cast<uint64_t>(t), static_cast<uint64_t>(batch)};
+    const uint64_t dq_str[2] = {static_cast<uint64_t>(hq) * kBD * 4, static_cast<uint64_t>(hq) * kBD * 4 * t};
+    const uint32_t box[3] = {16, 32, 1};
+    rc = tensor_map(&acc_maps[0], dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_dims, dq_str, box,
+                    CU_TENSOR_MAP_SWIZZLE_64B);
+    if (!rc && dkv_acc != nullptr) {
+      const uint64_t kv_dims[3] = {static_cast<uint64_t>(hk) * 2 * kBD, static_cast<uint64_t>(t),
+                                   static_cast<uint64_t>(batch)};
+      const uint64_t kv_str[2] = {static_cast<uint64_t>(hk) * 2 * kBD * 4, static_cast<uint64_t>(hk) * 2 * kBD * 4 * t};
+      rc = tensor_map(&acc_maps[1], dkv_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, kv_dims, kv_str, box,
+                      CU_TENSOR_MAP_SWIZZLE_64B);
+    } else {
+      acc_maps[1] = acc_maps[0];  // unused: no split items
+    }
+    if (rc) return rc;
+  }
+  launch(attn_bwd_tc_kernel, grid, kBwdThreads, kSmemGen, s, maps[0], maps[1], maps[2], maps[3], acc_maps[0],
+         acc_maps[1], p);
   SJ_LAUNCH_CHECK("attn_bwd_tc");
   const size_t quads = rows * (hq + (dkv_acc ? hk : 0)) * (kBD / 8);
   launch(attn_dq_finish_kernel, static_cast<unsigned>((quads + 255) / 256), 256, 0, s, dq_acc,
