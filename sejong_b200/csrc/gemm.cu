@@ -169,11 +169,24 @@ SJ_DEVICE Unit unit_of(const GemmParams& p, const int* grp, int tile) {
   return u;
 }
 
-// OPS: the epilogue reads operands from global memory (a residual, the RoPE table, a bias), which it
-// prefetches into registers before the accumulator is ready; without them (plain store, split-K
-// accumulate, SwiGLU) those registers go to overlapping a unit's second TMEM read with the
-// arithmetic of its first half (local SwiGLU product 51.5 -> 45.4 us).
-template <int BN, bool A_MN, bool B_MN, bool OPS>
+// Epilogue kinds, each its own kernel instance (a kernel that carried every epilogue missed in the
+// instruction cache on a quarter of its fetches): plain (store, split-K accumulate), SwiGLU,
+// residual (with an optional bias), RoPE, bias (with an optional GELU).
+constexpr int kEkPlain = 0, kEkSwiglu = 1, kEkResidual = 2, kEkRope = 3, kEkBias = 4;
+
+__host__ __device__ constexpr int epilogue_kind(int epilogue) {
+  return epilogue == SJ_EPI_SWIGLU                                            ? kEkSwiglu
+         : (epilogue == SJ_EPI_RESIDUAL || epilogue == SJ_EPI_BIAS_RESIDUAL) ? kEkResidual
+         : epilogue == SJ_EPI_ROPE                                            ? kEkRope
+         : (epilogue == SJ_EPI_BIAS || epilogue == SJ_EPI_BIAS_GELU)         ? kEkBias
+                                                                              : kEkPlain;
+}
+
+// OPS (residual, RoPE, bias): the epilogue reads operands from global memory (a residual, the RoPE
+// table, a bias), which it prefetches into registers before the accumulator is ready; without them
+// (plain store, split-K accumulate, SwiGLU) those registers go to overlapping a unit's second TMEM
+// read with the arithmetic of its first half (local SwiGLU product 51.5 -> 45.4 us).  CF32: C is f32.
+template <int BN, bool A_MN, bool B_MN, int EK, bool CF32>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_h,
@@ -181,7 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Cfg = GemmCfg<BN>;
   constexpr uint32_t IDESC = umma_idesc_bf16(kBM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
   const int stages = p.stages;
-  const bool swiglu = p.epilogue == SJ_EPI_SWIGLU;
+  constexpr bool OPS = EK == kEkResidual || EK == kEkRope || EK == kEkBias;
+  constexpr bool swiglu = EK == kEkSwiglu;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -312,10 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = ew >> 2;           // takes column units c with c % 2 == half
     uint8_t* my_c = staging_c + ew * 4096;  // one 32 x 128 B slab per warp
     uint8_t* my_h = staging_h + ew * 2048;
-    const bool residual = OPS && (p.epilogue == SJ_EPI_RESIDUAL || p.epilogue == SJ_EPI_BIAS_RESIDUAL);
-    const bool rope = OPS && p.epilogue == SJ_EPI_ROPE;
-    const bool gelu = p.epilogue == SJ_EPI_BIAS_GELU;
-    const float* bias = OPS ? p.bias : nullptr;
+    constexpr bool residual = EK == kEkResidual;
+    constexpr bool rope = EK == kEkRope;
+    const bool gelu = EK == kEkBias && p.epilogue == SJ_EPI_BIAS_GELU;
+    const float* bias = (EK == kEkBias || EK == kEkResidual) ? p.bias : nullptr;
     int local = 0;
     for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
       const Unit u = unit_of(p, grp, tile);
@@ -332,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this lane's position) are read into `pre` before the accumulator is ready, so that their
       // latency overlaps this tile's main loop instead of following each TMEM read.
       uint32_t pre[64];
-      if (p.c_f32) {
+      if constexpr (CF32) {
         // f32 units are 32 columns; the warp's i-th unit (c = half + 2i) uses pre[32 (i & 1) ...],
         // refilled with unit i + 2 once unit i has consumed it.
         constexpr int kUnits = BN / 64;
@@ -466,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // two halves of 32 columns: (RoPE pairs, SwiGLU gate|up blocks and residual all stay
             // within a half)
             uint32_t rr[2][32];
-            if (!OPS) {  // both halves requested; the second completes during the first's arithmetic
+            if constexpr (!OPS) {  // both halves requested; the second completes during the first's arithmetic
               tmem_ld_32x32b_x32(taddr + c * 64, rr[0]);
               tmem_wait_ld();
               tmem_ld_32x32b_x32(taddr + c * 64 + 32, rr[1]);
@@ -474,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int hb = 0; hb < 2; ++hb) {
               uint32_t r[32];
-              if (OPS) {
+              if constexpr (OPS) {
                 tmem_ld_32x32b_x32(taddr + c * 64 + 32 * hb, r);
                 tmem_wait_ld();
               } else {
@@ -494,7 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               }
               uint32_t w[16];
-              if (swiglu) {
+              if constexpr (swiglu) {
                 // columns come as blocks of 16 gate then the same 16 up features; g and u are
                 // rounded to bf16 before h = silu(g) * u (projection.py:464-470)
                 uint32_t hw[8];
@@ -512,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 stage_chunk64(hbuf, lane, 2 * hb, hw[0], hw[1], hw[2], hw[3]);
                 stage_chunk64(hbuf, lane, 2 * hb + 1, hw[4], hw[5], hw[6], hw[7]);
-              } else if (rope) {
+              } else if constexpr (rope) {
                 if (col0 < p.rope_cols && row_ok) {
 #pragma unroll
                   for (int j = 0; j < 32; j += 2) {  // pair (32 hb + j) / 2 of the row's (cos, sin)
@@ -523,12 +537,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     v[j + 1] = a * sn + b * cs;
                   }
                 }
-              } else if (residual && row_ok) {
+              } else if constexpr (residual) {
+                if (row_ok) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                  const float2 a = unpack_bf16x2(pre[32 * i + 16 * hb + j]);
-                  v[2 * j] += a.x;
-                  v[2 * j + 1] += a.y;
+                  for (int j = 0; j < 16; ++j) {
+                    const float2 a = unpack_bf16x2(pre[32 * i + 16 * hb + j]);
+                    v[2 * j] += a.x;
+                    v[2 * j + 1] += a.y;
+                  }
                 }
               }
 #pragma unroll
@@ -622,13 +638,11 @@ int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, 
                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int EK, bool CF32>
 static int launch_gemm(const CUtensorMap* maps, const GemmParams& p, int grid, int smem, cudaStream_t stream) {
-  const bool ops = p.epilogue == SJ_EPI_RESIDUAL || p.epilogue == SJ_EPI_BIAS_RESIDUAL || p.epilogue == SJ_EPI_ROPE ||
-                   p.bias != nullptr;
-  auto kernel = ops ? gemm_tcgen05_kernel<BN, A_MN, B_MN, true> : gemm_tcgen05_kernel<BN, A_MN, B_MN, false>;
-  static KernelAttrOnce attr_once[2];  // one per template instance
-  const int attr_rc = ensure_max_smem(attr_once[ops ? 1 : 0], reinterpret_cast<const void*>(kernel), kSmemLimit,
+  auto kernel = gemm_tcgen05_kernel<BN, A_MN, B_MN, EK, CF32>;
+  static KernelAttrOnce attr_once;  // one per template instance
+  const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(kernel), kSmemLimit,
                                       "gemm shared-memory attribute");
   if (attr_rc != SJ_OK) return attr_rc;
   launch(kernel, grid, kThreads, smem, stream, maps[0], maps[1], maps[2], maps[3], p);
@@ -636,13 +650,34 @@ static int launch_gemm(const CUtensorMap* maps, const GemmParams& p, int grid, i
   return SJ_OK;
 }
 
+// Instances: the plain epilogue for every operand major and C type; the others (forward products,
+// A K-major) for the C types they take -- SwiGLU and RoPE write bf16, residual and bias either.
+template <int BN, bool A_MN, bool B_MN>
+static int dispatch_epilogue(const CUtensorMap* maps, const GemmParams& p, int grid, int smem, cudaStream_t s) {
+  const int ek = epilogue_kind(p.epilogue);
+  if (ek == kEkPlain)
+    return p.c_f32 ? launch_gemm<BN, A_MN, B_MN, kEkPlain, true>(maps, p, grid, smem, s)
+                   : launch_gemm<BN, A_MN, B_MN, kEkPlain, false>(maps, p, grid, smem, s);
+  if constexpr (!A_MN) {
+    if (ek == kEkSwiglu && !p.c_f32) return launch_gemm<BN, false, B_MN, kEkSwiglu, false>(maps, p, grid, smem, s);
+    if (ek == kEkRope && !p.c_f32) return launch_gemm<BN, false, B_MN, kEkRope, false>(maps, p, grid, smem, s);
+    if (ek == kEkResidual)
+      return p.c_f32 ? launch_gemm<BN, false, B_MN, kEkResidual, true>(maps, p, grid, smem, s)
+                     : launch_gemm<BN, false, B_MN, kEkResidual, false>(maps, p, grid, smem, s);
+    if (ek == kEkBias)
+      return p.c_f32 ? launch_gemm<BN, false, B_MN, kEkBias, true>(maps, p, grid, smem, s)
+                     : launch_gemm<BN, false, B_MN, kEkBias, false>(maps, p, grid, smem, s);
+  }
+  return fail(SJ_ERR_UNSUPPORTED, "sj_gemm: epilogue %d with an M-major A or this C type", p.epilogue);
+}
+
 template <int BN>
 static int dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap* maps, const GemmParams& p, int grid, int smem,
                            cudaStream_t s) {
-  if (!a_mn && b_mn) return launch_gemm<BN, false, true>(maps, p, grid, smem, s);
-  if (!a_mn && !b_mn) return launch_gemm<BN, false, false>(maps, p, grid, smem, s);
-  if (a_mn && b_mn) return launch_gemm<BN, true, true>(maps, p, grid, smem, s);
-  return launch_gemm<BN, true, false>(maps, p, grid, smem, s);
+  if (!a_mn && b_mn) return dispatch_epilogue<BN, false, true>(maps, p, grid, smem, s);
+  if (!a_mn && !b_mn) return dispatch_epilogue<BN, false, false>(maps, p, grid, smem, s);
+  if (a_mn && b_mn) return dispatch_epilogue<BN, true, true>(maps, p, grid, smem, s);
+  return dispatch_epilogue<BN, true, false>(maps, p, grid, smem, s);
 }
 
 }  // namespace sj
