@@ -135,6 +135,12 @@ int sj_gemm_bias(const void* a, int lda, int a_trans, const void* b, int ldb, in
                  int c_dtype, int m, int n, int k, int epilogue, float alpha, const float* bias, void* aux,
                  int ld_aux, void* stream);
 
+/* The tile plan sj_gemm / sj_gemm_bias would launch for this shape on the current device:
+ * plan[0] = tile width BN (128, 192 or 256), plan[1] = split-K count, plan[2] = 1 when the product
+ * runs on CTA pairs (tcgen05 cta_group::2, 256-row tiles).  Nothing is launched.  Counterpart of
+ * the reference's per-shape grid choice (crates/sejong-gpu/src/projection_ops.rs:6-79). */
+int sj_gemm_plan(int m, int n, int k, int a_trans, int b_trans, int c_dtype, int epilogue, int split_k, int* plan);
+
 /* ------------------------------------------------------------------ normalisation, embedding, elementwise */
 /* Engine::norm / rmsnorm (crates/sejong-gpu/src/lib.rs:688-699; kernels.py:54-61).
  * x [rows,d] (x_dtype bf16 or f32), w f32 [d]; y bf16 [rows,d]; inv_rms f32 [rows] (optional).

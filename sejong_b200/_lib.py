@@ -26,6 +26,7 @@ SIGNATURES = {
     "sj_zipf_bytes": (c_int, [c_u64, c_double, c_void_p, c_size_t]),
     "sj_corpus_batch": (c_int, [c_void_p, c_size_t, c_u64p, c_int, c_int, c_void_p, c_void_p]),
     "sj_blake3": (c_int, [c_void_p, c_void_p, c_int, c_void_p]),
+    "sj_gemm_plan": (c_int, [c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "sj_gemm": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
                         c_int, c_float, c_void_p, c_int, c_int, c_int, c_float, c_int, c_void_p]),
     "sj_gemm_grouped": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_int,

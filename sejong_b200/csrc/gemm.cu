@@ -18,6 +18,7 @@
 // A and B may each be K-major or MN-major in global memory (the UMMA descriptor's major bit), so
 // forward (A K-major, B N-major), input-gradient (A K-major, B K-major) and weight-gradient
 // (A M-major, B N-major) products all read their operands in place.
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -69,6 +70,7 @@ constexpr int kStagingC = kEpilogueWarps * 4096;  // one 32 rows x 128 B slab pe
 constexpr int kStagingH = kEpilogueWarps * 2048;  // SwiGLU h output: 32 rows x 64 B per warp
 constexpr int kBarrierBytes = 512;  // barriers, then (grouped products) the group offsets
 constexpr int kMaxGroups = 63;
+constexpr int kPairStages = 6;  // a pair CTA's stage is 32 KB at BN = 256
 
 template <int BN>
 struct GemmCfg {
@@ -97,6 +99,96 @@ SJ_DEVICE float tanh_approx(float x) {
   asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// ---- CTA pairs (tcgen05 cta_group::2): two CTAs of a cluster compute one 256-row tile.  Each loads
+// its own 128 rows of A and half of the tile's B into its own shared memory, the even CTA issues
+// the M = 256 products for both, and each CTA's tensor memory holds the accumulator rows it owns.
+SJ_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of this CTA's shared-memory variable `p` in the shared memory of cluster CTA `rank`.
+SJ_DEVICE uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+// Bounded wait with cluster-scope acquire: the barrier receives arrivals released by the other CTA.
+SJ_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+  auto try_once = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_once()) return true;
+  const uint64_t start = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (try_once()) return true;
+    if (abort != nullptr && *abort) return false;
+    if (globaltimer() - start > kWaitLimitNs) {
+      record_error(code);
+      if (abort != nullptr) *abort = 1;
+      return false;
+    }
+  }
+}
+SJ_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of a cluster CTA (address from cluster_addr), releasing at cluster scope.
+SJ_DEVICE void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Tile load whose completion is counted on the pair's even-CTA barrier `cluster_bar`; the data lands
+// in this CTA's shared memory.
+SJ_DEVICE void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t cluster_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
+      : "memory");
+}
+SJ_DEVICE void umma_f16_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on `bar` (same offset) in both CTAs of the pair when this thread's pair products complete.
+SJ_DEVICE void umma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// Arrive once on this CTA's `bar` when this thread's pair products complete.
+SJ_DEVICE void umma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+SJ_DEVICE void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+SJ_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+SJ_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
 SJ_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 SJ_DEVICE void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 SJ_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
@@ -186,20 +278,27 @@ __host__ __device__ constexpr int epilogue_kind(int epilogue) {
 // table, a bias), which it prefetches into registers before the accumulator is ready; without them
 // (plain store, split-K accumulate, SwiGLU) those registers go to overlapping a unit's second TMEM
 // read with the arithmetic of its first half (local SwiGLU product 51.5 -> 45.4 us).  CF32: C is f32.
-template <int BN, bool A_MN, bool B_MN, int EK, bool CF32>
+// PAIR: a CTA pair computes 256 x BN tiles (cta_group::2); each CTA holds 128 rows of A and BN / 2
+// rows of B per stage, so a stage is a third smaller at BN = 256 and more of them fit.
+template <int BN, bool A_MN, bool B_MN, int EK, bool CF32, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                         const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_h,
                         const GemmParams p) {
   using Cfg = GemmCfg<BN>;
-  constexpr uint32_t IDESC = umma_idesc_bf16(kBM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+  static_assert(!PAIR || !A_MN, "CTA pairs take a K-major A");
+  constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows (K-major) or columns (MN-major) of B this CTA loads
+  constexpr uint32_t B_BYTES = B_ROWS * kBK * 2;
+  constexpr uint32_t STAGE_BYTES = Cfg::A_BYTES + B_BYTES;
+  constexpr int TILE_M = PAIR ? 2 * kBM : kBM;
+  constexpr uint32_t IDESC = umma_idesc_bf16(TILE_M, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
   const int stages = p.stages;
   constexpr bool OPS = EK == kEkResidual || EK == kEkRope || EK == kEkBias;
   constexpr bool swiglu = EK == kEkSwiglu;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* staging_c = smem + stages * Cfg::STAGE_BYTES;
+  uint8_t* staging_c = smem + stages * STAGE_BYTES;
   uint8_t* staging_h = staging_c + kStagingC;
   uint64_t* full = reinterpret_cast<uint64_t*>(staging_c + kStagingC + (swiglu ? kStagingH : 0));
   uint64_t* empty = full + stages;
@@ -213,6 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int tiles_mn = p.m_tiles * p.n_tiles;
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;       // 0: the CTA that issues the pair's products
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int unit_stride = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -221,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], kEpilogueWarps);
+      mbar_init(&acc_empty[b], (PAIR ? 2 : 1) * kEpilogueWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -231,11 +333,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_map(&map_c);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   pdl_wait();  // operands may come from the previous kernel
   if (p.group_mode != 0) {
@@ -253,46 +361,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       int it = 0;
-      for (int tile = blockIdx.x; tile < total_tiles && !*abort_flag; tile += gridDim.x) {
+      for (int tile = unit0; tile < total_tiles && !*abort_flag; tile += unit_stride) {
         const Unit u = unit_of(p, grp, tile);
-        const int m0 = u.mb * kBM, n0 = u.nb * BN;
+        const int m0 = u.mb * TILE_M + static_cast<int>(rank) * kBM;
+        const int n0 = u.nb * BN + static_cast<int>(rank) * B_ROWS;
         for (int kb = u.kb_begin; kb < u.kb_end; ++kb, ++it) {
           const int s = it % stages;
           const uint32_t round = static_cast<uint32_t>(it / stages);
           if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag, SJ_DEV_GEMM_PRODUCER_WAIT)) break;
-          uint8_t* sa = smem + s * Cfg::STAGE_BYTES;
+          uint8_t* sa = smem + s * STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
-          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
           const int k0 = kb * kBK;
-          if (A_MN) {
-            tma_load_2d(sa, &map_a, &full[s], m0, k0);
-            tma_load_2d(sa + 8192, &map_a, &full[s], m0 + 64, k0);
-          } else {
-            tma_load_2d(sa, &map_a, &full[s], k0, m0);
-          }
-          if (B_MN) {
+          if constexpr (PAIR) {
+            // both CTAs' copies complete on the even CTA's barrier, which expects the bytes of both
+            if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * STAGE_BYTES);
+            const uint32_t bar = cluster_addr(&full[s], 0);
+            tma_load_2d_pair(sa, &map_a, bar, k0, m0);
+            if (B_MN) {
 #pragma unroll
-            for (int c = 0; c < BN / 64; ++c)
-              tma_load_2d(sb + c * 8192, &map_b, &full[s], n0 + 64 * c, k0 + u.b_off);
+              for (int c = 0; c < B_ROWS / 64; ++c) tma_load_2d_pair(sb + c * 8192, &map_b, bar, n0 + 64 * c, k0);
+            } else {
+              tma_load_2d_pair(sb, &map_b, bar, k0, n0);
+            }
           } else {
-            tma_load_2d(sb, &map_b, &full[s], k0, n0 + u.b_off);
+            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            if (A_MN) {
+              tma_load_2d(sa, &map_a, &full[s], m0, k0);
+              tma_load_2d(sa + 8192, &map_a, &full[s], m0 + 64, k0);
+            } else {
+              tma_load_2d(sa, &map_a, &full[s], k0, m0);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int c = 0; c < BN / 64; ++c)
+                tma_load_2d(sb + c * 8192, &map_b, &full[s], n0 + 64 * c, k0 + u.b_off);
+            } else {
+              tma_load_2d(sb, &map_b, &full[s], k0, n0 + u.b_off);
+            }
           }
         }
       }
-      // drain: wait (bounded) for the copies still in flight into the most recent stages
-      for (int j = max(0, it - stages); j < it; ++j)
-        mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, nullptr, SJ_DEV_GEMM_DRAIN_WAIT);
+      // drain: wait (bounded) for the copies still in flight into the most recent stages (a pair's
+      // odd CTA cannot see its copies complete: they are counted on the even CTA's barriers, whose
+      // MMA thread waits for every stage before the CTAs meet at the closing cluster barrier)
+      if (!PAIR || rank == 0)
+        for (int j = max(0, it - stages); j < it; ++j)
+          mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, nullptr, SJ_DEV_GEMM_DRAIN_WAIT);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || rank == 0)) {
       int it = 0, local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < total_tiles && ok; tile += gridDim.x, ++local) {
+      for (int tile = unit0; tile < total_tiles && ok; tile += unit_stride, ++local) {
         const Unit u = unit_of(p, grp, tile);
         const int kb_begin = u.kb_begin, kb_end = u.kb_end;
         const int buf = local & 1;
         const uint32_t use = static_cast<uint32_t>(local >> 1);
-        if (!mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, SJ_DEV_GEMM_MMA_WAIT)) break;
+        const bool acc_free = PAIR ? mbar_wait_cluster(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, SJ_DEV_GEMM_MMA_WAIT)
+                                   : mbar_wait(&acc_empty[buf], (use & 1u) ^ 1u, abort_flag, SJ_DEV_GEMM_MMA_WAIT);
+        if (!acc_free) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
         for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
@@ -303,21 +430,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + s * Cfg::STAGE_BYTES);
+          const uint32_t a_base = smem_u32(smem + s * STAGE_BYTES);
           const uint32_t b_base = a_base + Cfg::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             const uint64_t da = A_MN ? umma_desc(a_base + kk * 2048, 8192, 1024) : umma_desc(a_base + kk * 32, 16, 1024);
             const uint64_t db = B_MN ? umma_desc(b_base + kk * 2048, 8192, 1024) : umma_desc(b_base + kk * 32, 16, 1024);
-            umma_f16(d_tmem, da, db, IDESC, (kb > kb_begin || kk > 0) ? 1u : 0u);
+            if constexpr (PAIR)
+              umma_f16_pair(d_tmem, da, db, IDESC, (kb > kb_begin || kk > 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, da, db, IDESC, (kb > kb_begin || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&empty[s]);
+          if constexpr (PAIR)
+            umma_commit_pair_both(&empty[s]);  // the stage is free in both CTAs
+          else
+            umma_commit(&empty[s]);
         }
         if (!ok) break;
-        umma_commit(&acc_full[buf]);
+        if constexpr (PAIR)
+          umma_commit_pair_both(&acc_full[buf]);
+        else
+          umma_commit(&acc_full[buf]);
       }
       // all issued MMAs must retire before TMEM is released
-      umma_commit(drain);
+      if constexpr (PAIR)
+        umma_commit_pair(drain);
+      else
+        umma_commit(drain);
       mbar_wait(drain, 0, nullptr, SJ_DEV_GEMM_DRAIN_WAIT);
     }
   } else {
@@ -331,14 +470,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool gelu = EK == kEkBias && p.epilogue == SJ_EPI_BIAS_GELU;
     const float* bias = (EK == kEkBias || EK == kEkResidual) ? p.bias : nullptr;
     int local = 0;
-    for (int tile = blockIdx.x; tile < total_tiles; tile += gridDim.x, ++local) {
+    // a pair's epilogue warps release the accumulator on the even CTA's barrier
+    const uint32_t acc_empty_bar0 = PAIR ? cluster_addr(&acc_empty[0], 0) : 0u;
+    for (int tile = unit0; tile < total_tiles; tile += unit_stride, ++local) {
       const Unit u = unit_of(p, grp, tile);
       const int mb = u.mb, nb = u.nb;
       const bool empty_unit = u.kb_end <= u.kb_begin;  // a group without reduction rows adds nothing
       const int c_off = u.c_off;
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
-      const int r0 = mb * kBM + quarter * 32;
+      const int r0 = mb * TILE_M + static_cast<int>(rank) * kBM + quarter * 32;
       const int row = r0 + lane;
       const bool row_ok = row < p.M;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
@@ -565,7 +706,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(acc_empty_bar0 + 8u * static_cast<uint32_t>(buf));
+        else
+          mbar_arrive(&acc_empty[buf]);
+      }
     }
     if (lane == 0) bulk_wait_all();  // staged slabs must be read out before the CTA exits
     __syncwarp();
@@ -573,9 +719,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the even CTA's products into this CTA's TMEM have retired
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 
@@ -638,46 +788,127 @@ int bf16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, 
                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EK, bool CF32>
+// `kernel` over clusters of two CTAs (programmatic serialization as in launch()).
+template <typename... KArgs, typename... Args>
+static void launch_pairs(void (*kernel)(KArgs...), int grid, int smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  [&](KArgs... coerced) {
+    void* pargs[] = {const_cast<void*>(static_cast<const void*>(&coerced))...};
+    cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kernel), pargs);
+  }(std::forward<Args>(args)...);
+}
+
+// Clusters of two CTAs (at the GEMM's thread count and the largest shared-memory size) that can be
+// resident at once on the current device: the pair kernel's persistent grid.  Asked once per device.
+static int max_pair_clusters() {
+  static std::atomic<int> cache[KernelAttrOnce::kMaxDevices];
+  static KernelAttrOnce attr_once;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const bool tracked = dev >= 0 && dev < KernelAttrOnce::kMaxDevices;
+  if (tracked) {
+    const int v = cache[dev].load(std::memory_order_acquire);
+    if (v > 0) return v;
+  }
+  auto kernel = gemm_tcgen05_kernel<256, false, false, kEkPlain, false, true>;
+  if (ensure_max_smem(attr_once, reinterpret_cast<const void*>(kernel), kSmemLimit, "gemm shared-memory attribute") !=
+      SJ_OK)
+    return 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * sm_count());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemLimit;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kernel), &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  if (tracked && n > 0) cache[dev].store(n, std::memory_order_release);
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EK, bool CF32, bool PAIR>
 static int launch_gemm(const CUtensorMap* maps, const GemmParams& p, int grid, int smem, cudaStream_t stream) {
-  auto kernel = gemm_tcgen05_kernel<BN, A_MN, B_MN, EK, CF32>;
+  auto kernel = gemm_tcgen05_kernel<BN, A_MN, B_MN, EK, CF32, PAIR>;
   static KernelAttrOnce attr_once;  // one per template instance
   const int attr_rc = ensure_max_smem(attr_once, reinterpret_cast<const void*>(kernel), kSmemLimit,
                                       "gemm shared-memory attribute");
   if (attr_rc != SJ_OK) return attr_rc;
-  launch(kernel, grid, kThreads, smem, stream, maps[0], maps[1], maps[2], maps[3], p);
+  if constexpr (PAIR)
+    launch_pairs(kernel, grid, smem, stream, maps[0], maps[1], maps[2], maps[3], p);
+  else
+    launch(kernel, grid, kThreads, smem, stream, maps[0], maps[1], maps[2], maps[3], p);
   SJ_LAUNCH_CHECK("gemm launch");
   return SJ_OK;
 }
 
 // Instances: the plain epilogue for every operand major and C type; the others (forward products,
 // A K-major) for the C types they take -- SwiGLU and RoPE write bf16, residual and bias either.
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, bool PAIR>
 static int dispatch_epilogue(const CUtensorMap* maps, const GemmParams& p, int grid, int smem, cudaStream_t s) {
   const int ek = epilogue_kind(p.epilogue);
-  if (ek == kEkPlain)
-    return p.c_f32 ? launch_gemm<BN, A_MN, B_MN, kEkPlain, true>(maps, p, grid, smem, s)
-                   : launch_gemm<BN, A_MN, B_MN, kEkPlain, false>(maps, p, grid, smem, s);
-  if constexpr (!A_MN) {
-    if (ek == kEkSwiglu && !p.c_f32) return launch_gemm<BN, false, B_MN, kEkSwiglu, false>(maps, p, grid, smem, s);
-    if (ek == kEkRope && !p.c_f32) return launch_gemm<BN, false, B_MN, kEkRope, false>(maps, p, grid, smem, s);
-    if (ek == kEkResidual)
-      return p.c_f32 ? launch_gemm<BN, false, B_MN, kEkResidual, true>(maps, p, grid, smem, s)
-                     : launch_gemm<BN, false, B_MN, kEkResidual, false>(maps, p, grid, smem, s);
-    if (ek == kEkBias)
-      return p.c_f32 ? launch_gemm<BN, false, B_MN, kEkBias, true>(maps, p, grid, smem, s)
-                     : launch_gemm<BN, false, B_MN, kEkBias, false>(maps, p, grid, smem, s);
+  if constexpr (PAIR) {  // pair instances: K-major A, BN = 256, plain and SwiGLU epilogues
+    static_assert(BN == 256 && !A_MN, "CTA pairs are instantiated at BN = 256 with a K-major A");
+    if (ek == kEkPlain)
+      return p.c_f32 ? launch_gemm<BN, false, B_MN, kEkPlain, true, true>(maps, p, grid, smem, s)
+                     : launch_gemm<BN, false, B_MN, kEkPlain, false, true>(maps, p, grid, smem, s);
+    if (ek == kEkSwiglu && !p.c_f32)
+      return launch_gemm<BN, false, B_MN, kEkSwiglu, false, true>(maps, p, grid, smem, s);
+    return fail(SJ_ERR_UNSUPPORTED, "sj_gemm: no CTA-pair kernel for epilogue %d", p.epilogue);
+  } else {
+    if (ek == kEkPlain)
+      return p.c_f32 ? launch_gemm<BN, A_MN, B_MN, kEkPlain, true, false>(maps, p, grid, smem, s)
+                     : launch_gemm<BN, A_MN, B_MN, kEkPlain, false, false>(maps, p, grid, smem, s);
+    if constexpr (!A_MN) {
+      if (ek == kEkSwiglu && !p.c_f32)
+        return launch_gemm<BN, false, B_MN, kEkSwiglu, false, false>(maps, p, grid, smem, s);
+      if (ek == kEkRope && !p.c_f32) return launch_gemm<BN, false, B_MN, kEkRope, false, false>(maps, p, grid, smem, s);
+      if (ek == kEkResidual)
+        return p.c_f32 ? launch_gemm<BN, false, B_MN, kEkResidual, true, false>(maps, p, grid, smem, s)
+                       : launch_gemm<BN, false, B_MN, kEkResidual, false, false>(maps, p, grid, smem, s);
+      if (ek == kEkBias)
+        return p.c_f32 ? launch_gemm<BN, false, B_MN, kEkBias, true, false>(maps, p, grid, smem, s)
+                       : launch_gemm<BN, false, B_MN, kEkBias, false, false>(maps, p, grid, smem, s);
+    }
+    return fail(SJ_ERR_UNSUPPORTED, "sj_gemm: epilogue %d with an M-major A or this C type", p.epilogue);
   }
-  return fail(SJ_ERR_UNSUPPORTED, "sj_gemm: epilogue %d with an M-major A or this C type", p.epilogue);
 }
 
 template <int BN>
-static int dispatch_majors(bool a_mn, bool b_mn, const CUtensorMap* maps, const GemmParams& p, int grid, int smem,
-                           cudaStream_t s) {
-  if (!a_mn && b_mn) return dispatch_epilogue<BN, false, true>(maps, p, grid, smem, s);
-  if (!a_mn && !b_mn) return dispatch_epilogue<BN, false, false>(maps, p, grid, smem, s);
-  if (a_mn && b_mn) return dispatch_epilogue<BN, true, true>(maps, p, grid, smem, s);
-  return dispatch_epilogue<BN, true, false>(maps, p, grid, smem, s);
+static int dispatch_majors(bool a_mn, bool b_mn, bool pair, const CUtensorMap* maps, const GemmParams& p, int grid,
+                           int smem, cudaStream_t s) {
+  if (pair) {
+    if constexpr (BN == 256) {
+      if (!a_mn)
+        return b_mn ? dispatch_epilogue<BN, false, true, true>(maps, p, grid, smem, s)
+                    : dispatch_epilogue<BN, false, false, true>(maps, p, grid, smem, s);
+    }
+    return fail(SJ_ERR_UNSUPPORTED, "sj_gemm: no CTA-pair kernel for this tile or operand layout");
+  }
+  if (!a_mn && b_mn) return dispatch_epilogue<BN, false, true, false>(maps, p, grid, smem, s);
+  if (!a_mn && !b_mn) return dispatch_epilogue<BN, false, false, false>(maps, p, grid, smem, s);
+  if (a_mn && b_mn) return dispatch_epilogue<BN, true, true, false>(maps, p, grid, smem, s);
+  return dispatch_epilogue<BN, true, false, false>(maps, p, grid, smem, s);
 }
 
 }  // namespace sj
@@ -692,7 +923,7 @@ struct Grouping {
 static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
                      int c_dtype, int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux,
                      int rope_cols, int rope_t, float rope_theta, int split_k, const float* bias, void* stream,
-                     const Grouping& grouping = Grouping()) {
+                     const Grouping& grouping = Grouping(), int* plan = nullptr) {
   if (m <= 0 || n <= 0 || k <= 0) return fail(SJ_ERR_SHAPE, "sj_gemm: empty problem %dx%dx%d", m, n, k);
   if (!a || !b || !c) return fail(SJ_ERR_ARGUMENT, "sj_gemm: null operand");
   if (!aligned16(a) || !aligned16(b) || !aligned16(c))
@@ -744,6 +975,7 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
   // Per FLOP a 128 x 256 tile is the most efficient (cost x1.0 per k-block), 128 x 192 costs 0.83
   // of its k-block time for 0.75 of its work, 128 x 128 about 0.8-0.88 for half of it.
   int bn = 128, splits = 1;
+  bool pair = false;
   const int candidates[3] = {128, 192, 256};
   if (epilogue == SJ_EPI_ACCUM) {
     // Weight gradients: time ~ waves x (k-blocks per unit + epilogue) x (k-block cost); split-K
@@ -796,16 +1028,30 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
         bn = cbn;
       }
     }
+    // CTA pairs: a 256 x 256 pair tile moves a third less operand data per CTA and k-block than
+    // a 128 x 256 tile (A: 128 rows, B: 128 rows), which shortens the k-block from about 920 to
+    // 780 cycles at K = 768 on B200.  That pays only where the main loop dominates: the gate/up
+    // product of the global stage (4096 x 4096 x 768: 33.1 -> 31.7 us).  Where the epilogue or
+    // the tile count bounds the time (K = 256 products, N = 768 / 1280 outputs) the pair is
+    // slower, since a pair's accumulator is free only when both CTAs' epilogues are done.
+    pair = !a_trans && grouping.mode == 0 && bn == 256 && m >= 8 * kBM && n >= 2048 && kb_total >= 12 &&
+           (epilogue == SJ_EPI_STORE || epilogue == SJ_EPI_SWIGLU) && max_pair_clusters() > 0;
   }
   if (grouping.mode != 0) splits = 1;
   const int n_tiles = (n + bn - 1) / bn;
   const int kb_per_split = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per_split - 1) / kb_per_split;  // no empty split
 
-  const int stage_bytes = (kBM + bn) * kBK * 2;
+  if (plan != nullptr) {  // the tile plan only (sj_gemm_plan)
+    plan[0] = bn;
+    plan[1] = splits;
+    plan[2] = pair ? 1 : 0;
+    return SJ_OK;
+  }
+  const int stage_bytes = (kBM + (pair ? bn / 2 : bn)) * kBK * 2;
   const int staging = kStagingC + (epilogue == SJ_EPI_SWIGLU ? kStagingH : 0);
-  // four stages: more never helped on B200 and cost up to 20% on large problems
-  const int stages = std::min(4, (kSmemLimit - 1024 - kBarrierBytes - staging) / stage_bytes);
+  // four stages for single CTAs: more never helped on B200 and cost up to 20% on large problems
+  const int stages = std::min(pair ? kPairStages : 4, (kSmemLimit - 1024 - kBarrierBytes - staging) / stage_bytes);
   if (stages < 2) return fail(SJ_ERR_CAPACITY, "sj_gemm: shared memory too small for the pipeline");
   const int smem = 1024 + stages * stage_bytes + staging + kBarrierBytes;
 
@@ -819,7 +1065,7 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
   if (b_trans)
     rc = bf16_map(&maps[1], b, static_cast<uint64_t>(k),
                   static_cast<uint64_t>(grouping.mode == 1 ? grouping.groups * grouping.b_rows : n), ldb, 64,
-                  static_cast<uint32_t>(bn));
+                  static_cast<uint32_t>(pair ? bn / 2 : bn));
   else
     rc = bf16_map(&maps[1], b, static_cast<uint64_t>(n),
                   static_cast<uint64_t>(grouping.mode == 1 ? grouping.groups * grouping.b_rows : k), ldb, 64, 64);
@@ -843,7 +1089,7 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
   p.M = m;
   p.N = n;
   p.K = k;
-  p.m_tiles = m_tiles;
+  p.m_tiles = pair ? (m + 2 * kBM - 1) / (2 * kBM) : m_tiles;
   p.n_tiles = n_tiles;
   p.splits = splits;
   p.kb_per_split = kb_per_split;
@@ -863,16 +1109,27 @@ static int gemm_impl(const void* a, int lda, int a_trans, const void* b, int ldb
   p.group_mode = grouping.mode;
   p.b_group_rows = grouping.b_rows;
   p.c_group_rows = grouping.c_rows;
-  const int total = m_tiles * n_tiles * splits * (grouping.mode == 2 ? grouping.groups : 1);
-  const int grid = std::min(total, sms);
+  const int total = p.m_tiles * n_tiles * splits * (grouping.mode == 2 ? grouping.groups : 1);
+  const int grid = pair ? 2 * std::min(total, max_pair_clusters()) : std::min(total, sms);
   const bool a_mn = a_trans != 0;   // A stored [K, M]
   const bool b_mn = b_trans == 0;   // B stored [K, N]
-  if (bn == 256) return dispatch_majors<256>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
-  if (bn == 192) return dispatch_majors<192>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
-  return dispatch_majors<128>(a_mn, b_mn, maps, p, grid, smem, as_stream(stream));
+  if (bn == 256) return dispatch_majors<256>(a_mn, b_mn, pair, maps, p, grid, smem, as_stream(stream));
+  if (bn == 192) return dispatch_majors<192>(a_mn, b_mn, pair, maps, p, grid, smem, as_stream(stream));
+  return dispatch_majors<128>(a_mn, b_mn, pair, maps, p, grid, smem, as_stream(stream));
 }
 
 }  // namespace sj
+
+extern "C" int sj_gemm_plan(int m, int n, int k, int a_trans, int b_trans, int c_dtype, int epilogue, int split_k,
+                            int* plan) {
+  if (!plan) return sj::fail(SJ_ERR_ARGUMENT, "sj_gemm_plan: null plan");
+  // operands are never read: aligned stand-in addresses pass the argument checks
+  void* dummy = reinterpret_cast<void*>(static_cast<uintptr_t>(256));
+  const int lda = a_trans ? m : k, ldb = b_trans ? k : n;
+  return sj::gemm_impl(dummy, (lda + 7) / 8 * 8, a_trans, dummy, (ldb + 7) / 8 * 8, b_trans, dummy, (n + 7) / 8 * 8,
+                       c_dtype, m, n, k, epilogue, 1.0f, dummy, (n + 7) / 8 * 8, 64, 1, 1.0f, split_k,
+                       static_cast<const float*>(dummy), nullptr, sj::Grouping(), plan);
+}
 
 extern "C" int sj_gemm(const void* a, int lda, int a_trans, const void* b, int ldb, int b_trans, void* c, int ldc,
                        int c_dtype, int m, int n, int k, int epilogue, float alpha, void* aux, int ld_aux,

@@ -165,6 +165,47 @@ def test_gemm_swiglu_epilogue():
     assert rel(gu, gu_ref) < 1e-2
 
 
+def gemm_plan(m, n, k, a_trans, b_trans, c_dtype, epi):
+    import ctypes
+    from sejong_b200 import _lib
+    plan = (ctypes.c_int * 3)()
+    assert _lib.load().sj_gemm_plan(m, n, k, a_trans, b_trans, c_dtype, epi, 0, plan) == 0
+    return list(plan)
+
+
+@pytest.mark.parametrize("m,n,k,b_trans", [(4224, 2048, 768, 0), (2048, 2304, 768, 1)])
+def test_gemm_cta_pairs(m, n, k, b_trans):
+    """Products the planner gives to CTA pairs (256-row tiles, tcgen05 cta_group::2), f32 and bf16
+    C: 4224 rows end in a pair tile whose odd CTA holds only rows past M."""
+    from sejong_b200._lib import SJ_BF16, SJ_F32
+    for cdt in (SJ_F32, SJ_BF16):
+        assert gemm_plan(m, n, k, 0, b_trans, cdt, 0) == [256, 1, 1]
+    a = bf(randn(m, k))
+    b = bf(randn(n, k) if b_trans else randn(k, n))
+    ref = ref_mm(a, 0, b, b_trans)
+    assert rel(gemm(a, 0, b, b_trans, m, n, k), ref) < 1e-4
+    assert rel(gemm(a, 0, b, b_trans, m, n, k, c_dtype=torch.bfloat16), ref) < 1e-2
+    check_device_error()
+
+
+def test_gemm_swiglu_cta_pairs():
+    """The global stage's gate/up product (4096 x 4096 x 768, SwiGLU epilogue) on CTA pairs."""
+    from sejong_b200.model import _interleave_cols
+    from sejong_b200._lib import SJ_BF16
+    m, k, f = 4096, 768, 2048
+    assert gemm_plan(m, 2 * f, k, 0, 0, SJ_BF16, 3) == [256, 1, 1]
+    x = bf(randn(m, k))
+    wg, wu = bf(randn(k, f, scale=0.1)), bf(randn(k, f, scale=0.1))
+    wgu = bf(torch.from_numpy(_interleave_cols(wg.float().cpu().numpy(), wu.float().cpu().numpy())).to(DEV))
+    h = torch.zeros(m, f, dtype=torch.bfloat16, device=DEV)
+    gu = gemm(x, 0, wgu, 0, m, 2 * f, k, c_dtype=torch.bfloat16, epi=3, aux=h, ld_aux=f)
+    g32, u32 = x.float() @ wg.float(), x.float() @ wu.float()
+    assert rel(h, ops.swiglu(bf(g32).double().cpu(), bf(u32).double().cpu())) < 2e-2
+    gu_ref = torch.from_numpy(_interleave_cols(g32.cpu().numpy(), u32.cpu().numpy()))
+    assert rel(gu, gu_ref) < 1e-2
+    check_device_error()
+
+
 def test_gemm_rope_epilogue():
     m, k, hq, hk, t = 256, 256, 4, 2, 128
     cq = (hq + 2 * hk) * 64
