@@ -59,7 +59,7 @@ CPU_SAMPLES = {"c1": (8, 512)}  # C1 is small enough for the CPU to run the whol
 # DRAM bytes (read + write) of all GEMM launches of one C3 step, from the ncu launch list of
 # `python bench.py --steps 1 --warmup 3 --no-cpu-baseline --no-kernel-timing` summarised in
 # profiles/c3_step_launch_list.txt (ncu flushes caches between launches: an upper bound)
-NCU_GEMM_DRAM_BYTES_PER_STEP = {"c3": 5.4995e9}
+NCU_GEMM_DRAM_BYTES_PER_STEP = {"c3": 5.492e9}
 NCU_TRAFFIC_SOURCE = ("ncu --metrics gpu__time_duration.sum,dram__bytes_read.sum,dram__bytes_write.sum launch list of "
                       "one C3 step (profiles/c3_step_launch_list.txt), summed over the GEMM launches; not measured in "
                       "this run")
